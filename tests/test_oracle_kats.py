@@ -1,0 +1,209 @@
+"""Pin the CPU oracle to the known answers in the reference's own unit tests.
+
+Each test cites the reference test it restates (chpe-qwen-engine, path:line).
+These run on CPU only.
+"""
+import json
+import os
+import struct
+
+import numpy as np
+import pytest
+
+import oracle_py as O
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def make_cell(quant_bits, flags=0, scale=0.0, bias=0.0, rows=0, cols=0):
+    """A zeroed 17408-byte Cell with TileMetadata/TileDims filled in
+    (geometry.zig:243-256, weight_archive.zig:92-105, chpe_engine.zig:150-155)."""
+    c = np.zeros(17408, np.uint8)
+    pl = 16448
+    c[pl + 20] = quant_bits
+    c[pl + 24:pl + 32] = np.frombuffer(struct.pack("<Q", flags), np.uint8)
+    c[pl + 32:pl + 48] = np.frombuffer(struct.pack("<ffII", scale, bias, rows, cols), np.uint8)
+    return c
+
+
+# chpe_engine.zig:1814-1838 "polymorphic GEMV 2-bit cell"
+def test_gemv_2bit_cell_kat():
+    c = make_cell(2, 0, 0.5, 0.0, 4, 128)
+    c[64:72] = 0x55  # fingerprints[0].words[0] = 0x5555555555555555 -> code 1
+    y = O.gemv_tile(c, np.ones(128, np.float32), 4)
+    assert y[0] == 16.0 and y[0] > 0 and not np.isnan(y[0])
+    assert list(y[1:]) == [0.0, 0.0, 0.0]
+
+
+# chpe_engine.zig:1840-1865 "polymorphic GEMV 4-bit cell"
+def test_gemv_4bit_cell_kat():
+    c = make_cell(4, 0, 0.25, 0.0, 4, 128)
+    c[64:64 + 64] = 0x99  # nibble 9 -> +1
+    y = O.gemv_tile(c, np.ones(128, np.float32), 4)
+    assert y[0] == 32.0
+    assert list(y[1:]) == [-256.0] * 3  # zero bytes decode to -8
+
+
+# chpe_engine.zig:1867-1891 "polymorphic GEMV 8-bit cell"
+def test_gemv_8bit_cell_kat():
+    c = make_cell(8, 0, 0.1, 0.0, 4, 128)
+    c[64:64 + 128] = 10
+    y = O.gemv_tile(c, np.ones(128, np.float32), 4)
+    assert y[0] == np.float32(1280.0) * np.float32(0.1)
+    assert abs(y[0] - 128.0) < 1e-4
+    assert list(y[1:]) == [0.0] * 3
+
+
+# chpe_engine.zig:1893-1933: forwardDecode(151644, 0) over 8192 zero bytes.
+@pytest.mark.parametrize("arch", [O.ARCH_3B, O.ARCH_9B, O.ARCH_72B])
+def test_mock_archive_forward(arch):
+    mock = np.zeros(8192, np.uint8)
+    e = O.OracleEngine(mock, arch, 16)
+    r = e.forward_decode(151644, 0)
+    assert r.all_finite and not np.isnan(r.hidden_norm) and r.hidden_norm > 0
+    # Synthetic fallbacks: logits 0.001*((v%13)-6) -> first v with v%13 == 12.
+    assert r.argmax_token == 12
+    assert r.max_logit == np.float32(0.001) * np.float32(6.0)
+    assert r.token0_logit == np.float32(0.001) * np.float32(-6.0)
+    f = e.facts()
+    assert f["archive_valid"] == 0 and f["quant_bits"] == 2
+
+
+# qwen_rope.zig:90-103 (pos 0 identity), :105-124 (norm), :149-162 (KAT at pos 1)
+def test_rope_kats():
+    vec = (np.arange(128, dtype=np.float32) + 1) * np.float32(0.1)
+    assert np.array_equal(O.apply_rope(vec, 0, 1, 128), vec)
+    r = O.apply_rope(vec, 1, 1, 128)
+    assert abs(r[0] - -5.415531) < 1e-4
+    assert abs(r[1] - -4.622832) < 1e-4
+    assert abs(r[64] - 3.596112) < 1e-4
+    assert abs(r[65] - 4.714808) < 1e-4
+    n0, n1 = float(np.sum(vec * vec)), float(np.sum(r * r))
+    assert abs(n1 - n0) / n0 < 1e-4
+
+
+# qwen_rope.zig:126-147: multi-head == per-head
+def test_rope_multihead_consistency():
+    v = (np.arange(4 * 128, dtype=np.float32) + 1) * np.float32(0.01)
+    multi = O.apply_rope(v, 2, 4, 128)
+    for h in range(4):
+        single = O.apply_rope(v[h * 128:(h + 1) * 128], 2, 1, 128)
+        assert np.array_equal(single, multi[h * 128:(h + 1) * 128])
+
+
+# qwen_mlp.zig:92-111: silu and SwiGLU
+def test_silu_swiglu_kats():
+    assert O.silu(0.0) == 0.0
+    assert abs(O.silu(1.0) - 0.7310586) < 1e-5
+    gate = [0.0, 1.0, -1.0, 2.0]
+    up = [5.0, 2.0, 3.0, 0.5]
+    out = [np.float32(O.silu(g)) * np.float32(u) for g, u in zip(gate, up)]
+    assert out[0] == 0.0
+    assert abs(out[1] - 1.462117) < 1e-4
+
+
+# qwen_rmsnorm.zig:73-90
+def test_rmsnorm_kat():
+    y = O.rms_norm(np.ones(2048, np.float32), np.full(2048, 2.0, np.float32))
+    assert np.all(np.abs(y - 2.0) < 1e-4)
+
+
+# qwen_attention.zig:144-169 (seq 1 pass-through) and :171-190 (bounds at seq 2)
+def test_attention_kats():
+    H, KV, HD = 16, 2, 128
+    k0 = np.full(KV * HD, 0.5, np.float32)
+    v0 = (np.arange(KV * HD, dtype=np.float32) + 1) * np.float32(0.1)
+    out = O.gqa_attention(np.ones(H * HD, np.float32), k0[None], v0[None], 0, H, KV, HD)
+    for h in range(H):
+        kv = h // (H // KV)
+        assert np.array_equal(out[h * HD:(h + 1) * HD], v0[kv * HD:(kv + 1) * HD])
+    kc = np.stack([np.full(KV * HD, 0.2, np.float32), np.full(KV * HD, 0.4, np.float32)])
+    vc = np.stack([np.full(KV * HD, 1.0, np.float32), np.full(KV * HD, 3.0, np.float32)])
+    out = O.gqa_attention(np.full(H * HD, 0.5, np.float32), kc, vc, 1, H, KV, HD)
+    assert np.all((out >= 1.0) & (out <= 3.0))
+
+
+# qwen3b_tensor_map.zig:21-538 (full table, parsed into the golden fixture)
+def test_3b_cell_map_matches_reference_table():
+    g = json.load(open(os.path.join(GOLDEN, "tensor_maps.json")))["qwen3b_cell"]
+    names = ["input_norm", "q_proj", "q_bias", "k_proj", "k_bias", "v_proj", "v_bias",
+             "o_proj", "post_norm", "gate_proj", "up_proj", "down_proj"]
+    for l, ref in enumerate(g["layers"]):
+        mine = dict(zip(names, O.map_3b_cell_layer(l)))
+        assert mine == {k: ref[k] for k in names}, l
+    assert g["consts"]["FINAL_NORM_RECORD"] == 94348
+
+
+# qwen72b_tensor_map.zig:89-112
+def test_72b_map_matches_reference_test():
+    g = json.load(open(os.path.join(GOLDEN, "tensor_maps.json")))["qwen72b"]["checks"]
+    names = ["input_norm", "q_proj", "q_bias", "k_proj", "k_bias", "v_proj", "v_bias",
+             "o_proj", "post_norm", "gate_proj", "up_proj", "down_proj"]
+    consts = {"RECORDS_PER_LAYER": 26789, "EMBED_TOKENS_RECORDS": 38016,
+              "FINAL_NORM_RECORD": 2181136, "LM_HEAD_RECORD_START": 2181137,
+              "TOTAL_RECORDS": 2219153}
+    for chk in g:
+        expr, val = chk["expr"], chk["value"]
+        if expr.startswith("LAYERS["):
+            l = int(expr[7:expr.index("]")])
+            field = expr.split(".")[1]
+            assert dict(zip(names, O.map_72b_layer(l)))[field] == val, expr
+        else:
+            assert consts[expr] == val, expr
+
+
+# qwen35_tensor_map.zig:7-1015 through getLayerInfo (chpe_engine.zig:1108-1131)
+def test_9b_map_matches_reference_table():
+    g = json.load(open(os.path.join(GOLDEN, "tensor_maps.json")))["qwen35_9b"]
+    e = O.OracleEngine(np.zeros(8192, np.uint8), O.ARCH_9B, 4)
+    for l, m in enumerate(g["layers"]):
+        li = e.layer_info(l)
+        full = m["is_full_attn"]
+        assert full == (l % 4 == 3)
+        assert li["input_norm"] == m["input_norm_tile"]
+        assert li["post_norm"] == m["post_norm_tile"]
+        for t in ("gate", "up", "down"):
+            assert li[f"{t}_proj"] == m[f"{t}_proj_tile"]
+            assert li[f"{t}_tiles"] == m[f"{t}_proj_tiles"]
+        if full:
+            for t in ("q", "k", "v", "o"):
+                assert li[f"{t}_proj"] == m[f"{t}_proj_tile"]
+                assert li[f"{t}_tiles"] == m[f"{t}_proj_tiles"]
+        else:  # Q8 reference-mode substitution
+            assert li["q_proj"] == m["in_proj_qkv_tile"] and li["q_tiles"] == m["in_proj_qkv_tiles"]
+            assert li["k_proj"] == m["in_proj_z_tile"] and li["k_tiles"] == m["in_proj_z_tiles"]
+            assert li["v_proj"] == m["in_proj_a_tile"] and li["v_tiles"] == 1
+            assert li["o_proj"] == m["out_proj_tile"] and li["o_tiles"] == m["out_proj_tiles"]
+        assert li["q_bias"] == li["k_bias"] == li["v_bias"] == -1
+    assert e.final_norm_index() == g["consts"]["FINAL_NORM_TILE"]
+
+
+def _hdr(magic=0x57415243, version=1, header_bytes=4096, count=0, rec=20480, cell=17408,
+         pre=3072, flags=0):
+    return struct.pack("<IIQQQQQQQ", magic, version, header_bytes, count, count, rec, cell, pre,
+                       flags)
+
+
+# weight_archive.zig:1048-1078 corruption errors, :1080-1107 dense support
+def test_archive_validation_errors():
+    assert O.validate(bytearray(100))[0] == 6  # FileTooSmall
+    buf = bytearray(4096)
+    buf[:64] = _hdr(magic=0xDEADBEEF)
+    assert O.validate(buf)[0] == 1  # InvalidMagic
+    buf[:64] = _hdr(rec=20480 + 64)
+    assert O.validate(buf)[0] == 3  # BadGeometry
+    buf[:64] = _hdr(count=1)
+    assert O.validate(buf)[0] == 4  # Truncated
+    dense = bytearray(4096 + 17408)
+    dense[:64] = _hdr(magic=0x45504843, count=1, rec=17408, cell=17408, pre=0)
+    rc, h = O.validate(dense)
+    assert rc == 0 and h.record_bytes == 17408 and h.prefetch_bytes == 0
+    raw = bytearray(4096 + 16384)
+    raw[:64] = _hdr(count=1, rec=16384, cell=16384, pre=0, flags=4)
+    assert O.validate(raw)[0] == 0
+    raw[:64] = _hdr(count=1, rec=16384, cell=17408, pre=0)
+    assert O.validate(raw)[0] == 3
+    buf[:64] = _hdr(version=2)
+    assert O.validate(buf)[0] == 2
+    buf[:64] = _hdr(header_bytes=8192)
+    assert O.validate(buf)[0] == 10
