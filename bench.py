@@ -1,0 +1,277 @@
+#!/usr/bin/env python3
+"""Benchmark: batch-1 greedy decode of chpe-qwen-engine's forwardDecode loop.
+
+Workload: Qwen2.5-3B in the repo's 4-bit dense-cell
+format (group-128 FP16 scales), random-init (seeded synthetic archive), a
+512-token prompt decoded token by token (untimed), then W warm-up and K timed
+greedy decode steps.  A step is one token through all 36 layers + LM head.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+value: tok/s with weights resident in HBM, device time (CUDA events on the
+engine stream) of K back-to-back greedy steps (each step's token is the
+previous argmax, fed back on the device).  e2e: the same steps through the C
+ABI with a pinned host->device copy of each token and a device->host copy of
+each step's logits and result, wall time.  With N > 1 (torchrun) every rank
+runs an independent replica on its own GPU (the 3B path does not shard) and
+value is the sum over ranks using the max over ranks of the time.
+--impl reference times the CPU restatement of the reference engine (the Zig
+reference cannot be built here) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import platform
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PROMPT = 512
+CONFIG_NAME = "qwen2.5-3b-w4-dense-cell"
+METRIC = "batch-1 greedy decode tok/s (Qwen2.5-3B 4-bit cells, ctx 512+)"
+BYTES_PER_WEIGHT_W4G = 0.5 + 2.0 / 128.0
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d.get("hbm_gbs", 6650.0)), "measured"
+    return 6650.0, "fallback"
+
+
+def cpu_isa() -> str:
+    try:
+        flags = open("/proc/cpuinfo").read()
+        isa = [f for f in ("avx512f", "avx2", "amx_tile") if f" {f}" in flags]
+        model = [l.split(":", 1)[1].strip() for l in flags.splitlines() if l.startswith("model name")]
+        return (model[0] if model else platform.processor()) + " [" + ",".join(isa) + "]"
+    except Exception:
+        return platform.processor()
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        self.out = ""
+        if self.proc:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        for line in (self.out or "").splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+
+
+def dist_setup(n):
+    if n <= 1:
+        return 0, 1, 0, None
+    import torch.distributed as dist
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", n))
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    dist.init_process_group("gloo", timeout=__import__("datetime").timedelta(seconds=600))
+    return rank, world, local, dist
+
+
+def max_over_ranks(dist, v: float) -> float:
+    if dist is None:
+        return v
+    import torch
+    t = torch.tensor([v], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(dist):
+    if dist is not None:
+        dist.barrier()
+
+
+def oracle_cpu_baseline(archive, steps: int, threads: int, toks) -> tuple[float, str]:
+    """The oracle (C restatement of the reference engine) decoding `steps`
+    tokens from position 0; returns tok/s."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle_py as O
+    e = O.OracleEngine(archive, O.ARCH_3B, PROMPT + 8, threads=threads)
+    e.forward_decode(int(toks[0]), 0)  # warm (page-in)
+    t0 = time.perf_counter()
+    for i in range(steps):
+        e.forward_decode(int(toks[i + 1]), i + 1)
+    dt = time.perf_counter() - t0
+    e.close()
+    return steps / dt, f"{steps} decode steps of the full model at positions 1..{steps}"
+
+
+def run_reference(args, rank, world, dist):
+    import chpe_qwen_engine_b200 as chpe
+    if rank != 0:
+        return
+    archive = chpe.synth_archive(chpe.SYNTH_3B_W4, 0, seed=0)
+    toks = np.random.default_rng(1).integers(0, 151936, args.steps + args.warmup + 2)
+    threads = os.cpu_count() or 1
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle_py as O
+    e = O.OracleEngine(archive, O.ARCH_3B, args.steps + args.warmup + 4, threads=threads)
+    for i in range(args.warmup):
+        e.forward_decode(int(toks[i]), i)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        e.forward_decode(int(toks[args.warmup + i]), args.warmup + i)
+    dt = time.perf_counter() - t0
+    v = args.steps / dt
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1000 / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u4->f32",
+        "data": "synthetic (seeded archive, random-init weights)",
+        "config": {"workload": CONFIG_NAME, "prompt": PROMPT, "archive_bytes": int(archive.size)},
+        "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": "port",
+                         "sample": f"{args.steps} decode steps at positions {args.warmup}..; "
+                                   f"CPU restatement of src/chpe_engine.zig ({cpu_isa()})"},
+        "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, rank, world, local, dist):
+    import chpe_qwen_engine_b200 as chpe
+    dev = local if world > 1 else 0
+    archive = chpe.synth_archive(chpe.SYNTH_3B_W4, 0, seed=0)
+    eng = chpe.Engine.from_bytes(archive, chpe.ARCH_3B, max_seq_len=2048, device=dev)
+    rng = np.random.default_rng(1)
+    prompt = rng.integers(0, 151936, PROMPT).astype(np.uint32)
+    eng.forward_tokens(prompt)  # positions 0..511, untimed
+    eng.bench_greedy(args.warmup)  # warm-up steps
+    barrier(dist)
+    with ClockSampler(dev) as cs:
+        ms = eng.bench_greedy(args.steps)
+    barrier(dist)
+    ms_max = max_over_ranks(dist, ms)
+    value = world * args.steps / (ms_max / 1000.0)
+
+    # e2e through the C ABI with host buffers
+    host_toks = rng.integers(0, 151936, args.steps).astype(np.uint32)
+    eng.forward_tokens(prompt[:PROMPT])
+    barrier(dist)
+    wall_ms, _ = eng.bench_host(host_toks)
+    wall_ms = max_over_ranks(dist, wall_ms)
+    e2e = world * args.steps / (wall_ms / 1000.0)
+
+    # roofline of the dominant kernel (fused RMSNorm + gate/up + SwiGLU GEMV)
+    kms, kbytes, klaunch = eng.bench_kernel(chpe.ROLE_GATEUP, rounds=3)
+    hbm, peak_kind = peaks()
+    achieved = kbytes / (kms / 1000.0) / 1e9
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tp):
+        traffic = json.load(open(tp)).get("gateup_w4_3b_bytes_per_launch")
+    # whole-step algorithmic bytes (all roles)
+    step_bytes = 0.0
+    per_role = {}
+    for role, name in ((chpe.ROLE_QKV, "qkv"), (chpe.ROLE_O, "o"), (chpe.ROLE_GATEUP, "gateup"),
+                       (chpe.ROLE_DOWN, "down"), (chpe.ROLE_LMHEAD, "lmhead")):
+        m, b, n = eng.bench_kernel(role, rounds=2)
+        launches_per_step = n // 2
+        step_bytes += b * launches_per_step
+        per_role[name] = {"avg_us": round(m * 1000, 2), "bytes_per_launch": b,
+                          "gbs": round(b / (m / 1000) / 1e9, 1)}
+    cpu = None
+    if rank == 0:
+        sample_steps = int(os.environ.get("CHPE_CPU_SAMPLE_STEPS", "3"))
+        v_cpu, sample = oracle_cpu_baseline(archive, sample_steps, 1, rng.integers(0, 151936, sample_steps + 2))
+        cpu = {"value": v_cpu, "unit": "tok/s", "cores": 1, "kind": "port",
+               "sample": sample + f"; CPU restatement of src/chpe_engine.zig, 1 thread ({cpu_isa()})"}
+    if rank != 0:
+        return
+    ms_step = ms_max / args.steps
+    line = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "u4->f32",
+        "data": "synthetic (seeded archive, random-init weights)",
+        "config": {"workload": CONFIG_NAME, "prompt": PROMPT, "positions": f"{PROMPT + args.warmup}.."
+                   f"{PROMPT + args.warmup + args.steps - 1}", "parallelism": f"replicas x{world}",
+                   "l2": "inputs larger than L2 (1.59 GB of weights per step)",
+                   "algorithmic_bytes_per_token": step_bytes,
+                   "weight_stream_gbs": step_bytes / (ms_step / 1000) / 1e9,
+                   "weight_stream_frac_of_measured_hbm": step_bytes / (ms_step / 1000) / 1e9 / hbm,
+                   "per_role": per_role},
+        "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4,
+                "d2h_bytes_per_step": eng.vocab * 4 + 24},
+        "roofline": {"kernel": "gemv_kernel<W4G,ROWTILE> fused RMSNorm+gate/up+SwiGLU", "bound": "hbm",
+                     "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "peak_kind": peak_kind, "traffic": traffic,
+                     "bytes_per_launch": kbytes, "avg_launch_us": kms * 1000},
+        "cpu_baseline": cpu,
+        "clocks": cs.summary(),
+        "gpu_launches": eng.kernels_per_step() * args.steps,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank, world, local, dist = dist_setup(args.gpus)
+    try:
+        if args.impl == "reference":
+            run_reference(args, rank, world, dist)
+        else:
+            run_ours(args, rank, world, local, dist)
+    finally:
+        if dist is not None:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

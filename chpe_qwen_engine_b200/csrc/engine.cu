@@ -1,0 +1,1063 @@
+// engine.cu -- CHPEEngine for B200: archive upload, per-call-site plans,
+// one decode step recorded as a chain of PDL kernels and replayed as a graph.
+#include "engine.h"
+
+#include <time.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "attention.cuh"
+#include "aux_kernels.cuh"
+#include "gemv.cuh"
+
+namespace chpe {
+
+#define CK(x)                                                                               \
+  do {                                                                                      \
+    cudaError_t e_ = (x);                                                                   \
+    if (e_ != cudaSuccess)                                                                  \
+      throw std::runtime_error(std::string(#x) + ": " + cudaGetErrorString(e_));            \
+  } while (0)
+
+enum OpType : int32_t {
+  OP_GEMV = 0, OP_GEN_ROW, OP_GEN_FLAT, OP_AUX, OP_ATTN, OP_EMBED, OP_NORM, OP_SWIGLU,
+  OP_PATTERN, OP_ARGMAX
+};
+
+// Roles of recorded ops (for per-kernel timing).
+enum Role : int32_t { ROLE_OTHER = 0, ROLE_QKV = 1, ROLE_ATTN = 2, ROLE_O = 3, ROLE_GATEUP = 4,
+                      ROLE_DOWN = 5, ROLE_LMHEAD = 6, ROLE_EMBED = 7 };
+
+struct Op {
+  int32_t type = 0, fmt = 0, kind = 0, threads = 256, hd = 128;
+  int32_t role = ROLE_OTHER;
+  double alg_bytes = 0;  // algorithmic weight bytes this op streams
+  dim3 grid{1, 1, 1};
+  size_t smem = 0;
+  GemvLaunch g{};
+  GenLaunch gen{};
+  AuxLaunch aux{};
+  AttnLaunch at{};
+  EmbedLaunch em{};
+  NormLaunch nm{};
+  SwigluLaunch sw{};
+  PatternLaunch pt{};
+  ArgmaxLaunch am{};
+};
+
+// ---- host restatements of small archive reads ------------------------------
+static inline uint16_t rd16(const uint8_t* p) { uint16_t v; memcpy(&v, p, 2); return v; }
+static inline uint32_t rd32(const uint8_t* p) { uint32_t v; memcpy(&v, p, 4); return v; }
+static inline uint64_t rd64(const uint8_t* p) { uint64_t v; memcpy(&v, p, 8); return v; }
+
+static uint64_t now_ns() {
+  struct timespec ts;
+  clock_gettime(CLOCK_MONOTONIC, &ts);
+  return (uint64_t)ts.tv_sec * 1000000000ull + (uint64_t)ts.tv_nsec;
+}
+
+static int fmt_bits(int fmt) {
+  switch (fmt) {
+    case FMT_W4G: case FMT_W4SB: return 4;
+    case FMT_W2G: case FMT_W2SB: return 2;
+    case FMT_W8: case FMT_I8RAW: return 8;
+    case FMT_F16: case FMT_BF16: return 16;
+    default: return 32;
+  }
+}
+
+static int fmt_cw(int fmt) {
+  switch (fmt) {
+    case FMT_W4G: case FMT_W4SB: return 32;
+    case FMT_W2G: case FMT_W2SB: return 64;
+    case FMT_W8: case FMT_I8RAW: return 16;
+    case FMT_F16: case FMT_BF16: return 8;
+    default: return 4;
+  }
+}
+
+uint64_t Engine::code_off(uint64_t tile) const {
+  if (f_.is_raw) return 4096 + tile * 16384ull;
+  if (f_.is_dense) return 4096 + tile * 17408ull + 64;
+  return 4096 + tile * 20480ull + 3072 + 64;
+}
+
+// chpe_engine.zig:1144-1170 unpackNorm, reading past the archive end as zeros.
+void Engine::unpack_norm(uint64_t tile, float* out) const {
+  const uint32_t D = arch_->D;
+  if (!f_.archive_valid || tile >= f_.record_count) {
+    for (uint32_t i = 0; i < D; i++) out[i] = 1.0f;
+    return;
+  }
+  uint64_t off = code_off(tile);
+  auto byte_at = [&](uint64_t o) -> uint8_t { return o < len_ ? host_[o] : 0; };
+  for (uint32_t i = 0; i < D; i++) {
+    if (D == 4096 && f_.is_raw) {
+      uint32_t b = (uint32_t)byte_at(off + 2 * i) | ((uint32_t)byte_at(off + 2 * i + 1) << 8);
+      uint32_t bits = b << 16;
+      memcpy(&out[i], &bits, 4);
+    } else {
+      uint8_t b[4] = {byte_at(off + 4 * i), byte_at(off + 4 * i + 1), byte_at(off + 4 * i + 2),
+                      byte_at(off + 4 * i + 3)};
+      memcpy(&out[i], b, 4);
+    }
+  }
+  bool all_zero = true;
+  for (uint32_t i = 0; i < D; i++) {
+    if (!std::isfinite(out[i])) {
+      for (uint32_t j = 0; j < D; j++) out[j] = 1.0f;
+      return;
+    }
+    if (out[i] != 0.0f) all_zero = false;
+  }
+  if (all_zero)
+    for (uint32_t i = 0; i < D; i++) out[i] = 1.0f;
+}
+
+// chpe_engine.zig:1172-1192 unpackBias.
+void Engine::unpack_bias(uint64_t tile, float* out, uint32_t n) const {
+  if (!f_.archive_valid || tile >= f_.record_count) {
+    for (uint32_t i = 0; i < n; i++) out[i] = 0.f;
+    return;
+  }
+  uint64_t off = code_off(tile);
+  auto byte_at = [&](uint64_t o) -> uint8_t { return o < len_ ? host_[o] : 0; };
+  for (uint32_t i = 0; i < n; i++) {
+    if (arch_->D == 4096 && f_.is_raw) {
+      uint32_t b = (uint32_t)byte_at(off + 2 * i) | ((uint32_t)byte_at(off + 2 * i + 1) << 8);
+      uint32_t bits = b << 16;
+      memcpy(&out[i], &bits, 4);
+    } else {
+      uint8_t b[4] = {byte_at(off + 4 * i), byte_at(off + 4 * i + 1), byte_at(off + 4 * i + 2),
+                      byte_at(off + 4 * i + 3)};
+      memcpy(&out[i], b, 4);
+    }
+    if (!std::isfinite(out[i])) out[i] = 0.f;
+  }
+}
+
+const float* Engine::upload_floats(const std::vector<float>& v) {
+  float* d = nullptr;
+  CK(cudaMalloc(&d, v.size() * sizeof(float)));
+  allocs_.push_back(d);
+  CK(cudaMemcpy(d, v.data(), v.size() * sizeof(float), cudaMemcpyHostToDevice));
+  return d;
+}
+
+// ---- construction: CHPEEngine.init (chpe_engine.zig:854-974) ---------------
+Engine::Engine(const uint8_t* bytes, uint64_t len, int arch, uint32_t max_seq, int device)
+    : arch_(chpe_arch_preset(arch)), arch_id_(arch), device_(device), max_seq_(max_seq),
+      host_(bytes), len_(len) {
+  if (!arch_) throw std::runtime_error("unknown architecture id");
+  if (max_seq_ == 0) throw std::runtime_error("max_seq_len must be > 0");
+  // format sniffing, :869-898
+  if (len >= 4096) {
+    uint32_t magic = rd32(bytes);
+    if (magic == CHPE_CHPE_MAGIC || magic == CHPE_ARCHIVE_MAGIC) {
+      f_.archive_valid = 1;
+      f_.record_count = rd64(bytes + 16);
+      uint64_t rec_b = rd64(bytes + 32), cell_b = rd64(bytes + 40), pre_b = rd64(bytes + 48),
+               flags = rd64(bytes + 56);
+      f_.is_dense = pre_b == 0 && rec_b == cell_b && rec_b == CHPE_CELL_BYTES;
+      f_.is_raw = rec_b == CHPE_TILE_CODE_BYTES;
+      f_.is_raw_fp16 = f_.is_raw && (flags & CHPE_FLAG_RAW_FP16) != 0;
+      if (f_.is_raw_fp16) {
+        f_.quant_bits = 16;
+      } else if (f_.is_raw) {
+        bool name9b = strstr(arch_->name, "9B") != nullptr;
+        bool sized = len < 10ull * 1024 * 1024 * 1024 && len > 7ull * 1024 * 1024 * 1024;
+        f_.quant_bits = (name9b && ((flags & 0x08) != 0 || sized)) ? 8 : 16;
+      } else if (f_.record_count > 0 && len >= 4096 + (f_.is_dense ? CHPE_CELL_BYTES : CHPE_RECORD_BYTES)) {
+        uint64_t cell_off = 4096 + (f_.is_dense ? 0 : CHPE_PREFETCH_BYTES);
+        f_.quant_bits = bytes[cell_off + CHPE_PAYLOAD_OFF + 20];
+        if (f_.quant_bits == 0) f_.quant_bits = 2;
+      }
+    }
+  }
+  f_.stride = f_.is_raw ? CHPE_TILE_CODE_BYTES : (f_.is_dense ? CHPE_CELL_BYTES : CHPE_RECORD_BYTES);
+  if (f_.is_raw_fp16 || (f_.is_raw && f_.quant_bits == 16)) f_.wpt = 8192;
+  else if (f_.quant_bits == 8) f_.wpt = 16384;
+  else if (f_.quant_bits == 4 || f_.quant_bits == 2) f_.wpt = 32768;
+  else f_.wpt = 8192;
+  // Records the header promises but the bytes do not hold are never read:
+  // the C ABI validates first; a raw engine over short bytes clamps here.
+  if (f_.archive_valid) {
+    uint64_t avail = len > 4096 ? (len - 4096) / f_.stride : 0;
+    if (f_.record_count > avail) f_.record_count = avail;
+  }
+
+  CK(cudaSetDevice(device_));
+  CK(cudaDeviceGetAttribute(&num_sms_, cudaDevAttrMultiProcessorCount, device_));
+  CK(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+
+  // Archive bytes to HBM verbatim, through pinned staging buffers, plus a
+  // zeroed tail so reads past the last record stay inside the allocation.
+  const uint64_t pad = 1ull << 20;
+  CK(cudaMalloc(&d_arc_, len + pad));
+  CK(cudaMemsetAsync(d_arc_ + len, 0, pad, stream_));
+  {
+    const uint64_t chunk = 64ull << 20;
+    uint8_t* stage[2] = {nullptr, nullptr};
+    cudaEvent_t ev[2];
+    CK(cudaMallocHost(&stage[0], chunk));
+    CK(cudaMallocHost(&stage[1], chunk));
+    CK(cudaEventCreateWithFlags(&ev[0], cudaEventDisableTiming));
+    CK(cudaEventCreateWithFlags(&ev[1], cudaEventDisableTiming));
+    int i = 0;
+    for (uint64_t off = 0; off < len; off += chunk, i ^= 1) {
+      uint64_t n = len - off < chunk ? len - off : chunk;
+      CK(cudaEventSynchronize(ev[i]));
+      memcpy(stage[i], bytes + off, n);
+      CK(cudaMemcpyAsync(d_arc_ + off, stage[i], n, cudaMemcpyHostToDevice, stream_));
+      CK(cudaEventRecord(ev[i], stream_));
+    }
+    CK(cudaStreamSynchronize(stream_));
+    cudaFreeHost(stage[0]);
+    cudaFreeHost(stage[1]);
+    cudaEventDestroy(ev[0]);
+    cudaEventDestroy(ev[1]);
+  }
+
+  const ChpeArch& A = *arch_;
+  auto dalloc = [&](size_t bytes_) -> void* {
+    void* p = nullptr;
+    CK(cudaMalloc(&p, bytes_ < 256 ? 256 : bytes_));
+    CK(cudaMemset(p, 0, bytes_ < 256 ? 256 : bytes_));
+    allocs_.push_back(p);
+    return p;
+  };
+  uint32_t maxproj = A.D;
+  if (A.H * A.HD > maxproj) maxproj = A.H * A.HD;
+  if (A.F > maxproj) maxproj = A.F;
+  d_hidden_ = (float*)dalloc(A.D * 4);
+  d_q_ = (float*)dalloc((size_t)A.H * A.HD * 4);
+  d_k_ = (float*)dalloc((size_t)A.KV * A.HD * 4);
+  d_v_ = (float*)dalloc((size_t)A.KV * A.HD * 4);
+  d_attn_ = (float*)dalloc(A.D * 4);
+  d_mlp_ = (float*)dalloc(A.F * 4);
+  d_tmp_ = (float*)dalloc(maxproj * 4);
+  d_tmp2_ = (float*)dalloc(maxproj * 4);
+  d_xn_ = (float*)dalloc(maxproj * 4);
+  d_logits_ = (float*)dalloc((size_t)A.V * 4);
+  const int G = A.H / A.KV;
+  const int nsplit = 16;
+  d_part_ = (float*)dalloc((size_t)A.KV * nsplit * G * (A.HD + 2) * 4);
+  d_counters_ = (uint32_t*)dalloc(A.KV * 4);
+  size_t kv_elems = (size_t)A.L * max_seq_ * A.KV * A.HD;
+  d_kc_ = (__half*)dalloc(kv_elems * 2);
+  d_vc_ = (__half*)dalloc(kv_elems * 2);
+  d_st_ = (StepState*)dalloc(sizeof(StepState));
+  d_res_ = (StepResult*)dalloc(sizeof(StepResult));
+  max_gen_ = max_seq_;
+  d_gen_ = (int32_t*)dalloc((size_t)max_gen_ * 4);
+  CK(cudaMallocHost(&h_st_, sizeof(StepState)));
+  CK(cudaMallocHost(&h_res_, sizeof(StepResult)));
+  h_tok_cap_ = max_seq_ + 1;
+  CK(cudaMallocHost(&h_tok_, h_tok_cap_ * 4));
+  memset(h_st_, 0, sizeof(StepState));
+  h_st_->finite = 1;
+  CK(cudaMemcpy(d_st_, h_st_, sizeof(StepState), cudaMemcpyHostToDevice));
+  // RoPE inverse frequencies, computed as applyRope does (chpe_engine.zig:200-202)
+  std::vector<float> invf(A.HD / 2);
+  for (uint32_t i = 0; i < A.HD / 2; i++) {
+    float fe = 2.0f * (float)i / (float)A.HD;
+    invf[i] = 1.0f / powf(A.theta, fe);
+  }
+  d_invfreq_ = const_cast<float*>(upload_floats(invf));
+
+  ops_ = new std::vector<Op>();
+  build_step();
+}
+
+Engine::~Engine() {
+  if (graph_) cudaGraphExecDestroy(graph_);
+  for (void* p : allocs_) cudaFree(p);
+  if (d_arc_) cudaFree(d_arc_);
+  if (h_st_) cudaFreeHost(h_st_);
+  if (h_res_) cudaFreeHost(h_res_);
+  if (h_tok_) cudaFreeHost(h_tok_);
+  if (stream_) cudaStreamDestroy(stream_);
+  delete ops_;
+}
+
+// ---- planning one gemvLinear call site -------------------------------------
+GemvSrc Engine::plan_linear(uint64_t tile_start, uint64_t num_tiles, uint32_t r_total,
+                            uint32_t c_total, uint32_t x_len, int accumulate, int64_t bias_tile) {
+  GemvSrc s{};
+  s.r_total = r_total;
+  s.c_total = c_total;
+  s.x_len = x_len;
+  s.arc = d_arc_;
+  if (!f_.archive_valid || tile_start >= f_.record_count) {
+    s.kind = accumulate ? SRC_NOOP : SRC_PATTERN;
+    return s;
+  }
+  uint64_t avail = num_tiles < f_.record_count - tile_start ? num_tiles : f_.record_count - tile_start;
+  s.n_tiles = (uint32_t)avail;
+  s.tile0 = code_off(tile_start);
+  s.stride = f_.stride;
+  if (bias_tile >= 0 && (uint64_t)bias_tile < f_.record_count) {
+    std::vector<float> b(r_total);
+    unpack_bias((uint64_t)bias_tile, b.data(), r_total);
+    s.bias = upload_floats(b);
+  }
+  if (f_.is_raw) {
+    s.kind = SRC_RAW;
+    s.fmt = f_.is_raw_fp16 ? FMT_F16 : (f_.quant_bits == 8 ? FMT_I8RAW : FMT_BF16);
+    s.flat_limit = avail * f_.wpt;
+    if (c_total % fmt_cw(s.fmt) != 0) throw std::runtime_error("raw tensor width not a multiple of the chunk width");
+    return s;
+  }
+  const uint8_t* base = host_;
+  auto cell_code = [&](uint64_t t) { return base + code_off(tile_start + t); };
+  if (c_total > 2048) {  // gemvCellFlat, wpt 32768
+    s.flat_limit = avail * 32768ull;
+    uint64_t need = ((uint64_t)r_total * c_total + 32767) / 32768;
+    uint64_t used = need < avail ? need : avail;
+    int fmt = -1;
+    bool uniform = true;
+    for (uint64_t t = 0; t < used; t++) {
+      const uint8_t* pl = cell_code(t) + 16384;
+      uint32_t qb = pl[20];
+      bool g = (rd64(pl + 24) & 1u) != 0;
+      int f = qb == 4 ? (g ? FMT_W4G : FMT_W4SB) : qb == 2 ? (g ? FMT_W2G : FMT_W2SB) : FMT_ZERO;
+      if (fmt < 0) fmt = f;
+      if (f != fmt) uniform = false;
+      uint32_t n = rd16(pl + 560);
+      if (n > 0 && n <= 64) s.has_aux = 1;
+    }
+    if (fmt < 0) fmt = FMT_ZERO;
+    s.fmt = fmt;
+    bool fast = uniform && fmt != FMT_ZERO && (c_total % fmt_cw(fmt)) == 0;
+    s.kind = fast ? SRC_FLAT : SRC_GEN_FLAT;
+    return s;
+  }
+  // row-tiled cells (gemvTilePolymorphic), row_base prefix with the
+  // reference's stop conditions (:1430-1442)
+  std::vector<uint32_t> cells, rowsv;
+  uint64_t row_base = 0;
+  for (uint64_t t = 0; t < avail; t++) {
+    if (row_base >= r_total) break;
+    uint32_t rows = rd32(cell_code(t) + 16384 + 40);
+    if (rows == 0) break;
+    cells.push_back((uint32_t)t);
+    rowsv.push_back(rows);
+    row_base += rows;
+  }
+  uint32_t covered = (uint32_t)(row_base < r_total ? row_base : r_total);
+  s.rows_covered = covered;
+  int fmt = -1;
+  bool uniform = !cells.empty();
+  uint32_t crow = 0, ccol = 0;
+  bool outl = false;
+  for (size_t i = 0; i < cells.size(); i++) {
+    const uint8_t* pl = cell_code(cells[i]) + 16384;
+    uint32_t qb = pl[20];
+    uint64_t fl = rd64(pl + 24);
+    bool g = (fl & 1u) != 0;
+    int f;
+    switch (qb) {
+      case 4: f = g ? FMT_W4G : FMT_W4SB; break;
+      case 8: f = FMT_W8; break;
+      case 16: f = (fl & CHPE_FLAG_RAW_FP16) ? FMT_F16 : FMT_BF16; break;
+      case 32: f = FMT_F32; break;
+      default: f = g ? FMT_W2G : FMT_W2SB; break;
+    }
+    uint32_t rows = rd32(pl + 40), cols = rd32(pl + 44);
+    if (i == 0) { fmt = f; crow = rows; ccol = cols; outl = g && rows == 16; }
+    if (f != fmt || rows != crow || cols != ccol) uniform = false;
+  }
+  s.fmt = fmt < 0 ? FMT_W4G : fmt;
+  s.cell_rows = crow;
+  s.cell_cols = ccol;
+  bool fast = uniform && fmt != FMT_W8 && ccol == c_total && x_len == c_total &&
+              (ccol % fmt_cw(fmt)) == 0 && (uint64_t)crow * ccol * fmt_bits(fmt) / 8 <= 16384;
+  if (fast) {
+    s.kind = SRC_ROWTILE;
+    s.outliers = (outl && (fmt == FMT_W4G || fmt == FMT_W2G)) ? OUTL_ADD : OUTL_NONE;
+    return s;
+  }
+  // per-row table for the generic kernel; every byte it may touch must lie
+  // inside the uploaded archive plus its zeroed tail
+  for (size_t i = 0; i < cells.size(); i++) {
+    const uint8_t* pl = cell_code(cells[i]) + 16384;
+    uint32_t qb = pl[20];
+    uint64_t rows = rd32(pl + 40), cols = rd32(pl + 44);
+    uint64_t bits = qb == 4 ? 4 : qb == 8 ? 8 : qb == 16 ? 16 : qb == 32 ? 32 : 2;
+    uint64_t last = code_off(tile_start + cells[i]) + rows * cols * bits / 8 + 16384 + 2 * rows * cols / 128 + 1024;
+    if (cols > (1u << 20) || last > len_ + (1ull << 20))
+      throw std::runtime_error("cell geometry reaches outside the archive");
+  }
+  s.kind = SRC_GEN_ROWTILE;
+  std::vector<uint32_t> rc(r_total, 0xFFFFFFFFu);
+  std::vector<uint16_t> ri(r_total, 0);
+  uint64_t rb = 0;
+  for (size_t i = 0; i < cells.size(); i++) {
+    for (uint32_t r = 0; r < rowsv[i] && rb + r < r_total; r++) {
+      rc[rb + r] = cells[i];
+      ri[rb + r] = (uint16_t)r;
+    }
+    rb += rowsv[i];
+  }
+  uint32_t* drc = nullptr;
+  uint16_t* dri = nullptr;
+  CK(cudaMalloc(&drc, rc.size() * 4));
+  CK(cudaMalloc(&dri, ri.size() * 2 + 16));
+  allocs_.push_back(drc);
+  allocs_.push_back(dri);
+  CK(cudaMemcpy(drc, rc.data(), rc.size() * 4, cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(dri, ri.data(), ri.size() * 2, cudaMemcpyHostToDevice));
+  s.row_cell = drc;
+  s.row_in_cell = dri;
+  return s;
+}
+
+static bool is_fast(const GemvSrc& s) {
+  return s.kind == SRC_RAW || s.kind == SRC_ROWTILE || s.kind == SRC_FLAT;
+}
+
+static size_t gemv_smem(int fmt, uint32_t ncols) {
+  uint32_t cw = fmt_cw(fmt);
+  uint32_t nchunks = (ncols + cw - 1) / cw;
+  uint32_t nslots = (nchunks + 31) / 32;
+  return ((size_t)nslots * 32 * cw + nchunks + 4) * sizeof(float);
+}
+
+static uint64_t weight_bytes(const GemvSrc& s) {
+  if (s.kind == SRC_RAW) {
+    uint64_t w = (uint64_t)s.r_total * s.c_total;
+    if (w > s.flat_limit) w = s.flat_limit;
+    return w * (s.fmt == FMT_I8RAW ? 1 : 2);
+  }
+  if (s.kind == SRC_FLAT) {
+    uint64_t need = ((uint64_t)s.r_total * s.c_total + 32767) / 32768;
+    if (need > s.n_tiles) need = s.n_tiles;
+    return need * s.stride;
+  }
+  if (s.kind == SRC_ROWTILE) {
+    uint64_t cells = (s.rows_covered + s.cell_rows - 1) / s.cell_rows;
+    return cells * s.stride;
+  }
+  return 0;
+}
+
+// Algorithmic bytes of a call site: the codes and scales of the weights it
+// actually needs (rows < r_total), no padding, metadata or unused tiles.
+static double alg_bytes_of(const GemvSrc& s) {
+  double w = (double)s.r_total * s.c_total;
+  if (s.kind == SRC_ROWTILE) w = (double)s.rows_covered * s.c_total;
+  if ((s.kind == SRC_FLAT || s.kind == SRC_RAW) && w > (double)s.flat_limit) w = (double)s.flat_limit;
+  switch (s.fmt) {
+    case FMT_W4G: return w * 0.5 + w / 128.0 * 2.0;
+    case FMT_W2G: return w * 0.25 + w / 128.0 * 2.0;
+    case FMT_W4SB: return w * 0.5;
+    case FMT_W2SB: return w * 0.25;
+    case FMT_W8: case FMT_I8RAW: return w;
+    case FMT_F16: case FMT_BF16: return w * 2.0;
+    case FMT_F32: return w * 4.0;
+  }
+  return 0.0;
+}
+
+void Engine::add_linear_ops(std::vector<Op>& ops, const GemvSrc* src, float* const* out, int nseg,
+                            int epi, const float* x, const float* gamma, int check_layer,
+                            uint32_t ncols, bool ignore_stop) {
+  const ChpeArch& A = *arch_;
+  bool fused = true;
+  for (int i = 0; i < nseg; i++) {
+    if (!is_fast(src[i]) || src[i].kind != src[0].kind || src[i].fmt != src[0].fmt) fused = false;
+    if (epi == EPI_SWIGLU && src[i].has_aux) fused = false;
+    if (epi == EPI_SWIGLU && src[i].r_total != src[0].r_total) fused = false;
+  }
+  bool logits_aux = epi == EPI_LOGITS && src[0].has_aux;
+  if (logits_aux) fused = false;
+
+  auto make_gemv = [&](const GemvSrc* ss, float* const* oo, int n, int e, const float* xx,
+                       const float* gg, int chk) {
+    Op op;
+    op.type = OP_GEMV;
+    op.fmt = ss[0].fmt;
+    op.kind = ss[0].kind;
+    GemvLaunch& g = op.g;
+    g.nseg = n;
+    g.epi = e;
+    uint32_t rows = 0;
+    for (int i = 0; i < n; i++) {
+      g.src[i] = ss[i];
+      g.out[i] = oo[i];
+      g.row_start[i] = rows;
+      rows += ss[i].r_total;
+      g.prefetch_bytes[i] = weight_bytes(ss[i]);
+      g.prefetch_base[i] = d_arc_ + ss[i].tile0;
+    }
+    g.row_start[n] = rows;
+    if (e == EPI_SWIGLU) { g.out[0] = oo[0]; g.row_start[1] = ss[0].r_total; }
+    g.x = xx;
+    g.gamma = gg;
+    g.norm = gg != nullptr;
+    g.eps = A.eps;
+    g.ncols = ncols;
+    g.check_layer = chk;
+    g.st = d_st_;
+    g.ignore_stop = ignore_stop;
+    g.res = d_res_;
+    g.gen_tokens = d_gen_;
+    g.max_gen = (int32_t)max_gen_;
+    for (int i = 0; i < n; i++)
+      if (ss[i].has_aux) g.xn_out = d_xn_;
+    size_t sm = gemv_smem(op.fmt, ncols);
+    op.smem = sm;
+    uint32_t jobs = e == EPI_SWIGLU ? ss[0].r_total : rows;
+    if (sm > 16384) {
+      op.threads = 512;
+      uint32_t cap = (uint32_t)num_sms_ * (sm > 100000 ? 1u : 2u);
+      uint32_t need = (jobs + 15) / 16;
+      op.grid = dim3(need < cap ? need : cap);
+    } else {
+      op.threads = 256;
+      uint32_t cap = (uint32_t)num_sms_ * 4u;
+      uint32_t need = (jobs + 7) / 8;
+      op.grid = dim3(need < cap ? need : cap);
+    }
+    if (op.grid.x == 0) op.grid.x = 1;
+    return op;
+  };
+  auto push_aux = [&](const GemvSrc& s, float* y, const float* xx) {
+    if (!s.has_aux || s.kind != SRC_FLAT) return;
+    Op op;
+    op.type = OP_AUX;
+    op.aux.src = s;
+    op.aux.y = y;
+    op.aux.x = xx;
+    op.aux.st = ignore_stop ? nullptr : d_st_;
+    uint64_t n = (uint64_t)s.n_tiles * 64;
+    op.grid = dim3((uint32_t)((n + 255) / 256));
+    op.threads = 256;
+    ops.push_back(op);
+  };
+
+  if (fused) {
+    Op op = make_gemv(src, out, nseg, epi, x, gamma, check_layer);
+    op.role = epi == EPI_SWIGLU ? ROLE_GATEUP : epi == EPI_LOGITS ? ROLE_LMHEAD
+              : (epi == EPI_ACCUM ? (ncols == arch_->D ? ROLE_O : ROLE_DOWN) : ROLE_QKV);
+    for (int i = 0; i < nseg; i++) op.alg_bytes += alg_bytes_of(src[i]);
+    ops.push_back(op);
+    for (int i = 0; i < nseg; i++) push_aux(src[i], epi == EPI_SWIGLU ? nullptr : out[i], gamma ? d_xn_ : x);
+    return;
+  }
+  // Decomposed: normalise once, then one op per tensor.
+  const float* xin = x;
+  if (gamma) {
+    Op op;
+    op.type = OP_NORM;
+    op.nm = NormLaunch{x, gamma, d_xn_, ncols, A.eps, check_layer, d_st_, ignore_stop ? 1 : 0};
+    op.grid = dim3((ncols + 255) / 256);
+    op.threads = 256;
+    ops.push_back(op);
+    xin = d_xn_;
+  }
+  float* seg_out[3] = {out[0], nseg > 1 ? out[1] : nullptr, nseg > 2 ? out[2] : nullptr};
+  if (epi == EPI_SWIGLU) { seg_out[0] = d_tmp_; seg_out[1] = d_tmp2_; }
+  for (int i = 0; i < nseg; i++) {
+    const GemvSrc& s = src[i];
+    int e = epi == EPI_ACCUM ? EPI_ACCUM : EPI_STORE;
+    if (s.kind == SRC_NOOP) continue;
+    if (s.kind == SRC_PATTERN) {
+      Op op;
+      op.type = OP_PATTERN;
+      op.pt = PatternLaunch{seg_out[i], s.r_total, ignore_stop ? nullptr : d_st_};
+      op.grid = dim3((s.r_total + 255) / 256);
+      ops.push_back(op);
+      continue;
+    }
+    if (is_fast(s)) {
+      Op op = make_gemv(&s, &seg_out[i], 1, e, xin, nullptr, -1);
+      ops.push_back(op);
+      push_aux(s, seg_out[i], xin);
+      continue;
+    }
+    Op op;
+    op.type = s.kind == SRC_GEN_ROWTILE ? OP_GEN_ROW : OP_GEN_FLAT;
+    op.gen = GenLaunch{s, seg_out[i], xin, e == EPI_ACCUM, ignore_stop ? nullptr : d_st_};
+    uint32_t need = (s.r_total + 7) / 8, cap = (uint32_t)num_sms_ * 8;
+    op.grid = dim3(need < cap ? need : cap);
+    ops.push_back(op);
+  }
+  if (epi == EPI_SWIGLU) {
+    Op op;
+    op.type = OP_SWIGLU;
+    op.sw = SwigluLaunch{d_tmp_, d_tmp2_, out[0], src[0].r_total, d_st_};
+    op.grid = dim3((src[0].r_total + 255) / 256);
+    ops.push_back(op);
+  }
+  if (epi == EPI_LOGITS) {
+    Op op;
+    op.type = OP_ARGMAX;
+    op.am = ArgmaxLaunch{out[0], src[0].r_total, src[0].kind == SRC_PATTERN ? 1 : 0, d_hidden_,
+                         A.D, d_st_, d_res_, d_gen_, (int32_t)max_gen_};
+    op.grid = dim3((uint32_t)num_sms_);
+    ops.push_back(op);
+  }
+}
+
+// ---- the decode step: forwardDecode (chpe_engine.zig:1663-1803) ------------
+void Engine::build_step() {
+  const ChpeArch& A = *arch_;
+  std::vector<Op>& ops = *ops_;
+  ops.clear();
+  {  // embedding
+    Op op;
+    op.type = OP_EMBED;
+    op.role = ROLE_EMBED;
+    EmbedLaunch& e = op.em;
+    e.arc = d_arc_;
+    e.record_count = f_.record_count;
+    e.stride = f_.stride;
+    e.prefix = f_.is_raw ? 0 : (f_.is_dense ? 64 : 3072 + 64);
+    e.D = A.D;
+    e.hidden = d_hidden_;
+    e.st = d_st_;
+    e.res = d_res_;
+    e.use_state = 1;
+    if (!f_.archive_valid || f_.record_count == 0) e.mode = EMB_PATTERN;
+    else if (f_.is_raw_fp16) e.mode = EMB_RAW_F16;
+    else if (f_.is_raw) e.mode = f_.quant_bits == 8 ? EMB_RAW_I8 : EMB_RAW_BF16;
+    else e.mode = EMB_CELL;
+    op.grid = dim3((A.D + 255) / 256);
+    ops.push_back(op);
+  }
+  const uint32_t qd = A.H * A.HD, kvd = A.KV * A.HD;
+  std::vector<float> gam(A.D);
+  for (uint32_t l = 0; l < A.L; l++) {
+    ChpeLayerInfo li;
+    chpe_layer_info(arch_id_, f_.is_raw, l, &li);
+    unpack_norm((uint64_t)li.input_norm, gam.data());
+    const float* g_in = upload_floats(gam);
+    unpack_norm((uint64_t)li.post_norm, gam.data());
+    const float* g_post = upload_floats(gam);
+    GemvSrc qkv[3] = {plan_linear(li.q_proj, li.q_tiles, qd, A.D, A.D, 0, li.q_bias),
+                      plan_linear(li.k_proj, li.k_tiles, kvd, A.D, A.D, 0, li.k_bias),
+                      plan_linear(li.v_proj, li.v_tiles, kvd, A.D, A.D, 0, li.v_bias)};
+    float* qkv_out[3] = {d_q_, d_k_, d_v_};
+    add_linear_ops(ops, qkv, qkv_out, 3, EPI_STORE, d_hidden_, g_in, (int)l - 1, A.D, false);
+    {
+      Op op;
+      op.type = OP_ATTN;
+      op.role = ROLE_ATTN;
+      op.hd = (int)A.HD;
+      AttnLaunch& at = op.at;
+      at.q = d_q_;
+      at.k = d_k_;
+      at.v = d_v_;
+      size_t lay = (size_t)l * max_seq_ * A.KV * A.HD;
+      at.kc = d_kc_ + lay;
+      at.vc = d_vc_ + lay;
+      at.out = d_attn_;
+      at.part = d_part_;
+      at.counters = d_counters_;
+      at.inv_freq = d_invfreq_;
+      at.st = d_st_;
+      at.H = (int)A.H;
+      at.KV = (int)A.KV;
+      at.HD = (int)A.HD;
+      at.nsplit = 16;
+      at.max_seq = (int32_t)max_seq_;
+      op.grid = dim3(16, A.KV);
+      op.threads = (int)(A.H / A.KV) * 32;
+      if (op.threads < (int)A.HD / 2) op.threads = (int)A.HD / 2;
+      ops.push_back(op);
+    }
+    GemvSrc o = plan_linear(li.o_proj, li.o_tiles, A.D, A.D, A.D, 1, -1);
+    float* o_out[1] = {d_hidden_};
+    add_linear_ops(ops, &o, o_out, 1, EPI_ACCUM, d_attn_, nullptr, -1, A.D, false);
+    GemvSrc gu[2] = {plan_linear(li.gate_proj, li.gate_tiles, A.F, A.D, A.D, 0, -1),
+                     plan_linear(li.up_proj, li.up_tiles, A.F, A.D, A.D, 0, -1)};
+    float* gu_out[2] = {d_mlp_, nullptr};
+    add_linear_ops(ops, gu, gu_out, 2, EPI_SWIGLU, d_hidden_, g_post, -1, A.D, false);
+    GemvSrc dn = plan_linear(li.down_proj, li.down_tiles, A.D, A.F, A.F, 1, -1);
+    float* dn_out[1] = {d_hidden_};
+    add_linear_ops(ops, &dn, dn_out, 1, EPI_ACCUM, d_mlp_, nullptr, -1, A.F, false);
+  }
+  // final norm + LM head (computeLmHead, :1554-1660) + argmax (:1775-1802)
+  unpack_norm((uint64_t)chpe_final_norm_index(arch_id_, f_.is_raw), gam.data());
+  const float* g_fin = upload_floats(gam);
+  GemvSrc lm{};
+  int64_t lhs, lht;
+  chpe_lm_head_span(arch_id_, &lhs, &lht);
+  if (!f_.archive_valid || f_.record_count == 0) {
+    lm.kind = SRC_PATTERN;
+    lm.r_total = A.V;
+  } else if (lhs >= 0 && (uint64_t)lhs < f_.record_count) {
+    lm = plan_linear((uint64_t)lhs, (uint64_t)lht, A.V, A.D, A.D, 0, -1);
+  } else if (!f_.is_raw) {
+    // tied embedding cells, 16 rows each, unpackEmbedRowCell semantics
+    lm.kind = SRC_ROWTILE;
+    lm.arc = d_arc_;
+    lm.r_total = A.V;
+    lm.c_total = A.D;
+    lm.x_len = A.D;
+    lm.cell_rows = 16;
+    lm.cell_cols = A.D;
+    lm.tile0 = code_off(0);
+    lm.stride = f_.stride;
+    lm.rows_covered = A.V;
+    uint64_t ncell = (A.V + 15) / 16;
+    if (ncell > f_.record_count) throw std::runtime_error("tied LM head: archive has too few records");
+    int fmt = -1;
+    bool repl = false;
+    for (uint64_t t = 0; t < ncell; t++) {
+      const uint8_t* pl = host_ + code_off(t) + 16384;
+      uint32_t qb = pl[20], rows = rd32(pl + 40);
+      bool g = (rd64(pl + 24) & 1u) != 0;
+      if ((rows != 16 && rows != 0) || qb == 8)
+        throw std::runtime_error("tied LM head: embedding cells must hold 16 rows of 2/4-bit codes");
+      int f = qb == 2 ? FMT_W2G : ((g || qb == 4) ? FMT_W4G : FMT_W4SB);
+      if (fmt < 0) fmt = f;
+      if (f != fmt) throw std::runtime_error("tied LM head: mixed embedding cell formats");
+      if (t == 0) repl = g;
+      if (g != repl) throw std::runtime_error("tied LM head: mixed outlier flags");
+    }
+    lm.fmt = fmt;
+    lm.outliers = (repl && fmt != FMT_W4SB) ? OUTL_REPLACE : OUTL_NONE;
+  } else {
+    // tied raw FP16/BF16 embedding rows
+    uint32_t rpt = 8192 / A.D ? 8192 / A.D : 1;
+    uint64_t tiles = (A.V + rpt - 1) / rpt;
+    if (tiles > f_.record_count) tiles = f_.record_count;
+    lm.kind = SRC_RAW;
+    lm.fmt = f_.is_raw_fp16 ? FMT_F16 : FMT_BF16;
+    lm.arc = d_arc_;
+    lm.r_total = A.V;
+    lm.c_total = A.D;
+    lm.x_len = A.D;
+    lm.tile0 = code_off(0);
+    lm.stride = f_.stride;
+    lm.flat_limit = tiles * 8192ull;
+    lm.n_tiles = (uint32_t)tiles;
+  }
+  float* lm_out[1] = {d_logits_};
+  add_linear_ops(ops, &lm, lm_out, 1, EPI_LOGITS, d_hidden_, g_fin, -1, A.D, true);
+
+}
+
+int Engine::kernels_per_step() const { return (int)ops_->size(); }
+
+// ---- launching --------------------------------------------------------------
+template <typename Kern, typename Arg>
+static void launch_pdl(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_t s, const Arg& a) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  CK(cudaLaunchKernelEx(&cfg, kern, a));
+}
+
+template <int FMT, int KIND, int TH>
+static void launch_gemv_t(const Op& op, cudaStream_t s) {
+  auto k = gemv_kernel<FMT, KIND, TH>;
+  static bool configured = false;
+  if (!configured) {
+    CK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    configured = true;
+  }
+  launch_pdl(k, op.grid, dim3(TH), op.smem, s, op.g);
+}
+
+template <int FMT, int KIND>
+static void launch_gemv_k(const Op& op, cudaStream_t s) {
+  if (op.threads == 512) launch_gemv_t<FMT, KIND, 512>(op, s);
+  else launch_gemv_t<FMT, KIND, 256>(op, s);
+}
+
+static void launch_gemv(const Op& op, cudaStream_t s) {
+  switch (op.kind) {
+    case SRC_RAW:
+      switch (op.fmt) {
+        case FMT_F16: return launch_gemv_k<FMT_F16, SRC_RAW>(op, s);
+        case FMT_BF16: return launch_gemv_k<FMT_BF16, SRC_RAW>(op, s);
+        case FMT_I8RAW: return launch_gemv_k<FMT_I8RAW, SRC_RAW>(op, s);
+      }
+      break;
+    case SRC_ROWTILE:
+      switch (op.fmt) {
+        case FMT_W4G: return launch_gemv_k<FMT_W4G, SRC_ROWTILE>(op, s);
+        case FMT_W4SB: return launch_gemv_k<FMT_W4SB, SRC_ROWTILE>(op, s);
+        case FMT_W2G: return launch_gemv_k<FMT_W2G, SRC_ROWTILE>(op, s);
+        case FMT_W2SB: return launch_gemv_k<FMT_W2SB, SRC_ROWTILE>(op, s);
+        case FMT_F16: return launch_gemv_k<FMT_F16, SRC_ROWTILE>(op, s);
+        case FMT_BF16: return launch_gemv_k<FMT_BF16, SRC_ROWTILE>(op, s);
+        case FMT_F32: return launch_gemv_k<FMT_F32, SRC_ROWTILE>(op, s);
+      }
+      break;
+    case SRC_FLAT:
+      switch (op.fmt) {
+        case FMT_W4G: return launch_gemv_k<FMT_W4G, SRC_FLAT>(op, s);
+        case FMT_W4SB: return launch_gemv_k<FMT_W4SB, SRC_FLAT>(op, s);
+        case FMT_W2G: return launch_gemv_k<FMT_W2G, SRC_FLAT>(op, s);
+        case FMT_W2SB: return launch_gemv_k<FMT_W2SB, SRC_FLAT>(op, s);
+      }
+      break;
+  }
+  throw std::runtime_error("no GEMV kernel for this (format, layout)");
+}
+
+void Engine::launch(const Op& op, cudaStream_t s) const {
+  switch (op.type) {
+    case OP_GEMV: return launch_gemv(op, s);
+    case OP_GEN_ROW: return launch_pdl(gemv_generic_rowtile, op.grid, dim3(256), 0, s, op.gen);
+    case OP_GEN_FLAT: return launch_pdl(gemv_generic_flat, op.grid, dim3(256), 0, s, op.gen);
+    case OP_AUX: return launch_pdl(flat_aux_fix, op.grid, dim3(256), 0, s, op.aux);
+    case OP_ATTN:
+      if (op.hd == 128) return launch_pdl(attention_kernel<128>, op.grid, dim3(op.threads), 0, s, op.at);
+      if (op.hd == 256) return launch_pdl(attention_kernel<256>, op.grid, dim3(op.threads), 0, s, op.at);
+      throw std::runtime_error("unsupported head_dim");
+    case OP_EMBED: return launch_pdl(embed_kernel, op.grid, dim3(256), 0, s, op.em);
+    case OP_NORM: return launch_pdl(rmsnorm_kernel, op.grid, dim3(256), 0, s, op.nm);
+    case OP_SWIGLU: return launch_pdl(swiglu_kernel, op.grid, dim3(256), 0, s, op.sw);
+    case OP_PATTERN: return launch_pdl(pattern_kernel, op.grid, dim3(256), 0, s, op.pt);
+    case OP_ARGMAX: return launch_pdl(argmax_kernel, op.grid, dim3(256), 0, s, op.am);
+  }
+}
+
+void Engine::record(cudaStream_t s) const {
+  for (const Op& op : *ops_) launch(op, s);
+}
+
+void Engine::ensure_graph() {
+  if (graph_) return;
+  // configure kernel attributes outside capture
+  cudaStream_t cs;
+  CK(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking));
+  record(stream_);  // warm launch also sets function attributes; result is discarded
+  CK(cudaStreamSynchronize(stream_));
+  cudaGraph_t g;
+  CK(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
+  record(cs);
+  CK(cudaStreamEndCapture(cs, &g));
+  CK(cudaGraphInstantiate(&graph_, g, 0));
+  CK(cudaGraphDestroy(g));
+  CK(cudaStreamDestroy(cs));
+}
+
+void Engine::run_steps(size_t n) {
+  for (size_t i = 0; i < n; i++) CK(cudaGraphLaunch(graph_, stream_));
+}
+
+void Engine::sync_result() {
+  CK(cudaMemcpyAsync(h_res_, d_res_, sizeof(StepResult), cudaMemcpyDeviceToHost, stream_));
+  CK(cudaStreamSynchronize(stream_));
+  last_ = *h_res_;
+}
+
+// Positions start_pos.. for the given tokens (forwardDecode per token).
+void Engine::forward(const uint32_t* toks, size_t n, uint32_t start_pos) {
+  if (n == 0) return;
+  if ((uint64_t)start_pos + n > max_seq_) throw std::runtime_error("sequence exceeds max_seq_len");
+  if (!graph_) {
+    // The warm-up launch inside ensure_graph runs one step on whatever state
+    // is current; run it on a scratch position that is overwritten below.
+    h_st_->token = (int32_t)toks[0];
+    h_st_->pos = (int32_t)start_pos;
+    h_st_->feed_argmax = 0;
+    h_st_->stop = 0;
+    h_st_->best = 0;
+    h_st_->finite = 1;
+    h_st_->done_ctas = 0;
+    h_st_->n_gen = 0;
+    CK(cudaMemcpyAsync(d_st_, h_st_, sizeof(StepState), cudaMemcpyHostToDevice, stream_));
+    ensure_graph();
+  }
+  auto t0 = now_ns();
+  h_st_->token = (int32_t)toks[0];
+  h_st_->pos = (int32_t)start_pos;
+  h_st_->feed_argmax = 0;
+  h_st_->stop = 0;
+  h_st_->best = 0;
+  h_st_->finite = 1;
+  h_st_->done_ctas = 0;
+  h_st_->n_gen = 0;
+  CK(cudaMemcpyAsync(d_st_, h_st_, sizeof(StepState), cudaMemcpyHostToDevice, stream_));
+  if (n + 1 > h_tok_cap_) throw std::runtime_error("token buffer too small");
+  for (size_t i = 0; i < n; i++) {
+    h_tok_[i] = toks[i];
+    if (i > 0)
+      CK(cudaMemcpyAsync(&d_st_->token, &h_tok_[i], 4, cudaMemcpyHostToDevice, stream_));
+    CK(cudaGraphLaunch(graph_, stream_));
+  }
+  sync_result();
+  last_ns_ = now_ns() - t0;
+  pos_ = start_pos + (uint32_t)n;
+}
+
+void Engine::generate(const uint32_t* prompt, size_t n_prompt, size_t n_gen, uint32_t* out_tokens) {
+  if (n_prompt == 0) throw std::runtime_error("empty prompt");
+  if (n_prompt + n_gen > max_seq_) throw std::runtime_error("sequence exceeds max_seq_len");
+  forward(prompt, n_prompt, 0);
+  if (n_gen == 0) return;
+  // the last prompt step's argmax is the first generated token
+  out_tokens[0] = last_.argmax_token;
+  int32_t one = 1, zero = 0;
+  CK(cudaMemcpyAsync(&d_st_->feed_argmax, &one, 4, cudaMemcpyHostToDevice, stream_));
+  CK(cudaMemcpyAsync(&d_st_->n_gen, &zero, 4, cudaMemcpyHostToDevice, stream_));
+  run_steps(n_gen - 1);
+  std::vector<int32_t> g(n_gen);
+  if (n_gen > 1)
+    CK(cudaMemcpyAsync(g.data(), d_gen_, (n_gen - 1) * 4, cudaMemcpyDeviceToHost, stream_));
+  CK(cudaMemcpyAsync(&d_st_->feed_argmax, &zero, 4, cudaMemcpyHostToDevice, stream_));
+  sync_result();
+  for (size_t i = 1; i < n_gen; i++) out_tokens[i] = (uint32_t)g[i - 1];
+  pos_ = (uint32_t)(n_prompt + n_gen - 1);
+}
+
+float Engine::timed_greedy_steps(size_t n) {
+  if (!graph_) throw std::runtime_error("run forward() first");
+  if ((uint64_t)pos_ + n > max_seq_) throw std::runtime_error("sequence exceeds max_seq_len");
+  int32_t one = 1, zero = 0;
+  CK(cudaMemcpyAsync(&d_st_->feed_argmax, &one, 4, cudaMemcpyHostToDevice, stream_));
+  CK(cudaMemcpyAsync(&d_st_->n_gen, &zero, 4, cudaMemcpyHostToDevice, stream_));
+  cudaEvent_t a, b;
+  CK(cudaEventCreate(&a));
+  CK(cudaEventCreate(&b));
+  CK(cudaStreamSynchronize(stream_));
+  CK(cudaEventRecord(a, stream_));
+  run_steps(n);
+  CK(cudaEventRecord(b, stream_));
+  CK(cudaMemcpyAsync(&d_st_->feed_argmax, &zero, 4, cudaMemcpyHostToDevice, stream_));
+  sync_result();
+  float ms = 0;
+  CK(cudaEventElapsedTime(&ms, a, b));
+  cudaEventDestroy(a);
+  cudaEventDestroy(b);
+  pos_ += (uint32_t)n;
+  return ms;
+}
+
+double Engine::timed_host_steps(const uint32_t* toks, size_t n, float* logits_host) {
+  if (!graph_) throw std::runtime_error("run forward() first");
+  if ((uint64_t)pos_ + n > max_seq_) throw std::runtime_error("sequence exceeds max_seq_len");
+  CK(cudaStreamSynchronize(stream_));
+  uint64_t t0 = now_ns();
+  for (size_t i = 0; i < n; i++) {
+    h_tok_[i % h_tok_cap_] = toks[i];
+    CK(cudaMemcpyAsync(&d_st_->token, &h_tok_[i % h_tok_cap_], 4, cudaMemcpyHostToDevice, stream_));
+    CK(cudaGraphLaunch(graph_, stream_));
+    CK(cudaMemcpyAsync(logits_host, d_logits_, (size_t)arch_->V * 4, cudaMemcpyDeviceToHost, stream_));
+    CK(cudaMemcpyAsync(h_res_, d_res_, sizeof(StepResult), cudaMemcpyDeviceToHost, stream_));
+    CK(cudaStreamSynchronize(stream_));
+  }
+  uint64_t t1 = now_ns();
+  last_ = *h_res_;
+  pos_ += (uint32_t)n;
+  return (double)(t1 - t0) / 1e6;
+}
+
+void Engine::copy_logits(float* out) const {
+  CK(cudaMemcpy(out, d_logits_, (size_t)arch_->V * 4, cudaMemcpyDeviceToHost));
+}
+
+void Engine::bench_role(int role, int rounds, float* avg_ms, double* bytes_per_launch, int* launches) {
+  if (!graph_) throw std::runtime_error("run forward() first");
+  std::vector<const Op*> sel;
+  for (const Op& op : *ops_)
+    if (op.role == role) sel.push_back(&op);
+  if (sel.empty()) throw std::runtime_error("no op with that role");
+  double bytes = 0;
+  for (const Op* op : sel) bytes += op->alg_bytes;
+  // Save the step state (the LM head's finalisation advances it), clear the
+  // stop flag so layer ops run, and restore the state afterwards.
+  StepState saved;
+  CK(cudaMemcpyAsync(h_st_, d_st_, sizeof(StepState), cudaMemcpyDeviceToHost, stream_));
+  CK(cudaStreamSynchronize(stream_));
+  saved = *h_st_;
+  int32_t zero = 0;
+  CK(cudaMemcpyAsync(&d_st_->stop, &zero, 4, cudaMemcpyHostToDevice, stream_));
+  for (const Op* op : sel) launch(*op, stream_);  // warm-up round
+  cudaEvent_t a, b;
+  CK(cudaEventCreate(&a));
+  CK(cudaEventCreate(&b));
+  CK(cudaStreamSynchronize(stream_));
+  CK(cudaEventRecord(a, stream_));
+  for (int r = 0; r < rounds; r++)
+    for (const Op* op : sel) launch(*op, stream_);
+  CK(cudaEventRecord(b, stream_));
+  CK(cudaEventSynchronize(b));
+  float ms = 0;
+  CK(cudaEventElapsedTime(&ms, a, b));
+  cudaEventDestroy(a);
+  cudaEventDestroy(b);
+  *h_st_ = saved;
+  CK(cudaMemcpyAsync(d_st_, h_st_, sizeof(StepState), cudaMemcpyHostToDevice, stream_));
+  CK(cudaStreamSynchronize(stream_));
+  int n = rounds * (int)sel.size();
+  *avg_ms = ms / (float)n;
+  *bytes_per_launch = bytes / (double)sel.size();
+  *launches = n;
+}
+
+// ---- probes used by the parity tests ----------------------------------------
+void Engine::debug_gemv_linear(uint64_t tile_start, uint64_t num_tiles, const float* x,
+                               uint64_t x_len, float* y, uint64_t r_total, uint64_t c_total,
+                               int accumulate, int64_t bias_tile) {
+  GemvSrc s = plan_linear(tile_start, num_tiles, (uint32_t)r_total, (uint32_t)c_total,
+                          (uint32_t)x_len, accumulate, bias_tile);
+  float *dx = nullptr, *dy = nullptr;
+  CK(cudaMalloc(&dx, x_len * 4 + 16));
+  CK(cudaMalloc(&dy, r_total * 4 + 16));
+  CK(cudaMemcpy(dx, x, x_len * 4, cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(dy, y, r_total * 4, cudaMemcpyHostToDevice));
+  // clear the step state's stop flag for the probe
+  int32_t zero = 0;
+  CK(cudaMemcpy(&d_st_->stop, &zero, 4, cudaMemcpyHostToDevice));
+  std::vector<Op> ops;
+  float* outs[1] = {dy};
+  add_linear_ops(ops, &s, outs, 1, accumulate ? EPI_ACCUM : EPI_STORE, dx, nullptr, -1,
+                 (uint32_t)c_total, false);
+  for (const Op& op : ops) launch(op, stream_);
+  CK(cudaStreamSynchronize(stream_));
+  CK(cudaMemcpy(y, dy, r_total * 4, cudaMemcpyDeviceToHost));
+  cudaFree(dx);
+  cudaFree(dy);
+}
+
+void Engine::debug_embed(uint32_t token, float* out) {
+  Op op = (*ops_)[0];
+  float* d = nullptr;
+  CK(cudaMalloc(&d, arch_->D * 4));
+  CK(cudaMemcpy(d, out, arch_->D * 4, cudaMemcpyHostToDevice));
+  op.em.hidden = d;
+  op.em.use_state = 0;
+  op.em.token = token;
+  launch(op, stream_);
+  CK(cudaStreamSynchronize(stream_));
+  CK(cudaMemcpy(out, d, arch_->D * 4, cudaMemcpyDeviceToHost));
+  cudaFree(d);
+}
+
+void Engine::debug_dequant_cell(uint64_t tile, int flat, float* out, uint64_t cap, uint64_t* n_out) {
+  if (f_.is_raw || tile >= f_.record_count) throw std::runtime_error("not a cell");
+  const uint8_t* pl = host_ + code_off(tile) + 16384;
+  uint64_t n = flat ? 32768 : (uint64_t)rd32(pl + 40) * rd32(pl + 44);
+  if (n > cap) n = cap;
+  float* d = nullptr;
+  CK(cudaMalloc(&d, n * 4 + 16));
+  DequantLaunch P{d_arc_ + code_off(tile), flat, d, (uint32_t)n};
+  dequant_kernel<<<64, 256, 0, stream_>>>(P);
+  CK(cudaGetLastError());
+  CK(cudaStreamSynchronize(stream_));
+  CK(cudaMemcpy(out, d, n * 4, cudaMemcpyDeviceToHost));
+  cudaFree(d);
+  *n_out = n;
+}
+
+}  // namespace chpe

@@ -1,0 +1,121 @@
+// engine.h -- the B200 decode engine behind the chpe C ABI.
+//
+// Mirrors CHPEEngine (chpe_engine.zig:820-1804): init sniffs the archive
+// format and sizes buffers, forwardDecode(token, pos) runs one token through
+// every layer.  Here the archive bytes live in HBM verbatim (the reference's
+// flat-index addressing, including its over-reads, then reads the same bytes),
+// every per-token op is a CUDA kernel, and one decode step is a CUDA graph of
+// PDL-chained kernels replayed per token with (token, pos) in device memory.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include "chpe_maps.h"
+#include "engine_types.h"
+
+namespace chpe {
+
+struct Op;  // one recorded kernel launch (engine.cu)
+
+struct EngineFacts {  // CHPEEngine fields after init sniffing (:862-918)
+  int archive_valid = 0, is_raw = 0, is_raw_fp16 = 0, is_dense = 0;
+  int quant_bits = 2;
+  uint64_t record_count = 0, stride = 0, wpt = 8192;
+};
+
+class Engine {
+ public:
+  // Counterpart of CHPEEngine.init over archive bytes the caller keeps alive
+  // for the engine's lifetime (`bytes` may be an mmap).  Throws std::runtime_error.
+  Engine(const uint8_t* bytes, uint64_t len, int arch, uint32_t max_seq, int device);
+  ~Engine();
+
+  const ChpeArch& arch() const { return *arch_; }
+  const EngineFacts& facts() const { return f_; }
+  uint32_t max_seq() const { return max_seq_; }
+
+  // forwardDecode over tokens at positions start_pos.. (blocking).
+  void forward(const uint32_t* toks, size_t n, uint32_t start_pos);
+  // Greedy generation on the device: prompt (n_prompt) then n_gen steps
+  // feeding each argmax back as the next token; out_tokens gets n_gen ids.
+  void generate(const uint32_t* prompt, size_t n_prompt, size_t n_gen, uint32_t* out_tokens);
+  // n greedy steps from the current position, timed with CUDA events on the
+  // engine stream; returns milliseconds.
+  float timed_greedy_steps(size_t n);
+  // Same workload through host round trips: per step a pinned H2D of the
+  // token and a D2H of the logits and result (wall time, milliseconds).
+  double timed_host_steps(const uint32_t* toks, size_t n, float* logits_host);
+
+  const StepResult& last_result() const { return last_; }
+  uint64_t last_elapsed_ns() const { return last_ns_; }
+  void copy_logits(float* out) const;  // last step's logits (vocab floats)
+  uint32_t current_pos() const { return pos_; }
+  int kernels_per_step() const;
+
+  // Times every recorded op of one role (ROLE_*) across all layers, `rounds`
+  // times, with CUDA events on the engine stream; returns the average
+  // milliseconds per launch and the algorithmic weight bytes per launch.
+  void bench_role(int role, int rounds, float* avg_ms, double* bytes_per_launch, int* launches);
+
+  // Test entry points that run one kernel family on host vectors.
+  void debug_gemv_linear(uint64_t tile_start, uint64_t num_tiles, const float* x, uint64_t x_len,
+                         float* y, uint64_t r_total, uint64_t c_total, int accumulate,
+                         int64_t bias_tile);
+  void debug_embed(uint32_t token, float* out);
+  void debug_dequant_cell(uint64_t tile, int flat, float* out, uint64_t cap, uint64_t* n_out);
+
+  cudaStream_t stream() const { return stream_; }
+
+ private:
+  GemvSrc plan_linear(uint64_t tile_start, uint64_t num_tiles, uint32_t r_total,
+                      uint32_t c_total, uint32_t x_len, int accumulate, int64_t bias_tile);
+  void unpack_norm(uint64_t tile, float* out) const;
+  void unpack_bias(uint64_t tile, float* out, uint32_t n) const;
+  uint64_t code_off(uint64_t tile) const;
+  const float* upload_floats(const std::vector<float>& v);
+  void build_step();
+  void add_linear_ops(std::vector<Op>& ops, const GemvSrc* src, float* const* out, int nseg,
+                      int epi, const float* x, const float* gamma, int check_layer,
+                      uint32_t ncols, bool ignore_stop);
+  void launch(const Op& op, cudaStream_t s) const;
+  void record(cudaStream_t s) const;
+  void run_steps(size_t n);
+  void sync_result();
+  void ensure_graph();
+
+  const ChpeArch* arch_;
+  int arch_id_;
+  int device_;
+  uint32_t max_seq_;
+  const uint8_t* host_;  // borrowed archive bytes
+  uint64_t len_;
+  EngineFacts f_;
+
+  cudaStream_t stream_ = nullptr;
+  cudaGraphExec_t graph_ = nullptr;
+  uint8_t* d_arc_ = nullptr;
+  std::vector<void*> allocs_;
+  float *d_hidden_, *d_q_, *d_k_, *d_v_, *d_attn_, *d_mlp_, *d_logits_, *d_xn_, *d_tmp_, *d_tmp2_;
+  float *d_part_, *d_invfreq_;
+  uint32_t* d_counters_;
+  __half *d_kc_, *d_vc_;
+  StepState* d_st_;
+  StepResult* d_res_;
+  int32_t* d_gen_;
+  uint32_t max_gen_ = 0;
+  StepState* h_st_;      // pinned
+  StepResult* h_res_;    // pinned
+  uint32_t* h_tok_;      // pinned token ring
+  size_t h_tok_cap_ = 0;
+  std::vector<Op>* ops_ = nullptr;
+  StepResult last_{};
+  uint64_t last_ns_ = 0;
+  uint32_t pos_ = 0;
+  int num_sms_ = 148;
+};
+
+}  // namespace chpe

@@ -1,0 +1,651 @@
+// gemv.cuh -- the weight-streaming GEMV family of the decode loop.
+//
+// One kernel template covers every gemvLinear call site
+// (chpe_engine.zig:1396-1489) whose tensor has a uniform format:
+//   * raw FP16 / BF16 / INT8 streams            (dotSegment, :1194-1254)
+//   * row-tiled cells W2/W4/W8/F16/F32            (gemvTile*, :223-581)
+//   * flat 32768-weight W4/W2 cells               (gemvCellFlat, :584-729)
+// A warp owns one output row: its lanes stream 16-byte chunks of codes with
+// 128-bit non-allocating loads, decode them in registers and FMA against x
+// staged once per CTA in shared memory (lane-permuted so each LDS.128 is
+// conflict-free), then reduce across the warp.  Epilogues fuse the bias,
+// the residual add and SwiGLU; the prologue fuses RMSNorm.
+//
+// Decode of a 4/2/8-bit code c into a float uses one PRMT: the code byte is
+// placed into bits 16..23 of 0x3F000000, giving f = 0.5 + c/256 exactly; a
+// chunk's sum over f*x is mapped back to sum over (c - offset)*x with the
+// chunk's x-sum, which costs no extra per-weight work.  Pairs of products use
+// the packed FFMA2 of sm_100.
+#pragma once
+#include "device_common.cuh"
+
+namespace chpe {
+
+enum Epi : int32_t { EPI_STORE = 0, EPI_ACCUM = 1, EPI_SWIGLU = 2, EPI_LOGITS = 3 };
+enum Outl : uint32_t { OUTL_NONE = 0, OUTL_ADD = 1, OUTL_REPLACE = 2 };
+
+struct GemvLaunch {
+  GemvSrc src[3];
+  float* out[3];
+  uint32_t row_start[4];  // prefix of output rows over segments
+  int32_t nseg;
+  int32_t epi;
+  const float* x;       // input vector when norm == 0
+  const float* gamma;   // RMSNorm gains when norm != 0 (x is then `hidden`)
+  float eps;
+  uint32_t ncols;       // length of x used (= c_total)
+  int32_t norm;
+  int32_t check_layer;  // layer whose end-of-layer finiteness check runs here, -1 none
+  StepState* st;
+  float* xn_out;        // optional copy of the staged x (normed) for later passes
+  uint64_t prefetch_bytes[3];  // bytes of each segment's weights to prefetch
+  const uint8_t* prefetch_base[3];
+  int32_t ignore_stop;  // the LM head always runs (the reference only breaks the layer loop)
+  StepResult* res;      // EPI_LOGITS: written by the last CTA
+  int32_t* gen_tokens;  // EPI_LOGITS: generated-token log (may be null)
+  int32_t max_gen;
+};
+
+// Ordered key for "first strict maximum": larger logit wins, then lower index.
+CHPE_DEV unsigned long long argmax_key(float v, uint32_t idx) {
+  uint32_t u = __float_as_uint(v);
+  uint32_t o = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((unsigned long long)o << 32) | (unsigned long long)(0xFFFFFFFFu - idx);
+}
+CHPE_DEV float key_value(unsigned long long k) {
+  uint32_t o = (uint32_t)(k >> 32);
+  uint32_t u = (o & 0x80000000u) ? (o & 0x7FFFFFFFu) : ~o;
+  return __uint_as_float(u);
+}
+
+template <int FMT> struct FmtInfo;
+template <> struct FmtInfo<FMT_W4G> { static constexpr int CW = 32, BITS = 4, GROUPED = 1, SB = 0; };
+template <> struct FmtInfo<FMT_W4SB> { static constexpr int CW = 32, BITS = 4, GROUPED = 0, SB = 1; };
+template <> struct FmtInfo<FMT_W2G> { static constexpr int CW = 64, BITS = 2, GROUPED = 1, SB = 0; };
+template <> struct FmtInfo<FMT_W2SB> { static constexpr int CW = 64, BITS = 2, GROUPED = 0, SB = 1; };
+template <> struct FmtInfo<FMT_W8> { static constexpr int CW = 16, BITS = 8, GROUPED = 0, SB = 0; };
+template <> struct FmtInfo<FMT_F16> { static constexpr int CW = 8, BITS = 16, GROUPED = 0, SB = 0; };
+template <> struct FmtInfo<FMT_BF16> { static constexpr int CW = 8, BITS = 16, GROUPED = 0, SB = 0; };
+template <> struct FmtInfo<FMT_F32> { static constexpr int CW = 4, BITS = 32, GROUPED = 0, SB = 0; };
+template <> struct FmtInfo<FMT_I8RAW> { static constexpr int CW = 16, BITS = 8, GROUPED = 0, SB = 0; };
+
+// Shared-memory position of column c for chunk width CW: lane L of slot j
+// reads quad q of its chunk at ((j*CW/4 + q)*32 + L)*4.
+template <int CW>
+CHPE_DEV uint32_t xpos(uint32_t c) {
+  uint32_t chunk = c / CW, L = chunk & 31u, j = chunk >> 5, q = (c % CW) >> 2;
+  return ((j * (CW / 4) + q) * 32u + L) * 4u + (c & 3u);
+}
+template <int CW>
+CHPE_DEV float4 xquad(const float* xs, uint32_t j, uint32_t q, uint32_t L) {
+  return reinterpret_cast<const float4*>(xs)[(j * (CW / 4) + q) * 32u + L];
+}
+
+constexpr uint32_t PRMT_HI = 0x3F000000u;  // bytes 4..7 = 00 00 00 3F
+
+// sum over the chunk of f(c)*x where f = 0.5 + code/256 (4-bit codes).
+CHPE_DEV float2 dot_w4(uint4 v, const float* xs, uint32_t j, uint32_t L) {
+  float2 acc = make_float2(0.f, 0.f);
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    uint32_t lo = w[i] & 0x0F0F0F0Fu, hi = (w[i] >> 4) & 0x0F0F0F0Fu;
+    float4 xa = xquad<32>(xs, j, 2 * i, L), xb = xquad<32>(xs, j, 2 * i + 1, L);
+    float f0 = __uint_as_float(prmt(lo, PRMT_HI, 0x7044u)), f1 = __uint_as_float(prmt(hi, PRMT_HI, 0x7044u));
+    float f2 = __uint_as_float(prmt(lo, PRMT_HI, 0x7144u)), f3 = __uint_as_float(prmt(hi, PRMT_HI, 0x7144u));
+    float f4 = __uint_as_float(prmt(lo, PRMT_HI, 0x7244u)), f5 = __uint_as_float(prmt(hi, PRMT_HI, 0x7244u));
+    float f6 = __uint_as_float(prmt(lo, PRMT_HI, 0x7344u)), f7 = __uint_as_float(prmt(hi, PRMT_HI, 0x7344u));
+    acc = ffma2(make_float2(f0, f1), make_float2(xa.x, xa.y), acc);
+    acc = ffma2(make_float2(f2, f3), make_float2(xa.z, xa.w), acc);
+    acc = ffma2(make_float2(f4, f5), make_float2(xb.x, xb.y), acc);
+    acc = ffma2(make_float2(f6, f7), make_float2(xb.z, xb.w), acc);
+  }
+  return acc;
+}
+
+// 2-bit codebook {0,1,-2,-1}: (code ^ 2) - 2; f = 0.5 + (code^2)/256.
+CHPE_DEV float2 dot_w2(uint4 v, const float* xs, uint32_t j, uint32_t L) {
+  float2 acc = make_float2(0.f, 0.f);
+  const uint32_t w[4] = {v.x ^ 0xAAAAAAAAu, v.y ^ 0xAAAAAAAAu, v.z ^ 0xAAAAAAAAu, v.w ^ 0xAAAAAAAAu};
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    uint32_t m0 = w[i] & 0x03030303u, m1 = (w[i] >> 2) & 0x03030303u;
+    uint32_t m2 = (w[i] >> 4) & 0x03030303u, m3 = (w[i] >> 6) & 0x03030303u;
+#pragma unroll
+    for (int b = 0; b < 4; b++) {
+      const uint32_t sel = 0x7044u | ((uint32_t)b << 8);
+      float4 xq = xquad<64>(xs, j, 4 * i + b, L);
+      float f0 = __uint_as_float(prmt(m0, PRMT_HI, sel)), f1 = __uint_as_float(prmt(m1, PRMT_HI, sel));
+      float f2 = __uint_as_float(prmt(m2, PRMT_HI, sel)), f3 = __uint_as_float(prmt(m3, PRMT_HI, sel));
+      acc = ffma2(make_float2(f0, f1), make_float2(xq.x, xq.y), acc);
+      acc = ffma2(make_float2(f2, f3), make_float2(xq.z, xq.w), acc);
+    }
+  }
+  return acc;
+}
+
+// int8: (b ^ 0x80) placed in the low byte of 2^23 gives 2^23 + b + 128;
+// subtracting 2^23 + 128 is exact.
+CHPE_DEV float2 dot_i8(uint4 v, const float* xs, uint32_t j, uint32_t L) {
+  float2 acc = make_float2(0.f, 0.f);
+  const float2 off = make_float2(-8388736.0f, -8388736.0f);
+  const uint32_t w[4] = {v.x ^ 0x80808080u, v.y ^ 0x80808080u, v.z ^ 0x80808080u, v.w ^ 0x80808080u};
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    float4 xq = xquad<16>(xs, j, i, L);
+    float2 a = make_float2(__uint_as_float(prmt(w[i], 0x4B000000u, 0x7440u)),
+                           __uint_as_float(prmt(w[i], 0x4B000000u, 0x7441u)));
+    float2 b = make_float2(__uint_as_float(prmt(w[i], 0x4B000000u, 0x7442u)),
+                           __uint_as_float(prmt(w[i], 0x4B000000u, 0x7443u)));
+    a = __fadd2_rn(a, off);
+    b = __fadd2_rn(b, off);
+    acc = ffma2(a, make_float2(xq.x, xq.y), acc);
+    acc = ffma2(b, make_float2(xq.z, xq.w), acc);
+  }
+  return acc;
+}
+
+CHPE_DEV float2 dot_f16(uint4 v, const float* xs, uint32_t j, uint32_t L) {
+  float2 acc = make_float2(0.f, 0.f);
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 2; i++) {
+    float4 xq = xquad<8>(xs, j, i, L);
+    float2 a = __half22float2(*reinterpret_cast<const __half2*>(&w[2 * i]));
+    float2 b = __half22float2(*reinterpret_cast<const __half2*>(&w[2 * i + 1]));
+    acc = ffma2(a, make_float2(xq.x, xq.y), acc);
+    acc = ffma2(b, make_float2(xq.z, xq.w), acc);
+  }
+  return acc;
+}
+
+CHPE_DEV float2 dot_bf16(uint4 v, const float* xs, uint32_t j, uint32_t L) {
+  float2 acc = make_float2(0.f, 0.f);
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 2; i++) {
+    float4 xq = xquad<8>(xs, j, i, L);
+    float2 a = make_float2(__uint_as_float(w[2 * i] << 16), __uint_as_float(w[2 * i] & 0xFFFF0000u));
+    float2 b = make_float2(__uint_as_float(w[2 * i + 1] << 16), __uint_as_float(w[2 * i + 1] & 0xFFFF0000u));
+    acc = ffma2(a, make_float2(xq.x, xq.y), acc);
+    acc = ffma2(b, make_float2(xq.z, xq.w), acc);
+  }
+  return acc;
+}
+
+CHPE_DEV float2 dot_f32(uint4 v, const float* xs, uint32_t j, uint32_t L) {
+  float4 xq = xquad<4>(xs, j, 0, L);
+  float2 acc = make_float2(__uint_as_float(v.x) * xq.x, __uint_as_float(v.y) * xq.y);
+  return ffma2(make_float2(__uint_as_float(v.z), __uint_as_float(v.w)), make_float2(xq.z, xq.w), acc);
+}
+
+// Sum over the chunk of (weight code value) * x, in the format's code domain.
+template <int FMT>
+CHPE_DEV float chunk_dot(uint4 v, const float* xs, float xsum, uint32_t j, uint32_t L) {
+  if constexpr (FMT == FMT_W4G || FMT == FMT_W4SB) {
+    float2 a = dot_w4(v, xs, j, L);
+    return 256.0f * (a.x + a.y) - 136.0f * xsum;  // sum (c - 8) x
+  } else if constexpr (FMT == FMT_W2G || FMT == FMT_W2SB) {
+    float2 a = dot_w2(v, xs, j, L);
+    return 256.0f * (a.x + a.y) - 130.0f * xsum;  // sum ((c^2) - 2) x
+  } else if constexpr (FMT == FMT_W8 || FMT == FMT_I8RAW) {
+    float2 a = dot_i8(v, xs, j, L);
+    return a.x + a.y;
+  } else if constexpr (FMT == FMT_F16) {
+    float2 a = dot_f16(v, xs, j, L);
+    return a.x + a.y;
+  } else if constexpr (FMT == FMT_BF16) {
+    float2 a = dot_bf16(v, xs, j, L);
+    return a.x + a.y;
+  } else {
+    float2 a = dot_f32(v, xs, j, L);
+    return a.x + a.y;
+  }
+}
+
+// Address of chunk `ch` of row r and its validity.
+template <int FMT, int KIND>
+CHPE_DEV const uint8_t* chunk_addr(const GemvSrc& s, uint32_t r, uint32_t ch, bool& ok,
+                                   const uint8_t*& payload, uint32_t& grp) {
+  using FI = FmtInfo<FMT>;
+  if constexpr (KIND == SRC_ROWTILE) {
+    uint32_t k = r / s.cell_rows, rin = r - k * s.cell_rows;
+    const uint8_t* cell = s.arc + s.tile0 + (uint64_t)k * s.stride;
+    payload = cell + 16384;
+    grp = rin * (s.cell_cols >> 7) + (ch * FI::CW >> 7);
+    ok = r < s.rows_covered;
+    return cell + (uint64_t)rin * (s.cell_cols * FI::BITS / 8) + 16u * ch;
+  } else if constexpr (KIND == SRC_FLAT) {
+    uint64_t f = (uint64_t)r * s.c_total + (uint64_t)FI::CW * ch;
+    ok = f < s.flat_limit;
+    uint64_t t = f >> 15;
+    uint32_t off = (uint32_t)(f & 32767u);
+    const uint8_t* cell = s.arc + s.tile0 + t * s.stride;
+    payload = cell + 16384;
+    grp = off >> 7;
+    return cell + off * FI::BITS / 8;
+  } else {  // SRC_RAW: tiles are contiguous
+    uint64_t f = (uint64_t)r * s.c_total + (uint64_t)FI::CW * ch;
+    ok = f < s.flat_limit;
+    payload = nullptr;
+    grp = 0;
+    return s.arc + s.tile0 + f * (FI::BITS / 8);
+  }
+}
+
+// Dot product of one row against the staged x for this lane's chunks.
+template <int FMT, int KIND>
+CHPE_DEV float row_dot(const GemvSrc& s, uint32_t r, const float* xs, const float* xsum,
+                       uint32_t nchunks, uint32_t L) {
+  using FI = FmtInfo<FMT>;
+  constexpr int UNR = 4;
+  float acc = 0.f;
+  const uint32_t nslots = (nchunks + 31) >> 5;
+  for (uint32_t j0 = 0; j0 < nslots; j0 += UNR) {
+    uint4 v[UNR];
+    bool ok[UNR];
+    const uint8_t* pl[UNR];
+    uint32_t grp[UNR];
+#pragma unroll
+    for (int u = 0; u < UNR; u++) {
+      uint32_t ch = L + 32u * (j0 + u);
+      ok[u] = false;
+      pl[u] = nullptr;
+      grp[u] = 0;
+      if (j0 + u < nslots && ch < nchunks) {
+        const uint8_t* a = chunk_addr<FMT, KIND>(s, r, ch, ok[u], pl[u], grp[u]);
+        if (ok[u]) v[u] = ld_stream(a);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < UNR; u++) {
+      if (!ok[u]) continue;
+      uint32_t ch = L + 32u * (j0 + u);
+      float xsm = xsum[ch];
+      float d = chunk_dot<FMT>(v[u], xs, xsm, j0 + u, L);
+      if constexpr (FI::GROUPED) {
+        acc = fmaf(d, ld_f16(pl[u] + 48 + 2 * grp[u]), acc);
+      } else if constexpr (FI::SB) {
+        acc = fmaf(d, ld_f32(pl[u] + 32), acc);
+        acc = fmaf(ld_f32(pl[u] + 36), xsm, acc);
+      } else {
+        acc += d;
+      }
+    }
+  }
+  return acc;
+}
+
+// Additive row outliers of W4G/W2G row-tiled cells with 16 rows
+// (chpe_engine.zig:244-256, 309-315): lanes 0..7 each add one term.
+// With OUTL_REPLACE (tied embedding head, unpackEmbedRowCell :1335-1344,
+// :1369-1378) the cell's decoded value at col is replaced instead: lane k adds
+// (w_k - decoded)*x unless a later entry names the same column.
+CHPE_DEV float outlier_term(const GemvSrc& s, uint32_t r, const float* xs, uint32_t L, int cw) {
+  if (L >= 8 || r >= s.rows_covered) return 0.f;
+  uint32_t k = r / s.cell_rows, rin = r - k * s.cell_rows;
+  const uint8_t* code = s.arc + s.tile0 + (uint64_t)k * s.stride;
+  const uint8_t* pl = code + 16384;
+  uint32_t col = ld_u16(pl + 816 + 2 * L);
+  if (col >= s.x_len) return 0.f;
+  float xv = (cw == 32) ? xs[xpos<32>(col)] : xs[xpos<64>(col)];
+  float w = ld_f16(pl + 560 + 2 * (rin * 8 + L));
+  if (s.outliers == OUTL_ADD) return w * xv;
+  for (uint32_t k2 = L + 1; k2 < 8; k2++)
+    if (ld_u16(pl + 816 + 2 * k2) == col) return 0.f;
+  float sc = ld_f16(pl + 48 + 2 * (rin * (s.cell_cols >> 7) + (col >> 7)));
+  float dec;
+  if (cw == 32) {
+    uint8_t b = code[rin * (s.cell_cols / 2) + col / 2];
+    dec = ((float)((col & 1) ? (b >> 4) & 15 : b & 15) - 8.0f) * sc;
+  } else {
+    const float CB[4] = {0.f, 1.f, -2.f, -1.f};
+    uint8_t b = code[rin * (s.cell_cols / 4) + col / 4];
+    dec = CB[(b >> (2 * (col & 3))) & 3] * sc;
+  }
+  return (w - dec) * xv;
+}
+
+template <int FMT, int KIND, int THREADS>
+__global__ void __launch_bounds__(THREADS) gemv_kernel(const __grid_constant__ GemvLaunch P) {
+  using FI = FmtInfo<FMT>;
+  extern __shared__ __align__(16) float smem[];
+  const uint32_t tid = threadIdx.x, L = tid & 31u, warp = tid >> 5;
+  const uint32_t nwarps = THREADS / 32;
+  const uint32_t ncols = P.ncols;
+  const uint32_t nchunks = (ncols + FI::CW - 1) / FI::CW;
+  const uint32_t nslots = (nchunks + 31) >> 5;
+  float* xs = smem;
+  float* xsum = smem + nslots * 32u * FI::CW;
+  __shared__ float red[THREADS / 32];
+
+  // Weight prefetch into L2 before waiting on the predecessor kernel.
+  for (int sg = 0; sg < 3; sg++) {
+    uint64_t nb = P.prefetch_bytes[sg];
+    if (!nb) continue;
+    uint64_t per = ((nb + gridDim.x - 1) / gridDim.x + 15) & ~15ull;
+    uint64_t b0 = per * blockIdx.x, b1 = b0 + per < nb ? b0 + per : nb;
+    for (uint64_t o = b0 + (uint64_t)tid * 16384; o < b1; o += (uint64_t)THREADS * 16384) {
+      uint64_t n = b1 - o < 16384 ? b1 - o : 16384;
+      n &= ~15ull;
+      if (n) prefetch_l2(P.prefetch_base[sg] + o, (uint32_t)n);
+    }
+  }
+  pdl_wait();
+  if (!P.ignore_stop && P.st->stop) return;
+
+  // ---- stage x (optionally RMSNorm'ed) into shared memory ----------------
+  const float* xin = P.x;
+  float ss = 0.f, tot = 0.f;
+  for (uint32_t c = tid; c < nslots * 32u * FI::CW; c += THREADS) {
+    float v = c < ncols ? xin[c] : 0.f;
+    if (P.norm) ss += v * v;
+    xs[xpos<FI::CW>(c)] = v;
+  }
+  if (P.norm) {
+    ss = warp_sum(ss);
+    if (L == 0) red[warp] = ss;
+    __syncthreads();
+    for (uint32_t w = 0; w < nwarps; w++) tot += red[w];
+    if (P.check_layer >= 0) {
+      // end-of-layer check of the reference's debug block (chpe_engine.zig:1753-1764)
+      int l = P.check_layer;
+      bool cond = l < 3 || (l >= 8 && l <= 16) || !isfinite(xin[0]);
+      if (cond && !isfinite(tot)) {
+        if (blockIdx.x == 0 && tid == 0) P.st->stop = 1;
+        return;
+      }
+    }
+    const float inv = 1.0f / sqrtf(tot / (float)ncols + P.eps);
+    __syncthreads();
+    for (uint32_t c = tid; c < ncols; c += THREADS) {
+      uint32_t p = xpos<FI::CW>(c);
+      xs[p] = xs[p] * inv * P.gamma[c];
+    }
+  }
+  __syncthreads();
+  for (uint32_t ch = tid; ch < nchunks; ch += THREADS) {
+    float s = 0.f;
+    for (int e = 0; e < FI::CW; e++) {
+      uint32_t c = ch * FI::CW + e;
+      if (c < ncols) s += xs[xpos<FI::CW>(c)];
+    }
+    xsum[ch] = s;
+  }
+  if (P.xn_out && blockIdx.x == 0)
+    for (uint32_t c = tid; c < ncols; c += THREADS) P.xn_out[c] = xs[xpos<FI::CW>(c)];
+  __syncthreads();
+  pdl_launch_dependents();
+
+  // ---- rows --------------------------------------------------------------
+  unsigned long long lbest = 0ull;  // EPI_LOGITS per-lane (lane 0) running best
+  uint32_t lfin = 1u;
+  const uint32_t total = P.epi == EPI_SWIGLU ? P.row_start[1] : P.row_start[P.nseg];
+  for (uint32_t job = blockIdx.x * nwarps + warp; job < total; job += gridDim.x * nwarps) {
+    if (P.epi == EPI_SWIGLU) {
+      float g = row_dot<FMT, KIND>(P.src[0], job, xs, xsum, nchunks, L);
+      float u = row_dot<FMT, KIND>(P.src[1], job, xs, xsum, nchunks, L);
+      if constexpr (KIND == SRC_ROWTILE && FI::GROUPED) {
+        if (P.src[0].outliers) g += outlier_term(P.src[0], job, xs, L, FI::CW);
+        if (P.src[1].outliers) u += outlier_term(P.src[1], job, xs, L, FI::CW);
+      }
+      g = warp_sum(g);
+      u = warp_sum(u);
+      if (L == 0) P.out[0][job] = silu_ref(g) * u;
+      continue;
+    }
+    int sg = 0;
+    while (sg + 1 < P.nseg && job >= P.row_start[sg + 1]) sg++;
+    const GemvSrc& s = P.src[sg];
+    uint32_t r = job - P.row_start[sg];
+    float d = row_dot<FMT, KIND>(s, r, xs, xsum, nchunks, L);
+    if constexpr (KIND == SRC_ROWTILE && FI::GROUPED) {
+      if (s.outliers) d += outlier_term(s, r, xs, L, FI::CW);
+    }
+    d = warp_sum(d);
+    if (L == 0) {
+      if constexpr (FMT == FMT_I8RAW) d *= 0.00373708f;
+      float* y = P.out[sg];
+      if (P.epi == EPI_LOGITS) {
+        y[r] = d;
+        if (!isfinite(d)) lfin = 0u;
+        if (d > -1e30f) {
+          unsigned long long kk = argmax_key(d, r);
+          lbest = kk > lbest ? kk : lbest;
+        }
+      } else if (P.epi == EPI_ACCUM) {
+        float v = y[r] + d;
+        if (s.bias) v += s.bias[r];
+        y[r] = v;
+      } else {
+        y[r] = s.bias ? d + s.bias[r] : d;
+      }
+    }
+  }
+  if (P.epi == EPI_LOGITS) {
+    // argmax / finiteness over this CTA, then one atomic each; the last CTA
+    // to arrive writes the step result (chpe_engine.zig:1775-1802).
+    __shared__ unsigned long long kbest[THREADS / 32];
+    __shared__ uint32_t kfin[THREADS / 32];
+    __shared__ int is_last;
+    if (L == 0) { kbest[warp] = lbest; kfin[warp] = lfin; }
+    __syncthreads();
+    if (tid == 0) {
+      unsigned long long b = 0ull;
+      uint32_t f = 1u;
+      for (uint32_t w = 0; w < nwarps; w++) { b = kbest[w] > b ? kbest[w] : b; f &= kfin[w]; }
+      if (b) atomicMax(&P.st->best, b);
+      if (!f) atomicAnd(&P.st->finite, 0u);
+      __threadfence();
+      unsigned prev = atomicAdd(&P.st->done_ctas, 1u);
+      is_last = prev == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (is_last && tid == 0) {
+      __threadfence();
+      unsigned long long b = atomicAdd(&P.st->best, 0ull);
+      StepResult R;
+      R.argmax_token = b ? 0xFFFFFFFFu - (uint32_t)(b & 0xFFFFFFFFull) : 0u;
+      R.max_logit = b ? key_value(b) : -1e30f;
+      R.token0_logit = __ldcg(P.out[0]);
+      R.hidden_norm = sqrtf(tot);
+      R.all_finite = (int32_t)atomicAdd(&P.st->finite, 0u);
+      R.pos = P.st->pos;
+      *P.res = R;
+      if (P.gen_tokens && P.st->n_gen < P.max_gen) P.gen_tokens[P.st->n_gen] = (int32_t)R.argmax_token;
+      P.st->n_gen += 1;
+      P.st->pos += 1;
+      P.st->best = 0ull;
+      P.st->finite = 1u;
+      P.st->done_ctas = 0u;
+    }
+  }
+}
+
+// ---- generic exact path (any cell format, per-tile dispatch) --------------
+// Restates gemvTilePolymorphic / gemvCellFlat one weight at a time; used for
+// archives whose tensors mix formats or geometries.
+CHPE_DEV float cell_weight_rowtile(const uint8_t* cell_code, uint32_t qb, uint64_t flags,
+                                   float scale, float bias, uint32_t cols, uint32_t rin,
+                                   uint32_t c) {
+  const uint8_t* pl = cell_code + 16384;
+  const bool g128 = (flags & 1u) != 0;
+  if (qb == 4) {
+    uint8_t b = cell_code[rin * (cols / 2) + c / 2];
+    int n = (c & 1) ? (b >> 4) & 15 : b & 15;
+    if (g128) return ((float)n - 8.0f) * ld_f16(pl + 48 + 2 * (rin * (cols / 128) + c / 128));
+    return (float)(n - 8) * scale + bias;
+  } else if (qb == 8) {
+    return (float)(int8_t)cell_code[rin * cols + c];
+  } else if (qb == 16) {
+    uint16_t h = ld_u16(cell_code + 2 * ((uint64_t)rin * cols + c));
+    return (flags & 4u) ? h2f(h) : bf2f(h);
+  } else if (qb == 32) {
+    return ld_f32(cell_code + 4 * ((uint64_t)rin * cols + c));
+  }
+  const float CB[4] = {0.f, 1.f, -2.f, -1.f};
+  uint8_t b = cell_code[rin * (cols / 4) + c / 4];
+  float cb = CB[(b >> (2 * (c & 3))) & 3];
+  if (g128) return cb * ld_f16(pl + 48 + 2 * (rin * (cols / 128) + c / 128));
+  return cb * scale + bias;
+}
+
+struct GenLaunch {
+  GemvSrc src;
+  float* y;
+  const float* x;
+  int32_t accumulate;
+  StepState* st;
+};
+
+// Row-tiled cells of any format: one warp per row.
+__global__ void __launch_bounds__(256) gemv_generic_rowtile(const __grid_constant__ GenLaunch P) {
+  pdl_wait();
+  if (P.st && P.st->stop) return;
+  const GemvSrc& s = P.src;
+  const uint32_t L = threadIdx.x & 31u;
+  for (uint32_t r = blockIdx.x * 8 + (threadIdx.x >> 5); r < s.r_total; r += gridDim.x * 8) {
+    uint32_t k = s.row_cell[r];
+    if (k == 0xFFFFFFFFu) {  // not covered by any cell: stays 0 (or untouched)
+      if (L == 0) {
+        float v = P.accumulate ? P.y[r] : 0.f;
+        if (s.bias) v += s.bias[r];
+        P.y[r] = v;
+      }
+      continue;
+    }
+    uint32_t rin = s.row_in_cell[r];
+    const uint8_t* code = s.arc + s.tile0 + (uint64_t)k * s.stride;
+    const uint8_t* pl = code + 16384;
+    uint32_t qb = pl[20];
+    uint64_t flags = *reinterpret_cast<const uint64_t*>(pl + 24);
+    float scale = ld_f32(pl + 32), bias = ld_f32(pl + 36);
+    uint32_t rows = *reinterpret_cast<const uint32_t*>(pl + 40);
+    uint32_t cols = *reinterpret_cast<const uint32_t*>(pl + 44);
+    bool g128 = (flags & 1u) != 0;
+    uint32_t ncols;
+    if ((qb == 4 || (qb != 8 && qb != 16 && qb != 32)) && g128)
+      ncols = min(cols / 128, s.x_len / 128) * 128;
+    else if (qb == 4)
+      ncols = min(cols / 2, s.x_len / 2) * 2;
+    else if (qb != 8 && qb != 16 && qb != 32)
+      ncols = min(cols / 4, s.x_len / 4) * 4;
+    else
+      ncols = min(cols, s.x_len);
+    float acc = 0.f;
+    for (uint32_t c = L; c < ncols; c += 32)
+      acc = fmaf(cell_weight_rowtile(code, qb, flags, scale, bias, cols, rin, c), P.x[c], acc);
+    if ((qb == 4 || (qb != 8 && qb != 16 && qb != 32)) && g128 && rows == 16 && L < 8) {
+      uint32_t col = ld_u16(pl + 816 + 2 * L);
+      float xv = col < s.x_len ? P.x[col] : 0.f;
+      acc = fmaf(ld_f16(pl + 560 + 2 * (rin * 8 + L)), xv, acc);
+    }
+    acc = warp_sum(acc);
+    if (qb == 8) acc = acc * scale + bias;
+    if (L == 0) {
+      float v = P.accumulate ? P.y[r] + acc : acc;
+      if (s.bias) v += s.bias[r];
+      P.y[r] = v;
+    }
+  }
+}
+
+// Flat cells of any format: one warp per row, per-chunk tile dispatch.
+__global__ void __launch_bounds__(256) gemv_generic_flat(const __grid_constant__ GenLaunch P) {
+  pdl_wait();
+  if (P.st && P.st->stop) return;
+  const GemvSrc& s = P.src;
+  const uint32_t L = threadIdx.x & 31u;
+  const float CB[4] = {0.f, 1.f, -2.f, -1.f};
+  for (uint32_t r = blockIdx.x * 8 + (threadIdx.x >> 5); r < s.r_total; r += gridDim.x * 8) {
+    float acc = 0.f;
+    uint64_t f0 = (uint64_t)r * s.c_total;
+    for (uint32_t c = L; c < s.c_total; c += 32) {
+      uint64_t f = f0 + c;
+      if (f >= s.flat_limit) break;
+      uint64_t t = f >> 15;
+      uint32_t off = (uint32_t)(f & 32767u);
+      const uint8_t* code = s.arc + s.tile0 + t * s.stride;
+      const uint8_t* pl = code + 16384;
+      uint32_t qb = pl[20];
+      uint64_t flags = *reinterpret_cast<const uint64_t*>(pl + 24);
+      bool g128 = (flags & 1u) != 0;
+      float w = 0.f;
+      if (qb == 4) {
+        uint8_t b = code[off / 2];
+        int n = (off & 1) ? (b >> 4) & 15 : b & 15;
+        w = g128 ? ((float)n - 8.0f) * ld_f16(pl + 48 + 2 * (off >> 7))
+                 : ((float)n - 8.0f) * ld_f32(pl + 32) + ld_f32(pl + 36);
+      } else if (qb == 2) {
+        uint8_t b = code[off / 4];
+        float cb = CB[(b >> (2 * (off & 3))) & 3];
+        w = g128 ? cb * ld_f16(pl + 48 + 2 * (off >> 7)) : cb * ld_f32(pl + 32) + ld_f32(pl + 36);
+      }
+      if (qb == 4 || qb == 2) {
+        uint32_t n = ld_u16(pl + 560);
+        if (n > 0 && n <= 64) {
+          for (uint32_t m = 0; m < n; m++)
+            if (ld_u16(pl + 690 + 2 * m) == off) w = ld_f16(pl + 562 + 2 * m);
+        }
+      }
+      acc = fmaf(w, P.x[c], acc);
+    }
+    acc = warp_sum(acc);
+    if (L == 0) {
+      float v = P.accumulate ? P.y[r] + acc : acc;
+      if (s.bias) v += s.bias[r];
+      P.y[r] = v;
+    }
+  }
+}
+
+// down_aux replacements of uniform flat cells: one thread per (tile, entry);
+// adds (replacement - decoded) * x to the row it lands in.  Only the last
+// entry for a given offset counts (later entries overwrite earlier ones).
+struct AuxLaunch {
+  GemvSrc src;
+  float* y;
+  const float* x;
+  StepState* st;
+};
+__global__ void flat_aux_fix(const __grid_constant__ AuxLaunch P) {
+  pdl_wait();
+  if (P.st && P.st->stop) return;
+  const GemvSrc& s = P.src;
+  const float CB[4] = {0.f, 1.f, -2.f, -1.f};
+  uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  uint64_t t = i >> 6;
+  uint32_t m = (uint32_t)(i & 63u);
+  if (t >= s.n_tiles) return;
+  const uint8_t* code = s.arc + s.tile0 + t * s.stride;
+  const uint8_t* pl = code + 16384;
+  uint32_t qb = pl[20];
+  if (qb != 4 && qb != 2) return;
+  uint32_t n = ld_u16(pl + 560);
+  if (n == 0 || n > 64 || m >= n) return;
+  uint32_t off = ld_u16(pl + 690 + 2 * m);
+  if (off >= 32768) return;
+  for (uint32_t m2 = m + 1; m2 < n; m2++)
+    if (ld_u16(pl + 690 + 2 * m2) == off) return;
+  uint64_t f = t * 32768u + off;
+  if (f >= s.flat_limit) return;
+  uint64_t r = f / s.c_total, c = f % s.c_total;
+  if (r >= s.r_total) return;
+  uint64_t flags = *reinterpret_cast<const uint64_t*>(pl + 24);
+  bool g128 = (flags & 1u) != 0;
+  float w;
+  if (qb == 4) {
+    uint8_t b = code[off / 2];
+    int nn = (off & 1) ? (b >> 4) & 15 : b & 15;
+    w = g128 ? ((float)nn - 8.0f) * ld_f16(pl + 48 + 2 * (off >> 7))
+             : ((float)nn - 8.0f) * ld_f32(pl + 32) + ld_f32(pl + 36);
+  } else {
+    uint8_t b = code[off / 4];
+    float cb = CB[(b >> (2 * (off & 3))) & 3];
+    w = g128 ? cb * ld_f16(pl + 48 + 2 * (off >> 7)) : cb * ld_f32(pl + 32) + ld_f32(pl + 36);
+  }
+  float repl = ld_f16(pl + 562 + 2 * m);
+  atomicAdd(&P.y[r], (repl - w) * P.x[c]);
+}
+
+}  // namespace chpe

@@ -1,0 +1,143 @@
+/*
+ * chpe.h -- C ABI of the B200 decode engine (libchpe.so).
+ *
+ * The first block is exactly the FFI surface of chpe-qwen-engine's
+ * src/chpe_c_api.zig: same names, argument meaning, sentinels and
+ * ownership.  Each declaration cites the reference interface it replaces.
+ * The second block adds entry points the reference lacks; the third holds
+ * test probes used by the parity suite.
+ *
+ * Threading: a context is not thread-safe (one context per thread), calls
+ * are synchronous, as in the reference.  Each context owns one CUDA stream on
+ * one device.
+ */
+#ifndef CHPE_H
+#define CHPE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- reference surface (src/chpe_c_api.zig) ------------------------------ */
+
+/* chpe_c_api.zig:25-48.  Opens and validates the archive (mmap, read-only),
+ * picks the architecture from the path ("9B"/"9b"/"qwen35" -> Qwen3.5-9B,
+ * "72B"/"72b" -> Qwen2.5-72B, else Qwen2.5-3B), uploads it to HBM and builds
+ * the engine with max_seq_len 2048 on CUDA device 0.  NULL on any failure. */
+void *chpe_init(const char *archive_path);
+
+/* chpe_c_api.zig:50-78.  Runs tokens[0..num_tokens) at positions
+ * 0..num_tokens-1 (a fresh sequence on every call), keeps the last step's
+ * logits, copies them to out_logits when it is non-NULL (vocab floats,
+ * unchecked) and returns the last argmax.  -1 when ctx or tokens is NULL,
+ * num_tokens is 0, num_tokens exceeds max_seq_len, or the device failed. */
+int chpe_forward_tokens(void *ctx, const uint32_t *tokens, size_t num_tokens,
+                        float *out_logits);
+
+/* chpe_c_api.zig:80-87.  Copies the last logits; returns vocab, or 0 when a
+ * pointer is NULL or max_len < vocab. */
+size_t chpe_get_last_logits(void *ctx, float *out_logits, size_t max_len);
+
+/* chpe_c_api.zig:89-105.  A NULL ctx answers for Qwen2.5-3B. */
+size_t chpe_get_vocab_size(void *ctx);
+size_t chpe_get_hidden_dim(void *ctx);
+size_t chpe_get_num_layers(void *ctx);
+
+/* chpe_c_api.zig:107-135.  Fields of the last ForwardResult
+ * (chpe_engine.zig:803-810); a NULL ctx returns 0. */
+uint64_t chpe_get_last_elapsed_ns(void *ctx);
+uint32_t chpe_get_last_argmax(void *ctx);
+float chpe_get_last_max_logit(void *ctx);
+float chpe_get_last_token0_logit(void *ctx);
+float chpe_get_last_hidden_norm(void *ctx);
+
+/* chpe_c_api.zig:137-143.  NULL-safe. */
+void chpe_free(void *ctx);
+
+/* ---- additions (no counterpart in the reference) ------------------------- */
+
+/* Architecture ids for the calls below; CHPE_ARCH_BY_PATH picks from the
+ * path as chpe_init does. */
+#define CHPE_ARCH_BY_PATH (-1)
+#define CHPE_ARCH_QWEN2_5_3B 0
+#define CHPE_ARCH_QWEN3_5_9B 1
+#define CHPE_ARCH_QWEN2_5_72B 2
+
+/* chpe_init with the architecture, max_seq_len and CUDA device chosen by the
+ * caller (chpe_init fixes them to path-derived, 2048 and 0). */
+void *chpe_init_ex(const char *archive_path, int arch, uint32_t max_seq_len, int device);
+
+/* The engine over archive bytes held by the caller (CHPEEngine.init,
+ * chpe_engine.zig:854, which takes bytes, not a path).  No header validation,
+ * exactly as the engine-level reference: an invalid archive runs the
+ * reference's synthetic fallbacks.  The bytes are copied to the device and
+ * must stay valid until chpe_free (small tensors are read from them at init). */
+void *chpe_init_bytes(const void *bytes, uint64_t len, int arch, uint32_t max_seq_len,
+                      int device);
+
+/* WeightArchive.validate (weight_archive.zig:152-172): 0 when valid, else the
+ * error: 1 InvalidMagic, 2 UnsupportedVersion, 3 BadGeometry, 4 Truncated,
+ * 6 FileTooSmall, 10 MisalignedHeader. */
+int chpe_validate_archive(const void *bytes, uint64_t len);
+
+/* One forwardDecode(token, pos) step that continues the current sequence
+ * (the reference's ABI can only restart at 0).  Returns the argmax or -1. */
+int chpe_decode_step(void *ctx, uint32_t token, uint32_t pos, float *out_logits);
+
+/* Greedy generation on the device: runs the prompt from position 0, then
+ * n_gen tokens, each the argmax of the step before, without host round
+ * trips.  out_tokens receives n_gen ids.  0 on success, -1 on error. */
+int chpe_generate(void *ctx, const uint32_t *prompt, size_t n_prompt, size_t n_gen,
+                  uint32_t *out_tokens);
+
+/* Benchmark helpers.  chpe_bench_greedy: n greedy steps from the current
+ * position, device time by CUDA events on the engine stream.
+ * chpe_bench_host: n steps with host tokens, each step copying its token in
+ * and its logits (to `logits`, vocab floats) and result out; wall time. */
+int chpe_bench_greedy(void *ctx, size_t n_steps, float *device_ms);
+int chpe_bench_host(void *ctx, const uint32_t *tokens, size_t n_steps, float *logits,
+                    double *wall_ms);
+
+/* Per-kernel timing for the roofline: launches every recorded op of one role
+ * (1 QKV, 2 attention, 3 O, 4 gate/up, 5 down, 6 LM head, 7 embedding)
+ * across all layers, `rounds` times, on the engine stream, so consecutive
+ * launches stream different layers' weights from HBM.  Gives the average
+ * milliseconds per launch, the algorithmic weight bytes per launch (codes +
+ * scales of the rows used) and the launch count.  Needs a prior forward. */
+int chpe_bench_kernel(void *ctx, int role, int rounds, float *avg_ms, double *bytes_per_launch,
+                      int *launches);
+
+/* all_finite of the last ForwardResult (1/0; 0 for NULL). */
+int chpe_get_last_all_finite(void *ctx);
+/* Kernels launched per decode step (graph nodes). */
+int chpe_kernels_per_step(void *ctx);
+/* Current sequence position (next step's pos). */
+uint32_t chpe_get_position(void *ctx);
+/* Last error message of ctx, or of the calling thread's last failed init
+ * when ctx is NULL; "" when none. */
+const char *chpe_last_error(void *ctx);
+
+/* ---- probes for the parity tests ------------------------------------------ */
+
+/* gemvLinear (chpe_engine.zig:1396) on the device over host vectors:
+ * y (r_total floats) is read (for accumulate) and written.  bias_tile < 0:
+ * none.  0 on success. */
+int chpe_probe_gemv_linear(void *ctx, uint64_t tile_start, uint64_t num_tiles, const float *x,
+                           uint64_t x_len, float *y, uint64_t r_total, uint64_t c_total,
+                           int accumulate, int64_t bias_tile);
+/* unpackEmbedRow (chpe_engine.zig:1491) for one token into out (hidden_dim
+ * floats, read first: rows the reference leaves unwritten keep them). */
+int chpe_probe_embed(void *ctx, uint32_t token, float *out);
+/* Dequantised weights of one cell as the reference materialises them
+ * (flat != 0: gemvCellFlat's 32768 tile weights; else rows*cols row-tiled
+ * weights).  *n_out receives the count.  0 on success. */
+int chpe_probe_dequant_cell(void *ctx, uint64_t tile, int flat, float *out, uint64_t cap,
+                            uint64_t *n_out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CHPE_H */

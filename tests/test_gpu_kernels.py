@@ -1,0 +1,108 @@
+"""Kernel-level parity on the GPU, through the C ABI probes, against the CPU
+oracle: bit-exact dequantised tiles and embedding rows; GEMV per call site
+within f32 accumulation-order tolerance."""
+import numpy as np
+import pytest
+
+import chpe_qwen_engine_b200 as chpe
+import oracle_py as O
+from _util import archive, assert_close_vec, oracle_threads
+
+pytestmark = pytest.mark.gpu
+
+CELL_CONFIGS = [
+    (chpe.SYNTH_3B_W4, 0),
+    (chpe.SYNTH_3B_W2, 0),
+    (chpe.SYNTH_3B_W4, chpe.SYNTH_OUTLIERS),
+    (chpe.SYNTH_3B_W4, chpe.SYNTH_NONGROUP | chpe.SYNTH_STANDARD),
+    (chpe.SYNTH_3B_W4, chpe.SYNTH_MIXED | chpe.SYNTH_BIAS),
+]
+
+
+def engines(cfg, flags, max_seq=64):
+    a = archive(cfg, flags)
+    e = chpe.Engine.from_bytes(a, chpe.SYNTH_ARCH[cfg], max_seq)
+    o = O.OracleEngine(a, chpe.SYNTH_ARCH[cfg], max_seq, threads=oracle_threads())
+    return a, e, o
+
+
+@pytest.mark.parametrize("cfg,flags", CELL_CONFIGS)
+def test_dequant_cells_bit_exact(cfg, flags):
+    a, e, o = engines(cfg, flags)
+    stride = 20480 if flags & chpe.SYNTH_STANDARD else 17408
+    pre = 3072 if flags & chpe.SYNTH_STANDARD else 0
+    tiles = []
+    for l in (0, 1, 7, 21, 35):
+        li = o.layer_info(l)
+        for name in ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj"):
+            tiles.append((li[name], False))
+            tiles.append((li[name] + 3, False))
+        tiles.append((li["down_proj"], True))
+        tiles.append((li["down_proj"] + 100, True))
+    tiles += [(0, False), (9495, False)]
+    for t, flat in tiles:
+        cell = a[4096 + t * stride + pre:4096 + t * stride + pre + 17408]
+        ref = O.dequant_cell(np.ascontiguousarray(cell), flat)
+        got = e.probe_dequant_cell(t, flat)
+        assert got.shape == ref.shape, (t, flat)
+        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), (t, flat)
+
+
+@pytest.mark.parametrize("cfg,flags", CELL_CONFIGS + [(chpe.SYNTH_3B_FP16_RAW, 0), (chpe.SYNTH_3B_BF16_RAW, 0)])
+def test_embedding_rows_bit_exact(cfg, flags):
+    a, e, o = engines(cfg, flags)
+    rng = np.random.default_rng(3)
+    for tok in [0, 1, 15, 16, 151935, 151936, 200000] + list(rng.integers(0, 151936, 12)):
+        init = np.full(o.hidden_dim, 7.0, np.float32)
+        ref = o.embed(int(tok), init.copy())
+        got = e.probe_embed(int(tok), init.copy())
+        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), tok
+
+
+def _call_sites(o, l):
+    li = o.layer_info(l)
+    D, F, qd, kvd = 2048, 11008, 2048, 256
+    return [
+        ("q", li["q_proj"], li["q_tiles"], qd, D, D, False, li["q_bias"]),
+        ("k", li["k_proj"], li["k_tiles"], kvd, D, D, False, li["k_bias"]),
+        ("v", li["v_proj"], li["v_tiles"], kvd, D, D, False, li["v_bias"]),
+        ("o", li["o_proj"], li["o_tiles"], D, D, D, True, -1),
+        ("gate", li["gate_proj"], li["gate_tiles"], F, D, D, False, -1),
+        ("up", li["up_proj"], li["up_tiles"], F, D, D, False, -1),
+        ("down", li["down_proj"], li["down_tiles"], D, F, F, True, -1),
+    ]
+
+
+@pytest.mark.parametrize("cfg,flags", CELL_CONFIGS + [(chpe.SYNTH_3B_FP16_RAW, 0)])
+def test_gemv_linear_call_sites(cfg, flags):
+    a, e, o = engines(cfg, flags)
+    rng = np.random.default_rng(11)
+    for l in (0, 5, 21):
+        for name, ts, nt, r, c, xl, acc, bias in _call_sites(o, l):
+            x = rng.standard_normal(xl).astype(np.float32)
+            y0 = rng.standard_normal(r).astype(np.float32) if acc else np.zeros(r, np.float32)
+            ref = o.gemv_linear(ts, nt, x, r, c, accumulate=acc, bias_tile=bias, y=y0.copy())
+            got = e.probe_gemv_linear(ts, nt, x, r, c, accumulate=acc, bias_tile=bias, y=y0.copy())
+            assert_close_vec(got, ref, 1e-4, f"layer {l} {name}")
+
+
+def test_gemv_partial_spans_and_past_end():
+    """Fewer tiles than rows (rows beyond stay 0), a start past the archive
+    (synthetic pattern / no-op), and a span cut by the archive's end."""
+    a, e, o = engines(chpe.SYNTH_3B_W4, 0)
+    rng = np.random.default_rng(5)
+    li = o.layer_info(3)
+    x = rng.standard_normal(2048).astype(np.float32)
+    xf = rng.standard_normal(11008).astype(np.float32)
+    cases = [
+        (li["q_proj"], 40, 2048, 2048, x, False),   # 40 row-tiled cells cover 640 rows
+        (li["down_proj"], 100, 2048, 11008, xf, False),  # flat: first 100 tiles only
+        (94349 + 5, 10, 300, 2048, x, False),        # past the end: pattern
+        (94349 + 5, 10, 300, 2048, x, True),         # past the end, accumulate: untouched
+        (94340, 50, 160, 2048, x, False),            # cut by the archive end
+    ]
+    for ts, nt, r, c, xv, acc in cases:
+        y0 = rng.standard_normal(r).astype(np.float32)
+        ref = o.gemv_linear(ts, nt, xv, r, c, accumulate=acc, y=y0.copy())
+        got = e.probe_gemv_linear(ts, nt, xv, r, c, accumulate=acc, y=y0.copy())
+        assert_close_vec(got, ref, 1e-4, f"{ts},{nt},{r},{c},{acc}")
