@@ -212,13 +212,15 @@ def run_ours(args, rank, world, local, dist):
     # whole-step algorithmic bytes (all roles)
     step_bytes = 0.0
     per_role = {}
-    for role, name in ((chpe.ROLE_QKV, "qkv"), (chpe.ROLE_O, "o"), (chpe.ROLE_GATEUP, "gateup"),
-                       (chpe.ROLE_DOWN, "down"), (chpe.ROLE_LMHEAD, "lmhead")):
+    for role, name in ((chpe.ROLE_QKV, "qkv"), (chpe.ROLE_ATTN, "attention"), (chpe.ROLE_O, "o"),
+                       (chpe.ROLE_GATEUP, "gateup"), (chpe.ROLE_DOWN, "down"),
+                       (chpe.ROLE_LMHEAD, "lmhead")):
         m, b, n = eng.bench_kernel(role, rounds=2)
         launches_per_step = n // 2
         step_bytes += b * launches_per_step
-        per_role[name] = {"avg_us": round(m * 1000, 2), "bytes_per_launch": b,
-                          "gbs": round(b / (m / 1000) / 1e9, 1)}
+        per_role[name] = {"avg_us": round(m * 1000, 2), "launches_per_step": launches_per_step,
+                          "bytes_per_launch": b,
+                          "gbs": round(b / (m / 1000) / 1e9, 1) if b else None}
     cpu = None
     if rank == 0:
         sample_steps = int(os.environ.get("CHPE_CPU_SAMPLE_STEPS", "3"))

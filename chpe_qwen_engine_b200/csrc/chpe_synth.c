@@ -262,6 +262,9 @@ static void write_rowtile(uint8_t *cell, const Plan *p, uint8_t fmt, uint16_t ro
       write_codes(codes, (size_t)rows * cols * b / 8, r);
       float s = rng_normal(r) * 0.01f;
       write_cell_meta(cell, (uint8_t)b, 0, s < 0 ? -s : s, rng_normal(r) * 0.001f, rows, cols);
+      /* the reference's embedding path reads group scales for every 4/2-bit
+       * cell whatever the flag says (unpackEmbedRowCell), so they are filled */
+      write_group_scales(pl, r);
       break;
     }
     case F_W8: {

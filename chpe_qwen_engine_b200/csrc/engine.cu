@@ -245,8 +245,8 @@ Engine::Engine(const uint8_t* bytes, uint64_t len, int arch, uint32_t max_seq, i
   d_xn_ = (float*)dalloc(maxproj * 4);
   d_logits_ = (float*)dalloc((size_t)A.V * 4);
   const int G = A.H / A.KV;
-  const int nsplit = 16;
-  d_part_ = (float*)dalloc((size_t)A.KV * nsplit * G * (A.HD + 2) * 4);
+  nsplit_ = (int)(128 / A.KV) < 16 ? 16 : (int)(128 / A.KV);
+  d_part_ = (float*)dalloc((size_t)A.KV * nsplit_ * G * (A.HD + 2) * 4);
   d_counters_ = (uint32_t*)dalloc(A.KV * 4);
   size_t kv_elems = (size_t)A.L * max_seq_ * A.KV * A.HD;
   d_kc_ = (__half*)dalloc(kv_elems * 2);
@@ -513,15 +513,27 @@ void Engine::add_linear_ops(std::vector<Op>& ops, const GemvSrc* src, float* con
     size_t sm = gemv_smem(op.fmt, ncols);
     op.smem = sm;
     uint32_t jobs = e == EPI_SWIGLU ? ss[0].r_total : rows;
+    // jobs a warp takes per iteration (see launch_gemv_k)
+    uint32_t jpi = 1;
+    if (op.kind == SRC_ROWTILE) {
+      int slots = 2048 / (32 * fmt_cw(op.fmt));
+      int unr = slots >= 8 ? 8 : slots;
+      jpi = (uint32_t)(8 / unr);
+      if (jpi < 2 && e == EPI_SWIGLU) jpi = 2;
+    } else {
+      jpi = e == EPI_SWIGLU ? 2 : 1;
+    }
+    if (e == EPI_SWIGLU) jpi /= 2;
+    if (jpi == 0) jpi = 1;
     if (sm > 16384) {
       op.threads = 512;
-      uint32_t cap = (uint32_t)num_sms_ * (sm > 100000 ? 1u : 2u);
-      uint32_t need = (jobs + 15) / 16;
+      uint32_t cap = (uint32_t)num_sms_;
+      uint32_t need = (jobs + 16 * jpi - 1) / (16 * jpi);
       op.grid = dim3(need < cap ? need : cap);
     } else {
       op.threads = 256;
-      uint32_t cap = (uint32_t)num_sms_ * 4u;
-      uint32_t need = (jobs + 7) / 8;
+      uint32_t cap = (uint32_t)num_sms_ * 2u;
+      uint32_t need = (jobs + 8 * jpi - 1) / (8 * jpi);
       op.grid = dim3(need < cap ? need : cap);
     }
     if (op.grid.x == 0) op.grid.x = 1;
@@ -665,9 +677,9 @@ void Engine::build_step() {
       at.H = (int)A.H;
       at.KV = (int)A.KV;
       at.HD = (int)A.HD;
-      at.nsplit = 16;
+      at.nsplit = nsplit_;
       at.max_seq = (int32_t)max_seq_;
-      op.grid = dim3(16, A.KV);
+      op.grid = dim3(nsplit_, A.KV);
       op.threads = (int)(A.H / A.KV) * 32;
       if (op.threads < (int)A.HD / 2) op.threads = (int)A.HD / 2;
       ops.push_back(op);
@@ -763,9 +775,9 @@ static void launch_pdl(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream
   CK(cudaLaunchKernelEx(&cfg, kern, a));
 }
 
-template <int FMT, int KIND, int TH>
+template <int FMT, int KIND, int TH, int NR, int UNR>
 static void launch_gemv_t(const Op& op, cudaStream_t s) {
-  auto k = gemv_kernel<FMT, KIND, TH>;
+  auto k = gemv_kernel<FMT, KIND, TH, NR, UNR>;
   static bool configured = false;
   if (!configured) {
     CK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
@@ -774,10 +786,29 @@ static void launch_gemv_t(const Op& op, cudaStream_t s) {
   launch_pdl(k, op.grid, dim3(TH), op.smem, s, op.g);
 }
 
+// Rows per warp iteration (NR) and chunk slots per row (UNR): row-tiled
+// tensors have 2048 columns, so their slot count is fixed by the format and
+// NR fills eight 16-byte loads per lane; wide flat/raw rows use 8 slots of
+// one row (or 4 slots of the gate and the up row).
 template <int FMT, int KIND>
 static void launch_gemv_k(const Op& op, cudaStream_t s) {
-  if (op.threads == 512) launch_gemv_t<FMT, KIND, 512>(op, s);
-  else launch_gemv_t<FMT, KIND, 256>(op, s);
+  constexpr int CW = FmtInfo<FMT>::CW;
+  constexpr int SLOTS2048 = 2048 / (32 * CW);
+  constexpr int RT_UNR = KIND == SRC_ROWTILE ? (SLOTS2048 >= 8 ? 8 : SLOTS2048) : 8;
+  constexpr int RT_NR = 8 / RT_UNR;
+  const bool swig = op.g.epi == EPI_SWIGLU;
+  if constexpr (KIND == SRC_ROWTILE && RT_NR >= 2) {
+    if (op.threads == 512) launch_gemv_t<FMT, KIND, 512, RT_NR, RT_UNR>(op, s);
+    else launch_gemv_t<FMT, KIND, 256, RT_NR, RT_UNR>(op, s);
+  } else {
+    if (swig) {
+      if (op.threads == 512) launch_gemv_t<FMT, KIND, 512, 2, 4>(op, s);
+      else launch_gemv_t<FMT, KIND, 256, 2, 4>(op, s);
+    } else {
+      if (op.threads == 512) launch_gemv_t<FMT, KIND, 512, 1, 8>(op, s);
+      else launch_gemv_t<FMT, KIND, 256, 1, 8>(op, s);
+    }
+  }
 }
 
 static void launch_gemv(const Op& op, cudaStream_t s) {

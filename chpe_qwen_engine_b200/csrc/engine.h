@@ -116,6 +116,7 @@ class Engine {
   uint64_t last_ns_ = 0;
   uint32_t pos_ = 0;
   int num_sms_ = 148;
+  int nsplit_ = 16;  // attention splits of the positions per kv head
 };
 
 }  // namespace chpe

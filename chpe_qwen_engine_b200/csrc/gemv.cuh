@@ -233,47 +233,56 @@ CHPE_DEV const uint8_t* chunk_addr(const GemvSrc& s, uint32_t r, uint32_t ch, bo
   }
 }
 
-// Dot product of one row against the staged x for this lane's chunks.
-template <int FMT, int KIND>
-CHPE_DEV float row_dot(const GemvSrc& s, uint32_t r, const float* xs, const float* xsum,
-                       uint32_t nchunks, uint32_t L) {
+// Dot products of NR rows against the staged x.  Every lane first issues the
+// 16-byte code loads (and the scale loads) of UNR chunk slots of all NR rows,
+// then decodes them, so a warp keeps NR*UNR*512 bytes of weights in flight.
+template <int FMT, int KIND, int NR, int UNR>
+CHPE_DEV void rows_dot(const GemvSrc* const* sp, const uint32_t* rr, const bool* vv, const float* xs,
+                       const float* xsum, uint32_t nchunks, uint32_t L, float* acc) {
   using FI = FmtInfo<FMT>;
-  constexpr int UNR = 4;
-  float acc = 0.f;
+#pragma unroll
+  for (int n = 0; n < NR; n++) acc[n] = 0.f;
   const uint32_t nslots = (nchunks + 31) >> 5;
   for (uint32_t j0 = 0; j0 < nslots; j0 += UNR) {
-    uint4 v[UNR];
-    bool ok[UNR];
-    const uint8_t* pl[UNR];
-    uint32_t grp[UNR];
+    uint4 v[NR][UNR];
+    float sc[NR][UNR], bi[NR][UNR];
+    bool ok[NR][UNR];
 #pragma unroll
-    for (int u = 0; u < UNR; u++) {
-      uint32_t ch = L + 32u * (j0 + u);
-      ok[u] = false;
-      pl[u] = nullptr;
-      grp[u] = 0;
-      if (j0 + u < nslots && ch < nchunks) {
-        const uint8_t* a = chunk_addr<FMT, KIND>(s, r, ch, ok[u], pl[u], grp[u]);
-        if (ok[u]) v[u] = ld_stream(a);
+    for (int n = 0; n < NR; n++) {
+#pragma unroll
+      for (int u = 0; u < UNR; u++) {
+        const uint32_t ch = L + 32u * (j0 + u);
+        ok[n][u] = false;
+        sc[n][u] = 1.f;
+        bi[n][u] = 0.f;
+        if (vv[n] && j0 + u < nslots && ch < nchunks) {
+          const uint8_t* pl;
+          uint32_t grp;
+          bool o;
+          const uint8_t* a = chunk_addr<FMT, KIND>(*sp[n], rr[n], ch, o, pl, grp);
+          ok[n][u] = o;
+          if (o) {
+            v[n][u] = ld_stream(a);
+            if constexpr (FI::GROUPED) sc[n][u] = ld_f16(pl + 48 + 2 * grp);
+            if constexpr (FI::SB) { sc[n][u] = ld_f32(pl + 32); bi[n][u] = ld_f32(pl + 36); }
+          }
+        }
       }
     }
 #pragma unroll
-    for (int u = 0; u < UNR; u++) {
-      if (!ok[u]) continue;
-      uint32_t ch = L + 32u * (j0 + u);
-      float xsm = xsum[ch];
-      float d = chunk_dot<FMT>(v[u], xs, xsm, j0 + u, L);
-      if constexpr (FI::GROUPED) {
-        acc = fmaf(d, ld_f16(pl[u] + 48 + 2 * grp[u]), acc);
-      } else if constexpr (FI::SB) {
-        acc = fmaf(d, ld_f32(pl[u] + 32), acc);
-        acc = fmaf(ld_f32(pl[u] + 36), xsm, acc);
-      } else {
-        acc += d;
+    for (int n = 0; n < NR; n++) {
+#pragma unroll
+      for (int u = 0; u < UNR; u++) {
+        if (!ok[n][u]) continue;
+        const uint32_t ch = L + 32u * (j0 + u);
+        const float xsm = xsum[ch];
+        const float d = chunk_dot<FMT>(v[n][u], xs, xsm, j0 + u, L);
+        if constexpr (FI::GROUPED) acc[n] = fmaf(d, sc[n][u], acc[n]);
+        else if constexpr (FI::SB) acc[n] = fmaf(bi[n][u], xsm, fmaf(d, sc[n][u], acc[n]));
+        else acc[n] += d;
       }
     }
   }
-  return acc;
 }
 
 // Additive row outliers of W4G/W2G row-tiled cells with 16 rows
@@ -306,8 +315,8 @@ CHPE_DEV float outlier_term(const GemvSrc& s, uint32_t r, const float* xs, uint3
   return (w - dec) * xv;
 }
 
-template <int FMT, int KIND, int THREADS>
-__global__ void __launch_bounds__(THREADS) gemv_kernel(const __grid_constant__ GemvLaunch P) {
+template <int FMT, int KIND, int THREADS, int NR, int UNR>
+__global__ void __launch_bounds__(THREADS, 65536 / (THREADS * 128)) gemv_kernel(const __grid_constant__ GemvLaunch P) {
   using FI = FmtInfo<FMT>;
   extern __shared__ __align__(16) float smem[];
   const uint32_t tid = threadIdx.x, L = tid & 31u, warp = tid >> 5;
@@ -380,32 +389,53 @@ __global__ void __launch_bounds__(THREADS) gemv_kernel(const __grid_constant__ G
   // ---- rows --------------------------------------------------------------
   unsigned long long lbest = 0ull;  // EPI_LOGITS per-lane (lane 0) running best
   uint32_t lfin = 1u;
-  const uint32_t total = P.epi == EPI_SWIGLU ? P.row_start[1] : P.row_start[P.nseg];
-  for (uint32_t job = blockIdx.x * nwarps + warp; job < total; job += gridDim.x * nwarps) {
-    if (P.epi == EPI_SWIGLU) {
-      float g = row_dot<FMT, KIND>(P.src[0], job, xs, xsum, nchunks, L);
-      float u = row_dot<FMT, KIND>(P.src[1], job, xs, xsum, nchunks, L);
-      if constexpr (KIND == SRC_ROWTILE && FI::GROUPED) {
-        if (P.src[0].outliers) g += outlier_term(P.src[0], job, xs, L, FI::CW);
-        if (P.src[1].outliers) u += outlier_term(P.src[1], job, xs, L, FI::CW);
+  const bool swig = P.epi == EPI_SWIGLU;
+  const uint32_t total = swig ? P.row_start[1] : P.row_start[P.nseg];
+  constexpr int JPI_PLAIN = NR;
+  const uint32_t jpi = swig ? (uint32_t)(NR / 2) : (uint32_t)JPI_PLAIN;  // jobs per iteration
+  for (uint32_t j0 = (blockIdx.x * nwarps + warp) * jpi; j0 < total; j0 += gridDim.x * nwarps * jpi) {
+    const GemvSrc* sp[NR];
+    uint32_t rr[NR], sg[NR];
+    bool vv[NR];
+#pragma unroll
+    for (int n = 0; n < NR; n++) {
+      uint32_t job = j0 + (swig ? (uint32_t)(n >> 1) : (uint32_t)n);
+      vv[n] = job < total;
+      uint32_t seg = 0, r = job;
+      if (swig) {
+        seg = (uint32_t)(n & 1);
+      } else {
+        while ((int)seg + 1 < P.nseg && job >= P.row_start[seg + 1]) seg++;
+        r = job - P.row_start[seg];
       }
-      g = warp_sum(g);
-      u = warp_sum(u);
-      if (L == 0) P.out[0][job] = silu_ref(g) * u;
+      sg[n] = seg;
+      rr[n] = r;
+      sp[n] = &P.src[seg];
+    }
+    float acc[NR];
+    rows_dot<FMT, KIND, NR, UNR>(sp, rr, vv, xs, xsum, nchunks, L, acc);
+#pragma unroll
+    for (int n = 0; n < NR; n++) {
+      if constexpr (KIND == SRC_ROWTILE && FI::GROUPED) {
+        if (vv[n] && sp[n]->outliers) acc[n] += outlier_term(*sp[n], rr[n], xs, L, FI::CW);
+      }
+      acc[n] = warp_sum(acc[n]);
+    }
+    if (L != 0) continue;
+    if (swig) {
+#pragma unroll
+      for (int n = 0; n + 1 < NR; n += 2)
+        if (vv[n]) P.out[0][rr[n]] = silu_ref(acc[n]) * acc[n + 1];
       continue;
     }
-    int sg = 0;
-    while (sg + 1 < P.nseg && job >= P.row_start[sg + 1]) sg++;
-    const GemvSrc& s = P.src[sg];
-    uint32_t r = job - P.row_start[sg];
-    float d = row_dot<FMT, KIND>(s, r, xs, xsum, nchunks, L);
-    if constexpr (KIND == SRC_ROWTILE && FI::GROUPED) {
-      if (s.outliers) d += outlier_term(s, r, xs, L, FI::CW);
-    }
-    d = warp_sum(d);
-    if (L == 0) {
+#pragma unroll
+    for (int n = 0; n < NR; n++) {
+      if (!vv[n]) continue;
+      float d = acc[n];
+      const uint32_t r = rr[n];
+      const GemvSrc& s = *sp[n];
       if constexpr (FMT == FMT_I8RAW) d *= 0.00373708f;
-      float* y = P.out[sg];
+      float* y = P.out[sg[n]];
       if (P.epi == EPI_LOGITS) {
         y[r] = d;
         if (!isfinite(d)) lfin = 0u;

@@ -30,7 +30,7 @@ def assert_logits_match(got: np.ndarray, ref: np.ndarray, what: str = ""):
     assert got.shape == ref.shape, what
     assert np.all(np.isfinite(got)) == np.all(np.isfinite(ref)), what
     err = float(np.max(np.abs(got.astype(np.float64) - ref.astype(np.float64))))
-    cos = cosine(got, ref)
+    cos = cosine(got, ref) if np.any(ref) or np.any(got) else 1.0
     assert err <= 2e-2, f"{what}: max-abs-err {err}"
     assert cos >= 0.9999, f"{what}: cosine {cos}"
     top2 = np.partition(ref, -2)[-2:]
