@@ -183,8 +183,8 @@ def run_ours(args, rank, world, local, dist):
     archive = chpe.synth_archive(chpe.SYNTH_3B_W4, 0, seed=0)
     eng = chpe.Engine.from_bytes(archive, chpe.ARCH_3B, max_seq_len=2048, device=dev)
     rng = np.random.default_rng(1)
-    prompt = rng.integers(0, 151936, PROMPT).astype(np.uint32)
-    eng.forward_tokens(prompt)  # positions 0..511, untimed
+    prompt = rng.integers(0, 151936, args.prompt).astype(np.uint32)
+    eng.forward_tokens(prompt)  # positions 0..prompt-1, untimed
     eng.bench_greedy(args.warmup)  # warm-up steps
     barrier(dist)
     with ClockSampler(dev) as cs:
@@ -195,7 +195,7 @@ def run_ours(args, rank, world, local, dist):
 
     # e2e through the C ABI with host buffers
     host_toks = rng.integers(0, 151936, args.steps).astype(np.uint32)
-    eng.forward_tokens(prompt[:PROMPT])
+    eng.forward_tokens(prompt)
     barrier(dist)
     wall_ms, _ = eng.bench_host(host_toks)
     wall_ms = max_over_ranks(dist, wall_ms)
@@ -235,8 +235,9 @@ def run_ours(args, rank, world, local, dist):
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "u4->f32",
         "data": "synthetic (seeded archive, random-init weights)",
-        "config": {"workload": CONFIG_NAME, "prompt": PROMPT, "positions": f"{PROMPT + args.warmup}.."
-                   f"{PROMPT + args.warmup + args.steps - 1}", "parallelism": f"replicas x{world}",
+        "config": {"workload": CONFIG_NAME, "prompt": args.prompt,
+                   "positions": f"{args.prompt + args.warmup}..{args.prompt + args.warmup + args.steps - 1}",
+                   "parallelism": f"replicas x{world}",
                    "l2": "inputs larger than L2 (1.59 GB of weights per step)",
                    "algorithmic_bytes_per_token": step_bytes,
                    "weight_stream_gbs": step_bytes / (ms_step / 1000) / 1e9,
@@ -261,6 +262,7 @@ def main():
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt tokens decoded before timing")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -3,10 +3,16 @@
 // Restates the forwardDecode attention block (chpe_engine.zig:1688-1734):
 // NeoX rotate-half RoPE on q and k (applyRope, :195-216), append k/v at
 // `pos`, then per query head softmax(q.k * 1/sqrt(hd)) over t <= pos and the
-// weighted sum of v.  Layout of the cache: [max_seq][kv_heads][head_dim] FP16
-// per layer.  One CTA per (kv head, split of the positions); warp g handles
-// query head kv*G + g with an online softmax; the last CTA of a kv head
-// (atomic arrival counter, reset by that CTA) merges the splits.
+// weighted sum of v.  Cache layout: [max_seq][kv_heads][head_dim] FP16 per
+// layer.
+//
+// One CTA per (kv head, split of the positions).  A CTA stages its positions
+// in tiles of ATT_TT rows: every thread issues its 16-byte K and V loads of
+// the tile at once into shared memory, then warp g (query head kv*G + g)
+// scores the tile from shared memory, lane per position, and folds it into an
+// online softmax.  The last CTA of a kv head (atomic arrival counter, reset by
+// that CTA) merges the splits: lanes over splits for the max and the sum,
+// lanes over head_dim for the weighted values.
 #pragma once
 #include "device_common.cuh"
 
@@ -27,14 +33,20 @@ struct AttnLaunch {
   int32_t max_seq;      // cache capacity; a step at pos >= max_seq is skipped
 };
 
+constexpr int ATT_TT = 32;  // positions per staged tile
+
 template <int HD>
 __global__ void __launch_bounds__(256) attention_kernel(const __grid_constant__ AttnLaunch P) {
-  constexpr int PER = HD / 32;  // elements per lane
+  constexpr int PER = HD / 32;     // head elements per lane
+  constexpr int KPAD = HD + 8;     // padded shared row (halves)
   const int G = P.H / P.KV;
   const int split = blockIdx.x, kvh = blockIdx.y;
   const int warp = threadIdx.x >> 5, L = threadIdx.x & 31;
   __shared__ float qs[8][HD];
   __shared__ float kn[HD], vn[HD];
+  __shared__ __align__(16) __half ks[ATT_TT][KPAD];
+  __shared__ __align__(16) __half vs[ATT_TT][KPAD];
+  __shared__ float ps[8][ATT_TT];
   __shared__ int last_flag;
 
   pdl_wait();
@@ -43,7 +55,7 @@ __global__ void __launch_bounds__(256) attention_kernel(const __grid_constant__ 
   if (pos < 0 || pos >= P.max_seq) return;  // the host never schedules this
   const float pf = (float)pos;
 
-  // RoPE on this warp's query head and (warp 0) on the new key.
+  // RoPE on this warp's query head, on the new key; copy of the new value.
   if (warp < G) {
     const float* qh = P.q + (size_t)(kvh * G + warp) * HD;
     for (int i = L; i < HD / 2; i += 32) {
@@ -54,8 +66,7 @@ __global__ void __launch_bounds__(256) attention_kernel(const __grid_constant__ 
       qs[warp][i + HD / 2] = x0 * s + x1 * c;
     }
   }
-  if (threadIdx.x < HD / 2) {
-    int i = threadIdx.x;
+  for (int i = threadIdx.x; i < HD / 2; i += blockDim.x) {
     const float* kh = P.k + (size_t)kvh * HD;
     float th = pf * P.inv_freq[i];
     float c = cosf(th), s = sinf(th);
@@ -81,35 +92,63 @@ __global__ void __launch_bounds__(256) attention_kernel(const __grid_constant__ 
   float m = -INFINITY, l = 0.f, acc[PER];
 #pragma unroll
   for (int e = 0; e < PER; e++) acc[e] = 0.f;
-  if (warp < G) {
-    float qv[PER];
+
+  constexpr int VPR = HD / 8;  // 16-byte vectors per row
+  for (int tb = t0; tb < t1; tb += ATT_TT) {
+    const int nt = min(ATT_TT, t1 - tb);
+    __syncthreads();  // previous tile consumed
+    for (int i = threadIdx.x; i < nt * VPR; i += blockDim.x) {
+      int r = i / VPR, c8 = (i % VPR) * 8, t = tb + r;
+      uint4 kv4, vv4;
+      if (t == pos) {  // this step's entry, from the values just computed
+        __half2 hk[4], hv[4];
 #pragma unroll
-    for (int e = 0; e < PER; e++) qv[e] = qs[warp][L + 32 * e];
-    for (int t = t0; t < t1; t++) {
-      float kv[PER], vv[PER];
-      if (t == pos) {
-#pragma unroll
-        for (int e = 0; e < PER; e++) { kv[e] = kn[L + 32 * e]; vv[e] = vn[L + 32 * e]; }
-      } else {
-        const __half* kr = P.kc + ((size_t)t * P.KV + kvh) * HD;
-        const __half* vr = P.vc + ((size_t)t * P.KV + kvh) * HD;
-#pragma unroll
-        for (int e = 0; e < PER; e++) {
-          kv[e] = __half2float(kr[L + 32 * e]);
-          vv[e] = __half2float(vr[L + 32 * e]);
+        for (int e = 0; e < 4; e++) {
+          hk[e] = __floats2half2_rn(kn[c8 + 2 * e], kn[c8 + 2 * e + 1]);
+          hv[e] = __floats2half2_rn(vn[c8 + 2 * e], vn[c8 + 2 * e + 1]);
         }
+        kv4 = *reinterpret_cast<uint4*>(hk);
+        vv4 = *reinterpret_cast<uint4*>(hv);
+      } else {
+        size_t off = ((size_t)t * P.KV + kvh) * HD + c8;
+        kv4 = *reinterpret_cast<const uint4*>(P.kc + off);
+        vv4 = *reinterpret_cast<const uint4*>(P.vc + off);
       }
-      float d = 0.f;
-#pragma unroll
-      for (int e = 0; e < PER; e++) d = fmaf(qv[e], kv[e], d);
-      float s = warp_sum(d) * scale;
-      float mn = fmaxf(m, s);
-      float corr = expf(m - mn), p = expf(s - mn);
-      l = l * corr + p;
-#pragma unroll
-      for (int e = 0; e < PER; e++) acc[e] = fmaf(p, vv[e], acc[e] * corr);
-      m = mn;
+      *reinterpret_cast<uint4*>(&ks[r][c8]) = kv4;
+      *reinterpret_cast<uint4*>(&vs[r][c8]) = vv4;
     }
+    __syncthreads();
+    if (warp < G) {
+      float sc = -INFINITY;  // lane = tile row
+      if (L < nt) {
+        float d = 0.f;
+#pragma unroll 8
+        for (int e = 0; e < HD; e += 2) {
+          float2 kf = __half22float2(*reinterpret_cast<const __half2*>(&ks[L][e]));
+          d = fmaf(qs[warp][e], kf.x, d);
+          d = fmaf(qs[warp][e + 1], kf.y, d);
+        }
+        sc = d * scale;
+      }
+      const float tmax = warp_max(sc);
+      const float mn = fmaxf(m, tmax);
+      const float p = (L < nt) ? expf(sc - mn) : 0.f;
+      const float corr = expf(m - mn);
+      l = l * corr + warp_sum(p);
+      ps[warp][L] = p;
+      __syncwarp();
+#pragma unroll
+      for (int e = 0; e < PER; e++) acc[e] *= corr;
+      for (int r = 0; r < nt; r++) {
+        const float pr = ps[warp][r];
+#pragma unroll
+        for (int e = 0; e < PER; e++) acc[e] = fmaf(pr, __half2float(vs[r][L + 32 * e]), acc[e]);
+      }
+      m = mn;
+      __syncwarp();
+    }
+  }
+  if (warp < G) {
     float* dst = P.part + (((size_t)kvh * P.nsplit + split) * G + warp) * (HD + 2);
 #pragma unroll
     for (int e = 0; e < PER; e++) dst[L + 32 * e] = acc[e];
@@ -128,20 +167,26 @@ __global__ void __launch_bounds__(256) attention_kernel(const __grid_constant__ 
     const float* src = P.part + ((size_t)kvh * P.nsplit * G + warp) * (HD + 2);
     const size_t sstride = (size_t)G * (HD + 2);
     float M = -INFINITY;
-    for (int s = 0; s < P.nsplit; s++) M = fmaxf(M, __ldcg(src + s * sstride + HD));
-    float den = 0.f, o[PER];
+    for (int s = L; s < P.nsplit; s += 32) M = fmaxf(M, __ldcg(src + s * sstride + HD));
+    M = warp_max(M);
+    float den = 0.f;
+    for (int s = L; s < P.nsplit; s += 32) {
+      float ms = __ldcg(src + s * sstride + HD);
+      if (ms != -INFINITY) den = fmaf(__ldcg(src + s * sstride + HD + 1), expf(ms - M), den);
+    }
+    den = warp_sum(den);
+    float o[PER];
 #pragma unroll
     for (int e = 0; e < PER; e++) o[e] = 0.f;
+#pragma unroll 4
     for (int s = 0; s < P.nsplit; s++) {
-      const float* ps = src + s * sstride;
-      float ms = __ldcg(ps + HD);
-      if (ms == -INFINITY) continue;
-      float w = expf(ms - M);
-      den = fmaf(__ldcg(ps + HD + 1), w, den);
+      const float* psrc = src + s * sstride;
+      const float ms = __ldcg(psrc + HD);
+      const float w = ms == -INFINITY ? 0.f : expf(ms - M);
 #pragma unroll
-      for (int e = 0; e < PER; e++) o[e] = fmaf(__ldcg(ps + L + 32 * e), w, o[e]);
+      for (int e = 0; e < PER; e++) o[e] = fmaf(__ldcg(psrc + L + 32 * e), w, o[e]);
     }
-    float inv = 1.0f / den;
+    const float inv = 1.0f / den;
     float* outp = P.out + (size_t)(kvh * G + warp) * HD;
 #pragma unroll
     for (int e = 0; e < PER; e++) outp[L + 32 * e] = o[e] * inv;

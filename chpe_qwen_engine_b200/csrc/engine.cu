@@ -998,7 +998,6 @@ void Engine::copy_logits(float* out) const {
 }
 
 void Engine::bench_role(int role, int rounds, float* avg_ms, double* bytes_per_launch, int* launches) {
-  if (!graph_) throw std::runtime_error("run forward() first");
   std::vector<const Op*> sel;
   for (const Op& op : *ops_)
     if (op.role == role) sel.push_back(&op);

@@ -344,45 +344,65 @@ __global__ void __launch_bounds__(THREADS, 65536 / (THREADS * 128)) gemv_kernel(
   if (!P.ignore_stop && P.st->stop) return;
 
   // ---- stage x (optionally RMSNorm'ed) into shared memory ----------------
+  // Each thread owns float4 quads q = tid + i*THREADS; all loads of a block of
+  // XV quads are issued before any is used.  The CW/4 quads of one chunk sit
+  // in consecutive lanes, so chunk x-sums are segmented shuffle reductions.
+  constexpr int XV = 8;
+  constexpr int QPC = FI::CW / 4;  // quads per chunk
   const float* xin = P.x;
-  float ss = 0.f, tot = 0.f;
-  for (uint32_t c = tid; c < nslots * 32u * FI::CW; c += THREADS) {
-    float v = c < ncols ? xin[c] : 0.f;
-    if (P.norm) ss += v * v;
-    xs[xpos<FI::CW>(c)] = v;
-  }
-  if (P.norm) {
-    ss = warp_sum(ss);
-    if (L == 0) red[warp] = ss;
-    __syncthreads();
-    for (uint32_t w = 0; w < nwarps; w++) tot += red[w];
-    if (P.check_layer >= 0) {
-      // end-of-layer check of the reference's debug block (chpe_engine.zig:1753-1764)
-      int l = P.check_layer;
-      bool cond = l < 3 || (l >= 8 && l <= 16) || !isfinite(xin[0]);
-      if (cond && !isfinite(tot)) {
-        if (blockIdx.x == 0 && tid == 0) P.st->stop = 1;
-        return;
+  float tot = 0.f;
+  const uint32_t nquads = ncols / 4;                      // ncols % 4 == 0
+  const uint32_t nquads_pad = nslots * 32u * (uint32_t)QPC;
+  const float4* x4 = reinterpret_cast<const float4*>(xin);
+  const float4* g4 = reinterpret_cast<const float4*>(P.gamma);
+  for (uint32_t q0 = 0; q0 < nquads_pad; q0 += THREADS * XV) {
+    float4 v[XV], g[XV];
+#pragma unroll
+    for (int i = 0; i < XV; i++) {
+      uint32_t q = q0 + tid + (uint32_t)i * THREADS;
+      v[i] = q < nquads ? x4[q] : make_float4(0.f, 0.f, 0.f, 0.f);
+      if (P.norm) g[i] = q < nquads ? g4[q] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    if (P.norm) {
+      // a norm prologue always fits one block (ncols = hidden_dim <= THREADS*XV*4)
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < XV; i++) ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+      ss = warp_sum(ss);
+      if (L == 0) red[warp] = ss;
+      __syncthreads();
+      for (uint32_t w = 0; w < nwarps; w++) tot += red[w];
+      if (P.check_layer >= 0) {
+        // end-of-layer check of the reference's debug block (chpe_engine.zig:1753-1764)
+        int l = P.check_layer;
+        bool cond = l < 3 || (l >= 8 && l <= 16) || !isfinite(xin[0]);
+        if (cond && !isfinite(tot)) {
+          if (blockIdx.x == 0 && tid == 0) P.st->stop = 1;
+          return;
+        }
+      }
+      const float inv = 1.0f / sqrtf(tot / (float)ncols + P.eps);
+#pragma unroll
+      for (int i = 0; i < XV; i++) {
+        v[i].x = v[i].x * inv * g[i].x;
+        v[i].y = v[i].y * inv * g[i].y;
+        v[i].z = v[i].z * inv * g[i].z;
+        v[i].w = v[i].w * inv * g[i].w;
       }
     }
-    const float inv = 1.0f / sqrtf(tot / (float)ncols + P.eps);
-    __syncthreads();
-    for (uint32_t c = tid; c < ncols; c += THREADS) {
-      uint32_t p = xpos<FI::CW>(c);
-      xs[p] = xs[p] * inv * P.gamma[c];
+#pragma unroll
+    for (int i = 0; i < XV; i++) {
+      uint32_t q = q0 + tid + (uint32_t)i * THREADS;
+      float qs = (v[i].x + v[i].y) + (v[i].z + v[i].w);
+#pragma unroll
+      for (int o = 1; o < QPC; o <<= 1) qs += __shfl_xor_sync(0xffffffffu, qs, o);
+      if (q < nquads_pad) {
+        *reinterpret_cast<float4*>(&xs[xpos<FI::CW>(q * 4)]) = v[i];
+        if ((q % QPC) == 0) xsum[q / QPC] = qs;
+        if (P.xn_out && blockIdx.x == 0 && q < nquads) reinterpret_cast<float4*>(P.xn_out)[q] = v[i];
+      }
     }
   }
-  __syncthreads();
-  for (uint32_t ch = tid; ch < nchunks; ch += THREADS) {
-    float s = 0.f;
-    for (int e = 0; e < FI::CW; e++) {
-      uint32_t c = ch * FI::CW + e;
-      if (c < ncols) s += xs[xpos<FI::CW>(c)];
-    }
-    xsum[ch] = s;
-  }
-  if (P.xn_out && blockIdx.x == 0)
-    for (uint32_t c = tid; c < ncols; c += THREADS) P.xn_out[c] = xs[xpos<FI::CW>(c)];
   __syncthreads();
   pdl_launch_dependents();
 
