@@ -61,16 +61,6 @@ static uint64_t now_ns() {
   return (uint64_t)ts.tv_sec * 1000000000ull + (uint64_t)ts.tv_nsec;
 }
 
-static int fmt_bits(int fmt) {
-  switch (fmt) {
-    case FMT_W4G: case FMT_W4SB: return 4;
-    case FMT_W2G: case FMT_W2SB: return 2;
-    case FMT_W8: case FMT_I8RAW: return 8;
-    case FMT_F16: case FMT_BF16: return 16;
-    default: return 32;
-  }
-}
-
 static int fmt_cw(int fmt) {
   switch (fmt) {
     case FMT_W4G: case FMT_W4SB: return 32;
@@ -375,8 +365,10 @@ GemvSrc Engine::plan_linear(uint64_t tile_start, uint64_t num_tiles, uint32_t r_
   s.fmt = fmt < 0 ? FMT_W4G : fmt;
   s.cell_rows = crow;
   s.cell_cols = ccol;
-  bool fast = uniform && fmt != FMT_W8 && ccol == c_total && x_len == c_total &&
-              (ccol % fmt_cw(fmt)) == 0 && (uint64_t)crow * ccol * fmt_bits(fmt) / 8 <= 16384;
+  // the fast row-tiled kernel takes full cells of 2048 columns
+  const uint32_t full_rows = fmt == FMT_F16 || fmt == FMT_BF16 ? 4u : 16u;
+  bool fast = uniform && fmt != FMT_W8 && fmt != FMT_F32 && ccol == 2048 && c_total == 2048 &&
+              x_len == 2048 && crow == full_rows;
   if (fast) {
     s.kind = SRC_ROWTILE;
     s.outliers = (outl && (fmt == FMT_W4G || fmt == FMT_W2G)) ? OUTL_ADD : OUTL_NONE;
@@ -425,7 +417,8 @@ static size_t gemv_smem(int fmt, uint32_t ncols) {
   uint32_t cw = fmt_cw(fmt);
   uint32_t nchunks = (ncols + cw - 1) / cw;
   uint32_t nslots = (nchunks + 31) / 32;
-  return ((size_t)nslots * 32 * cw + nchunks + 4) * sizeof(float);
+  // x staged per lane slot, then one x-sum per (padded) chunk slot
+  return ((size_t)nslots * 32 * cw + (size_t)nslots * 32 + 4) * sizeof(float);
 }
 
 static uint64_t weight_bytes(const GemvSrc& s) {
@@ -518,10 +511,10 @@ void Engine::add_linear_ops(std::vector<Op>& ops, const GemvSrc* src, float* con
     if (op.kind == SRC_ROWTILE) {
       int slots = 2048 / (32 * fmt_cw(op.fmt));
       int unr = slots >= 8 ? 8 : slots;
-      jpi = (uint32_t)(8 / unr);
+      jpi = unr == 1 ? 4u : (uint32_t)(8 / unr);
       if (jpi < 2 && e == EPI_SWIGLU) jpi = 2;
     } else {
-      jpi = e == EPI_SWIGLU ? 2 : 1;
+      jpi = 2;
     }
     if (e == EPI_SWIGLU) jpi /= 2;
     if (jpi == 0) jpi = 1;
@@ -794,20 +787,17 @@ template <int FMT, int KIND>
 static void launch_gemv_k(const Op& op, cudaStream_t s) {
   constexpr int CW = FmtInfo<FMT>::CW;
   constexpr int SLOTS2048 = 2048 / (32 * CW);
-  constexpr int RT_UNR = KIND == SRC_ROWTILE ? (SLOTS2048 >= 8 ? 8 : SLOTS2048) : 8;
-  constexpr int RT_NR = 8 / RT_UNR;
+  constexpr int RT_UNR = KIND == SRC_ROWTILE ? (SLOTS2048 >= 8 ? 8 : SLOTS2048) : 4;
+  constexpr int RT_NR = RT_UNR == 1 ? 4 : 8 / RT_UNR;  // 2-bit cells: 4 rows of one slot
   const bool swig = op.g.epi == EPI_SWIGLU;
   if constexpr (KIND == SRC_ROWTILE && RT_NR >= 2) {
     if (op.threads == 512) launch_gemv_t<FMT, KIND, 512, RT_NR, RT_UNR>(op, s);
     else launch_gemv_t<FMT, KIND, 256, RT_NR, RT_UNR>(op, s);
   } else {
-    if (swig) {
-      if (op.threads == 512) launch_gemv_t<FMT, KIND, 512, 2, 4>(op, s);
-      else launch_gemv_t<FMT, KIND, 256, 2, 4>(op, s);
-    } else {
-      if (op.threads == 512) launch_gemv_t<FMT, KIND, 512, 1, 8>(op, s);
-      else launch_gemv_t<FMT, KIND, 256, 1, 8>(op, s);
-    }
+    // wide rows: two rows (or the gate and the up row) of four slots each
+    (void)swig;
+    if (op.threads == 512) launch_gemv_t<FMT, KIND, 512, 2, 4>(op, s);
+    else launch_gemv_t<FMT, KIND, 256, 2, 4>(op, s);
   }
 }
 

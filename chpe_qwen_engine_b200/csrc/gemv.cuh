@@ -59,15 +59,17 @@ CHPE_DEV float key_value(unsigned long long k) {
 }
 
 template <int FMT> struct FmtInfo;
-template <> struct FmtInfo<FMT_W4G> { static constexpr int CW = 32, BITS = 4, GROUPED = 1, SB = 0; };
-template <> struct FmtInfo<FMT_W4SB> { static constexpr int CW = 32, BITS = 4, GROUPED = 0, SB = 1; };
-template <> struct FmtInfo<FMT_W2G> { static constexpr int CW = 64, BITS = 2, GROUPED = 1, SB = 0; };
-template <> struct FmtInfo<FMT_W2SB> { static constexpr int CW = 64, BITS = 2, GROUPED = 0, SB = 1; };
-template <> struct FmtInfo<FMT_W8> { static constexpr int CW = 16, BITS = 8, GROUPED = 0, SB = 0; };
-template <> struct FmtInfo<FMT_F16> { static constexpr int CW = 8, BITS = 16, GROUPED = 0, SB = 0; };
-template <> struct FmtInfo<FMT_BF16> { static constexpr int CW = 8, BITS = 16, GROUPED = 0, SB = 0; };
-template <> struct FmtInfo<FMT_F32> { static constexpr int CW = 4, BITS = 32, GROUPED = 0, SB = 0; };
-template <> struct FmtInfo<FMT_I8RAW> { static constexpr int CW = 16, BITS = 8, GROUPED = 0, SB = 0; };
+// CW: columns per 16-byte chunk; CELL_ROWS: rows of a full row-tiled cell
+// of 2048 columns (the only row-tiled geometry the fast path takes).
+template <> struct FmtInfo<FMT_W4G> { static constexpr int CW = 32, BITS = 4, GROUPED = 1, SB = 0, CELL_ROWS = 16; };
+template <> struct FmtInfo<FMT_W4SB> { static constexpr int CW = 32, BITS = 4, GROUPED = 0, SB = 1, CELL_ROWS = 16; };
+template <> struct FmtInfo<FMT_W2G> { static constexpr int CW = 64, BITS = 2, GROUPED = 1, SB = 0, CELL_ROWS = 16; };
+template <> struct FmtInfo<FMT_W2SB> { static constexpr int CW = 64, BITS = 2, GROUPED = 0, SB = 1, CELL_ROWS = 16; };
+template <> struct FmtInfo<FMT_W8> { static constexpr int CW = 16, BITS = 8, GROUPED = 0, SB = 0, CELL_ROWS = 8; };
+template <> struct FmtInfo<FMT_F16> { static constexpr int CW = 8, BITS = 16, GROUPED = 0, SB = 0, CELL_ROWS = 4; };
+template <> struct FmtInfo<FMT_BF16> { static constexpr int CW = 8, BITS = 16, GROUPED = 0, SB = 0, CELL_ROWS = 4; };
+template <> struct FmtInfo<FMT_F32> { static constexpr int CW = 4, BITS = 32, GROUPED = 0, SB = 0, CELL_ROWS = 2; };
+template <> struct FmtInfo<FMT_I8RAW> { static constexpr int CW = 16, BITS = 8, GROUPED = 0, SB = 0, CELL_ROWS = 1; };
 
 // Shared-memory position of column c for chunk width CW: lane L of slot j
 // reads quad q of its chunk at ((j*CW/4 + q)*32 + L)*4.
@@ -83,124 +85,61 @@ CHPE_DEV float4 xquad(const float* xs, uint32_t j, uint32_t q, uint32_t L) {
 
 constexpr uint32_t PRMT_HI = 0x3F000000u;  // bytes 4..7 = 00 00 00 3F
 
-// sum over the chunk of f(c)*x where f = 0.5 + code/256 (4-bit codes).
-CHPE_DEV float2 dot_w4(uint4 v, const float* xs, uint32_t j, uint32_t L) {
-  float2 acc = make_float2(0.f, 0.f);
-  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-  for (int i = 0; i < 4; i++) {
-    uint32_t lo = w[i] & 0x0F0F0F0Fu, hi = (w[i] >> 4) & 0x0F0F0F0Fu;
-    float4 xa = xquad<32>(xs, j, 2 * i, L), xb = xquad<32>(xs, j, 2 * i + 1, L);
-    float f0 = __uint_as_float(prmt(lo, PRMT_HI, 0x7044u)), f1 = __uint_as_float(prmt(hi, PRMT_HI, 0x7044u));
-    float f2 = __uint_as_float(prmt(lo, PRMT_HI, 0x7144u)), f3 = __uint_as_float(prmt(hi, PRMT_HI, 0x7144u));
-    float f4 = __uint_as_float(prmt(lo, PRMT_HI, 0x7244u)), f5 = __uint_as_float(prmt(hi, PRMT_HI, 0x7244u));
-    float f6 = __uint_as_float(prmt(lo, PRMT_HI, 0x7344u)), f7 = __uint_as_float(prmt(hi, PRMT_HI, 0x7344u));
-    acc = ffma2(make_float2(f0, f1), make_float2(xa.x, xa.y), acc);
-    acc = ffma2(make_float2(f2, f3), make_float2(xa.z, xa.w), acc);
-    acc = ffma2(make_float2(f4, f5), make_float2(xb.x, xb.y), acc);
-    acc = ffma2(make_float2(f6, f7), make_float2(xb.z, xb.w), acc);
-  }
-  return acc;
+CHPE_DEV uint32_t word_of(const uint4& v, int i) {
+  return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
 }
 
-// 2-bit codebook {0,1,-2,-1}: (code ^ 2) - 2; f = 0.5 + (code^2)/256.
-CHPE_DEV float2 dot_w2(uint4 v, const float* xs, uint32_t j, uint32_t L) {
-  float2 acc = make_float2(0.f, 0.f);
-  const uint32_t w[4] = {v.x ^ 0xAAAAAAAAu, v.y ^ 0xAAAAAAAAu, v.z ^ 0xAAAAAAAAu, v.w ^ 0xAAAAAAAAu};
-#pragma unroll
-  for (int i = 0; i < 4; i++) {
-    uint32_t m0 = w[i] & 0x03030303u, m1 = (w[i] >> 2) & 0x03030303u;
-    uint32_t m2 = (w[i] >> 4) & 0x03030303u, m3 = (w[i] >> 6) & 0x03030303u;
-#pragma unroll
-    for (int b = 0; b < 4; b++) {
-      const uint32_t sel = 0x7044u | ((uint32_t)b << 8);
-      float4 xq = xquad<64>(xs, j, 4 * i + b, L);
-      float f0 = __uint_as_float(prmt(m0, PRMT_HI, sel)), f1 = __uint_as_float(prmt(m1, PRMT_HI, sel));
-      float f2 = __uint_as_float(prmt(m2, PRMT_HI, sel)), f3 = __uint_as_float(prmt(m3, PRMT_HI, sel));
-      acc = ffma2(make_float2(f0, f1), make_float2(xq.x, xq.y), acc);
-      acc = ffma2(make_float2(f2, f3), make_float2(xq.z, xq.w), acc);
-    }
-  }
-  return acc;
-}
-
-// int8: (b ^ 0x80) placed in the low byte of 2^23 gives 2^23 + b + 128;
-// subtracting 2^23 + 128 is exact.
-CHPE_DEV float2 dot_i8(uint4 v, const float* xs, uint32_t j, uint32_t L) {
-  float2 acc = make_float2(0.f, 0.f);
-  const float2 off = make_float2(-8388736.0f, -8388736.0f);
-  const uint32_t w[4] = {v.x ^ 0x80808080u, v.y ^ 0x80808080u, v.z ^ 0x80808080u, v.w ^ 0x80808080u};
-#pragma unroll
-  for (int i = 0; i < 4; i++) {
-    float4 xq = xquad<16>(xs, j, i, L);
-    float2 a = make_float2(__uint_as_float(prmt(w[i], 0x4B000000u, 0x7440u)),
-                           __uint_as_float(prmt(w[i], 0x4B000000u, 0x7441u)));
-    float2 b = make_float2(__uint_as_float(prmt(w[i], 0x4B000000u, 0x7442u)),
-                           __uint_as_float(prmt(w[i], 0x4B000000u, 0x7443u)));
-    a = __fadd2_rn(a, off);
-    b = __fadd2_rn(b, off);
-    acc = ffma2(a, make_float2(xq.x, xq.y), acc);
-    acc = ffma2(b, make_float2(xq.z, xq.w), acc);
-  }
-  return acc;
-}
-
-CHPE_DEV float2 dot_f16(uint4 v, const float* xs, uint32_t j, uint32_t L) {
-  float2 acc = make_float2(0.f, 0.f);
-  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-  for (int i = 0; i < 2; i++) {
-    float4 xq = xquad<8>(xs, j, i, L);
-    float2 a = __half22float2(*reinterpret_cast<const __half2*>(&w[2 * i]));
-    float2 b = __half22float2(*reinterpret_cast<const __half2*>(&w[2 * i + 1]));
-    acc = ffma2(a, make_float2(xq.x, xq.y), acc);
-    acc = ffma2(b, make_float2(xq.z, xq.w), acc);
-  }
-  return acc;
-}
-
-CHPE_DEV float2 dot_bf16(uint4 v, const float* xs, uint32_t j, uint32_t L) {
-  float2 acc = make_float2(0.f, 0.f);
-  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-  for (int i = 0; i < 2; i++) {
-    float4 xq = xquad<8>(xs, j, i, L);
-    float2 a = make_float2(__uint_as_float(w[2 * i] << 16), __uint_as_float(w[2 * i] & 0xFFFF0000u));
-    float2 b = make_float2(__uint_as_float(w[2 * i + 1] << 16), __uint_as_float(w[2 * i + 1] & 0xFFFF0000u));
-    acc = ffma2(a, make_float2(xq.x, xq.y), acc);
-    acc = ffma2(b, make_float2(xq.z, xq.w), acc);
-  }
-  return acc;
-}
-
-CHPE_DEV float2 dot_f32(uint4 v, const float* xs, uint32_t j, uint32_t L) {
-  float4 xq = xquad<4>(xs, j, 0, L);
-  float2 acc = make_float2(__uint_as_float(v.x) * xq.x, __uint_as_float(v.y) * xq.y);
-  return ffma2(make_float2(__uint_as_float(v.z), __uint_as_float(v.w)), make_float2(xq.z, xq.w), acc);
-}
-
-// Sum over the chunk of (weight code value) * x, in the format's code domain.
+// Accumulate the 4 columns of quad q (columns 4q..4q+3 of the chunk) of one
+// 16-byte chunk against x quad xq.  Code formats accumulate f(c)*x with
+// f = 0.5 + code/256 (exact), mapped back per chunk in chunk_finish.
 template <int FMT>
-CHPE_DEV float chunk_dot(uint4 v, const float* xs, float xsum, uint32_t j, uint32_t L) {
+CHPE_DEV void quad_fma(const uint4& v, int q, float4 xq, float2& acc) {
   if constexpr (FMT == FMT_W4G || FMT == FMT_W4SB) {
-    float2 a = dot_w4(v, xs, j, L);
-    return 256.0f * (a.x + a.y) - 136.0f * xsum;  // sum (c - 8) x
+    const uint32_t w = word_of(v, q >> 1);
+    const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
+    const uint32_t s0 = 0x7044u | ((uint32_t)(2 * (q & 1)) << 8), s1 = s0 + 0x100u;
+    acc = ffma2(make_float2(__uint_as_float(prmt(lo, PRMT_HI, s0)), __uint_as_float(prmt(hi, PRMT_HI, s0))),
+                make_float2(xq.x, xq.y), acc);
+    acc = ffma2(make_float2(__uint_as_float(prmt(lo, PRMT_HI, s1)), __uint_as_float(prmt(hi, PRMT_HI, s1))),
+                make_float2(xq.z, xq.w), acc);
   } else if constexpr (FMT == FMT_W2G || FMT == FMT_W2SB) {
-    float2 a = dot_w2(v, xs, j, L);
-    return 256.0f * (a.x + a.y) - 130.0f * xsum;  // sum ((c^2) - 2) x
+    // codebook {0,1,-2,-1} = (code ^ 2) - 2
+    const uint32_t w = word_of(v, q >> 2) ^ 0xAAAAAAAAu;
+    const uint32_t sel = 0x7044u | ((uint32_t)(q & 3) << 8);
+    const uint32_t m0 = w & 0x03030303u, m1 = (w >> 2) & 0x03030303u;
+    const uint32_t m2 = (w >> 4) & 0x03030303u, m3 = (w >> 6) & 0x03030303u;
+    acc = ffma2(make_float2(__uint_as_float(prmt(m0, PRMT_HI, sel)), __uint_as_float(prmt(m1, PRMT_HI, sel))),
+                make_float2(xq.x, xq.y), acc);
+    acc = ffma2(make_float2(__uint_as_float(prmt(m2, PRMT_HI, sel)), __uint_as_float(prmt(m3, PRMT_HI, sel))),
+                make_float2(xq.z, xq.w), acc);
   } else if constexpr (FMT == FMT_W8 || FMT == FMT_I8RAW) {
-    float2 a = dot_i8(v, xs, j, L);
-    return a.x + a.y;
+    // (b ^ 0x80) in the low byte of 2^23 is 2^23 + b + 128; the subtraction is exact
+    const uint32_t w = word_of(v, q) ^ 0x80808080u;
+    const float2 off = make_float2(-8388736.0f, -8388736.0f);
+    float2 a = make_float2(__uint_as_float(prmt(w, 0x4B000000u, 0x7440u)), __uint_as_float(prmt(w, 0x4B000000u, 0x7441u)));
+    float2 b = make_float2(__uint_as_float(prmt(w, 0x4B000000u, 0x7442u)), __uint_as_float(prmt(w, 0x4B000000u, 0x7443u)));
+    acc = ffma2(__fadd2_rn(a, off), make_float2(xq.x, xq.y), acc);
+    acc = ffma2(__fadd2_rn(b, off), make_float2(xq.z, xq.w), acc);
   } else if constexpr (FMT == FMT_F16) {
-    float2 a = dot_f16(v, xs, j, L);
-    return a.x + a.y;
+    const uint32_t w0 = word_of(v, 2 * q), w1 = word_of(v, 2 * q + 1);
+    acc = ffma2(__half22float2(*reinterpret_cast<const __half2*>(&w0)), make_float2(xq.x, xq.y), acc);
+    acc = ffma2(__half22float2(*reinterpret_cast<const __half2*>(&w1)), make_float2(xq.z, xq.w), acc);
   } else if constexpr (FMT == FMT_BF16) {
-    float2 a = dot_bf16(v, xs, j, L);
-    return a.x + a.y;
-  } else {
-    float2 a = dot_f32(v, xs, j, L);
-    return a.x + a.y;
+    const uint32_t w0 = word_of(v, 2 * q), w1 = word_of(v, 2 * q + 1);
+    acc = ffma2(make_float2(__uint_as_float(w0 << 16), __uint_as_float(w0 & 0xFFFF0000u)), make_float2(xq.x, xq.y), acc);
+    acc = ffma2(make_float2(__uint_as_float(w1 << 16), __uint_as_float(w1 & 0xFFFF0000u)), make_float2(xq.z, xq.w), acc);
+  } else {  // F32: the chunk is one quad
+    acc = ffma2(make_float2(__uint_as_float(v.x), __uint_as_float(v.y)), make_float2(xq.x, xq.y), acc);
+    acc = ffma2(make_float2(__uint_as_float(v.z), __uint_as_float(v.w)), make_float2(xq.z, xq.w), acc);
   }
+}
+
+// Chunk sum of (weight code value) * x from the quad accumulators.
+template <int FMT>
+CHPE_DEV float chunk_finish(float2 a, float xsum) {
+  if constexpr (FMT == FMT_W4G || FMT == FMT_W4SB) return 256.0f * (a.x + a.y) - 136.0f * xsum;  // (c-8) x
+  else if constexpr (FMT == FMT_W2G || FMT == FMT_W2SB) return 256.0f * (a.x + a.y) - 130.0f * xsum;
+  else return a.x + a.y;
 }
 
 // Address of chunk `ch` of row r and its validity.
@@ -234,15 +173,39 @@ CHPE_DEV const uint8_t* chunk_addr(const GemvSrc& s, uint32_t r, uint32_t ch, bo
 }
 
 // Dot products of NR rows against the staged x.  Every lane first issues the
-// 16-byte code loads (and the scale loads) of UNR chunk slots of all NR rows,
-// then decodes them, so a warp keeps NR*UNR*512 bytes of weights in flight.
+// 16-byte code loads (and scale loads) of UNR chunk slots of all NR rows,
+// then walks the slots quad by quad: each x quad is read from shared memory
+// once and applied to all NR rows.  A warp keeps NR*UNR*512 bytes in flight.
+//
+// Row-tiled tensors (KIND == SRC_ROWTILE) always have 2048 columns and full
+// cells here, so no chunk needs a bounds test and the cell geometry is fixed.
 template <int FMT, int KIND, int NR, int UNR>
 CHPE_DEV void rows_dot(const GemvSrc* const* sp, const uint32_t* rr, const bool* vv, const float* xs,
                        const float* xsum, uint32_t nchunks, uint32_t L, float* acc) {
   using FI = FmtInfo<FMT>;
+  constexpr int QPC = FI::CW / 4;
+  constexpr bool RT = KIND == SRC_ROWTILE;
 #pragma unroll
   for (int n = 0; n < NR; n++) acc[n] = 0.f;
-  const uint32_t nslots = (nchunks + 31) >> 5;
+  const uint32_t nslots = RT ? (uint32_t)UNR : (nchunks + 31) >> 5;
+  // per-row bases (row-tiled: cell and row inside it, shifts only)
+  const uint8_t* rowp[NR];
+  const uint8_t* scp[NR];
+#pragma unroll
+  for (int n = 0; n < NR; n++) {
+    if constexpr (RT) {
+      const GemvSrc& s = *sp[n];
+      const uint32_t r = rr[n];
+      const uint32_t k = r / FI::CELL_ROWS, rin = r % FI::CELL_ROWS;
+      const uint8_t* cell = s.arc + s.tile0 + (uint64_t)k * s.stride;
+      rowp[n] = cell + rin * (2048u * FI::BITS / 8);
+      scp[n] = cell + 16384;
+      if constexpr (FI::GROUPED) scp[n] += 48 + 2 * rin * 16;
+    } else {
+      rowp[n] = nullptr;
+      scp[n] = nullptr;
+    }
+  }
   for (uint32_t j0 = 0; j0 < nslots; j0 += UNR) {
     uint4 v[NR][UNR];
     float sc[NR][UNR], bi[NR][UNR];
@@ -252,31 +215,52 @@ CHPE_DEV void rows_dot(const GemvSrc* const* sp, const uint32_t* rr, const bool*
 #pragma unroll
       for (int u = 0; u < UNR; u++) {
         const uint32_t ch = L + 32u * (j0 + u);
-        ok[n][u] = false;
         sc[n][u] = 1.f;
         bi[n][u] = 0.f;
-        if (vv[n] && j0 + u < nslots && ch < nchunks) {
-          const uint8_t* pl;
-          uint32_t grp;
-          bool o;
-          const uint8_t* a = chunk_addr<FMT, KIND>(*sp[n], rr[n], ch, o, pl, grp);
-          ok[n][u] = o;
-          if (o) {
-            v[n][u] = ld_stream(a);
-            if constexpr (FI::GROUPED) sc[n][u] = ld_f16(pl + 48 + 2 * grp);
-            if constexpr (FI::SB) { sc[n][u] = ld_f32(pl + 32); bi[n][u] = ld_f32(pl + 36); }
+        if constexpr (RT) {
+          ok[n][u] = vv[n] && rr[n] < sp[n]->rows_covered;
+          if (ok[n][u]) {
+            v[n][u] = ld_stream(rowp[n] + 16u * ch);
+            if constexpr (FI::GROUPED) sc[n][u] = ld_f16(scp[n] + 2 * (ch * FI::CW / 128));
+            if constexpr (FI::SB) { sc[n][u] = ld_f32(scp[n] + 32); bi[n][u] = ld_f32(scp[n] + 36); }
+          }
+        } else {
+          ok[n][u] = false;
+          if (vv[n] && j0 + u < nslots && ch < nchunks) {
+            const uint8_t* pl;
+            uint32_t grp;
+            bool o;
+            const uint8_t* a = chunk_addr<FMT, KIND>(*sp[n], rr[n], ch, o, pl, grp);
+            ok[n][u] = o;
+            if (o) {
+              v[n][u] = ld_stream(a);
+              if constexpr (FI::GROUPED) sc[n][u] = ld_f16(pl + 48 + 2 * grp);
+              if constexpr (FI::SB) { sc[n][u] = ld_f32(pl + 32); bi[n][u] = ld_f32(pl + 36); }
+            }
           }
         }
+        if (!ok[n][u]) v[n][u] = make_uint4(0u, 0u, 0u, 0u);
       }
     }
 #pragma unroll
-    for (int n = 0; n < NR; n++) {
+    for (int u = 0; u < UNR; u++) {
+      if (!RT && j0 + u >= nslots) break;
+      const uint32_t ch = L + 32u * (j0 + u);
+      const bool chv = RT || ch < nchunks;
+      float2 a2[NR];
 #pragma unroll
-      for (int u = 0; u < UNR; u++) {
+      for (int n = 0; n < NR; n++) a2[n] = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int q = 0; q < QPC; q++) {
+        const float4 xq = xquad<FI::CW>(xs, j0 + u, q, L);
+#pragma unroll
+        for (int n = 0; n < NR; n++) quad_fma<FMT>(v[n][u], q, xq, a2[n]);
+      }
+      const float xsm = chv ? xsum[chv ? ch : 0] : 0.f;
+#pragma unroll
+      for (int n = 0; n < NR; n++) {
         if (!ok[n][u]) continue;
-        const uint32_t ch = L + 32u * (j0 + u);
-        const float xsm = xsum[ch];
-        const float d = chunk_dot<FMT>(v[n][u], xs, xsm, j0 + u, L);
+        const float d = chunk_finish<FMT>(a2[n], xsm);
         if constexpr (FI::GROUPED) acc[n] = fmaf(d, sc[n][u], acc[n]);
         else if constexpr (FI::SB) acc[n] = fmaf(bi[n][u], xsm, fmaf(d, sc[n][u], acc[n]));
         else acc[n] += d;
