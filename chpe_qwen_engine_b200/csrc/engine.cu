@@ -506,18 +506,9 @@ void Engine::add_linear_ops(std::vector<Op>& ops, const GemvSrc* src, float* con
     size_t sm = gemv_smem(op.fmt, ncols);
     op.smem = sm;
     uint32_t jobs = e == EPI_SWIGLU ? ss[0].r_total : rows;
-    // jobs a warp takes per iteration (see launch_gemv_k)
-    uint32_t jpi = 1;
-    if (op.kind == SRC_ROWTILE) {
-      int slots = 2048 / (32 * fmt_cw(op.fmt));
-      int unr = slots >= 8 ? 8 : slots;
-      jpi = unr == 1 ? 4u : (uint32_t)(8 / unr);
-      if (jpi < 2 && e == EPI_SWIGLU) jpi = 2;
-    } else {
-      jpi = 2;
-    }
+    // jobs a warp takes per iteration (gemv_nr)
+    uint32_t jpi = (uint32_t)gemv_nr(op.fmt, op.kind);
     if (e == EPI_SWIGLU) jpi /= 2;
-    if (jpi == 0) jpi = 1;
     if (sm > 16384) {
       op.threads = 512;
       uint32_t cap = (uint32_t)num_sms_;
@@ -779,26 +770,11 @@ static void launch_gemv_t(const Op& op, cudaStream_t s) {
   launch_pdl(k, op.grid, dim3(TH), op.smem, s, op.g);
 }
 
-// Rows per warp iteration (NR) and chunk slots per row (UNR): row-tiled
-// tensors have 2048 columns, so their slot count is fixed by the format and
-// NR fills eight 16-byte loads per lane; wide flat/raw rows use 8 slots of
-// one row (or 4 slots of the gate and the up row).
 template <int FMT, int KIND>
 static void launch_gemv_k(const Op& op, cudaStream_t s) {
-  constexpr int CW = FmtInfo<FMT>::CW;
-  constexpr int SLOTS2048 = 2048 / (32 * CW);
-  constexpr int RT_UNR = KIND == SRC_ROWTILE ? (SLOTS2048 >= 8 ? 8 : SLOTS2048) : 4;
-  constexpr int RT_NR = RT_UNR == 1 ? 4 : 8 / RT_UNR;  // 2-bit cells: 4 rows of one slot
-  const bool swig = op.g.epi == EPI_SWIGLU;
-  if constexpr (KIND == SRC_ROWTILE && RT_NR >= 2) {
-    if (op.threads == 512) launch_gemv_t<FMT, KIND, 512, RT_NR, RT_UNR>(op, s);
-    else launch_gemv_t<FMT, KIND, 256, RT_NR, RT_UNR>(op, s);
-  } else {
-    // wide rows: two rows (or the gate and the up row) of four slots each
-    (void)swig;
-    if (op.threads == 512) launch_gemv_t<FMT, KIND, 512, 2, 4>(op, s);
-    else launch_gemv_t<FMT, KIND, 256, 2, 4>(op, s);
-  }
+  constexpr int NR = gemv_nr(FMT, KIND), UNR = gemv_unr(FMT, KIND);
+  if (op.threads == 512) launch_gemv_t<FMT, KIND, 512, NR, UNR>(op, s);
+  else launch_gemv_t<FMT, KIND, 256, NR, UNR>(op, s);
 }
 
 static void launch_gemv(const Op& op, cudaStream_t s) {

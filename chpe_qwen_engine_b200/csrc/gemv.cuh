@@ -89,57 +89,87 @@ CHPE_DEV uint32_t word_of(const uint4& v, int i) {
   return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
 }
 
+// Packed pairs of floats live in 64-bit registers; every product pair is one
+// fma.rn.f32x2.  The decoded weights are produced straight into the halves of
+// a 64-bit register, so no moves are needed to form the pairs.
+typedef unsigned long long f2x;
+
+CHPE_DEV f2x pack2(float a, float b) {
+  f2x r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+CHPE_DEV float2 unpack2(f2x v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+CHPE_DEV void fma2x(f2x& acc, f2x a, f2x x) {
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(a), "l"(x));
+}
+// Two codes -> (0.5 + c0/256, 0.5 + c1/256) with one PRMT each, then FMA.
+CHPE_DEV void code_pair_fma(f2x& acc, uint32_t wa, uint32_t wb, uint32_t sel, f2x x) {
+  asm("{\n\t.reg .b32 a, b;\n\t.reg .b64 p;\n\t"
+      "prmt.b32 a, %1, %3, %4;\n\tprmt.b32 b, %2, %3, %4;\n\t"
+      "mov.b64 p, {a, b};\n\tfma.rn.f32x2 %0, p, %5, %0;\n\t}"
+      : "+l"(acc)
+      : "r"(wa), "r"(wb), "r"(PRMT_HI), "r"(sel), "l"(x));
+}
+
 // Accumulate the 4 columns of quad q (columns 4q..4q+3 of the chunk) of one
-// 16-byte chunk against x quad xq.  Code formats accumulate f(c)*x with
-// f = 0.5 + code/256 (exact), mapped back per chunk in chunk_finish.
+// 16-byte chunk against the x quad (x01, x23).  Code formats accumulate
+// f(c)*x with f = 0.5 + code/256 (exact), mapped back per chunk in
+// chunk_finish.
 template <int FMT>
-CHPE_DEV void quad_fma(const uint4& v, int q, float4 xq, float2& acc) {
+CHPE_DEV void quad_fma(const uint4& v, int q, f2x x01, f2x x23, f2x& acc) {
   if constexpr (FMT == FMT_W4G || FMT == FMT_W4SB) {
     const uint32_t w = word_of(v, q >> 1);
     const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
     const uint32_t s0 = 0x7044u | ((uint32_t)(2 * (q & 1)) << 8), s1 = s0 + 0x100u;
-    acc = ffma2(make_float2(__uint_as_float(prmt(lo, PRMT_HI, s0)), __uint_as_float(prmt(hi, PRMT_HI, s0))),
-                make_float2(xq.x, xq.y), acc);
-    acc = ffma2(make_float2(__uint_as_float(prmt(lo, PRMT_HI, s1)), __uint_as_float(prmt(hi, PRMT_HI, s1))),
-                make_float2(xq.z, xq.w), acc);
+    code_pair_fma(acc, lo, hi, s0, x01);  // columns 4q, 4q+1
+    code_pair_fma(acc, lo, hi, s1, x23);  // columns 4q+2, 4q+3
   } else if constexpr (FMT == FMT_W2G || FMT == FMT_W2SB) {
     // codebook {0,1,-2,-1} = (code ^ 2) - 2
     const uint32_t w = word_of(v, q >> 2) ^ 0xAAAAAAAAu;
     const uint32_t sel = 0x7044u | ((uint32_t)(q & 3) << 8);
     const uint32_t m0 = w & 0x03030303u, m1 = (w >> 2) & 0x03030303u;
     const uint32_t m2 = (w >> 4) & 0x03030303u, m3 = (w >> 6) & 0x03030303u;
-    acc = ffma2(make_float2(__uint_as_float(prmt(m0, PRMT_HI, sel)), __uint_as_float(prmt(m1, PRMT_HI, sel))),
-                make_float2(xq.x, xq.y), acc);
-    acc = ffma2(make_float2(__uint_as_float(prmt(m2, PRMT_HI, sel)), __uint_as_float(prmt(m3, PRMT_HI, sel))),
-                make_float2(xq.z, xq.w), acc);
+    code_pair_fma(acc, m0, m1, sel, x01);
+    code_pair_fma(acc, m2, m3, sel, x23);
   } else if constexpr (FMT == FMT_W8 || FMT == FMT_I8RAW) {
     // (b ^ 0x80) in the low byte of 2^23 is 2^23 + b + 128; the subtraction is exact
     const uint32_t w = word_of(v, q) ^ 0x80808080u;
-    const float2 off = make_float2(-8388736.0f, -8388736.0f);
-    float2 a = make_float2(__uint_as_float(prmt(w, 0x4B000000u, 0x7440u)), __uint_as_float(prmt(w, 0x4B000000u, 0x7441u)));
-    float2 b = make_float2(__uint_as_float(prmt(w, 0x4B000000u, 0x7442u)), __uint_as_float(prmt(w, 0x4B000000u, 0x7443u)));
-    acc = ffma2(__fadd2_rn(a, off), make_float2(xq.x, xq.y), acc);
-    acc = ffma2(__fadd2_rn(b, off), make_float2(xq.z, xq.w), acc);
+    const f2x off = pack2(-8388736.0f, -8388736.0f);
+    f2x a = pack2(__uint_as_float(prmt(w, 0x4B000000u, 0x7440u)), __uint_as_float(prmt(w, 0x4B000000u, 0x7441u)));
+    f2x b = pack2(__uint_as_float(prmt(w, 0x4B000000u, 0x7442u)), __uint_as_float(prmt(w, 0x4B000000u, 0x7443u)));
+    asm("add.rn.f32x2 %0, %0, %1;" : "+l"(a) : "l"(off));
+    asm("add.rn.f32x2 %0, %0, %1;" : "+l"(b) : "l"(off));
+    fma2x(acc, a, x01);
+    fma2x(acc, b, x23);
   } else if constexpr (FMT == FMT_F16) {
     const uint32_t w0 = word_of(v, 2 * q), w1 = word_of(v, 2 * q + 1);
-    acc = ffma2(__half22float2(*reinterpret_cast<const __half2*>(&w0)), make_float2(xq.x, xq.y), acc);
-    acc = ffma2(__half22float2(*reinterpret_cast<const __half2*>(&w1)), make_float2(xq.z, xq.w), acc);
+    float2 a = __half22float2(*reinterpret_cast<const __half2*>(&w0));
+    float2 b = __half22float2(*reinterpret_cast<const __half2*>(&w1));
+    fma2x(acc, pack2(a.x, a.y), x01);
+    fma2x(acc, pack2(b.x, b.y), x23);
   } else if constexpr (FMT == FMT_BF16) {
     const uint32_t w0 = word_of(v, 2 * q), w1 = word_of(v, 2 * q + 1);
-    acc = ffma2(make_float2(__uint_as_float(w0 << 16), __uint_as_float(w0 & 0xFFFF0000u)), make_float2(xq.x, xq.y), acc);
-    acc = ffma2(make_float2(__uint_as_float(w1 << 16), __uint_as_float(w1 & 0xFFFF0000u)), make_float2(xq.z, xq.w), acc);
+    fma2x(acc, pack2(__uint_as_float(w0 << 16), __uint_as_float(w0 & 0xFFFF0000u)), x01);
+    fma2x(acc, pack2(__uint_as_float(w1 << 16), __uint_as_float(w1 & 0xFFFF0000u)), x23);
   } else {  // F32: the chunk is one quad
-    acc = ffma2(make_float2(__uint_as_float(v.x), __uint_as_float(v.y)), make_float2(xq.x, xq.y), acc);
-    acc = ffma2(make_float2(__uint_as_float(v.z), __uint_as_float(v.w)), make_float2(xq.z, xq.w), acc);
+    fma2x(acc, pack2(__uint_as_float(v.x), __uint_as_float(v.y)), x01);
+    fma2x(acc, pack2(__uint_as_float(v.z), __uint_as_float(v.w)), x23);
   }
 }
 
 // Chunk sum of (weight code value) * x from the quad accumulators.
 template <int FMT>
-CHPE_DEV float chunk_finish(float2 a, float xsum) {
-  if constexpr (FMT == FMT_W4G || FMT == FMT_W4SB) return 256.0f * (a.x + a.y) - 136.0f * xsum;  // (c-8) x
-  else if constexpr (FMT == FMT_W2G || FMT == FMT_W2SB) return 256.0f * (a.x + a.y) - 130.0f * xsum;
-  else return a.x + a.y;
+CHPE_DEV float chunk_finish(f2x a0, f2x a1, float xsum) {
+  const float2 p = unpack2(a0), r = unpack2(a1);
+  const float s = (p.x + r.x) + (p.y + r.y);
+  if constexpr (FMT == FMT_W4G || FMT == FMT_W4SB) return 256.0f * s - 136.0f * xsum;  // (c-8) x
+  else if constexpr (FMT == FMT_W2G || FMT == FMT_W2SB) return 256.0f * s - 130.0f * xsum;
+  else return s;
 }
 
 // Address of chunk `ch` of row r and its validity.
@@ -172,6 +202,18 @@ CHPE_DEV const uint8_t* chunk_addr(const GemvSrc& s, uint32_t r, uint32_t ch, bo
   }
 }
 
+// Rows per warp iteration (NR) and chunk slots loaded per row at a time (UNR)
+// for a (format, layout): eight 16-byte loads per lane in flight, except for
+// 2-bit rows (one slot each, four rows).  The host sizes grids with the same
+// rule (jobs per iteration = NR, or NR/2 gate+up pairs for SwiGLU).
+__host__ __device__ constexpr int gemv_nr(int fmt, int kind) {
+  return kind == SRC_ROWTILE && (fmt == FMT_W4G || fmt == FMT_W4SB || fmt == FMT_W2G || fmt == FMT_W2SB) ? 4 : 2;
+}
+__host__ __device__ constexpr int gemv_unr(int fmt, int kind) {
+  return kind == SRC_ROWTILE && (fmt == FMT_W2G || fmt == FMT_W2SB) ? 1
+         : kind == SRC_ROWTILE && (fmt == FMT_W4G || fmt == FMT_W4SB) ? 2 : 4;
+}
+
 // Dot products of NR rows against the staged x.  Every lane first issues the
 // 16-byte code loads (and scale loads) of UNR chunk slots of all NR rows,
 // then walks the slots quad by quad: each x quad is read from shared memory
@@ -187,15 +229,20 @@ CHPE_DEV void rows_dot(const GemvSrc* const* sp, const uint32_t* rr, const bool*
   constexpr bool RT = KIND == SRC_ROWTILE;
 #pragma unroll
   for (int n = 0; n < NR; n++) acc[n] = 0.f;
-  const uint32_t nslots = RT ? (uint32_t)UNR : (nchunks + 31) >> 5;
-  // per-row bases (row-tiled: cell and row inside it, shifts only)
+  // row-tiled rows are 2048 columns: a compile-time slot count
+  const uint32_t nslots = RT ? (uint32_t)(2048 / (32 * FI::CW)) : (nchunks + 31) >> 5;
+  // per-row bases (row-tiled: cell and row inside it, shifts only; rows past
+  // the covered range load a covered row and are dropped at the end)
   const uint8_t* rowp[NR];
   const uint8_t* scp[NR];
+  bool rok[NR];
 #pragma unroll
   for (int n = 0; n < NR; n++) {
+    rok[n] = vv[n];
     if constexpr (RT) {
       const GemvSrc& s = *sp[n];
-      const uint32_t r = rr[n];
+      rok[n] = vv[n] && rr[n] < s.rows_covered;
+      const uint32_t r = rok[n] ? rr[n] : 0u;
       const uint32_t k = r / FI::CELL_ROWS, rin = r % FI::CELL_ROWS;
       const uint8_t* cell = s.arc + s.tile0 + (uint64_t)k * s.stride;
       rowp[n] = cell + rin * (2048u * FI::BITS / 8);
@@ -218,14 +265,13 @@ CHPE_DEV void rows_dot(const GemvSrc* const* sp, const uint32_t* rr, const bool*
         sc[n][u] = 1.f;
         bi[n][u] = 0.f;
         if constexpr (RT) {
-          ok[n][u] = vv[n] && rr[n] < sp[n]->rows_covered;
-          if (ok[n][u]) {
-            v[n][u] = ld_stream(rowp[n] + 16u * ch);
-            if constexpr (FI::GROUPED) sc[n][u] = ld_f16(scp[n] + 2 * (ch * FI::CW / 128));
-            if constexpr (FI::SB) { sc[n][u] = ld_f32(scp[n] + 32); bi[n][u] = ld_f32(scp[n] + 36); }
-          }
+          ok[n][u] = rok[n];
+          v[n][u] = ld_stream(rowp[n] + 16u * ch);
+          if constexpr (FI::GROUPED) sc[n][u] = ld_f16(scp[n] + 2 * (ch * FI::CW / 128));
+          if constexpr (FI::SB) { sc[n][u] = ld_f32(scp[n] + 32); bi[n][u] = ld_f32(scp[n] + 36); }
         } else {
           ok[n][u] = false;
+          v[n][u] = make_uint4(0u, 0u, 0u, 0u);
           if (vv[n] && j0 + u < nslots && ch < nchunks) {
             const uint8_t* pl;
             uint32_t grp;
@@ -239,7 +285,6 @@ CHPE_DEV void rows_dot(const GemvSrc* const* sp, const uint32_t* rr, const bool*
             }
           }
         }
-        if (!ok[n][u]) v[n][u] = make_uint4(0u, 0u, 0u, 0u);
       }
     }
 #pragma unroll
@@ -247,23 +292,24 @@ CHPE_DEV void rows_dot(const GemvSrc* const* sp, const uint32_t* rr, const bool*
       if (!RT && j0 + u >= nslots) break;
       const uint32_t ch = L + 32u * (j0 + u);
       const bool chv = RT || ch < nchunks;
-      float2 a2[NR];
+      f2x a2[NR][2];
 #pragma unroll
-      for (int n = 0; n < NR; n++) a2[n] = make_float2(0.f, 0.f);
+      for (int n = 0; n < NR; n++) a2[n][0] = a2[n][1] = 0ull;
 #pragma unroll
       for (int q = 0; q < QPC; q++) {
-        const float4 xq = xquad<FI::CW>(xs, j0 + u, q, L);
+        const ulonglong2 xq = reinterpret_cast<const ulonglong2*>(xs)[((j0 + u) * QPC + q) * 32u + L];
 #pragma unroll
-        for (int n = 0; n < NR; n++) quad_fma<FMT>(v[n][u], q, xq, a2[n]);
+        for (int n = 0; n < NR; n++) quad_fma<FMT>(v[n][u], q, xq.x, xq.y, a2[n][q & 1]);
       }
       const float xsm = chv ? xsum[chv ? ch : 0] : 0.f;
 #pragma unroll
       for (int n = 0; n < NR; n++) {
-        if (!ok[n][u]) continue;
-        const float d = chunk_finish<FMT>(a2[n], xsm);
-        if constexpr (FI::GROUPED) acc[n] = fmaf(d, sc[n][u], acc[n]);
-        else if constexpr (FI::SB) acc[n] = fmaf(bi[n][u], xsm, fmaf(d, sc[n][u], acc[n]));
-        else acc[n] += d;
+        const float d = chunk_finish<FMT>(a2[n][0], a2[n][1], xsm);
+        float t;
+        if constexpr (FI::GROUPED) t = fmaf(d, sc[n][u], acc[n]);
+        else if constexpr (FI::SB) t = fmaf(bi[n][u], xsm, fmaf(d, sc[n][u], acc[n]));
+        else t = acc[n] + d;
+        acc[n] = ok[n][u] ? t : acc[n];
       }
     }
   }
