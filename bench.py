@@ -263,9 +263,22 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt tokens decoded before timing")
+    ap.add_argument("--kernel-only", default=None,
+                    choices=["qkv", "attention", "o", "gateup", "down", "lmhead"],
+                    help="profiling case: build the engine (max_seq_len 64) and only launch this "
+                         "op of every layer, --steps rounds after one warm-up round")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.kernel_only:
+        import chpe_qwen_engine_b200 as chpe
+        roles = {"qkv": chpe.ROLE_QKV, "attention": chpe.ROLE_ATTN, "o": chpe.ROLE_O,
+                 "gateup": chpe.ROLE_GATEUP, "down": chpe.ROLE_DOWN, "lmhead": chpe.ROLE_LMHEAD}
+        eng = chpe.Engine.from_bytes(chpe.synth_archive(chpe.SYNTH_3B_W4, 0, seed=0), chpe.ARCH_3B, 64)
+        ms, b, n = eng.bench_kernel(roles[args.kernel_only], rounds=max(1, args.steps))
+        print(json.dumps({"kernel": args.kernel_only, "avg_us": ms * 1000, "bytes_per_launch": b,
+                          "gbs": b / (ms / 1000) / 1e9 if b else None, "launches": n}))
+        return
     rank, world, local, dist = dist_setup(args.gpus)
     try:
         if args.impl == "reference":

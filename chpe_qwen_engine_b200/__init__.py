@@ -57,6 +57,7 @@ SYMBOLS = [
     ("chpe_get_position", _U32, [_P]),
     ("chpe_last_error", C.c_char_p, [_P]),
     ("chpe_probe_gemv_linear", _I, [_P, _U64, _U64, _FP, _U64, _FP, _U64, _U64, _I, _I64]),
+    ("chpe_probe_attention", _I, [_P, _U32, _U32, _FP, _FP, _FP, _FP]),
     ("chpe_probe_embed", _I, [_P, _U32, _FP]),
     ("chpe_probe_dequant_cell", _I, [_P, _U64, _I, _FP, _U64, C.POINTER(C.c_uint64)]),
 ]
@@ -253,6 +254,15 @@ class Engine:
                                         c_total, int(accumulate), bias_tile) != 0:
             raise ChpeError(self._err())
         return y
+
+    def probe_attention(self, layer: int, pos: int, q, k, v) -> np.ndarray:
+        q = np.ascontiguousarray(q, np.float32)
+        k = np.ascontiguousarray(k, np.float32)
+        v = np.ascontiguousarray(v, np.float32)
+        out = np.empty(q.size, np.float32)
+        if lib().chpe_probe_attention(self.ctx, layer, pos, _fp(q), _fp(k), _fp(v), _fp(out)) != 0:
+            raise ChpeError(self._err())
+        return out
 
     def probe_embed(self, token: int, init: np.ndarray | None = None) -> np.ndarray:
         out = np.zeros(self.hidden_dim, np.float32) if init is None else np.array(init, np.float32)

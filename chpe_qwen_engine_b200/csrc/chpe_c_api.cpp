@@ -273,6 +273,19 @@ int chpe_probe_gemv_linear(void* ctx, uint64_t tile_start, uint64_t num_tiles, c
   return 0;
 }
 
+int chpe_probe_attention(void* ctx, uint32_t layer, uint32_t pos, const float* q, const float* k,
+                         const float* v, float* out) {
+  if (!ctx || !q || !k || !v || !out) return -1;
+  Ctx* c = (Ctx*)ctx;
+  try {
+    c->engine->debug_attention(layer, pos, q, k, v, out);
+  } catch (const std::exception& e) {
+    c->err = e.what();
+    return -1;
+  }
+  return 0;
+}
+
 int chpe_probe_embed(void* ctx, uint32_t token, float* out) {
   if (!ctx || !out) return -1;
   Ctx* c = (Ctx*)ctx;

@@ -1026,6 +1026,34 @@ void Engine::debug_gemv_linear(uint64_t tile_start, uint64_t num_tiles, const fl
   cudaFree(dy);
 }
 
+void Engine::debug_attention(uint32_t layer, uint32_t pos, const float* q, const float* k,
+                             const float* v, float* out) {
+  const ChpeArch& A = *arch_;
+  if (layer >= A.L || pos >= max_seq_) throw std::runtime_error("layer or position out of range");
+  const Op* att = nullptr;
+  uint32_t seen = 0;
+  for (const Op& op : *ops_)
+    if (op.type == OP_ATTN && seen++ == layer) att = &op;
+  if (!att) throw std::runtime_error("no attention op");
+  const size_t nq = (size_t)A.H * A.HD, nkv = (size_t)A.KV * A.HD;
+  CK(cudaMemcpyAsync(d_q_, q, nq * 4, cudaMemcpyHostToDevice, stream_));
+  CK(cudaMemcpyAsync(d_k_, k, nkv * 4, cudaMemcpyHostToDevice, stream_));
+  CK(cudaMemcpyAsync(d_v_, v, nkv * 4, cudaMemcpyHostToDevice, stream_));
+  // step state: this position, no early exit
+  CK(cudaMemcpyAsync(h_st_, d_st_, sizeof(StepState), cudaMemcpyDeviceToHost, stream_));
+  CK(cudaStreamSynchronize(stream_));
+  StepState saved = *h_st_;
+  h_st_->pos = (int32_t)pos;
+  h_st_->stop = 0;
+  CK(cudaMemcpyAsync(d_st_, h_st_, sizeof(StepState), cudaMemcpyHostToDevice, stream_));
+  launch(*att, stream_);
+  CK(cudaMemcpyAsync(out, d_attn_, nq * 4, cudaMemcpyDeviceToHost, stream_));
+  CK(cudaStreamSynchronize(stream_));
+  *h_st_ = saved;
+  CK(cudaMemcpyAsync(d_st_, h_st_, sizeof(StepState), cudaMemcpyHostToDevice, stream_));
+  CK(cudaStreamSynchronize(stream_));
+}
+
 void Engine::debug_embed(uint32_t token, float* out) {
   Op op = (*ops_)[0];
   float* d = nullptr;

@@ -66,6 +66,11 @@ class Engine {
                          float* y, uint64_t r_total, uint64_t c_total, int accumulate,
                          int64_t bias_tile);
   void debug_embed(uint32_t token, float* out);
+  // The decode attention kernel of `layer` at position pos on host vectors:
+  // q [H*HD], k/v [KV*HD] (un-rotated), appends k/v to that layer's cache at
+  // pos and returns the attention output [H*HD].
+  void debug_attention(uint32_t layer, uint32_t pos, const float* q, const float* k, const float* v,
+                       float* out);
   void debug_dequant_cell(uint64_t tile, int flat, float* out, uint64_t cap, uint64_t* n_out);
 
   cudaStream_t stream() const { return stream_; }

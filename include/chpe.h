@@ -128,6 +128,13 @@ const char *chpe_last_error(void *ctx);
 int chpe_probe_gemv_linear(void *ctx, uint64_t tile_start, uint64_t num_tiles, const float *x,
                            uint64_t x_len, float *y, uint64_t r_total, uint64_t c_total,
                            int accumulate, int64_t bias_tile);
+/* The decode attention of one layer (chpe_engine.zig:1688-1734: RoPE on q
+ * and k, append k/v to the layer's cache at `pos`, GQA softmax over t <= pos)
+ * on host vectors q [heads*head_dim], k and v [kv_heads*head_dim]; writes
+ * out [heads*head_dim].  Positions 0..pos-1 of the layer's cache are whatever
+ * earlier steps or calls left there.  0 on success. */
+int chpe_probe_attention(void *ctx, uint32_t layer, uint32_t pos, const float *q, const float *k,
+                         const float *v, float *out);
 /* unpackEmbedRow (chpe_engine.zig:1491) for one token into out (hidden_dim
  * floats, read first: rows the reference leaves unwritten keep them). */
 int chpe_probe_embed(void *ctx, uint32_t token, float *out);

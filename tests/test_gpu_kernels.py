@@ -106,3 +106,27 @@ def test_gemv_partial_spans_and_past_end():
         ref = o.gemv_linear(ts, nt, xv, r, c, accumulate=acc, y=y0.copy())
         got = e.probe_gemv_linear(ts, nt, xv, r, c, accumulate=acc, y=y0.copy())
         assert_close_vec(got, ref, 1e-4, f"{ts},{nt},{r},{c},{acc}")
+
+
+@pytest.mark.parametrize("arch", [chpe.ARCH_3B, chpe.ARCH_9B, chpe.ARCH_72B])
+def test_attention_against_oracle(arch):
+    """RoPE + KV append + GQA softmax (chpe_engine.zig:1688-1734) over a
+    growing cache, one call per position, against the oracle's f32 path."""
+    mock = np.zeros(8192, np.uint8)  # the attention op does not read weights
+    e = chpe.Engine.from_bytes(mock, arch, 96)
+    A = {chpe.ARCH_3B: (16, 2, 128), chpe.ARCH_9B: (16, 4, 256), chpe.ARCH_72B: (64, 8, 128)}[arch]
+    H, KV, HD = A
+    rng = np.random.default_rng(arch + 7)
+    kc = np.zeros((96, KV * HD), np.float32)
+    vc = np.zeros((96, KV * HD), np.float32)
+    for pos in list(range(0, 40)) + [40, 41]:
+        q = rng.standard_normal(H * HD).astype(np.float32)
+        k = rng.standard_normal(KV * HD).astype(np.float32)
+        v = rng.standard_normal(KV * HD).astype(np.float32)
+        got = e.probe_attention(2, pos, q, k, v)
+        qr = O.apply_rope(q, pos, H, HD)
+        kc[pos] = O.apply_rope(k, pos, KV, HD)
+        vc[pos] = v
+        ref = O.gqa_attention(qr, kc[:pos + 1], vc[:pos + 1], pos, H, KV, HD)
+        # the cache holds FP16 (the reference holds f32): tolerance of fp16 rounding
+        assert_close_vec(got, ref, 4e-3, f"pos {pos}")
