@@ -57,6 +57,7 @@ SYMBOLS = [
     ("chpe_get_position", _U32, [_P]),
     ("chpe_last_error", C.c_char_p, [_P]),
     ("chpe_probe_gemv_linear", _I, [_P, _U64, _U64, _FP, _U64, _FP, _U64, _U64, _I, _I64]),
+    ("chpe_attention_decode_noalloc", _I, [_P, _P, _P, _P, _P, _P, _U32, _U32, _U32, _U32, _U32, _F, _P]),
     ("chpe_probe_attention", _I, [_P, _U32, _U32, _FP, _FP, _FP, _FP]),
     ("chpe_probe_embed", _I, [_P, _U32, _FP]),
     ("chpe_probe_dequant_cell", _I, [_P, _U64, _I, _FP, _U64, C.POINTER(C.c_uint64)]),

@@ -120,6 +120,29 @@ uint32_t chpe_get_position(void *ctx);
  * when ctx is NULL; "" when none. */
 const char *chpe_last_error(void *ctx);
 
+/* Decode attention for callers that cannot allocate device memory (code
+ * recorded into a CUDA graph, runtimes that only hand out memory from their
+ * own pools, plugins inside a host process that owns allocation).  No
+ * counterpart in the reference.  It is the attention step of
+ * chpe_probe_attention (RoPE on q and k with theta rope_theta, append k/v at
+ * pos, GQA softmax over positions 0..pos) on device pointers the caller owns:
+ * q [num_heads*head_dim] and k, v [num_kv_heads*head_dim] float; k_cache and
+ * v_cache FP16 [max_seq_len][num_kv_heads][head_dim]; out
+ * [num_heads*head_dim] float; stream a cudaStream_t (NULL: default stream).
+ * It allocates nothing: its scratch is a fixed 1 MiB static device array per
+ * GPU, held until the library unloads.  The first call on a device resolves
+ * that array's address (make it before any stream capture).  Calls share
+ * the array, so calls that overlap on the GPU race; each call clears what it
+ * needs.  Limits: head_dim 128 or 256, at most 8 query heads per kv head,
+ * num_kv_heads * nsplit * (num_heads/num_kv_heads) * (head_dim+2) * 4 bytes of
+ * partials + 4 KiB within 1 MiB (nsplit = max(16, 128/num_kv_heads)).
+ * Returns 0, -1 for invalid arguments, -2 when the sizes exceed the scratch
+ * limit, -3 for a CUDA error. */
+int chpe_attention_decode_noalloc(const float *q, const float *k, const float *v, void *k_cache,
+                                  void *v_cache, float *out, uint32_t pos, uint32_t max_seq_len,
+                                  uint32_t num_heads, uint32_t num_kv_heads, uint32_t head_dim,
+                                  float rope_theta, void *stream);
+
 /* ---- probes for the parity tests ------------------------------------------ */
 
 /* gemvLinear (chpe_engine.zig:1396) on the device over host vectors:
