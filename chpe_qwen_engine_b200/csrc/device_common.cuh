@@ -55,5 +55,39 @@ CHPE_DEV float2 ffma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c)
 // The reference's silu (chpe_engine.zig:159).
 CHPE_DEV float silu_ref(float z) { return z / (1.0f + expf(-z)); }
 
-// Bounded spin helpers never needed here: every cross-CTA hand-off in these
-// kernels is an atomic counter checked once by the last arriving CTA.
+// ---- shared-memory barriers and bulk copies (TMA, non-tensor) -------------
+CHPE_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+CHPE_DEV void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+CHPE_DEV void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+CHPE_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+CHPE_DEV void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+// Bulk copy global -> this CTA's shared memory, completing on `bar`.  Both
+// addresses 16-byte aligned, size a multiple of 16.
+CHPE_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+CHPE_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Every wait is bounded: try_wait suspends for a bounded time per call, and
+// after this many calls the caller records a device timeout and gives up.
+constexpr uint32_t kMaxWaitPolls = 1u << 22;
+CHPE_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kMaxWaitPolls; i++)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}

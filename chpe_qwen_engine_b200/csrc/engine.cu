@@ -5,6 +5,7 @@
 #include <time.h>
 
 #include <cmath>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <stdexcept>
@@ -14,6 +15,7 @@
 #include "attention.cuh"
 #include "aux_kernels.cuh"
 #include "gemv.cuh"
+#include "gemv_tma.cuh"
 
 namespace chpe {
 
@@ -26,8 +28,9 @@ namespace chpe {
 
 enum OpType : int32_t {
   OP_GEMV = 0, OP_GEN_ROW, OP_GEN_FLAT, OP_AUX, OP_ATTN, OP_EMBED, OP_NORM, OP_SWIGLU,
-  OP_PATTERN, OP_ARGMAX
+  OP_PATTERN, OP_ARGMAX, OP_TMA
 };
+constexpr int kTmaStages = 4;
 
 // Roles of recorded ops (for per-kernel timing).
 enum Role : int32_t { ROLE_OTHER = 0, ROLE_QKV = 1, ROLE_ATTN = 2, ROLE_O = 3, ROLE_GATEUP = 4,
@@ -48,6 +51,7 @@ struct Op {
   SwigluLaunch sw{};
   PatternLaunch pt{};
   ArgmaxLaunch am{};
+  TmaLaunch tm{};
 };
 
 // ---- host restatements of small archive reads ------------------------------
@@ -59,6 +63,16 @@ static uint64_t now_ns() {
   struct timespec ts;
   clock_gettime(CLOCK_MONOTONIC, &ts);
   return (uint64_t)ts.tv_sec * 1000000000ull + (uint64_t)ts.tv_nsec;
+}
+
+static int fmt_bits(int fmt) {
+  switch (fmt) {
+    case FMT_W4G: case FMT_W4SB: return 4;
+    case FMT_W2G: case FMT_W2SB: return 2;
+    case FMT_W8: case FMT_I8RAW: return 8;
+    case FMT_F16: case FMT_BF16: return 16;
+    default: return 32;
+  }
 }
 
 static int fmt_cw(int fmt) {
@@ -537,6 +551,66 @@ void Engine::add_linear_ops(std::vector<Op>& ops, const GemvSrc* src, float* con
     ops.push_back(op);
   };
 
+  // Row-block tensors (full 2048-wide rows, contiguous codes) go through the
+  // TMA-pipelined kernel.
+  auto tma_rows = [&](const GemvSrc& g) -> uint32_t {  // rows per block, 0 = not eligible
+    if (ncols != 2048 || g.c_total != 2048) return 0;
+    if (g.kind == SRC_ROWTILE) {
+      uint32_t R = (g.fmt == FMT_F16 || g.fmt == FMT_BF16) ? 4u
+                   : (g.fmt == FMT_W4G || g.fmt == FMT_W4SB || g.fmt == FMT_W2G || g.fmt == FMT_W2SB) ? 16u : 0u;
+      if (!R || g.cell_rows != R || g.rows_covered != g.r_total || g.r_total % R) return 0;
+      return R;
+    }
+    if (g.kind == SRC_RAW && (g.fmt == FMT_F16 || g.fmt == FMT_BF16) && g.stride == 16384 &&
+        g.r_total % 4 == 0 && g.flat_limit >= (uint64_t)g.r_total * 2048)
+      return 4;
+    return 0;
+  };
+  bool tma = fused && !getenv("CHPE_NO_TMA");
+  for (int i = 0; i < nseg && tma; i++) tma = tma_rows(src[i]) != 0;
+  if (tma) {
+    Op op;
+    op.type = OP_TMA;
+    op.fmt = src[0].fmt;
+    op.kind = src[0].kind;
+    op.threads = 512;
+    op.role = epi == EPI_SWIGLU ? ROLE_GATEUP : epi == EPI_LOGITS ? ROLE_LMHEAD
+              : (epi == EPI_ACCUM ? (ncols == arch_->D ? ROLE_O : ROLE_DOWN) : ROLE_QKV);
+    TmaLaunch& t = op.tm;
+    const uint32_t R = tma_rows(src[0]);
+    uint32_t units = 0;
+    for (int i = 0; i < nseg; i++) {
+      t.src[i] = src[i];
+      t.out[i] = out[i];
+      t.unit_start[i] = units;
+      units += src[i].r_total / R;
+      op.alg_bytes += alg_bytes_of(src[i]);
+    }
+    t.unit_start[nseg] = units;
+    if (epi == EPI_SWIGLU) t.unit_start[1] = src[0].r_total / R;
+    t.nseg = nseg;
+    t.epi = epi;
+    t.x = x;
+    t.gamma = gamma;
+    t.norm = gamma != nullptr;
+    t.eps = arch_->eps;
+    t.check_layer = check_layer;
+    t.st = d_st_;
+    t.ignore_stop = ignore_stop;
+    t.res = d_res_;
+    t.gen_tokens = d_gen_;
+    t.max_gen = (int32_t)max_gen_;
+    t.payload = src[0].kind == SRC_ROWTILE && src[0].fmt != FMT_F16 && src[0].fmt != FMT_BF16;
+    const uint32_t rowb = 2048u * (uint32_t)fmt_bits(src[0].fmt) / 8u;
+    const uint32_t part = R * rowb + (t.payload ? kPayloadHead : 0u);
+    const uint32_t stage = ((epi == EPI_SWIGLU ? 2u : 1u) * part + 127u) & ~127u;
+    op.smem = kTmaStageOff + (size_t)kTmaStages * stage;
+    const uint32_t jobs = epi == EPI_SWIGLU ? t.unit_start[1] : units;
+    op.grid = dim3(jobs < (uint32_t)num_sms_ ? jobs : (uint32_t)num_sms_);
+    ops.push_back(op);
+    return;
+  }
+
   if (fused) {
     Op op = make_gemv(src, out, nseg, epi, x, gamma, check_layer);
     op.role = epi == EPI_SWIGLU ? ROLE_GATEUP : epi == EPI_LOGITS ? ROLE_LMHEAD
@@ -809,8 +883,32 @@ static void launch_gemv(const Op& op, cudaStream_t s) {
   throw std::runtime_error("no GEMV kernel for this (format, layout)");
 }
 
+template <int FMT>
+static void launch_tma_t(const Op& op, cudaStream_t s) {
+  auto k = gemv_tma_kernel<FMT, kTmaStages>;
+  static bool configured = false;
+  if (!configured) {
+    CK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 210 * 1024));
+    configured = true;
+  }
+  launch_pdl(k, op.grid, dim3(512), op.smem, s, op.tm);
+}
+
+static void launch_tma(const Op& op, cudaStream_t s) {
+  switch (op.fmt) {
+    case FMT_W4G: return launch_tma_t<FMT_W4G>(op, s);
+    case FMT_W4SB: return launch_tma_t<FMT_W4SB>(op, s);
+    case FMT_W2G: return launch_tma_t<FMT_W2G>(op, s);
+    case FMT_W2SB: return launch_tma_t<FMT_W2SB>(op, s);
+    case FMT_F16: return launch_tma_t<FMT_F16>(op, s);
+    case FMT_BF16: return launch_tma_t<FMT_BF16>(op, s);
+  }
+  throw std::runtime_error("no TMA kernel for this format");
+}
+
 void Engine::launch(const Op& op, cudaStream_t s) const {
   switch (op.type) {
+    case OP_TMA: return launch_tma(op, s);
     case OP_GEMV: return launch_gemv(op, s);
     case OP_GEN_ROW: return launch_pdl(gemv_generic_rowtile, op.grid, dim3(256), 0, s, op.gen);
     case OP_GEN_FLAT: return launch_pdl(gemv_generic_flat, op.grid, dim3(256), 0, s, op.gen);
@@ -853,8 +951,10 @@ void Engine::run_steps(size_t n) {
 
 void Engine::sync_result() {
   CK(cudaMemcpyAsync(h_res_, d_res_, sizeof(StepResult), cudaMemcpyDeviceToHost, stream_));
+  CK(cudaMemcpyAsync(&h_st_->err, &d_st_->err, 4, cudaMemcpyDeviceToHost, stream_));
   CK(cudaStreamSynchronize(stream_));
   last_ = *h_res_;
+  if (h_st_->err) throw std::runtime_error("a device wait timed out (bounded mbarrier wait)");
 }
 
 // Positions start_pos.. for the given tokens (forwardDecode per token).

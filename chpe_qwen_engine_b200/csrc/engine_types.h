@@ -61,7 +61,7 @@ struct StepState {
   uint32_t finite;     // 1 until a non-finite logit is seen
   uint32_t done_ctas;  // LM-head CTAs finished (last one finalises)
   int32_t n_gen;       // generated-token counter (chpe_generate)
-  int32_t pad_;
+  int32_t err;         // non-zero: a kernel gave up a bounded wait (device timeout)
 };
 
 // Result of one forward step (chpe_engine.zig:803 ForwardResult).
