@@ -35,9 +35,17 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 PROMPT = 512
-CONFIG_NAME = "qwen2.5-3b-w4-dense-cell"
-METRIC = "batch-1 greedy decode tok/s (Qwen2.5-3B 4-bit cells, ctx 512+)"
-BYTES_PER_WEIGHT_W4G = 0.5 + 2.0 / 128.0
+METRIC = "batch-1 greedy decode tok/s (weight stream vs HBM roofline)"
+
+# Workloads: synthetic archive, architecture preset, prompt
+# length decoded before timing, and the layer count of the model.
+MODELS = {
+    "3b-w4": dict(synth="SYNTH_3B_W4", arch="ARCH_3B", prompt=512, name="qwen2.5-3b-w4-dense-cell"),
+    "3b-w2": dict(synth="SYNTH_3B_W2", arch="ARCH_3B", prompt=512, name="qwen2.5-3b-w2-dense-cell"),
+    "3b-fp16": dict(synth="SYNTH_3B_FP16_RAW", arch="ARCH_3B", prompt=32, name="qwen2.5-3b-fp16-raw"),
+    "9b-w4": dict(synth="SYNTH_9B_W4", arch="ARCH_9B", prompt=1024, name="qwen3.5-9b-w4-flat-cell"),
+    "72b-w4": dict(synth="SYNTH_72B_W4", arch="ARCH_72B", prompt=2048, name="qwen2.5-72b-w4-flat-cell"),
+}
 
 
 def peaks():
@@ -131,12 +139,12 @@ def barrier(dist):
         dist.barrier()
 
 
-def oracle_cpu_baseline(archive, steps: int, threads: int, toks) -> tuple[float, str]:
+def oracle_cpu_baseline(archive, arch: int, steps: int, threads: int, toks) -> tuple[float, str]:
     """The oracle (C restatement of the reference engine) decoding `steps`
     tokens from position 0; returns tok/s."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle_py as O
-    e = O.OracleEngine(archive, O.ARCH_3B, PROMPT + 8, threads=threads)
+    e = O.OracleEngine(archive, arch, steps + 8, threads=threads)
     e.forward_decode(int(toks[0]), 0)  # warm (page-in)
     t0 = time.perf_counter()
     for i in range(steps):
@@ -150,28 +158,37 @@ def run_reference(args, rank, world, dist):
     import chpe_qwen_engine_b200 as chpe
     if rank != 0:
         return
-    archive = chpe.synth_archive(chpe.SYNTH_3B_W4, 0, seed=0)
-    toks = np.random.default_rng(1).integers(0, 151936, args.steps + args.warmup + 2)
+    M = MODELS[args.model]
+    archive = chpe.synth_archive(getattr(chpe, M["synth"]), 0, seed=0)
+    arch = getattr(chpe, M["arch"])
     threads = os.cpu_count() or 1
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle_py as O
-    e = O.OracleEngine(archive, O.ARCH_3B, args.steps + args.warmup + 4, threads=threads)
-    for i in range(args.warmup):
-        e.forward_decode(int(toks[i]), i)
+    e = O.OracleEngine(archive, arch, args.steps + args.warmup + 4, threads=threads)
+    toks = np.random.default_rng(1).integers(0, 151936, args.steps + args.warmup + 2)
+    # bounded sample: at most ~60 s of timed CPU work
     t0 = time.perf_counter()
-    for i in range(args.steps):
-        e.forward_decode(int(toks[args.warmup + i]), args.warmup + i)
+    e.forward_decode(int(toks[0]), 0)
+    per = time.perf_counter() - t0
+    warm = max(0, min(args.warmup, int(20.0 / max(per, 1e-3))) - 1)
+    steps = max(1, min(args.steps, int(60.0 / max(per, 1e-3))))
+    for i in range(warm):
+        e.forward_decode(int(toks[1 + i]), 1 + i)
+    p0 = 1 + warm
+    t0 = time.perf_counter()
+    for i in range(steps):
+        e.forward_decode(int(toks[p0 + i]), p0 + i)
     dt = time.perf_counter() - t0
-    v = args.steps / dt
+    v = steps / dt
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1000 / args.steps,
+        "steps": steps, "warmup": warm + 1, "ms_per_step": dt * 1000 / steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u4->f32",
         "data": "synthetic (seeded archive, random-init weights)",
-        "config": {"workload": CONFIG_NAME, "prompt": PROMPT, "archive_bytes": int(archive.size)},
+        "config": {"workload": M["name"], "archive_bytes": int(archive.size)},
         "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": "port",
-                         "sample": f"{args.steps} decode steps at positions {args.warmup}..; "
-                                   f"CPU restatement of src/chpe_engine.zig ({cpu_isa()})"},
+                         "sample": f"{steps} decode steps at positions {p0}..{p0 + steps - 1} "
+                                   f"(short context); CPU restatement of src/chpe_engine.zig ({cpu_isa()})"},
         "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -179,9 +196,12 @@ def run_reference(args, rank, world, dist):
 
 def run_ours(args, rank, world, local, dist):
     import chpe_qwen_engine_b200 as chpe
+    M = MODELS[args.model]
     dev = local if world > 1 else 0
-    archive = chpe.synth_archive(chpe.SYNTH_3B_W4, 0, seed=0)
-    eng = chpe.Engine.from_bytes(archive, chpe.ARCH_3B, max_seq_len=2048, device=dev)
+    archive = chpe.synth_archive(getattr(chpe, M["synth"]), 0, seed=0)
+    arch = getattr(chpe, M["arch"])
+    eng = chpe.Engine.from_bytes(archive, arch, max_seq_len=args.prompt + args.warmup + 2 * args.steps + 64,
+                                 device=dev)
     rng = np.random.default_rng(1)
     prompt = rng.integers(0, 151936, args.prompt).astype(np.uint32)
     eng.forward_tokens(prompt)  # positions 0..prompt-1, untimed
@@ -223,10 +243,14 @@ def run_ours(args, rank, world, local, dist):
                           "gbs": round(b / (m / 1000) / 1e9, 1) if b else None}
     cpu = None
     if rank == 0:
-        sample_steps = int(os.environ.get("CHPE_CPU_SAMPLE_STEPS", "3"))
-        v_cpu, sample = oracle_cpu_baseline(archive, sample_steps, 1, rng.integers(0, 151936, sample_steps + 2))
-        cpu = {"value": v_cpu, "unit": "tok/s", "cores": 1, "kind": "port",
-               "sample": sample + f"; CPU restatement of src/chpe_engine.zig, 1 thread ({cpu_isa()})"}
+        # ~10-30 s of single-thread CPU work: 3 steps of 3B, 1 of the larger models
+        big = archive.size > 4e9
+        sample_steps = int(os.environ.get("CHPE_CPU_SAMPLE_STEPS", "1" if big else "3"))
+        threads = (os.cpu_count() or 1) if archive.size > 20e9 else 1
+        v_cpu, sample = oracle_cpu_baseline(archive, arch, sample_steps, threads,
+                                            rng.integers(0, 151936, sample_steps + 2))
+        cpu = {"value": v_cpu, "unit": "tok/s", "cores": threads, "kind": "port",
+               "sample": sample + f"; CPU restatement of src/chpe_engine.zig, {threads} thread(s) ({cpu_isa()})"}
     if rank != 0:
         return
     ms_step = ms_max / args.steps
@@ -235,17 +259,18 @@ def run_ours(args, rank, world, local, dist):
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "u4->f32",
         "data": "synthetic (seeded archive, random-init weights)",
-        "config": {"workload": CONFIG_NAME, "prompt": args.prompt,
+        "config": {"workload": M["name"], "prompt": args.prompt,
                    "positions": f"{args.prompt + args.warmup}..{args.prompt + args.warmup + args.steps - 1}",
                    "parallelism": f"replicas x{world}",
-                   "l2": "inputs larger than L2 (1.59 GB of weights per step)",
+                   "l2": f"inputs larger than L2 ({step_bytes / 1e9:.2f} GB of weights per step)",
                    "algorithmic_bytes_per_token": step_bytes,
                    "weight_stream_gbs": step_bytes / (ms_step / 1000) / 1e9,
                    "weight_stream_frac_of_measured_hbm": step_bytes / (ms_step / 1000) / 1e9 / hbm,
                    "per_role": per_role},
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": eng.vocab * 4 + 24},
-        "roofline": {"kernel": "gemv_kernel<W4G,ROWTILE> fused RMSNorm+gate/up+SwiGLU", "bound": "hbm",
+        "roofline": {"kernel": eng.op_kernel_name(chpe.ROLE_GATEUP) + " fused RMSNorm+gate/up+SwiGLU",
+                     "bound": "hbm",
                      "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "peak_kind": peak_kind, "traffic": traffic,
                      "bytes_per_launch": kbytes, "avg_launch_us": kms * 1000},
@@ -262,7 +287,9 @@ def main():
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt tokens decoded before timing")
+    ap.add_argument("--model", default="3b-w4", choices=sorted(MODELS))
+    ap.add_argument("--prompt", type=int, default=None,
+                    help="prompt tokens decoded before timing (default: the model's config)")
     ap.add_argument("--kernel-only", default=None,
                     choices=["qkv", "attention", "o", "gateup", "down", "lmhead"],
                     help="profiling case: build the engine (max_seq_len 64) and only launch this "
@@ -270,11 +297,15 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.prompt is None:
+        args.prompt = MODELS[args.model]["prompt"]
     if args.kernel_only:
         import chpe_qwen_engine_b200 as chpe
         roles = {"qkv": chpe.ROLE_QKV, "attention": chpe.ROLE_ATTN, "o": chpe.ROLE_O,
                  "gateup": chpe.ROLE_GATEUP, "down": chpe.ROLE_DOWN, "lmhead": chpe.ROLE_LMHEAD}
-        eng = chpe.Engine.from_bytes(chpe.synth_archive(chpe.SYNTH_3B_W4, 0, seed=0), chpe.ARCH_3B, 64)
+        M = MODELS[args.model]
+        eng = chpe.Engine.from_bytes(chpe.synth_archive(getattr(chpe, M["synth"]), 0, seed=0),
+                                     getattr(chpe, M["arch"]), 64)
         ms, b, n = eng.bench_kernel(roles[args.kernel_only], rounds=max(1, args.steps))
         print(json.dumps({"kernel": args.kernel_only, "avg_us": ms * 1000, "bytes_per_launch": b,
                           "gbs": b / (ms / 1000) / 1e9 if b else None, "launches": n}))

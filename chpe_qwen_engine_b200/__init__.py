@@ -52,6 +52,11 @@ SYMBOLS = [
     ("chpe_bench_greedy", _I, [_P, _S, _FP]),
     ("chpe_bench_host", _I, [_P, _U32P, _S, _FP, C.POINTER(C.c_double)]),
     ("chpe_bench_kernel", _I, [_P, _I, _I, _FP, C.POINTER(C.c_double), C.POINTER(C.c_int)]),
+    ("chpe_role_kernel_name", C.c_char_p, [_P, _I]),
+    ("chpe_init_tp", _P, [C.c_char_p, _I, C.c_uint32, _I, _I, _I]),
+    ("chpe_init_tp_bytes", _P, [_P, C.c_uint64, _I, C.c_uint32, _I, _I, _I]),
+    ("chpe_tp_export_handle", _I, [_P, C.c_char_p]),
+    ("chpe_tp_connect", _I, [_P, C.c_char_p, _I]),
     ("chpe_get_last_all_finite", _I, [_P]),
     ("chpe_kernels_per_step", _I, [_P]),
     ("chpe_get_position", _U32, [_P]),
@@ -171,6 +176,40 @@ class Engine:
         a = np.ascontiguousarray(archive, dtype=np.uint8)
         return cls(lib().chpe_init_bytes(a.ctypes.data, a.size, arch, max_seq_len, device), keepalive=a)
 
+    @classmethod
+    def tensor_parallel(cls, archive, arch: int, rank: int, world: int, max_seq_len: int = 2048,
+                        device: int | None = None, all_gather=None):
+        """Rank `rank` of a tensor-parallel engine over `world` GPUs of this node
+        (one process per GPU).  `archive` is a path (every rank maps the same
+        file) or a uint8 array.  `all_gather(bytes) -> list[bytes]` exchanges the
+        64-byte CUDA IPC handles between ranks in rank order; by default it is
+        torch.distributed.all_gather_object on the default process group."""
+        L = lib()
+        dev = rank if device is None else device
+        if isinstance(archive, (str, bytes, os.PathLike)):
+            ctx = L.chpe_init_tp(os.fsencode(archive), arch, max_seq_len, dev, rank, world)
+            keep = None
+        else:
+            keep = np.ascontiguousarray(archive, dtype=np.uint8)
+            ctx = L.chpe_init_tp_bytes(keep.ctypes.data, keep.size, arch, max_seq_len, dev, rank, world)
+        eng = cls(ctx, keepalive=keep)
+        h = C.create_string_buffer(64)
+        if L.chpe_tp_export_handle(eng.ctx, h) != 0:
+            raise ChpeError(eng._err())
+        if all_gather is None:
+            import torch.distributed as dist
+
+            def all_gather(b):
+                out = [None] * world
+                dist.all_gather_object(out, b)
+                return out
+        handles = all_gather(h.raw)
+        if len(handles) != world or any(len(x) != 64 for x in handles):
+            raise ChpeError("tensor parallel: bad handle exchange")
+        if L.chpe_tp_connect(eng.ctx, b"".join(handles), world) != 0:
+            raise ChpeError(eng._err())
+        return eng
+
     def close(self):
         if getattr(self, "ctx", None):
             lib().chpe_free(self.ctx)
@@ -239,6 +278,10 @@ class Engine:
         if lib().chpe_bench_kernel(self.ctx, role, rounds, C.byref(ms), C.byref(b), C.byref(n)) != 0:
             raise ChpeError(self._err())
         return ms.value, b.value, n.value
+
+    def op_kernel_name(self, role: int) -> str:
+        """Kernel that runs the first op of `role`."""
+        return (lib().chpe_role_kernel_name(self.ctx, role) or b"").decode()
 
     def kernels_per_step(self) -> int:
         return lib().chpe_kernels_per_step(self.ctx)

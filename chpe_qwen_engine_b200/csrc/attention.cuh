@@ -29,14 +29,31 @@ struct AttnLaunch {
   uint32_t* counters;   // [KV], zero between steps
   const float* inv_freq;// [HD/2]
   StepState* st;
-  int32_t H, KV, HD, nsplit;
+  int32_t H, KV, HD, nsplit;  // H, KV: this rank's heads (all of them on one GPU)
   int32_t max_seq;      // cache capacity; a step at pos >= max_seq is skipped
+  TpLink tp;            // tensor parallel: out lies in the exchange region
 };
 
 constexpr int ATT_TT = 32;  // positions per staged tile
+// Splits of the positions per kv head.  The merge keeps one weight per split
+// in two registers per lane, so at most 64.
+constexpr int kAttnSplits = 16;
+static_assert(kAttnSplits <= 64, "attention merge holds at most 64 split weights");
+
+template <int HD>
+CHPE_DEV void attention_body(const AttnLaunch& P);
 
 template <int HD>
 __global__ void __launch_bounds__(256) attention_kernel(const __grid_constant__ AttnLaunch P) {
+  attention_body<HD>(P);
+  if (P.tp.world > 1) {  // every CTA arrives once, after any output it wrote
+    __syncthreads();
+    if (threadIdx.x == 0) tp_signal(P.tp, P.tp.signal_sig);
+  }
+}
+
+template <int HD>
+CHPE_DEV void attention_body(const AttnLaunch& P) {
   constexpr int PER = HD / 32;     // head elements per lane
   constexpr int KPAD = HD + 8;     // padded shared row (halves)
   const int G = P.H / P.KV;
@@ -175,21 +192,38 @@ __global__ void __launch_bounds__(256) attention_kernel(const __grid_constant__ 
       if (ms != -INFINITY) den = fmaf(__ldcg(src + s * sstride + HD + 1), expf(ms - M), den);
     }
     den = warp_sum(den);
+    // weights of the splits, lanes over splits, then the values in batches of
+    // 8 splits whose loads are all issued before they are used
+    float wl[2];
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      const int s = L + 32 * h;
+      const float ms = s < P.nsplit ? __ldcg(src + s * sstride + HD) : -INFINITY;
+      wl[h] = ms == -INFINITY ? 0.f : expf(ms - M);
+    }
     float o[PER];
 #pragma unroll
     for (int e = 0; e < PER; e++) o[e] = 0.f;
-#pragma unroll 4
-    for (int s = 0; s < P.nsplit; s++) {
-      const float* psrc = src + s * sstride;
-      const float ms = __ldcg(psrc + HD);
-      const float w = ms == -INFINITY ? 0.f : expf(ms - M);
+    for (int s0 = 0; s0 < P.nsplit; s0 += 8) {
+      float a[8][PER];
 #pragma unroll
-      for (int e = 0; e < PER; e++) o[e] = fmaf(__ldcg(psrc + L + 32 * e), w, o[e]);
+      for (int b = 0; b < 8; b++) {
+        const int s = s0 + b;
+#pragma unroll
+        for (int e = 0; e < PER; e++) a[b][e] = s < P.nsplit ? __ldcg(src + s * sstride + L + 32 * e) : 0.f;
+      }
+#pragma unroll
+      for (int b = 0; b < 8; b++) {
+        const int s = s0 + b;
+        const float w = __shfl_sync(0xffffffffu, (s & 32) ? wl[1] : wl[0], s & 31);
+#pragma unroll
+        for (int e = 0; e < PER; e++) o[e] = fmaf(a[b][e], w, o[e]);
+      }
     }
     const float inv = 1.0f / den;
     float* outp = P.out + (size_t)(kvh * G + warp) * HD;
 #pragma unroll
-    for (int e = 0; e < PER; e++) outp[L + 32 * e] = o[e] * inv;
+    for (int e = 0; e < PER; e++) tp_put(P.tp, outp, L + 32 * e, o[e] * inv);
   }
   if (threadIdx.x == 0) P.counters[kvh] = 0;
 }

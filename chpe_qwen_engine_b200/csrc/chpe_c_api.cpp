@@ -27,6 +27,7 @@ struct Ctx {
   uint64_t last_elapsed_ns = 0;
   int last_finite = 0;
   std::string err;
+  std::string name;  // chpe_role_kernel_name result
 };
 
 thread_local std::string g_init_error;
@@ -64,10 +65,10 @@ int validate(const uint8_t* b, uint64_t len) {
 }
 
 void* make_ctx(const uint8_t* bytes, uint64_t len, const uint8_t* owned_map, int arch,
-               uint32_t max_seq, int device) {
+               uint32_t max_seq, int device, int tp_rank = 0, int tp_world = 1) {
   Ctx* c = new Ctx();
   try {
-    c->engine = new chpe::Engine(bytes, len, arch, max_seq, device);
+    c->engine = new chpe::Engine(bytes, len, arch, max_seq, device, tp_rank, tp_world);
   } catch (const std::exception& e) {
     g_init_error = e.what();
     if (owned_map) munmap(const_cast<uint8_t*>(owned_map), len);
@@ -82,7 +83,8 @@ void* make_ctx(const uint8_t* bytes, uint64_t len, const uint8_t* owned_map, int
 }
 
 // WeightArchive.openPosix (weight_archive.zig:184-222): read-only private map.
-void* open_path(const char* path, int arch, uint32_t max_seq, int device) {
+void* open_path(const char* path, int arch, uint32_t max_seq, int device, int tp_rank = 0,
+                int tp_world = 1) {
   if (!path) { g_init_error = "null path"; return nullptr; }
   int fd = open(path, O_RDONLY);
   if (fd < 0) { g_init_error = "cannot open archive"; return nullptr; }
@@ -105,7 +107,7 @@ void* open_path(const char* path, int arch, uint32_t max_seq, int device) {
     return nullptr;
   }
   if (arch == CHPE_ARCH_BY_PATH) arch = arch_from_path(path);
-  return make_ctx((const uint8_t*)m, len, (const uint8_t*)m, arch, max_seq, device);
+  return make_ctx((const uint8_t*)m, len, (const uint8_t*)m, arch, max_seq, device, tp_rank, tp_world);
 }
 
 void store_result(Ctx* c) {
@@ -129,6 +131,41 @@ void* chpe_init(const char* archive_path) {
 
 void* chpe_init_ex(const char* archive_path, int arch, uint32_t max_seq_len, int device) {
   return open_path(archive_path, arch, max_seq_len, device);
+}
+
+void* chpe_init_tp(const char* archive_path, int arch, uint32_t max_seq_len, int device, int rank,
+                   int world) {
+  return open_path(archive_path, arch, max_seq_len, device, rank, world);
+}
+
+void* chpe_init_tp_bytes(const void* bytes, uint64_t len, int arch, uint32_t max_seq_len, int device,
+                         int rank, int world) {
+  if (!bytes) { g_init_error = "null bytes"; return nullptr; }
+  return make_ctx((const uint8_t*)bytes, len, nullptr, arch, max_seq_len, device, rank, world);
+}
+
+int chpe_tp_export_handle(void* ctx, uint8_t* handle64) {
+  if (!ctx || !handle64) return -1;
+  Ctx* c = (Ctx*)ctx;
+  try {
+    c->engine->tp_export(handle64);
+  } catch (const std::exception& e) {
+    c->err = e.what();
+    return -1;
+  }
+  return 0;
+}
+
+int chpe_tp_connect(void* ctx, const uint8_t* handles, int world) {
+  if (!ctx || !handles) return -1;
+  Ctx* c = (Ctx*)ctx;
+  try {
+    c->engine->tp_connect(handles, world);
+  } catch (const std::exception& e) {
+    c->err = e.what();
+    return -1;
+  }
+  return 0;
 }
 
 void* chpe_init_bytes(const void* bytes, uint64_t len, int arch, uint32_t max_seq_len, int device) {
@@ -218,6 +255,18 @@ int chpe_bench_kernel(void* ctx, int role, int rounds, float* avg_ms, double* by
     return -1;
   }
   return 0;
+}
+
+const char* chpe_role_kernel_name(void* ctx, int role) {
+  if (!ctx) return "";
+  Ctx* c = (Ctx*)ctx;
+  try {
+    c->name = c->engine->role_kernel_name(role);
+  } catch (const std::exception& e) {
+    c->err = e.what();
+    c->name.clear();
+  }
+  return c->name.c_str();
 }
 
 size_t chpe_get_last_logits(void* ctx, float* out, size_t max_len) {

@@ -223,9 +223,14 @@ static void write_group_scales(uint8_t *pl, Rng *r) {
 }
 
 static void write_codes(uint8_t *codes, size_t n, Rng *r) {
-  for (size_t i = 0; i < n; i += 8) {
+  size_t i = 0;
+  for (; i + 8 <= n; i += 8) {
     uint64_t v = rng_next(r);
-    memcpy(codes + i, &v, n - i < 8 ? n - i : 8);
+    memcpy(codes + i, &v, 8);
+  }
+  if (i < n) {
+    uint64_t v = rng_next(r);
+    memcpy(codes + i, &v, n - i);
   }
 }
 

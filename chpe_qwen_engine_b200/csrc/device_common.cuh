@@ -91,3 +91,46 @@ CHPE_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
   return false;
 }
+
+// ---- tensor-parallel exchange over peer memory ------------------------------
+template <class T>
+CHPE_DEV T* tp_at(T* p, const chpe::TpLink& t, int r) {
+  return reinterpret_cast<T*>(reinterpret_cast<char*>(p) + t.delta[r]);
+}
+CHPE_DEV unsigned long long ld_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+CHPE_DEV void red_add_release_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+// Bounded wait until this rank's counter `kind` reaches `target`.
+CHPE_DEV bool tp_wait_count(const chpe::TpLink& t, int kind, unsigned long long target) {
+  for (uint32_t i = 0; i < kMaxWaitPolls; i++) {
+    if (ld_acquire_sys(&t.sh->sig[kind]) >= target) return true;
+    __nanosleep(64);
+  }
+  return false;
+}
+// The wait a kernel does before reading its input (no-op on one GPU).
+CHPE_DEV bool tp_wait(const chpe::TpLink& t) {
+  if (t.world <= 1 || t.wait_sig < 0) return true;
+  const unsigned long long e = *reinterpret_cast<volatile const uint32_t*>(&t.sh->epoch);
+  return tp_wait_count(t, t.wait_sig, (e * t.wait_per_step + t.wait_index) * t.wait_units);
+}
+// One arrival on every rank; call after this CTA's output stores (and a
+// barrier over the threads that made them).
+CHPE_DEV void tp_signal(const chpe::TpLink& t, int kind) {
+  if (t.world <= 1 || kind < 0) return;
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+  for (int r = 0; r < t.world; r++) red_add_release_sys(&tp_at(t.sh, t, r)->sig[kind], 1ull);
+}
+// Store v at y[i] on this rank, or on every rank when the output is exchanged.
+CHPE_DEV void tp_put(const chpe::TpLink& t, float* y, uint32_t i, float v) {
+  if (t.bcast && t.world > 1) {
+    for (int r = 0; r < t.world; r++) tp_at(y, t, r)[i] = v;
+  } else {
+    y[i] = v;
+  }
+}

@@ -16,6 +16,7 @@
 #include "aux_kernels.cuh"
 #include "gemv.cuh"
 #include "gemv_tma.cuh"
+#include "gemv_flat_tma.cuh"
 
 namespace chpe {
 
@@ -28,9 +29,11 @@ namespace chpe {
 
 enum OpType : int32_t {
   OP_GEMV = 0, OP_GEN_ROW, OP_GEN_FLAT, OP_AUX, OP_ATTN, OP_EMBED, OP_NORM, OP_SWIGLU,
-  OP_PATTERN, OP_ARGMAX, OP_TMA
+  OP_PATTERN, OP_ARGMAX, OP_TMA, OP_FLAT_TMA
 };
 constexpr int kTmaStages = 4;
+constexpr uint32_t kFlatSmemLimit = 227u * 1024u - 1024u;  // dynamic shared memory of one flat-TMA CTA
+constexpr uint32_t kFlatStagesWanted = 12;
 
 // Roles of recorded ops (for per-kernel timing).
 enum Role : int32_t { ROLE_OTHER = 0, ROLE_QKV = 1, ROLE_ATTN = 2, ROLE_O = 3, ROLE_GATEUP = 4,
@@ -52,6 +55,7 @@ struct Op {
   PatternLaunch pt{};
   ArgmaxLaunch am{};
   TmaLaunch tm{};
+  FlatTmaLaunch fl{};
 };
 
 // ---- host restatements of small archive reads ------------------------------
@@ -154,11 +158,14 @@ const float* Engine::upload_floats(const std::vector<float>& v) {
 }
 
 // ---- construction: CHPEEngine.init (chpe_engine.zig:854-974) ---------------
-Engine::Engine(const uint8_t* bytes, uint64_t len, int arch, uint32_t max_seq, int device)
+Engine::Engine(const uint8_t* bytes, uint64_t len, int arch, uint32_t max_seq, int device, int tp_rank,
+               int tp_world)
     : arch_(chpe_arch_preset(arch)), arch_id_(arch), device_(device), max_seq_(max_seq),
-      host_(bytes), len_(len) {
+      host_(bytes), len_(len), tp_rank_(tp_rank), tp_world_(tp_world) {
   if (!arch_) throw std::runtime_error("unknown architecture id");
   if (max_seq_ == 0) throw std::runtime_error("max_seq_len must be > 0");
+  if (tp_world < 1 || tp_world > kTpMax || tp_rank < 0 || tp_rank >= tp_world)
+    throw std::runtime_error("tensor parallel rank/world out of range (world 1..8)");
   // format sniffing, :869-898
   if (len >= 4096) {
     uint32_t magic = rd32(bytes);
@@ -238,24 +245,41 @@ Engine::Engine(const uint8_t* bytes, uint64_t len, int arch, uint32_t max_seq, i
   uint32_t maxproj = A.D;
   if (A.H * A.HD > maxproj) maxproj = A.H * A.HD;
   if (A.F > maxproj) maxproj = A.F;
-  d_hidden_ = (float*)dalloc(A.D * 4);
+  // Exchange region: everything another tensor-parallel rank reads or writes
+  // (one allocation, so one CUDA IPC handle maps it).
+  {
+    auto al = [](size_t x) { return (x + 255) & ~(size_t)255; };
+    const size_t attn_n = (size_t)(A.H * A.HD > A.D ? A.H * A.HD : A.D);
+    size_t off = 0;
+    const size_t o_st = off; off += al(sizeof(StepState));
+    const size_t o_sh = off; off += al(sizeof(TpShared));
+    const size_t o_hid = off; off += al((size_t)A.D * 4);
+    const size_t o_attn = off; off += al(attn_n * 4);
+    const size_t o_mlp = off; off += al((size_t)A.F * 4);
+    const size_t o_log = off; off += al((size_t)A.V * 4);
+    region_bytes_ = off;
+    CK(cudaMalloc(&d_region_, region_bytes_));
+    CK(cudaMemset(d_region_, 0, region_bytes_));
+    d_st_ = (StepState*)(d_region_ + o_st);
+    d_tpsh_ = (TpShared*)(d_region_ + o_sh);
+    d_hidden_ = (float*)(d_region_ + o_hid);
+    d_attn_ = (float*)(d_region_ + o_attn);
+    d_mlp_ = (float*)(d_region_ + o_mlp);
+    d_logits_ = (float*)(d_region_ + o_log);
+  }
   d_q_ = (float*)dalloc((size_t)A.H * A.HD * 4);
   d_k_ = (float*)dalloc((size_t)A.KV * A.HD * 4);
   d_v_ = (float*)dalloc((size_t)A.KV * A.HD * 4);
-  d_attn_ = (float*)dalloc(A.D * 4);
-  d_mlp_ = (float*)dalloc(A.F * 4);
   d_tmp_ = (float*)dalloc(maxproj * 4);
   d_tmp2_ = (float*)dalloc(maxproj * 4);
   d_xn_ = (float*)dalloc(maxproj * 4);
-  d_logits_ = (float*)dalloc((size_t)A.V * 4);
   const int G = A.H / A.KV;
-  nsplit_ = (int)(128 / A.KV) < 16 ? 16 : (int)(128 / A.KV);
+  nsplit_ = kAttnSplits;
   d_part_ = (float*)dalloc((size_t)A.KV * nsplit_ * G * (A.HD + 2) * 4);
   d_counters_ = (uint32_t*)dalloc(A.KV * 4);
   size_t kv_elems = (size_t)A.L * max_seq_ * A.KV * A.HD;
   d_kc_ = (__half*)dalloc(kv_elems * 2);
   d_vc_ = (__half*)dalloc(kv_elems * 2);
-  d_st_ = (StepState*)dalloc(sizeof(StepState));
   d_res_ = (StepResult*)dalloc(sizeof(StepResult));
   max_gen_ = max_seq_;
   d_gen_ = (int32_t*)dalloc((size_t)max_gen_ * 4);
@@ -265,6 +289,7 @@ Engine::Engine(const uint8_t* bytes, uint64_t len, int arch, uint32_t max_seq, i
   CK(cudaMallocHost(&h_tok_, h_tok_cap_ * 4));
   memset(h_st_, 0, sizeof(StepState));
   h_st_->finite = 1;
+  h_st_->gather = 1;
   CK(cudaMemcpy(d_st_, h_st_, sizeof(StepState), cudaMemcpyHostToDevice));
   // RoPE inverse frequencies, computed as applyRope does (chpe_engine.zig:200-202)
   std::vector<float> invf(A.HD / 2);
@@ -275,11 +300,13 @@ Engine::Engine(const uint8_t* bytes, uint64_t len, int arch, uint32_t max_seq, i
   d_invfreq_ = const_cast<float*>(upload_floats(invf));
 
   ops_ = new std::vector<Op>();
-  build_step();
+  if (tp_world_ == 1) build_step();  // tensor parallel: after tp_connect
 }
 
 Engine::~Engine() {
   if (graph_) cudaGraphExecDestroy(graph_);
+  for (void* p : ipc_open_) cudaIpcCloseMemHandle(p);
+  if (d_region_) cudaFree(d_region_);
   for (void* p : allocs_) cudaFree(p);
   if (d_arc_) cudaFree(d_arc_);
   if (h_st_) cudaFreeHost(h_st_);
@@ -386,6 +413,17 @@ GemvSrc Engine::plan_linear(uint64_t tile_start, uint64_t num_tiles, uint32_t r_
   if (fast) {
     s.kind = SRC_ROWTILE;
     s.outliers = (outl && (fmt == FMT_W4G || fmt == FMT_W2G)) ? OUTL_ADD : OUTL_NONE;
+    if (s.outliers == OUTL_ADD) {
+      // An additive outlier term whose 128 weights are all +0.0 adds exactly
+      // 0 for finite x, so such tensors skip it.  (With an inf/NaN x the
+      // reference's term would give NaN; the main dot is then non-finite too.)
+      bool any = false;
+      for (size_t i = 0; i < cells.size() && !any; i++) {
+        const uint8_t* pl = cell_code(cells[i]) + 16384;
+        for (int b = 560; b < 816 && !any; b++) any = pl[b] != 0;
+      }
+      if (!any) s.outliers = OUTL_NONE;
+    }
     return s;
   }
   // per-row table for the generic kernel; every byte it may touch must lie
@@ -473,7 +511,8 @@ static double alg_bytes_of(const GemvSrc& s) {
 
 void Engine::add_linear_ops(std::vector<Op>& ops, const GemvSrc* src, float* const* out, int nseg,
                             int epi, const float* x, const float* gamma, int check_layer,
-                            uint32_t ncols, bool ignore_stop) {
+                            uint32_t ncols, bool ignore_stop, const TpLink* tp) {
+  const bool tp_on = tp && tp->world > 1;
   const ChpeArch& A = *arch_;
   bool fused = true;
   for (int i = 0; i < nseg; i++) {
@@ -566,7 +605,79 @@ void Engine::add_linear_ops(std::vector<Op>& ops, const GemvSrc* src, float* con
       return 4;
     return 0;
   };
+  // Flat cells and raw streams of any width go through the warp-specialised
+  // flat TMA kernel when every segment is covered in full.
+  auto flat_ok = [&](const GemvSrc& g) -> bool {
+    const int f = g.fmt;
+    uint32_t wpp;
+    if (g.kind == SRC_FLAT && (f == FMT_W4G || f == FMT_W4SB || f == FMT_W2G || f == FMT_W2SB)) wpp = 32768;
+    else if (g.kind == SRC_RAW && (f == FMT_F16 || f == FMT_BF16 || f == FMT_I8RAW)) wpp = 16384u * 8u / (uint32_t)fmt_bits(f);
+    else return false;
+    const uint32_t cw = (uint32_t)fmt_cw(f);
+    const uint64_t w = (uint64_t)(g.row0 + g.r_total) * g.c_total;
+    // a consumer warp's run of a piece (wpp/cw/16 chunks) spans at most two rows
+    if (gamma && ncols > 16384) return false;  // the fused RMSNorm loads x in one batch
+    return g.c_total == ncols && ncols % cw == 0 && (wpp / cw / 16) * cw <= ncols && w <= g.flat_limit &&
+           w < (1ull << 32) && g.r_total > 0;
+  };
   bool tma = fused && !getenv("CHPE_NO_TMA");
+  bool flat = tma && !getenv("CHPE_NO_FLAT_TMA");
+  for (int i = 0; i < nseg && flat; i++) flat = flat_ok(src[i]);
+  if (flat) {
+    Op op;
+    op.type = OP_FLAT_TMA;
+    op.fmt = src[0].fmt;
+    op.kind = src[0].kind;
+    op.threads = (int)kFlatThreads;
+    op.role = epi == EPI_SWIGLU ? ROLE_GATEUP : epi == EPI_LOGITS ? ROLE_LMHEAD
+              : (epi == EPI_ACCUM ? (ncols == arch_->D ? ROLE_O : ROLE_DOWN) : ROLE_QKV);
+    FlatTmaLaunch& t = op.fl;
+    uint32_t rows = 0;
+    for (int i = 0; i < nseg; i++) {
+      t.src[i] = src[i];
+      t.out[i] = out[i];
+      t.row_start[i] = rows;
+      rows += src[i].r_total;
+      op.alg_bytes += alg_bytes_of(src[i]);
+    }
+    t.row_start[nseg] = rows;
+    if (epi == EPI_SWIGLU) t.row_start[1] = src[0].r_total;
+    const uint32_t Rt = epi == EPI_SWIGLU ? src[0].r_total : rows;
+    const uint32_t G = Rt < (uint32_t)num_sms_ ? Rt : (uint32_t)num_sms_;
+    t.nseg = nseg;
+    t.epi = epi;
+    t.ncols = ncols;
+    t.rpc = (Rt + G - 1) / G;
+    t.x = x;
+    t.gamma = gamma;
+    t.norm = gamma != nullptr;
+    t.eps = arch_->eps;
+    t.check_layer = check_layer;
+    t.st = d_st_;
+    t.ignore_stop = ignore_stop;
+    t.res = d_res_;
+    t.gen_tokens = d_gen_;
+    t.max_gen = (int32_t)max_gen_;
+    t.xn_out = nullptr;
+    for (int i = 0; i < nseg; i++)
+      if (src[i].has_aux) t.xn_out = d_xn_;
+    if (tp_on) t.tp = *tp;
+    const uint32_t nparts = epi == EPI_SWIGLU ? 2u : 1u;
+    const uint32_t cw = (uint32_t)fmt_cw(op.fmt);
+    const uint32_t fixed = flat_layout(ncols, cw, t.rpc, nparts, 0).total;
+    const uint32_t budget = kFlatSmemLimit > fixed ? kFlatSmemLimit - fixed : 0u;
+    uint32_t nst = budget / kFlatStageBytes;
+    if (nst > kFlatStagesWanted) nst = kFlatStagesWanted;
+    if (nst >= 2) {
+      t.nst = nst;
+      op.smem = flat_layout(ncols, cw, t.rpc, nparts, nst).total;
+      op.grid = dim3(G);
+      ops.push_back(op);
+      for (int i = 0; i < nseg; i++) push_aux(src[i], epi == EPI_SWIGLU ? nullptr : out[i], gamma ? d_xn_ : x);
+      return;
+    }
+  }
+  if (tp_on) throw std::runtime_error("tensor parallel: a projection does not fit the flat TMA kernel");
   for (int i = 0; i < nseg && tma; i++) tma = tma_rows(src[i]) != 0;
   if (tma) {
     Op op;
@@ -675,32 +786,251 @@ void Engine::add_linear_ops(std::vector<Op>& ops, const GemvSrc* src, float* con
   }
 }
 
+// Embedding of the step's token (unpackEmbedRow, chpe_engine.zig:1491-1552).
+void Engine::push_embed(std::vector<Op>& ops) {
+  const ChpeArch& A = *arch_;
+  Op op;
+  op.type = OP_EMBED;
+  op.role = ROLE_EMBED;
+  EmbedLaunch& e = op.em;
+  e.arc = d_arc_;
+  e.record_count = f_.record_count;
+  e.stride = f_.stride;
+  e.prefix = f_.is_raw ? 0 : (f_.is_dense ? 64 : 3072 + 64);
+  e.D = A.D;
+  e.hidden = d_hidden_;
+  e.st = d_st_;
+  e.res = d_res_;
+  e.use_state = 1;
+  if (!f_.archive_valid || f_.record_count == 0) e.mode = EMB_PATTERN;
+  else if (f_.is_raw_fp16) e.mode = EMB_RAW_F16;
+  else if (f_.is_raw) e.mode = f_.quant_bits == 8 ? EMB_RAW_I8 : EMB_RAW_BF16;
+  else e.mode = EMB_CELL;
+  op.grid = dim3((A.D + 255) / 256);
+  ops.push_back(op);
+}
+
+// The LM head source (computeLmHead, chpe_engine.zig:1554-1660): an untied
+// span of cells, tied embedding cells, or tied raw rows.
+GemvSrc Engine::plan_lm_head() {
+  const ChpeArch& A = *arch_;
+  GemvSrc lm{};
+  int64_t lhs, lht;
+  chpe_lm_head_span(arch_id_, &lhs, &lht);
+  if (!f_.archive_valid || f_.record_count == 0) {
+    lm.kind = SRC_PATTERN;
+    lm.r_total = A.V;
+  } else if (lhs >= 0 && (uint64_t)lhs < f_.record_count) {
+    lm = plan_linear((uint64_t)lhs, (uint64_t)lht, A.V, A.D, A.D, 0, -1);
+  } else if (!f_.is_raw) {
+    // tied embedding cells, 16 rows each, unpackEmbedRowCell semantics
+    lm.kind = SRC_ROWTILE;
+    lm.arc = d_arc_;
+    lm.r_total = A.V;
+    lm.c_total = A.D;
+    lm.x_len = A.D;
+    lm.cell_rows = 16;
+    lm.cell_cols = A.D;
+    lm.tile0 = code_off(0);
+    lm.stride = f_.stride;
+    lm.rows_covered = A.V;
+    uint64_t ncell = (A.V + 15) / 16;
+    if (ncell > f_.record_count) throw std::runtime_error("tied LM head: archive has too few records");
+    int fmt = -1;
+    bool repl = false;
+    for (uint64_t t = 0; t < ncell; t++) {
+      const uint8_t* pl = host_ + code_off(t) + 16384;
+      uint32_t qb = pl[20], rows = rd32(pl + 40);
+      bool g = (rd64(pl + 24) & 1u) != 0;
+      if ((rows != 16 && rows != 0) || qb == 8)
+        throw std::runtime_error("tied LM head: embedding cells must hold 16 rows of 2/4-bit codes");
+      int f = qb == 2 ? FMT_W2G : ((g || qb == 4) ? FMT_W4G : FMT_W4SB);
+      if (fmt < 0) fmt = f;
+      if (f != fmt) throw std::runtime_error("tied LM head: mixed embedding cell formats");
+      if (t == 0) repl = g;
+      if (g != repl) throw std::runtime_error("tied LM head: mixed outlier flags");
+    }
+    lm.fmt = fmt;
+    lm.outliers = (repl && fmt != FMT_W4SB) ? OUTL_REPLACE : OUTL_NONE;
+  } else {
+    // tied raw FP16/BF16 embedding rows
+    uint32_t rpt = 8192 / A.D ? 8192 / A.D : 1;
+    uint64_t tiles = (A.V + rpt - 1) / rpt;
+    if (tiles > f_.record_count) tiles = f_.record_count;
+    lm.kind = SRC_RAW;
+    lm.fmt = f_.is_raw_fp16 ? FMT_F16 : FMT_BF16;
+    lm.arc = d_arc_;
+    lm.r_total = A.V;
+    lm.c_total = A.D;
+    lm.x_len = A.D;
+    lm.tile0 = code_off(0);
+    lm.stride = f_.stride;
+    lm.flat_limit = tiles * 8192ull;
+    lm.n_tiles = (uint32_t)tiles;
+  }
+  return lm;
+}
+
+// ---- tensor parallelism ------------------------------------------------------
+void Engine::tp_export(uint8_t* handle64) const {
+  cudaIpcMemHandle_t h;
+  CK(cudaSetDevice(device_));
+  CK(cudaIpcGetMemHandle(&h, d_region_));
+  static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
+  memcpy(handle64, &h, 64);
+}
+
+void Engine::tp_connect(const uint8_t* handles, int world) {
+  if (world != tp_world_) throw std::runtime_error("tp_connect: world size differs from init");
+  if (!ipc_open_.empty() || !ops_->empty()) throw std::runtime_error("tp_connect: already connected");
+  CK(cudaSetDevice(device_));
+  for (int r = 0; r < world; r++) {
+    if (r == tp_rank_) {
+      tp_delta_[r] = 0;
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handles + 64 * r, 64);
+    void* p = nullptr;
+    CK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+    ipc_open_.push_back(p);
+    tp_delta_[r] = (long long)((uint8_t*)p - d_region_);
+  }
+  build_step_tp();
+}
+
+// One decode step over this rank's slices.  Every projection is split by
+// output rows (contiguous flat ranges of the row-major weight stream): q/k/v
+// by heads, O and down by hidden rows, gate/up by FFN rows, the LM head by
+// vocabulary rows.  Each output element is computed whole on one rank, with
+// the same kernel and summation order as on one GPU, so results do not depend
+// on the rank count.  Exchanges (written by the producing kernel straight into
+// every rank's region, then counted): attention heads -> attn, O rows ->
+// hidden, SwiGLU rows -> mlp, down rows -> hidden, logits (when gathered).
+void Engine::build_step_tp() {
+  const ChpeArch& A = *arch_;
+  std::vector<Op>& ops = *ops_;
+  ops.clear();
+  const uint32_t N = (uint32_t)tp_world_, R = (uint32_t)tp_rank_;
+  if (!f_.archive_valid || f_.record_count == 0)
+    throw std::runtime_error("tensor parallel: needs a valid archive");
+  if (A.H % N || A.D % N || A.F % N || A.V % N)
+    throw std::runtime_error("tensor parallel: heads, hidden, FFN and vocabulary must divide by the rank count");
+  const uint32_t G = A.H / A.KV, hq = A.H / N, h0 = R * hq;
+  uint32_t kv0 = h0 / G, kvl;
+  if (hq >= G) {
+    if (hq % G) throw std::runtime_error("tensor parallel: query heads per rank must cover whole kv groups");
+    kvl = hq / G;
+  } else {
+    if (G % hq) throw std::runtime_error("tensor parallel: query heads per rank must divide a kv group");
+    kvl = 1;
+  }
+  const uint32_t dl = A.D / N, d0 = R * dl, fl = A.F / N, f0 = R * fl, vl = A.V / N, v0 = R * vl;
+  const uint32_t qd = A.H * A.HD, kvd = A.KV * A.HD;
+  auto grid_of = [&](uint32_t rows) { return rows < (uint32_t)num_sms_ ? rows : (uint32_t)num_sms_; };
+  const unsigned long long u_att = (unsigned long long)N * nsplit_ * kvl;
+  const unsigned long long u_d = (unsigned long long)N * grid_of(dl);  // O and down
+  const unsigned long long u_gu = (unsigned long long)N * grid_of(fl);
+  TpLink base{};
+  base.world = (int32_t)N;
+  base.rank = (int32_t)R;
+  for (int r = 0; r < kTpMax; r++) base.delta[r] = tp_delta_[r];
+  base.sh = d_tpsh_;
+  base.wait_sig = -1;
+  base.signal_sig = -1;
+  base.wait_per_step = A.L;
+  auto link = [&](int wait_sig, uint32_t wait_index, unsigned long long units, int signal_sig, int bcast) {
+    TpLink t = base;
+    t.wait_sig = wait_sig;
+    t.wait_index = wait_index;
+    t.wait_units = units;
+    t.signal_sig = signal_sig;
+    t.bcast = bcast;
+    return t;
+  };
+  auto narrow = [&](GemvSrc s, uint32_t r0, uint32_t n) {
+    if (s.kind != SRC_FLAT && s.kind != SRC_RAW)
+      throw std::runtime_error("tensor parallel: every projection must be flat cells or a raw stream");
+    if (s.has_aux) throw std::runtime_error("tensor parallel: down_aux replacement cells are not supported");
+    s.row0 = r0;
+    s.r_total = n;
+    if (s.bias) s.bias += r0;
+    return s;
+  };
+
+  push_embed(ops);
+  std::vector<float> gam(A.D);
+  for (uint32_t l = 0; l < A.L; l++) {
+    ChpeLayerInfo li;
+    chpe_layer_info(arch_id_, f_.is_raw, l, &li);
+    unpack_norm((uint64_t)li.input_norm, gam.data());
+    const float* g_in = upload_floats(gam);
+    unpack_norm((uint64_t)li.post_norm, gam.data());
+    const float* g_post = upload_floats(gam);
+    GemvSrc qkv[3] = {
+        narrow(plan_linear(li.q_proj, li.q_tiles, qd, A.D, A.D, 0, li.q_bias), h0 * A.HD, hq * A.HD),
+        narrow(plan_linear(li.k_proj, li.k_tiles, kvd, A.D, A.D, 0, li.k_bias), kv0 * A.HD, kvl * A.HD),
+        narrow(plan_linear(li.v_proj, li.v_tiles, kvd, A.D, A.D, 0, li.v_bias), kv0 * A.HD, kvl * A.HD)};
+    float* qkv_out[3] = {d_q_, d_k_, d_v_};
+    TpLink t_qkv = link(l ? SIG_DOWN : -1, l, u_d, -1, 0);
+    add_linear_ops(ops, qkv, qkv_out, 3, EPI_STORE, d_hidden_, g_in, (int)l - 1, A.D, false, &t_qkv);
+    {
+      Op op;
+      op.type = OP_ATTN;
+      op.role = ROLE_ATTN;
+      op.hd = (int)A.HD;
+      AttnLaunch& at = op.at;
+      at.q = d_q_;
+      at.k = d_k_;
+      at.v = d_v_;
+      size_t lay = (size_t)l * max_seq_ * kvl * A.HD;  // this rank's kv heads only
+      at.kc = d_kc_ + lay;
+      at.vc = d_vc_ + lay;
+      at.out = d_attn_ + (size_t)h0 * A.HD;
+      at.part = d_part_;
+      at.counters = d_counters_;
+      at.inv_freq = d_invfreq_;
+      at.st = d_st_;
+      at.H = (int)hq;
+      at.KV = (int)kvl;
+      at.HD = (int)A.HD;
+      at.nsplit = nsplit_;
+      at.max_seq = (int32_t)max_seq_;
+      at.tp = link(-1, 0, 0, SIG_ATT, 1);
+      op.grid = dim3(nsplit_, kvl);
+      op.threads = (int)(hq / kvl) * 32;
+      if (op.threads < (int)A.HD / 2) op.threads = (int)A.HD / 2;
+      ops.push_back(op);
+    }
+    GemvSrc o = narrow(plan_linear(li.o_proj, li.o_tiles, A.D, A.D, A.D, 1, -1), d0, dl);
+    float* o_out[1] = {d_hidden_ + d0};
+    TpLink t_o = link(SIG_ATT, l + 1, u_att, SIG_O, 1);
+    add_linear_ops(ops, &o, o_out, 1, EPI_ACCUM, d_attn_, nullptr, -1, A.D, false, &t_o);
+    GemvSrc gu[2] = {narrow(plan_linear(li.gate_proj, li.gate_tiles, A.F, A.D, A.D, 0, -1), f0, fl),
+                     narrow(plan_linear(li.up_proj, li.up_tiles, A.F, A.D, A.D, 0, -1), f0, fl)};
+    float* gu_out[2] = {d_mlp_ + f0, nullptr};
+    TpLink t_gu = link(SIG_O, l + 1, u_d, SIG_GU, 1);
+    add_linear_ops(ops, gu, gu_out, 2, EPI_SWIGLU, d_hidden_, g_post, -1, A.D, false, &t_gu);
+    GemvSrc dn = narrow(plan_linear(li.down_proj, li.down_tiles, A.D, A.F, A.F, 1, -1), d0, dl);
+    float* dn_out[1] = {d_hidden_ + d0};
+    TpLink t_dn = link(SIG_GU, l + 1, u_gu, SIG_DOWN, 1);
+    add_linear_ops(ops, &dn, dn_out, 1, EPI_ACCUM, d_mlp_, nullptr, -1, A.F, false, &t_dn);
+  }
+  unpack_norm((uint64_t)chpe_final_norm_index(arch_id_, f_.is_raw), gam.data());
+  const float* g_fin = upload_floats(gam);
+  GemvSrc lm = narrow(plan_lm_head(), v0, vl);
+  float* lm_out[1] = {d_logits_ + v0};
+  TpLink t_lm = link(SIG_DOWN, A.L, u_d, SIG_LM, 1);
+  t_lm.lm_units = (unsigned long long)N * grid_of(vl);
+  add_linear_ops(ops, &lm, lm_out, 1, EPI_LOGITS, d_hidden_, g_fin, -1, A.D, true, &t_lm);
+}
+
 // ---- the decode step: forwardDecode (chpe_engine.zig:1663-1803) ------------
 void Engine::build_step() {
   const ChpeArch& A = *arch_;
   std::vector<Op>& ops = *ops_;
   ops.clear();
-  {  // embedding
-    Op op;
-    op.type = OP_EMBED;
-    op.role = ROLE_EMBED;
-    EmbedLaunch& e = op.em;
-    e.arc = d_arc_;
-    e.record_count = f_.record_count;
-    e.stride = f_.stride;
-    e.prefix = f_.is_raw ? 0 : (f_.is_dense ? 64 : 3072 + 64);
-    e.D = A.D;
-    e.hidden = d_hidden_;
-    e.st = d_st_;
-    e.res = d_res_;
-    e.use_state = 1;
-    if (!f_.archive_valid || f_.record_count == 0) e.mode = EMB_PATTERN;
-    else if (f_.is_raw_fp16) e.mode = EMB_RAW_F16;
-    else if (f_.is_raw) e.mode = f_.quant_bits == 8 ? EMB_RAW_I8 : EMB_RAW_BF16;
-    else e.mode = EMB_CELL;
-    op.grid = dim3((A.D + 255) / 256);
-    ops.push_back(op);
-  }
+  push_embed(ops);
   const uint32_t qd = A.H * A.HD, kvd = A.KV * A.HD;
   std::vector<float> gam(A.D);
   for (uint32_t l = 0; l < A.L; l++) {
@@ -756,60 +1086,7 @@ void Engine::build_step() {
   // final norm + LM head (computeLmHead, :1554-1660) + argmax (:1775-1802)
   unpack_norm((uint64_t)chpe_final_norm_index(arch_id_, f_.is_raw), gam.data());
   const float* g_fin = upload_floats(gam);
-  GemvSrc lm{};
-  int64_t lhs, lht;
-  chpe_lm_head_span(arch_id_, &lhs, &lht);
-  if (!f_.archive_valid || f_.record_count == 0) {
-    lm.kind = SRC_PATTERN;
-    lm.r_total = A.V;
-  } else if (lhs >= 0 && (uint64_t)lhs < f_.record_count) {
-    lm = plan_linear((uint64_t)lhs, (uint64_t)lht, A.V, A.D, A.D, 0, -1);
-  } else if (!f_.is_raw) {
-    // tied embedding cells, 16 rows each, unpackEmbedRowCell semantics
-    lm.kind = SRC_ROWTILE;
-    lm.arc = d_arc_;
-    lm.r_total = A.V;
-    lm.c_total = A.D;
-    lm.x_len = A.D;
-    lm.cell_rows = 16;
-    lm.cell_cols = A.D;
-    lm.tile0 = code_off(0);
-    lm.stride = f_.stride;
-    lm.rows_covered = A.V;
-    uint64_t ncell = (A.V + 15) / 16;
-    if (ncell > f_.record_count) throw std::runtime_error("tied LM head: archive has too few records");
-    int fmt = -1;
-    bool repl = false;
-    for (uint64_t t = 0; t < ncell; t++) {
-      const uint8_t* pl = host_ + code_off(t) + 16384;
-      uint32_t qb = pl[20], rows = rd32(pl + 40);
-      bool g = (rd64(pl + 24) & 1u) != 0;
-      if ((rows != 16 && rows != 0) || qb == 8)
-        throw std::runtime_error("tied LM head: embedding cells must hold 16 rows of 2/4-bit codes");
-      int f = qb == 2 ? FMT_W2G : ((g || qb == 4) ? FMT_W4G : FMT_W4SB);
-      if (fmt < 0) fmt = f;
-      if (f != fmt) throw std::runtime_error("tied LM head: mixed embedding cell formats");
-      if (t == 0) repl = g;
-      if (g != repl) throw std::runtime_error("tied LM head: mixed outlier flags");
-    }
-    lm.fmt = fmt;
-    lm.outliers = (repl && fmt != FMT_W4SB) ? OUTL_REPLACE : OUTL_NONE;
-  } else {
-    // tied raw FP16/BF16 embedding rows
-    uint32_t rpt = 8192 / A.D ? 8192 / A.D : 1;
-    uint64_t tiles = (A.V + rpt - 1) / rpt;
-    if (tiles > f_.record_count) tiles = f_.record_count;
-    lm.kind = SRC_RAW;
-    lm.fmt = f_.is_raw_fp16 ? FMT_F16 : FMT_BF16;
-    lm.arc = d_arc_;
-    lm.r_total = A.V;
-    lm.c_total = A.D;
-    lm.x_len = A.D;
-    lm.tile0 = code_off(0);
-    lm.stride = f_.stride;
-    lm.flat_limit = tiles * 8192ull;
-    lm.n_tiles = (uint32_t)tiles;
-  }
+  GemvSrc lm = plan_lm_head();
   float* lm_out[1] = {d_logits_};
   add_linear_ops(ops, &lm, lm_out, 1, EPI_LOGITS, d_hidden_, g_fin, -1, A.D, true);
 
@@ -906,8 +1183,65 @@ static void launch_tma(const Op& op, cudaStream_t s) {
   throw std::runtime_error("no TMA kernel for this format");
 }
 
+template <int FMT, int KIND>
+static void launch_flat_t(const Op& op, cudaStream_t s) {
+  auto k = gemv_flat_tma_kernel<FMT, KIND>;
+  static bool configured = false;
+  if (!configured) {
+    CK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFlatSmemLimit));
+    configured = true;
+  }
+  launch_pdl(k, op.grid, dim3(kFlatThreads), op.smem, s, op.fl);
+}
+
+static void launch_flat(const Op& op, cudaStream_t s) {
+  if (op.kind == SRC_FLAT) {
+    switch (op.fmt) {
+      case FMT_W4G: return launch_flat_t<FMT_W4G, SRC_FLAT>(op, s);
+      case FMT_W4SB: return launch_flat_t<FMT_W4SB, SRC_FLAT>(op, s);
+      case FMT_W2G: return launch_flat_t<FMT_W2G, SRC_FLAT>(op, s);
+      case FMT_W2SB: return launch_flat_t<FMT_W2SB, SRC_FLAT>(op, s);
+    }
+  } else if (op.kind == SRC_RAW) {
+    switch (op.fmt) {
+      case FMT_F16: return launch_flat_t<FMT_F16, SRC_RAW>(op, s);
+      case FMT_BF16: return launch_flat_t<FMT_BF16, SRC_RAW>(op, s);
+      case FMT_I8RAW: return launch_flat_t<FMT_I8RAW, SRC_RAW>(op, s);
+    }
+  }
+  throw std::runtime_error("no flat TMA kernel for this (format, layout)");
+}
+
+static const char* fmt_name(int fmt) {
+  static const char* N[] = {"W4G", "W4SB", "W2G", "W2SB", "W8", "F16", "BF16", "F32", "I8RAW", "ZERO"};
+  return fmt >= 0 && fmt <= 9 ? N[fmt] : "?";
+}
+static const char* kind_name(int kind) {
+  static const char* N[] = {"NOOP", "PATTERN", "RAW", "ROWTILE", "FLAT", "GEN_ROWTILE", "GEN_FLAT"};
+  return kind >= 0 && kind <= 6 ? N[kind] : "?";
+}
+
+std::string Engine::role_kernel_name(int role) const {
+  for (const Op& op : *ops_) {
+    if (op.role != role) continue;
+    const std::string fk = std::string("<") + fmt_name(op.fmt) + "," + kind_name(op.kind) + ">";
+    switch (op.type) {
+      case OP_FLAT_TMA: return "gemv_flat_tma_kernel" + fk;
+      case OP_TMA: return "gemv_tma_kernel" + fk;
+      case OP_GEMV: return "gemv_kernel" + fk;
+      case OP_ATTN: return "attention_kernel<" + std::to_string(op.hd) + ">";
+      case OP_EMBED: return "embed_kernel";
+      case OP_GEN_ROW: return "gemv_generic_rowtile";
+      case OP_GEN_FLAT: return "gemv_generic_flat";
+      default: return "op" + std::to_string(op.type);
+    }
+  }
+  return "";
+}
+
 void Engine::launch(const Op& op, cudaStream_t s) const {
   switch (op.type) {
+    case OP_FLAT_TMA: return launch_flat(op, s);
     case OP_TMA: return launch_tma(op, s);
     case OP_GEMV: return launch_gemv(op, s);
     case OP_GEN_ROW: return launch_pdl(gemv_generic_rowtile, op.grid, dim3(256), 0, s, op.gen);
@@ -960,6 +1294,7 @@ void Engine::sync_result() {
 // Positions start_pos.. for the given tokens (forwardDecode per token).
 void Engine::forward(const uint32_t* toks, size_t n, uint32_t start_pos) {
   if (n == 0) return;
+  if (ops_->empty()) throw std::runtime_error("tensor parallel engine: call tp_connect first");
   if ((uint64_t)start_pos + n > max_seq_) throw std::runtime_error("sequence exceeds max_seq_len");
   if (!graph_) {
     // The warm-up launch inside ensure_graph runs one step on whatever state
@@ -1023,6 +1358,8 @@ float Engine::timed_greedy_steps(size_t n) {
   int32_t one = 1, zero = 0;
   CK(cudaMemcpyAsync(&d_st_->feed_argmax, &one, 4, cudaMemcpyHostToDevice, stream_));
   CK(cudaMemcpyAsync(&d_st_->n_gen, &zero, 4, cudaMemcpyHostToDevice, stream_));
+  // greedy steps need only the argmax: ranks keep their own logit slices
+  CK(cudaMemcpyAsync(&d_st_->gather, &zero, 4, cudaMemcpyHostToDevice, stream_));
   cudaEvent_t a, b;
   CK(cudaEventCreate(&a));
   CK(cudaEventCreate(&b));
@@ -1031,6 +1368,7 @@ float Engine::timed_greedy_steps(size_t n) {
   run_steps(n);
   CK(cudaEventRecord(b, stream_));
   CK(cudaMemcpyAsync(&d_st_->feed_argmax, &zero, 4, cudaMemcpyHostToDevice, stream_));
+  CK(cudaMemcpyAsync(&d_st_->gather, &one, 4, cudaMemcpyHostToDevice, stream_));
   sync_result();
   float ms = 0;
   CK(cudaEventElapsedTime(&ms, a, b));
@@ -1064,6 +1402,8 @@ void Engine::copy_logits(float* out) const {
 }
 
 void Engine::bench_role(int role, int rounds, float* avg_ms, double* bytes_per_launch, int* launches) {
+  if (tp_world_ > 1)
+    throw std::runtime_error("per-role timing launches one role alone; not available with tensor parallelism");
   std::vector<const Op*> sel;
   for (const Op& op : *ops_)
     if (op.role == role) sel.push_back(&op);

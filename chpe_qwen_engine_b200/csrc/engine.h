@@ -31,8 +31,18 @@ class Engine {
  public:
   // Counterpart of CHPEEngine.init over archive bytes the caller keeps alive
   // for the engine's lifetime (`bytes` may be an mmap).  Throws std::runtime_error.
-  Engine(const uint8_t* bytes, uint64_t len, int arch, uint32_t max_seq, int device);
+  // With tp_world > 1 the engine is rank tp_rank of a tensor-parallel group
+  // (one process per GPU) and is usable after tp_connect().
+  Engine(const uint8_t* bytes, uint64_t len, int arch, uint32_t max_seq, int device, int tp_rank = 0,
+         int tp_world = 1);
   ~Engine();
+
+  // Tensor parallel set-up: the CUDA IPC handle (64 bytes) of this rank's
+  // exchange region, then every rank's handles in rank order; builds the step.
+  void tp_export(uint8_t* handle64) const;
+  void tp_connect(const uint8_t* handles, int world);
+  int tp_world() const { return tp_world_; }
+  int tp_rank() const { return tp_rank_; }
 
   const ChpeArch& arch() const { return *arch_; }
   const EngineFacts& facts() const { return f_; }
@@ -60,6 +70,7 @@ class Engine {
   // times, with CUDA events on the engine stream; returns the average
   // milliseconds per launch and the algorithmic weight bytes per launch.
   void bench_role(int role, int rounds, float* avg_ms, double* bytes_per_launch, int* launches);
+  std::string role_kernel_name(int role) const;
 
   // Test entry points that run one kernel family on host vectors.
   void debug_gemv_linear(uint64_t tile_start, uint64_t num_tiles, const float* x, uint64_t x_len,
@@ -83,9 +94,12 @@ class Engine {
   uint64_t code_off(uint64_t tile) const;
   const float* upload_floats(const std::vector<float>& v);
   void build_step();
+  void build_step_tp();
+  void push_embed(std::vector<Op>& ops);
+  GemvSrc plan_lm_head();
   void add_linear_ops(std::vector<Op>& ops, const GemvSrc* src, float* const* out, int nseg,
                       int epi, const float* x, const float* gamma, int check_layer,
-                      uint32_t ncols, bool ignore_stop);
+                      uint32_t ncols, bool ignore_stop, const TpLink* tp = nullptr);
   void launch(const Op& op, cudaStream_t s) const;
   void record(cudaStream_t s) const;
   void run_steps(size_t n);
@@ -122,6 +136,14 @@ class Engine {
   uint32_t pos_ = 0;
   int num_sms_ = 148;
   int nsplit_ = 16;  // attention splits of the positions per kv head
+
+  // tensor parallelism
+  int tp_rank_ = 0, tp_world_ = 1;
+  uint8_t* d_region_ = nullptr;  // exchange region: step state, counters, hidden, attn, mlp, logits
+  size_t region_bytes_ = 0;
+  TpShared* d_tpsh_ = nullptr;
+  long long tp_delta_[kTpMax] = {};
+  std::vector<void*> ipc_open_;
 };
 
 }  // namespace chpe

@@ -41,7 +41,7 @@ struct GemvSrc {
   uint32_t outliers;      // ROWTILE W4G/W2G with rows == 16: additive outliers
   uint32_t has_aux;       // FLAT: some tile carries down_aux replacements
   uint32_t n_tiles;       // available tiles
-  uint32_t pad_;
+  uint32_t row0;          // FLAT/RAW: first tensor row of this call (a tensor-parallel slice)
   const uint8_t* arc;     // device archive (byte 0)
   uint64_t tile0;         // byte offset of tile_start's code area
   uint64_t stride;        // bytes between tiles
@@ -62,6 +62,40 @@ struct StepState {
   uint32_t done_ctas;  // LM-head CTAs finished (last one finalises)
   int32_t n_gen;       // generated-token counter (chpe_generate)
   int32_t err;         // non-zero: a kernel gave up a bounded wait (device timeout)
+  int32_t gather;      // tensor parallel: 1 = every rank receives the full logits
+  int32_t pad_;
+};
+
+// ---- tensor parallelism (one process per GPU) ------------------------------
+// Every rank owns one exchange region (step state, these counters, hidden,
+// attention output, MLP activation, logits) mapped into every other rank
+// through CUDA IPC.  A producing kernel writes its output rows into every
+// rank's region and then adds 1 to counter `kind` on every rank (release,
+// system scope); the consuming kernel waits until its own counter reaches the
+// arrivals of all ranks for that (step, layer).
+constexpr int kTpMax = 8;
+enum TpSig : int32_t { SIG_ATT = 0, SIG_O = 1, SIG_GU = 2, SIG_DOWN = 3, SIG_LM = 4, SIG_KINDS = 5 };
+
+struct TpShared {
+  unsigned long long sig[8];  // arrivals per kind since the engine was built
+  uint32_t epoch;             // decode steps completed (advanced by the LM head)
+  float token0;               // logit of token 0 (from the rank that owns vocab row 0)
+  uint32_t pad_[14];
+};
+
+struct TpLink {
+  int32_t world;               // 1: single GPU, nothing exchanged
+  int32_t rank;
+  long long delta[kTpMax];     // byte distance from this rank's region to rank r's
+  TpShared* sh;                // this rank's counters
+  int32_t wait_sig;            // kind to wait for before reading x, -1 none
+  int32_t signal_sig;          // kind to signal after the outputs, -1 none
+  uint32_t wait_index;         // target = (epoch * wait_per_step + wait_index) * wait_units
+  uint32_t wait_per_step;
+  unsigned long long wait_units;  // arrivals per (step, layer) of the awaited kind
+  unsigned long long lm_units;    // LM head: arrivals per step of all ranks' CTAs
+  int32_t bcast;               // 1: outputs lie in the region; write them on every rank
+  int32_t pad_;
 };
 
 // Result of one forward step (chpe_engine.zig:803 ForwardResult).

@@ -1,0 +1,491 @@
+// gemv_flat_tma.cuh -- GEMV over flat weight streams with a warp-specialised
+// TMA pipeline.
+//
+// Covers the two layouts whose rows run across tile boundaries:
+//   * flat cells (gemvCellFlat, chpe_engine.zig:583-703, dispatch :1443-1454):
+//     each 32768-weight cell holds a slice of the row-major [rows x cols]
+//     stream, with its scales in the cell payload (group g = offset/128 of the
+//     cell, or one scale/bias per cell);
+//   * raw tiles (dotSegment, :1194-1254, :1455-1479): one contiguous FP16 /
+//     BF16 / int8 stream.
+// Every tensor of the 72B and 9B archives and the 3B down projection (11008
+// columns) take one of these.
+//
+// Work split: CTA b owns rows [Rt*b/G, Rt*(b+1)/G) of the concatenated call
+// (q|k|v, or gate and up for SwiGLU), i.e. one contiguous flat range per
+// tensor.  The range is cut at tile boundaries into pieces of at most one
+// tile (16 KiB of codes).  A producer warp streams the pieces with
+// cp.async.bulk into an NST-stage ring; full[s] completes on the copied bytes,
+// empty[s] on one arrival per consumer warp, so no CTA-wide barrier sits in
+// the loop.  The first NST pieces are requested before the programmatic
+// dependent-launch wait.
+//
+// Consumers: 16 warps.  Warp w decodes chunks [w*CPWARP, (w+1)*CPWARP) of each
+// piece, lane L the chunks w*CPWARP + L + 32j.  A warp's run spans at most two
+// rows (CPWARP*CW <= cols, checked by the host), so a lane keeps two partial
+// sums; the warp reduces them and lane 0 adds them to its own per-row slots
+// wacc[part][warp][row].  After the last piece the slots are summed over the
+// warps in a fixed order, so results do not depend on timing.  x sits in
+// shared memory in the lane-permuted layout (xpos), which keeps the quad
+// loads of consecutive chunks conflict free, with one x-sum per chunk.
+//
+// Waits are bounded (kMaxWaitPolls); a timeout records StepState::err, the
+// CTA stops consuming, the producer waits (bounded) for the copies it issued
+// and the outputs of the CTA are not written.
+#pragma once
+#include "gemv.cuh"
+#include "gemv_tma.cuh"
+
+namespace chpe {
+
+struct FlatTmaLaunch {
+  GemvSrc src[3];
+  float* out[3];
+  uint32_t row_start[4];   // prefix of rows over segments (SwiGLU: [0, rows])
+  int32_t nseg;
+  int32_t epi;
+  uint32_t ncols;          // x length = columns of every segment
+  uint32_t rpc;            // max rows per CTA (size of the per-warp row slots)
+  uint32_t nst;            // stages in the ring (<= kFlatMaxStages)
+  const float* x;          // hidden when norm != 0, else the input vector
+  const float* gamma;
+  float eps;
+  int32_t norm;
+  int32_t check_layer;
+  StepState* st;
+  int32_t ignore_stop;
+  StepResult* res;
+  int32_t* gen_tokens;
+  int32_t max_gen;
+  float* xn_out;           // normalised x for the down_aux fix-up op (or null)
+  TpLink tp;               // tensor-parallel wait / exchange / signal (world 1: none)
+};
+
+constexpr uint32_t kFlatStageBytes = 16384 + 896;  // codes + payload head (832) rounded to 128
+constexpr uint32_t kFlatMaxStages = 16;
+constexpr uint32_t kFlatThreads = 544;             // 16 consumer warps + 1 producer warp
+constexpr uint32_t kFlatMaxRanges = 8;
+
+struct FlatRange {
+  uint32_t src;     // index into src[]
+  uint32_t part;    // 0, or 1 for the up half of SwiGLU
+  uint32_t fa0, fb0;// tensor-relative flat weight range [fa0, fb0)
+  uint32_t k0;      // first tile
+  uint32_t pstart;  // index of its first piece
+  int32_t lrbase;   // tensor row + lrbase = CTA-local row
+  uint32_t pad;
+};
+
+struct FlatLayout {
+  uint32_t x, xs, wacc, bars, ranges, total;
+};
+
+// Shared-memory layout, shared by host (size) and kernel (offsets).
+__host__ __device__ inline FlatLayout flat_layout(uint32_t ncols, uint32_t cw, uint32_t rpc, uint32_t nparts,
+                                                  uint32_t nst) {
+  FlatLayout l;
+  const uint32_t nchunks = ncols / cw, slots = (nchunks + 31) / 32;
+  l.x = nst * kFlatStageBytes;
+  l.xs = l.x + slots * 32 * cw * 4;
+  l.wacc = l.xs + slots * 32 * 4;
+  l.bars = (l.wacc + nparts * 16 * rpc * 4 + 15) & ~15u;
+  l.ranges = l.bars + 2 * kFlatMaxStages * 8;
+  l.total = l.ranges + kFlatMaxRanges * (uint32_t)sizeof(FlatRange);
+  return l;
+}
+
+// Weights per piece: a flat cell, or 16 KiB of a raw stream.
+template <int FMT, int KIND>
+__host__ __device__ constexpr uint32_t flat_wpp() {
+  return KIND == SRC_FLAT ? 32768u : 16384u * 8u / (uint32_t)FmtInfo<FMT>::BITS;
+}
+
+// Bounded wait that also gives up once another warp has flagged an error.
+CHPE_DEV bool mbar_wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* bad) {
+  for (uint32_t i = 0; i < kMaxWaitPolls; i++) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 255u && *bad) return false;
+  }
+  return false;
+}
+CHPE_DEV void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+CHPE_DEV void consumer_sync() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
+
+template <int FMT, int KIND>
+__global__ void __launch_bounds__(kFlatThreads, 1) gemv_flat_tma_kernel(const __grid_constant__ FlatTmaLaunch P) {
+  using FI = FmtInfo<FMT>;
+  constexpr uint32_t CW = FI::CW, QPC = CW / 4;
+  constexpr uint32_t WPP = flat_wpp<FMT, KIND>();
+  constexpr uint32_t NCH = WPP / CW;        // chunks in a full piece
+  constexpr uint32_t CPWARP = NCH / 16;     // chunks per consumer warp
+  constexpr uint32_t CPL = CPWARP / 32;     // chunks per lane
+  static_assert(CPL >= 1 && CPWARP % 32 == 0, "piece geometry");
+  static_assert(NCH * 16 <= 16384, "a piece fits a stage");
+
+  extern __shared__ __align__(128) uint8_t fsm[];
+  const uint32_t tid = threadIdx.x, warp = tid >> 5, L = tid & 31;
+  const bool swig = P.epi == EPI_SWIGLU;
+  const uint32_t nparts = swig ? 2u : 1u;
+  const uint32_t C = P.ncols, nst = P.nst;
+  const FlatLayout lay = flat_layout(C, CW, P.rpc, nparts, nst);
+  float* xsh = reinterpret_cast<float*>(fsm + lay.x);
+  float* xsc = reinterpret_cast<float*>(fsm + lay.xs);
+  float* wacc = reinterpret_cast<float*>(fsm + lay.wacc);
+  uint64_t* full = reinterpret_cast<uint64_t*>(fsm + lay.bars);
+  uint64_t* empty = full + kFlatMaxStages;
+  FlatRange* rg = reinterpret_cast<FlatRange*>(fsm + lay.ranges);
+  __shared__ float sred[16];
+  __shared__ unsigned long long kbest[16];
+  __shared__ uint32_t kfin[16];
+  __shared__ uint32_t s_npieces, s_nranges;
+  __shared__ int s_abort, s_is_last;
+  __shared__ volatile int s_bad;
+
+  const uint32_t Rt = P.row_start[swig ? 1 : P.nseg];
+  const uint32_t R0 = (uint32_t)((uint64_t)Rt * blockIdx.x / gridDim.x);
+  const uint32_t R1 = (uint32_t)((uint64_t)Rt * (blockIdx.x + 1) / gridDim.x);
+
+  if (tid == 0) {
+    // this CTA's flat ranges, gate pieces before up pieces for SwiGLU
+    uint32_t n = 0, pieces = 0;
+    for (uint32_t p = 0; p < nparts; p++) {
+      const uint32_t nsg = swig ? 1u : (uint32_t)P.nseg;
+      for (uint32_t g = 0; g < nsg; g++) {
+        const uint32_t si = swig ? p : g;
+        const uint32_t S0 = swig ? 0u : P.row_start[g], S1 = swig ? Rt : P.row_start[g + 1];
+        const uint32_t a = R0 > S0 ? R0 : S0, b = R1 < S1 ? R1 : S1;
+        if (a >= b) continue;
+        FlatRange r;
+        r.src = si;
+        r.part = p;
+        const uint32_t row0 = P.src[si].row0;  // tensor row of the call's row 0
+        r.fa0 = (a - S0 + row0) * C;
+        r.fb0 = (b - S0 + row0) * C;
+        r.k0 = r.fa0 / WPP;
+        r.pstart = pieces;
+        r.lrbase = (int32_t)S0 - (int32_t)R0 - (int32_t)row0;
+        r.pad = 0;
+        rg[n++] = r;
+        pieces += (r.fb0 - 1) / WPP - r.k0 + 1;
+      }
+    }
+    s_nranges = n;
+    s_npieces = pieces;
+    s_abort = 0;
+    s_bad = 0;
+    for (uint32_t i = 0; i < nst; i++) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 16);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const uint32_t npieces = s_npieces, nranges = s_nranges;
+
+  // piece i -> (range, tile k, flat range [fa, fb))
+  auto locate = [&](uint32_t i, uint32_t& ri, uint32_t& k, uint32_t& fa, uint32_t& fb) {
+    while (ri + 1 < nranges && i >= rg[ri + 1].pstart) ri++;
+    const FlatRange& r = rg[ri];
+    k = r.k0 + (i - r.pstart);
+    fa = k * WPP > r.fa0 ? k * WPP : r.fa0;
+    fb = (k + 1) * WPP < r.fb0 ? (k + 1) * WPP : r.fb0;
+  };
+
+  // ---- producer warp ------------------------------------------------------
+  if (warp == 16) {
+    uint32_t ri = 0, issued = 0;
+    auto issue = [&](uint32_t i) {
+      uint32_t k, fa, fb;
+      locate(i, ri, k, fa, fb);
+      const GemvSrc& s = P.src[rg[ri].src];
+      uint8_t* dst = fsm + (i % nst) * kFlatStageBytes;
+      const uint32_t bytes = (fb - fa) * FI::BITS / 8;
+      const uint8_t* codes;
+      const uint8_t* tile = s.arc + s.tile0 + (uint64_t)k * s.stride;
+      if constexpr (KIND == SRC_FLAT) codes = tile + (fa - k * WPP) * FI::BITS / 8;
+      else codes = s.arc + s.tile0 + (uint64_t)fa * FI::BITS / 8;
+      const uint32_t extra = KIND == SRC_FLAT ? kPayloadHead : 0u;
+      mbar_expect_tx(&full[i % nst], bytes + extra);
+      bulk_g2s(dst, codes, bytes, &full[i % nst]);
+      if constexpr (KIND == SRC_FLAT) bulk_g2s(dst + 16384, tile + 16384, kPayloadHead, &full[i % nst]);
+    };
+    auto drain = [&]() {  // copies in flight complete before the CTA exits
+      const uint32_t from = issued > nst ? issued - nst : 0u;
+      for (uint32_t i = from; i < issued; i++) mbar_wait(&full[i % nst], (i / nst) & 1u);
+    };
+    if (L == 0) {
+      const uint32_t npre = npieces < nst ? npieces : nst;
+      for (; issued < npre; issued++) issue(issued);
+    }
+    __syncthreads();  // consumers' prologue done: s_abort is final
+    if (L != 0) return;
+    if (s_abort) { drain(); return; }
+    for (; issued < npieces; issued++) {
+      const uint32_t i = issued, s = i % nst;
+      if (!mbar_wait_or_abort(&empty[s], ((i / nst) - 1u) & 1u, &s_bad)) {
+        atomicExch(&P.st->err, 1);
+        s_bad = 1;
+        break;
+      }
+      fence_proxy_async_smem();
+      issue(i);
+    }
+    drain();
+    return;
+  }
+
+  // ---- consumers: x (optionally RMSNorm'ed) into shared memory --------------
+  pdl_wait();
+  if (tid == 0) {
+    int ab = (!P.ignore_stop && P.st->stop) ? 1 : 0;
+    if (!ab && !tp_wait(P.tp)) {  // inputs from the other ranks
+      atomicExch(&P.st->err, 1);
+      ab = 1;
+    }
+    s_abort = ab;
+  }
+  consumer_sync();
+  const bool stop = s_abort != 0;
+  float tot = 0.f;
+  const uint32_t nq = C / 4;
+  const float4* x4 = reinterpret_cast<const float4*>(P.x);
+  if (!stop) {
+    for (uint32_t i = tid; i < nparts * 16 * P.rpc; i += 512) wacc[i] = 0.f;
+    if (!P.norm) {
+      // all loads of a batch in flight before any is stored
+      for (uint32_t q0 = 0; q0 < nq; q0 += 512u * 8u) {
+        float4 v[8];
+#pragma unroll
+        for (uint32_t u = 0; u < 8; u++) {
+          const uint32_t q = q0 + tid + 512u * u;
+          if (q < nq) v[u] = x4[q];
+        }
+#pragma unroll
+        for (uint32_t u = 0; u < 8; u++) {
+          const uint32_t q = q0 + tid + 512u * u;
+          if (q < nq) *reinterpret_cast<float4*>(&xsh[xpos<CW>(4 * q)]) = v[u];
+        }
+      }
+    } else {
+      // RMSNorm: x and gamma in one batch (the host sends cols <= 16384 here)
+      const float4* g4 = reinterpret_cast<const float4*>(P.gamma);
+      float4 v[8], g[8];
+      float ss = 0.f;
+#pragma unroll
+      for (uint32_t u = 0; u < 8; u++) {
+        const uint32_t q = tid + 512u * u;
+        if (q < nq) { v[u] = x4[q]; g[u] = g4[q]; }
+      }
+#pragma unroll
+      for (uint32_t u = 0; u < 8; u++)
+        if (tid + 512u * u < nq) ss += v[u].x * v[u].x + v[u].y * v[u].y + v[u].z * v[u].z + v[u].w * v[u].w;
+      ss = warp_sum(ss);
+      if (L == 0) sred[warp] = ss;
+      consumer_sync();
+      for (int w = 0; w < 16; w++) tot += sred[w];
+      if (P.check_layer >= 0) {
+        // end-of-layer check of the reference's debug block (chpe_engine.zig:1753-1764)
+        const int l = P.check_layer;
+        const bool cond = l < 3 || (l >= 8 && l <= 16) || !isfinite(P.x[0]);
+        if (cond && !isfinite(tot)) {
+          if (blockIdx.x == 0 && tid == 0) P.st->stop = 1;
+          if (tid == 0) s_abort = 1;
+        }
+      }
+      const float inv = 1.0f / sqrtf(tot / (float)C + P.eps);
+#pragma unroll
+      for (uint32_t u = 0; u < 8; u++) {
+        const uint32_t q = tid + 512u * u;
+        if (q < nq) {
+          float4 o;
+          o.x = v[u].x * inv * g[u].x;
+          o.y = v[u].y * inv * g[u].y;
+          o.z = v[u].z * inv * g[u].z;
+          o.w = v[u].w * inv * g[u].w;
+          *reinterpret_cast<float4*>(&xsh[xpos<CW>(4 * q)]) = o;
+          if (P.xn_out && blockIdx.x == 0) reinterpret_cast<float4*>(P.xn_out)[q] = o;
+        }
+      }
+    }
+  }
+  __syncthreads();  // with the producer: abort decision is final
+  if (s_abort) {
+    if (tid == 0) tp_signal(P.tp, P.tp.signal_sig);  // every CTA arrives once per launch
+    return;
+  }
+  for (uint32_t cc = tid; cc < C / CW; cc += 512) {
+    float s = 0.f;
+#pragma unroll
+    for (uint32_t q = 0; q < QPC; q++) {
+      const float4 t = xquad<CW>(xsh, cc >> 5, q, cc & 31u);
+      s += (t.x + t.y) + (t.z + t.w);
+    }
+    xsc[cc] = s;
+  }
+  consumer_sync();
+  pdl_launch_dependents();
+
+  // ---- main loop ----------------------------------------------------------
+  const uint32_t NCC = C / CW;  // chunks per row
+  const float invC = 1.0f / (float)C;
+  uint32_t ri = 0;
+  const uint32_t c0 = warp * CPWARP;
+  bool failed = false;
+  for (uint32_t i = 0; i < npieces; i++) {
+    const uint32_t s = i % nst;
+    if (!mbar_wait_or_abort(&full[s], (i / nst) & 1u, &s_bad)) {
+      if (L == 0) { atomicExch(&P.st->err, 1); s_bad = 1; }
+      failed = true;
+      break;
+    }
+    uint32_t k, fa, fb;
+    locate(i, ri, k, fa, fb);
+    const uint32_t nch = (fb - fa) / CW;
+    if (c0 < nch) {
+      const uint8_t* stg = fsm + s * kFlatStageBytes;
+      const uint8_t* pl = stg + 16384;
+      const uint32_t fw = fa + c0 * CW;
+      // row of the warp's first chunk: a float quotient corrected to exact
+      uint32_t rA = (uint32_t)((float)fw * invC);
+      if (rA * C > fw) rA--;
+      else if ((rA + 1) * C <= fw) rA++;
+      const uint32_t ccA = (fw - rA * C) / CW + L;  // chunk-in-row of this lane's j = 0
+      const uint32_t gbase = (KIND == SRC_FLAT ? fa - k * WPP : 0u) + (c0 + L) * CW;  // cell offset, j = 0
+      float sA = 0.f, sB = 0.f;
+      float psc = 1.f, pbi = 0.f;
+      if constexpr (FI::SB) { psc = ld_f32(pl + 32); pbi = ld_f32(pl + 36); }
+      bool crossed = false;
+#pragma unroll
+      for (uint32_t j = 0; j < CPL; j++) {
+        const uint32_t ci = c0 + L + 32u * j;
+        if (ci < nch) {
+          uint32_t cc = ccA + 32u * j;
+          const bool second = cc >= NCC;  // the run wraps into row rA + 1
+          cc = second ? cc - NCC : cc;
+          crossed |= second;
+          const uint4 v = *reinterpret_cast<const uint4*>(stg + 16u * ci);
+          const ulonglong2* xq = reinterpret_cast<const ulonglong2*>(xsh) + ((cc >> 5) * QPC * 32u + (cc & 31u));
+          f2x a0 = 0ull, a1 = 0ull;
+#pragma unroll
+          for (uint32_t q = 0; q < QPC; q++) {
+            const ulonglong2 xv = xq[32u * q];
+            quad_fma<FMT>(v, (int)q, xv.x, xv.y, (q & 1) ? a1 : a0);
+          }
+          const float xsm = xsc[cc];
+          const float d = chunk_finish<FMT>(a0, a1, xsm);
+          float t;
+          if constexpr (FI::GROUPED) t = d * ld_f16(pl + 48 + 2 * ((gbase + 32u * CW * j) >> 7));
+          else if constexpr (FI::SB) t = fmaf(pbi, xsm, d * psc);
+          else t = d;
+          if (second) sB += t; else sA += t;
+        }
+      }
+      // both sums in one butterfly: lanes 0-15 reduce sA, lanes 16-31 sB
+      const bool hi = (L & 16u) != 0;
+      float keep = hi ? sB : sA;
+      keep += __shfl_xor_sync(0xffffffffu, hi ? sA : sB, 16);
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) keep += __shfl_xor_sync(0xffffffffu, keep, o);
+      const bool any2 = __any_sync(0xffffffffu, crossed);
+      if (L == 0 || (L == 16 && any2)) {
+        const FlatRange& r = rg[ri];
+        wacc[(r.part * 16 + warp) * P.rpc + (uint32_t)((int32_t)rA + r.lrbase) + (L >> 4)] += keep;
+      }
+    }
+    __syncwarp();
+    if (L == 0) mbar_arrive(&empty[s]);
+  }
+  (void)failed;
+  consumer_sync();
+  if (s_bad) {
+    if (tid == 0) tp_signal(P.tp, P.tp.signal_sig);
+    return;
+  }
+
+  // ---- epilogue: rows of this CTA -----------------------------------------
+  unsigned long long lbest = 0ull;
+  uint32_t lfin = 1u;
+  const uint32_t nrows = R1 - R0;
+  for (uint32_t lr = tid; lr < nrows; lr += 512) {
+    float d0 = 0.f, d1 = 0.f;
+#pragma unroll
+    for (int w = 0; w < 16; w++) d0 += wacc[w * P.rpc + lr];
+    if constexpr (FMT == FMT_I8RAW) d0 *= 0.00373708f;  // raw int8 dot scale (chpe_engine.zig:1236)
+    if (swig) {
+#pragma unroll
+      for (int w = 0; w < 16; w++) d1 += wacc[(16 + w) * P.rpc + lr];
+      if constexpr (FMT == FMT_I8RAW) d1 *= 0.00373708f;
+      tp_put(P.tp, P.out[0], R0 + lr, silu_ref(d0) * d1);
+      continue;
+    }
+    const uint32_t gr = R0 + lr;
+    uint32_t seg = 0;
+    while ((int)seg + 1 < P.nseg && gr >= P.row_start[seg + 1]) seg++;
+    const uint32_t r = gr - P.row_start[seg];
+    const GemvSrc& s = P.src[seg];
+    float* y = P.out[seg];
+    if (P.epi == EPI_LOGITS) {
+      const uint32_t vr = r + s.row0;  // vocabulary index
+      if (P.tp.world > 1 && P.st->gather) tp_put(P.tp, y, r, d0);
+      else y[r] = d0;
+      if (vr == 0 && P.tp.world > 1)
+        for (int rr = 0; rr < P.tp.world; rr++) tp_at(P.tp.sh, P.tp, rr)->token0 = d0;
+      if (!isfinite(d0)) lfin = 0u;
+      if (d0 > -1e30f) {
+        const unsigned long long kk = argmax_key(d0, vr);
+        lbest = kk > lbest ? kk : lbest;
+      }
+    } else if (P.epi == EPI_ACCUM) {
+      float v = y[r] + d0;
+      if (s.bias) v += s.bias[r];
+      tp_put(P.tp, y, r, v);
+    } else {
+      tp_put(P.tp, y, r, s.bias ? d0 + s.bias[r] : d0);
+    }
+  }
+  if (P.epi == EPI_LOGITS) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long ob = __shfl_xor_sync(0xffffffffu, lbest, o);
+      lbest = ob > lbest ? ob : lbest;
+    }
+    lfin = __all_sync(0xffffffffu, lfin != 0u) ? 1u : 0u;
+    if (L == 0) { kbest[warp] = lbest; kfin[warp] = lfin; }
+    consumer_sync();
+    if (tid == 0) {
+      unsigned long long b = 0ull;
+      uint32_t f = 1u;
+      for (int w = 0; w < 16; w++) { b = kbest[w] > b ? kbest[w] : b; f &= kfin[w]; }
+      const int nr = P.tp.world > 1 ? P.tp.world : 1;
+      for (int rr = 0; rr < nr; rr++) {  // argmax and finiteness on every rank
+        StepState* st = nr > 1 ? tp_at(P.st, P.tp, rr) : P.st;
+        if (b) atomicMax_system(&st->best, b);
+        if (!f) atomicAnd_system(&st->finite, 0u);
+      }
+      tp_signal(P.tp, P.tp.signal_sig);
+      __threadfence();
+      s_is_last = atomicAdd(&P.st->done_ctas, 1u) == gridDim.x - 1;
+    }
+    consumer_sync();
+    if (s_is_last && tid == 0) {
+      float t0;
+      if (P.tp.world > 1) {
+        // every rank's LM-head CTAs have reported to this rank
+        const unsigned long long e = P.tp.sh->epoch;
+        if (!tp_wait_count(P.tp, SIG_LM, (e + 1ull) * P.tp.lm_units)) atomicExch(&P.st->err, 1);
+        t0 = *reinterpret_cast<volatile float*>(&P.tp.sh->token0);
+        P.tp.sh->epoch = (uint32_t)(e + 1ull);
+      } else {
+        t0 = __ldcg(P.out[0]);
+      }
+      finalize_logits(P.st, P.res, t0, tot, P.gen_tokens, P.max_gen);
+    }
+    return;
+  }
+  consumer_sync();
+  if (tid == 0) tp_signal(P.tp, P.tp.signal_sig);
+}
+
+}  // namespace chpe

@@ -54,14 +54,14 @@ constexpr uint32_t kTmaStageOff = 9216;  // x copy 8 KiB, barriers 256 B, partia
 
 // Last-CTA finalisation of a step (chpe_engine.zig:1775-1802): argmax key,
 // finiteness, token-0 logit, hidden norm; advances the step state.
-CHPE_DEV void finalize_logits(StepState* st, StepResult* res, const float* logits, float hidden_ss,
+CHPE_DEV void finalize_logits(StepState* st, StepResult* res, float token0, float hidden_ss,
                               int32_t* gen_tokens, int32_t max_gen) {
   __threadfence();
   unsigned long long b = atomicAdd(&st->best, 0ull);
   StepResult Rr;
   Rr.argmax_token = b ? 0xFFFFFFFFu - (uint32_t)(b & 0xFFFFFFFFull) : 0u;
   Rr.max_logit = b ? key_value(b) : -1e30f;
-  Rr.token0_logit = __ldcg(logits);
+  Rr.token0_logit = token0;
   Rr.hidden_norm = sqrtf(hidden_ss);
   Rr.all_finite = (int32_t)atomicAdd(&st->finite, 0u);
   Rr.pos = st->pos;
@@ -86,7 +86,7 @@ __global__ void __launch_bounds__(512, 1) gemv_tma_kernel(const __grid_constant_
   static_assert(SL >= 1 && CPW % 32 == 0, "row geometry");
 
   extern __shared__ __align__(128) uint8_t tsm[];
-  float* xsh = reinterpret_cast<float*>(tsm);                  // x copy (outlier lookups)
+  float* xsh = reinterpret_cast<float*>(tsm);                  // x, lane-permuted (xpos)
   uint64_t* bars = reinterpret_cast<uint64_t*>(tsm + 8192);   // NST (<= 32) barriers
   float* red = reinterpret_cast<float*>(tsm + 8192 + 256);    // [2 units][2 parts][32] partials
   uint8_t* stages = tsm + kTmaStageOff;
@@ -175,9 +175,9 @@ __global__ void __launch_bounds__(512, 1) gemv_tma_kernel(const __grid_constant_
       o.y = v.y * inv * g.y;
       o.z = v.z * inv * g.z;
       o.w = v.w * inv * g.w;
-      reinterpret_cast<float4*>(xsh)[tid] = o;
+      *reinterpret_cast<float4*>(&xsh[xpos<CW>(4 * tid)]) = o;
     } else {
-      reinterpret_cast<float4*>(xsh)[tid] = v;
+      *reinterpret_cast<float4*>(&xsh[xpos<CW>(4 * tid)]) = v;
     }
   }
   __syncthreads();
@@ -186,13 +186,15 @@ __global__ void __launch_bounds__(512, 1) gemv_tma_kernel(const __grid_constant_
   float xsm[SL];
 #pragma unroll
   for (int j = 0; j < SL; j++) {
-    const uint32_t col0 = (wq * CPW + L + 32u * j) * CW;
+    // x is staged lane-permuted (xpos): quad q of chunk c = L + 32*jj sits at
+    // ((jj*QPC + q)*32 + L)*4, so these 128-bit loads are conflict free
+    const uint32_t jj = (wq * CPW) / 32 + j;
     float s = 0.f;
 #pragma unroll
-    for (int e = 0; e < CW; e += 4) {
-      const float4 t = *reinterpret_cast<const float4*>(&xsh[col0 + e]);
-      xp[j][e / 2] = pack2(t.x, t.y);
-      xp[j][e / 2 + 1] = pack2(t.z, t.w);
+    for (int q = 0; q < QPC; q++) {
+      const float4 t = xquad<CW>(xsh, jj, q, L);
+      xp[j][2 * q] = pack2(t.x, t.y);
+      xp[j][2 * q + 1] = pack2(t.z, t.w);
       s += (t.x + t.y) + (t.z + t.w);
     }
     xsm[j] = s;
@@ -244,8 +246,9 @@ __global__ void __launch_bounds__(512, 1) gemv_tma_kernel(const __grid_constant_
           const uint32_t col = ld_u16(pl + 816 + 2 * L);
           if (col < s.x_len) {
             const float w = ld_f16(pl + 560 + 2 * (rw * 8 + L));
+            const float xcol = xsh[xpos<CW>(col)];
             if (s.outliers == OUTL_ADD) {
-              acc = fmaf(w, xsh[col], acc);
+              acc = fmaf(w, xcol, acc);
             } else {
               bool later = false;
               for (uint32_t k2 = L + 1; k2 < 8; k2++) later |= ld_u16(pl + 816 + 2 * k2) == col;
@@ -260,7 +263,7 @@ __global__ void __launch_bounds__(512, 1) gemv_tma_kernel(const __grid_constant_
                   const uint8_t b = rowp[col / 4];
                   dec = CB[(b >> (2 * (col & 3))) & 3] * sc;
                 }
-                acc = fmaf(w - dec, xsh[col], acc);
+                acc = fmaf(w - dec, xcol, acc);
               }
             }
           }
@@ -321,7 +324,7 @@ __global__ void __launch_bounds__(512, 1) gemv_tma_kernel(const __grid_constant_
       is_last = atomicAdd(&P.st->done_ctas, 1u) == gridDim.x - 1;
     }
     __syncthreads();
-    if (is_last && tid == 0) finalize_logits(P.st, P.res, P.out[0], tot, P.gen_tokens, P.max_gen);
+    if (is_last && tid == 0) finalize_logits(P.st, P.res, __ldcg(P.out[0]), tot, P.gen_tokens, P.max_gen);
   }
 }
 

@@ -78,6 +78,24 @@ void *chpe_init_ex(const char *archive_path, int arch, uint32_t max_seq_len, int
 void *chpe_init_bytes(const void *bytes, uint64_t len, int arch, uint32_t max_seq_len,
                       int device);
 
+/* Tensor parallelism over the GPUs of one node, one process per GPU (an
+ * extension: the reference engine is single-threaded CPU code).  Every rank
+ * opens the same archive (path: a shared read-only mmap, or bytes) with its
+ * rank and the world size (1..8), exports the 64-byte CUDA IPC handle of its
+ * exchange region, receives every rank's handles in rank order (any host
+ * transport: the Python layer uses torch.distributed), and connects; after
+ * that every rank calls the same forward / generate / bench functions in
+ * lockstep.  Heads, hidden, FFN rows and vocabulary must divide by world; all
+ * projections must be flat cells or raw streams (the 9B and 72B archives).
+ * Results equal the single-GPU engine's: each output element is computed
+ * whole on one rank.  Returns NULL / -1 on failure (chpe_last_error). */
+void *chpe_init_tp(const char *archive_path, int arch, uint32_t max_seq_len, int device, int rank,
+                   int world);
+void *chpe_init_tp_bytes(const void *bytes, uint64_t len, int arch, uint32_t max_seq_len, int device,
+                         int rank, int world);
+int chpe_tp_export_handle(void *ctx, uint8_t *handle64);
+int chpe_tp_connect(void *ctx, const uint8_t *handles, int world);
+
 /* WeightArchive.validate (weight_archive.zig:152-172): 0 when valid, else the
  * error: 1 InvalidMagic, 2 UnsupportedVersion, 3 BadGeometry, 4 Truncated,
  * 6 FileTooSmall, 10 MisalignedHeader. */
@@ -109,6 +127,11 @@ int chpe_bench_host(void *ctx, const uint32_t *tokens, size_t n_steps, float *lo
  * scales of the rows used) and the launch count.  Needs a prior forward. */
 int chpe_bench_kernel(void *ctx, int role, int rounds, float *avg_ms, double *bytes_per_launch,
                       int *launches);
+
+/* Name of the kernel that runs the first op of a role (same role numbers as
+ * chpe_bench_kernel), e.g. "gemv_flat_tma_kernel<W4G,FLAT>"; "" when the
+ * role has no op or ctx is NULL.  The string lives as long as ctx. */
+const char *chpe_role_kernel_name(void *ctx, int role);
 
 /* all_finite of the last ForwardResult (1/0; 0 for NULL). */
 int chpe_get_last_all_finite(void *ctx);

@@ -108,6 +108,29 @@ def test_gemv_partial_spans_and_past_end():
         assert_close_vec(got, ref, 1e-4, f"{ts},{nt},{r},{c},{acc}")
 
 
+# (rows, cols) read from the 3B down-projection tiles (688 flat cells, or 2752
+# raw FP16 tiles): the widths of the 9B/72B tensors (4096, 8192, 12288,
+# 29568), widths just past one consumer warp's run, a handful of rows, a width
+# that is not a multiple of the chunk width, and a span longer than the tiles
+# given (not covered in full).
+FLAT_SHAPES = [(2048, 8192), (700, 29568), (4000, 4096), (1500, 12288), (9000, 2112), (5, 8192),
+               (3, 29568), (1, 4096), (700, 30000), (770, 29568)]
+
+
+@pytest.mark.parametrize("cfg", [chpe.SYNTH_3B_W4, chpe.SYNTH_3B_W2, chpe.SYNTH_3B_FP16_RAW])
+def test_gemv_flat_widths(cfg):
+    a, e, o = engines(cfg, 0)
+    li = o.layer_info(4)
+    rng = np.random.default_rng(17)
+    for r, c in FLAT_SHAPES:
+        for acc in (False, True):
+            x = rng.standard_normal(c).astype(np.float32)
+            y0 = rng.standard_normal(r).astype(np.float32)
+            ref = o.gemv_linear(li["down_proj"], li["down_tiles"], x, r, c, accumulate=acc, y=y0.copy())
+            got = e.probe_gemv_linear(li["down_proj"], li["down_tiles"], x, r, c, accumulate=acc, y=y0.copy())
+            assert_close_vec(got, ref, 1e-4, f"{r}x{c} acc={acc}")
+
+
 @pytest.mark.parametrize("arch", [chpe.ARCH_3B, chpe.ARCH_9B, chpe.ARCH_72B])
 def test_attention_against_oracle(arch):
     """RoPE + KV append + GQA softmax (chpe_engine.zig:1688-1734) over a
