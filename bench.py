@@ -43,8 +43,10 @@ MODELS = {
     "3b-w4": dict(synth="SYNTH_3B_W4", arch="ARCH_3B", prompt=512, name="qwen2.5-3b-w4-dense-cell"),
     "3b-w2": dict(synth="SYNTH_3B_W2", arch="ARCH_3B", prompt=512, name="qwen2.5-3b-w2-dense-cell"),
     "3b-fp16": dict(synth="SYNTH_3B_FP16_RAW", arch="ARCH_3B", prompt=32, name="qwen2.5-3b-fp16-raw"),
-    "9b-w4": dict(synth="SYNTH_9B_W4", arch="ARCH_9B", prompt=1024, name="qwen3.5-9b-w4-flat-cell"),
-    "72b-w4": dict(synth="SYNTH_72B_W4", arch="ARCH_72B", prompt=2048, name="qwen2.5-72b-w4-flat-cell"),
+    "9b-w4": dict(synth="SYNTH_9B_W4", arch="ARCH_9B", prompt=1024, name="qwen3.5-9b-w4-flat-cell",
+                  tp=True),
+    "72b-w4": dict(synth="SYNTH_72B_W4", arch="ARCH_72B", prompt=2048, name="qwen2.5-72b-w4-flat-cell",
+                   tp=True),
 }
 
 
@@ -134,6 +136,15 @@ def max_over_ranks(dist, v: float) -> float:
     return float(t.item())
 
 
+def sum_over_ranks(dist, v: float) -> float:
+    if dist is None:
+        return v
+    import torch
+    t = torch.tensor([v], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
 def barrier(dist):
     if dist is not None:
         dist.barrier()
@@ -194,14 +205,37 @@ def run_reference(args, rank, world, dist):
     print(json.dumps(line), flush=True)
 
 
+def shared_archive_path(chpe, cfg: int, rank: int, dist) -> str:
+    """Rank 0 writes the seeded archive once to a local file that every rank
+    maps read-only (one copy in the page cache, not one per rank)."""
+    import shutil
+    import tempfile
+    need = chpe.synth_lib().chpe_synth_bytes(cfg, 0) + (1 << 30)
+    dirs = [d for d in ("/dev/shm", tempfile.gettempdir(), ROOT) if os.path.isdir(d)]
+    dirs = [d for d in dirs if shutil.disk_usage(d).free > need] or [ROOT]
+    path = os.path.join(dirs[0], f"chpe_bench_{cfg}.chpe")
+    if rank == 0 and not (os.path.exists(path) and os.path.getsize(path) == need - (1 << 30)):
+        chpe.synth_write(path, cfg, 0, seed=0)
+    barrier(dist)
+    return path
+
+
 def run_ours(args, rank, world, local, dist):
     import chpe_qwen_engine_b200 as chpe
     M = MODELS[args.model]
     dev = local if world > 1 else 0
-    archive = chpe.synth_archive(getattr(chpe, M["synth"]), 0, seed=0)
+    cfg = getattr(chpe, M["synth"])
     arch = getattr(chpe, M["arch"])
-    eng = chpe.Engine.from_bytes(archive, arch, max_seq_len=args.prompt + args.warmup + 2 * args.steps + 64,
-                                 device=dev)
+    max_seq = args.prompt + args.warmup + 2 * args.steps + 64
+    tp = world > 1 and M.get("tp", False)
+    if tp:
+        # tensor parallel: rank r of `world` GPUs over one shared archive file
+        path = shared_archive_path(chpe, cfg, rank, dist)
+        archive = None
+        eng = chpe.Engine.tensor_parallel(path, arch, rank, world, max_seq_len=max_seq, device=dev)
+    else:
+        archive = chpe.synth_archive(cfg, 0, seed=0)
+        eng = chpe.Engine.from_bytes(archive, arch, max_seq_len=max_seq, device=dev)
     rng = np.random.default_rng(1)
     prompt = rng.integers(0, 151936, args.prompt).astype(np.uint32)
     eng.forward_tokens(prompt)  # positions 0..prompt-1, untimed
@@ -211,7 +245,8 @@ def run_ours(args, rank, world, local, dist):
         ms = eng.bench_greedy(args.steps)
     barrier(dist)
     ms_max = max_over_ranks(dist, ms)
-    value = world * args.steps / (ms_max / 1000.0)
+    # replicas decode `world` independent streams; tensor parallel decodes one
+    value = (1 if tp else world) * args.steps / (ms_max / 1000.0)
 
     # e2e through the C ABI with host buffers
     host_toks = rng.integers(0, 151936, args.steps).astype(np.uint32)
@@ -219,29 +254,46 @@ def run_ours(args, rank, world, local, dist):
     barrier(dist)
     wall_ms, _ = eng.bench_host(host_toks)
     wall_ms = max_over_ranks(dist, wall_ms)
-    e2e = world * args.steps / (wall_ms / 1000.0)
+    e2e = (1 if tp else world) * args.steps / (wall_ms / 1000.0)
 
-    # roofline of the dominant kernel (fused RMSNorm + gate/up + SwiGLU GEMV)
-    kms, kbytes, klaunch = eng.bench_kernel(chpe.ROLE_GATEUP, rounds=3)
     hbm, peak_kind = peaks()
-    achieved = kbytes / (kms / 1000.0) / 1e9
     traffic = None
-    tp = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(tp):
-        traffic = json.load(open(tp)).get("gateup_w4_3b_bytes_per_launch")
-    # whole-step algorithmic bytes (all roles)
-    step_bytes = 0.0
+    tf = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tf):
+        traffic = json.load(open(tf)).get(f"gateup_{args.model}_bytes_per_launch")
     per_role = {}
-    for role, name in ((chpe.ROLE_QKV, "qkv"), (chpe.ROLE_ATTN, "attention"), (chpe.ROLE_O, "o"),
-                       (chpe.ROLE_GATEUP, "gateup"), (chpe.ROLE_DOWN, "down"),
-                       (chpe.ROLE_LMHEAD, "lmhead")):
-        m, b, n = eng.bench_kernel(role, rounds=2)
-        launches_per_step = n // 2
-        step_bytes += b * launches_per_step
-        per_role[name] = {"avg_us": round(m * 1000, 2), "launches_per_step": launches_per_step,
-                          "bytes_per_launch": b,
-                          "gbs": round(b / (m / 1000) / 1e9, 1) if b else None}
+    step_bytes = 0.0
+    if not tp:
+        # roofline of the dominant kernel (fused RMSNorm + gate/up + SwiGLU GEMV)
+        kms, kbytes, klaunch = eng.bench_kernel(chpe.ROLE_GATEUP, rounds=3)
+        achieved = kbytes / (kms / 1000.0) / 1e9
+        # whole-step algorithmic bytes (all roles)
+        for role, name in ((chpe.ROLE_QKV, "qkv"), (chpe.ROLE_ATTN, "attention"), (chpe.ROLE_O, "o"),
+                           (chpe.ROLE_GATEUP, "gateup"), (chpe.ROLE_DOWN, "down"),
+                           (chpe.ROLE_LMHEAD, "lmhead")):
+            m, b, n = eng.bench_kernel(role, rounds=2)
+            launches_per_step = n // 2
+            step_bytes += b * launches_per_step
+            per_role[name] = {"avg_us": round(m * 1000, 2), "launches_per_step": launches_per_step,
+                              "bytes_per_launch": b,
+                              "gbs": round(b / (m / 1000) / 1e9, 1) if b else None}
+        roof = {"kernel": eng.op_kernel_name(chpe.ROLE_GATEUP) + " fused RMSNorm+gate/up+SwiGLU",
+                "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                "peak_kind": peak_kind, "traffic": traffic, "bytes_per_launch": kbytes,
+                "avg_launch_us": kms * 1000}
+    else:
+        # one role cannot run alone across ranks (its exchanges wait on the
+        # others): the roofline here is the whole step's weight stream per GPU
+        mine = eng.step_weight_bytes()
+        step_bytes = sum_over_ranks(dist, mine)
+        per_gpu = max_over_ranks(dist, mine) / (ms_max / args.steps / 1000.0) / 1e9
+        roof = {"kernel": "whole decode step per GPU (all kernels, exchanges included)", "bound": "hbm",
+                "achieved": per_gpu, "peak": hbm, "unit": "GB/s", "frac": per_gpu / hbm,
+                "peak_kind": peak_kind, "traffic": None, "bytes_per_launch": step_bytes / world,
+                "avg_launch_us": ms_max / args.steps * 1000}
     cpu = None
+    if rank == 0 and archive is None:
+        archive = np.memmap(path, dtype=np.uint8, mode="r")
     if rank == 0:
         # ~10-30 s of single-thread CPU work: 3 steps of 3B, 1 of the larger models
         big = archive.size > 4e9
@@ -257,11 +309,11 @@ def run_ours(args, rank, world, local, dist):
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "u4->f32",
+        "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "u4->f32",
         "data": "synthetic (seeded archive, random-init weights)",
         "config": {"workload": M["name"], "prompt": args.prompt,
                    "positions": f"{args.prompt + args.warmup}..{args.prompt + args.warmup + args.steps - 1}",
-                   "parallelism": f"replicas x{world}",
+                   "parallelism": f"tp{world}" if tp else f"replicas x{world}",
                    "l2": f"inputs larger than L2 ({step_bytes / 1e9:.2f} GB of weights per step)",
                    "algorithmic_bytes_per_token": step_bytes,
                    "weight_stream_gbs": step_bytes / (ms_step / 1000) / 1e9,
@@ -269,11 +321,7 @@ def run_ours(args, rank, world, local, dist):
                    "per_role": per_role},
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": eng.vocab * 4 + 24},
-        "roofline": {"kernel": eng.op_kernel_name(chpe.ROLE_GATEUP) + " fused RMSNorm+gate/up+SwiGLU",
-                     "bound": "hbm",
-                     "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                     "peak_kind": peak_kind, "traffic": traffic,
-                     "bytes_per_launch": kbytes, "avg_launch_us": kms * 1000},
+        "roofline": roof,
         "cpu_baseline": cpu,
         "clocks": cs.summary(),
         "gpu_launches": eng.kernels_per_step() * args.steps,
@@ -291,14 +339,29 @@ def main():
     ap.add_argument("--prompt", type=int, default=None,
                     help="prompt tokens decoded before timing (default: the model's config)")
     ap.add_argument("--kernel-only", default=None,
-                    choices=["qkv", "attention", "o", "gateup", "down", "lmhead"],
+                    choices=["qkv", "attention", "o", "gateup", "down", "lmhead", "flat-aligned", "flat-stream"],
                     help="profiling case: build the engine (max_seq_len 64) and only launch this "
-                         "op of every layer, --steps rounds after one warm-up round")
+                         "op of every layer, --steps rounds after one warm-up round; flat-aligned / "
+                         "flat-stream: one flat GEMV over 2064 contiguous 4-bit cells of the 3B "
+                         "archive (35 MB) read as 8192 columns (aligned cells) or 29568 columns "
+                         "(72B down width), --steps launches")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.prompt is None:
         args.prompt = MODELS[args.model]["prompt"]
+    if args.kernel_only in ("flat-aligned", "flat-stream"):
+        import chpe_qwen_engine_b200 as chpe
+        eng = chpe.Engine.from_bytes(chpe.synth_archive(chpe.SYNTH_3B_W4, 0, seed=0), chpe.ARCH_3B, 64)
+        tile0, ntiles = 9497, 2064  # layer 0 down, gate, up: contiguous 4-bit cells
+        cols = 8192 if args.kernel_only == "flat-aligned" else 29568
+        rows = ntiles * 32768 // cols
+        x = np.random.default_rng(3).standard_normal(cols).astype(np.float32)
+        for _ in range(max(1, args.steps)):
+            y = eng.probe_gemv_linear(tile0, ntiles, x, rows, cols)
+        print(json.dumps({"kernel": args.kernel_only, "rows": rows, "cols": cols,
+                          "kernel_name": "gemv_flat_tma_kernel", "y0": float(y[0])}))
+        return
     if args.kernel_only:
         import chpe_qwen_engine_b200 as chpe
         roles = {"qkv": chpe.ROLE_QKV, "attention": chpe.ROLE_ATTN, "o": chpe.ROLE_O,

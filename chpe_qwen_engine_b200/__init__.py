@@ -57,6 +57,8 @@ SYMBOLS = [
     ("chpe_init_tp_bytes", _P, [_P, C.c_uint64, _I, C.c_uint32, _I, _I, _I]),
     ("chpe_tp_export_handle", _I, [_P, C.c_char_p]),
     ("chpe_tp_connect", _I, [_P, C.c_char_p, _I]),
+    ("chpe_tp_slice", _I, [_I, _I, _I, _U32P]),
+    ("chpe_step_weight_bytes", C.c_double, [_P]),
     ("chpe_get_last_all_finite", _I, [_P]),
     ("chpe_kernels_per_step", _I, [_P]),
     ("chpe_get_position", _U32, [_P]),
@@ -151,6 +153,15 @@ def _u32p(a: np.ndarray):
 
 class ChpeError(RuntimeError):
     pass
+
+
+def tp_slice(arch: int, rank: int, world: int) -> dict:
+    """Rows one tensor-parallel rank owns (chpe_tp_slice); no GPU needed."""
+    out = np.zeros(10, np.uint32)
+    if lib().chpe_tp_slice(arch, rank, world, _u32p(out)) != 0:
+        raise ValueError(f"architecture {arch} does not split over {world} ranks")
+    keys = ("hq", "h0", "kv0", "kvl", "dl", "d0", "fl", "f0", "vl", "v0")
+    return {k: int(v) for k, v in zip(keys, out)}
 
 
 class Engine:
@@ -282,6 +293,10 @@ class Engine:
     def op_kernel_name(self, role: int) -> str:
         """Kernel that runs the first op of `role`."""
         return (lib().chpe_role_kernel_name(self.ctx, role) or b"").decode()
+
+    def step_weight_bytes(self) -> float:
+        """Algorithmic weight bytes one step streams on this rank."""
+        return lib().chpe_step_weight_bytes(self.ctx)
 
     def kernels_per_step(self) -> int:
         return lib().chpe_kernels_per_step(self.ctx)

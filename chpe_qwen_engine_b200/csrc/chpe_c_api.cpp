@@ -156,6 +156,14 @@ int chpe_tp_export_handle(void* ctx, uint8_t* handle64) {
   return 0;
 }
 
+int chpe_tp_slice(int arch, int rank, int world, uint32_t out[10]) {
+  ChpeTpSlice sl;
+  if (!out || chpe_tp_slice_of(arch, rank, world, &sl) != 0) return -1;
+  const uint32_t v[10] = {sl.hq, sl.h0, sl.kv0, sl.kvl, sl.dl, sl.d0, sl.fl, sl.f0, sl.vl, sl.v0};
+  memcpy(out, v, sizeof(v));
+  return 0;
+}
+
 int chpe_tp_connect(void* ctx, const uint8_t* handles, int world) {
   if (!ctx || !handles) return -1;
   Ctx* c = (Ctx*)ctx;
@@ -255,6 +263,11 @@ int chpe_bench_kernel(void* ctx, int role, int rounds, float* avg_ms, double* by
     return -1;
   }
   return 0;
+}
+
+double chpe_step_weight_bytes(void* ctx) {
+  if (!ctx) return 0.0;
+  return ((Ctx*)ctx)->engine->step_weight_bytes();
 }
 
 const char* chpe_role_kernel_name(void* ctx, int role) {

@@ -100,3 +100,30 @@ int64_t chpe_total_records(int arch, int is_raw) {
   if (arch == CHPE_ARCH_72B) return 2219153;
   return 546681;
 }
+
+int chpe_tp_slice_of(int arch, int rank, int world, ChpeTpSlice *out) {
+  const ChpeArch *A = chpe_arch_preset(arch);
+  if (!A || !out || world < 1 || rank < 0 || rank >= world) return -1;
+  const uint32_t N = (uint32_t)world, R = (uint32_t)rank;
+  if (A->H % N || A->D % N || A->F % N || A->V % N) return -1;
+  const uint32_t G = A->H / A->KV, hq = A->H / N;
+  ChpeTpSlice s;
+  s.hq = hq;
+  s.h0 = R * hq;
+  s.kv0 = s.h0 / G;
+  if (hq >= G) {
+    if (hq % G) return -1;
+    s.kvl = hq / G;
+  } else {
+    if (G % hq) return -1;
+    s.kvl = 1;
+  }
+  s.dl = A->D / N;
+  s.d0 = R * s.dl;
+  s.fl = A->F / N;
+  s.f0 = R * s.fl;
+  s.vl = A->V / N;
+  s.v0 = R * s.vl;
+  *out = s;
+  return 0;
+}

@@ -60,7 +60,16 @@ typedef struct {
       linear_norm, out_proj, q_norm, k_norm;
 } Chpe9bExtra;
 
+/* One tensor-parallel rank's slices (rows of every projection): query heads
+ * [h0, h0+hq), kv heads [kv0, kv0+kvl), hidden rows [d0, d0+dl) of O and
+ * down, FFN rows [f0, f0+fl) of gate/up, vocabulary rows [v0, v0+vl). */
+typedef struct {
+  uint32_t hq, h0, kv0, kvl, dl, d0, fl, f0, vl, v0;
+} ChpeTpSlice;
+
 const ChpeArch *chpe_arch_preset(int arch);
+/* 0, or -1 when the architecture does not split over `world` ranks. */
+int chpe_tp_slice_of(int arch, int rank, int world, ChpeTpSlice *out);
 void chpe_layer_info(int arch, int is_raw, size_t l, ChpeLayerInfo *out);
 void chpe_9b_extra(size_t l, Chpe9bExtra *out);
 int64_t chpe_final_norm_index(int arch, int is_raw);

@@ -102,13 +102,14 @@ CHPE_DEV unsigned long long ld_acquire_sys(const unsigned long long* p) {
   asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
-CHPE_DEV void red_add_release_sys(unsigned long long* p, unsigned long long v) {
-  asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+CHPE_DEV void red_add_relaxed_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("red.relaxed.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 // Bounded wait until this rank's counter `kind` reaches `target`.
 CHPE_DEV bool tp_wait_count(const chpe::TpLink& t, int kind, unsigned long long target) {
   for (uint32_t i = 0; i < kMaxWaitPolls; i++) {
     if (ld_acquire_sys(&t.sh->sig[kind]) >= target) return true;
+    if ((i & 1023u) == 0u && t.err && *reinterpret_cast<volatile const int32_t*>(t.err)) return false;
     __nanosleep(64);
   }
   return false;
@@ -120,11 +121,14 @@ CHPE_DEV bool tp_wait(const chpe::TpLink& t) {
   return tp_wait_count(t, t.wait_sig, (e * t.wait_per_step + t.wait_index) * t.wait_units);
 }
 // One arrival on every rank; call after this CTA's output stores (and a
-// barrier over the threads that made them).
+// barrier over the threads that made them).  One system-scope fence, then
+// relaxed additions: the fence orders every earlier store of the CTA (made
+// visible to this thread by the barrier) before each addition (release
+// pattern), without a fence per rank.
 CHPE_DEV void tp_signal(const chpe::TpLink& t, int kind) {
   if (t.world <= 1 || kind < 0) return;
   asm volatile("fence.acq_rel.sys;" ::: "memory");
-  for (int r = 0; r < t.world; r++) red_add_release_sys(&tp_at(t.sh, t, r)->sig[kind], 1ull);
+  for (int r = 0; r < t.world; r++) red_add_relaxed_sys(&tp_at(t.sh, t, r)->sig[kind], 1ull);
 }
 // Store v at y[i] on this rank, or on every rank when the output is exchanged.
 CHPE_DEV void tp_put(const chpe::TpLink& t, float* y, uint32_t i, float v) {

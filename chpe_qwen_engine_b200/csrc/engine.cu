@@ -496,7 +496,11 @@ static uint64_t weight_bytes(const GemvSrc& s) {
 static double alg_bytes_of(const GemvSrc& s) {
   double w = (double)s.r_total * s.c_total;
   if (s.kind == SRC_ROWTILE) w = (double)s.rows_covered * s.c_total;
-  if ((s.kind == SRC_FLAT || s.kind == SRC_RAW) && w > (double)s.flat_limit) w = (double)s.flat_limit;
+  if (s.kind == SRC_FLAT || s.kind == SRC_RAW) {  // weights of rows row0.. that the tiles hold
+    const double first = (double)s.row0 * s.c_total;
+    const double avail = (double)s.flat_limit > first ? (double)s.flat_limit - first : 0.0;
+    if (w > avail) w = avail;
+  }
   switch (s.fmt) {
     case FMT_W4G: return w * 0.5 + w / 128.0 * 2.0;
     case FMT_W2G: return w * 0.25 + w / 128.0 * 2.0;
@@ -615,9 +619,9 @@ void Engine::add_linear_ops(std::vector<Op>& ops, const GemvSrc* src, float* con
     else return false;
     const uint32_t cw = (uint32_t)fmt_cw(f);
     const uint64_t w = (uint64_t)(g.row0 + g.r_total) * g.c_total;
-    // a consumer warp's run of a piece (wpp/cw/16 chunks) spans at most two rows
+    // a consumer warp's run of a piece (wpp/cw/8 chunks) spans at most two rows
     if (gamma && ncols > 16384) return false;  // the fused RMSNorm loads x in one batch
-    return g.c_total == ncols && ncols % cw == 0 && (wpp / cw / 16) * cw <= ncols && w <= g.flat_limit &&
+    return g.c_total == ncols && ncols % cw == 0 && (wpp / cw / kFlatConsumerWarps) * cw <= ncols &&
            w < (1ull << 32) && g.r_total > 0;
   };
   bool tma = fused && !getenv("CHPE_NO_TMA");
@@ -643,11 +647,26 @@ void Engine::add_linear_ops(std::vector<Op>& ops, const GemvSrc* src, float* con
     t.row_start[nseg] = rows;
     if (epi == EPI_SWIGLU) t.row_start[1] = src[0].r_total;
     const uint32_t Rt = epi == EPI_SWIGLU ? src[0].r_total : rows;
-    const uint32_t G = Rt < (uint32_t)num_sms_ ? Rt : (uint32_t)num_sms_;
+    // Aligned cells (rows start at cell boundaries): 4/2-bit flat cells whose
+    // width divides 32768 into 32..256 column chunks, every segment a whole
+    // number of cells.
+    uint32_t rc = 0;
+    {
+      const uint32_t cw = (uint32_t)fmt_cw(op.fmt);
+      bool al = op.kind == SRC_FLAT && 32768u % ncols == 0 && (ncols / cw) % 32u == 0 &&
+                ncols / cw <= kFlatConsumers && kFlatConsumers % (ncols / cw) == 0 && !getenv("CHPE_NO_ALIGNED");
+      const uint32_t cell_rows = 32768u / ncols;
+      for (int i = 0; i < nseg && al; i++)
+        al = src[i].r_total % cell_rows == 0 && src[i].row0 % cell_rows == 0;
+      if (al) rc = cell_rows;
+    }
+    const uint32_t RU = rc ? rc : 1u, Ut = Rt / RU;
+    const uint32_t G = Ut < (uint32_t)num_sms_ ? Ut : (uint32_t)num_sms_;
+    t.rc = rc;
     t.nseg = nseg;
     t.epi = epi;
     t.ncols = ncols;
-    t.rpc = (Rt + G - 1) / G;
+    t.rpc = RU * ((Ut + G - 1) / G);
     t.x = x;
     t.gamma = gamma;
     t.norm = gamma != nullptr;
@@ -914,28 +933,23 @@ void Engine::build_step_tp() {
   const uint32_t N = (uint32_t)tp_world_, R = (uint32_t)tp_rank_;
   if (!f_.archive_valid || f_.record_count == 0)
     throw std::runtime_error("tensor parallel: needs a valid archive");
-  if (A.H % N || A.D % N || A.F % N || A.V % N)
-    throw std::runtime_error("tensor parallel: heads, hidden, FFN and vocabulary must divide by the rank count");
-  const uint32_t G = A.H / A.KV, hq = A.H / N, h0 = R * hq;
-  uint32_t kv0 = h0 / G, kvl;
-  if (hq >= G) {
-    if (hq % G) throw std::runtime_error("tensor parallel: query heads per rank must cover whole kv groups");
-    kvl = hq / G;
-  } else {
-    if (G % hq) throw std::runtime_error("tensor parallel: query heads per rank must divide a kv group");
-    kvl = 1;
-  }
-  const uint32_t dl = A.D / N, d0 = R * dl, fl = A.F / N, f0 = R * fl, vl = A.V / N, v0 = R * vl;
+  ChpeTpSlice sl;
+  if (chpe_tp_slice_of(arch_id_, (int)R, (int)N, &sl) != 0)
+    throw std::runtime_error("tensor parallel: heads, hidden, FFN and vocabulary must split evenly over the ranks");
+  const uint32_t hq = sl.hq, h0 = sl.h0, kv0 = sl.kv0, kvl = sl.kvl;
+  const uint32_t dl = sl.dl, d0 = sl.d0, fl = sl.fl, f0 = sl.f0, vl = sl.vl, v0 = sl.v0;
   const uint32_t qd = A.H * A.HD, kvd = A.KV * A.HD;
-  auto grid_of = [&](uint32_t rows) { return rows < (uint32_t)num_sms_ ? rows : (uint32_t)num_sms_; };
+  // arrivals per (step, layer) of each exchange: every rank launches the same
+  // grids, so N x this rank's grid of the producing op
   const unsigned long long u_att = (unsigned long long)N * nsplit_ * kvl;
-  const unsigned long long u_d = (unsigned long long)N * grid_of(dl);  // O and down
-  const unsigned long long u_gu = (unsigned long long)N * grid_of(fl);
+  unsigned long long u_o = 0, u_gu = 0, u_dn = 0;
+  auto units_of_last = [&]() { return (unsigned long long)N * ops.back().grid.x; };
   TpLink base{};
   base.world = (int32_t)N;
   base.rank = (int32_t)R;
   for (int r = 0; r < kTpMax; r++) base.delta[r] = tp_delta_[r];
   base.sh = d_tpsh_;
+  base.err = &d_st_->err;
   base.wait_sig = -1;
   base.signal_sig = -1;
   base.wait_per_step = A.L;
@@ -972,7 +986,7 @@ void Engine::build_step_tp() {
         narrow(plan_linear(li.k_proj, li.k_tiles, kvd, A.D, A.D, 0, li.k_bias), kv0 * A.HD, kvl * A.HD),
         narrow(plan_linear(li.v_proj, li.v_tiles, kvd, A.D, A.D, 0, li.v_bias), kv0 * A.HD, kvl * A.HD)};
     float* qkv_out[3] = {d_q_, d_k_, d_v_};
-    TpLink t_qkv = link(l ? SIG_DOWN : -1, l, u_d, -1, 0);
+    TpLink t_qkv = link(l ? SIG_DOWN : -1, l, u_dn, -1, 0);
     add_linear_ops(ops, qkv, qkv_out, 3, EPI_STORE, d_hidden_, g_in, (int)l - 1, A.D, false, &t_qkv);
     {
       Op op;
@@ -1006,23 +1020,26 @@ void Engine::build_step_tp() {
     float* o_out[1] = {d_hidden_ + d0};
     TpLink t_o = link(SIG_ATT, l + 1, u_att, SIG_O, 1);
     add_linear_ops(ops, &o, o_out, 1, EPI_ACCUM, d_attn_, nullptr, -1, A.D, false, &t_o);
+    u_o = units_of_last();
     GemvSrc gu[2] = {narrow(plan_linear(li.gate_proj, li.gate_tiles, A.F, A.D, A.D, 0, -1), f0, fl),
                      narrow(plan_linear(li.up_proj, li.up_tiles, A.F, A.D, A.D, 0, -1), f0, fl)};
     float* gu_out[2] = {d_mlp_ + f0, nullptr};
-    TpLink t_gu = link(SIG_O, l + 1, u_d, SIG_GU, 1);
+    TpLink t_gu = link(SIG_O, l + 1, u_o, SIG_GU, 1);
     add_linear_ops(ops, gu, gu_out, 2, EPI_SWIGLU, d_hidden_, g_post, -1, A.D, false, &t_gu);
+    u_gu = units_of_last();
     GemvSrc dn = narrow(plan_linear(li.down_proj, li.down_tiles, A.D, A.F, A.F, 1, -1), d0, dl);
     float* dn_out[1] = {d_hidden_ + d0};
     TpLink t_dn = link(SIG_GU, l + 1, u_gu, SIG_DOWN, 1);
     add_linear_ops(ops, &dn, dn_out, 1, EPI_ACCUM, d_mlp_, nullptr, -1, A.F, false, &t_dn);
+    u_dn = units_of_last();
   }
   unpack_norm((uint64_t)chpe_final_norm_index(arch_id_, f_.is_raw), gam.data());
   const float* g_fin = upload_floats(gam);
   GemvSrc lm = narrow(plan_lm_head(), v0, vl);
   float* lm_out[1] = {d_logits_ + v0};
-  TpLink t_lm = link(SIG_DOWN, A.L, u_d, SIG_LM, 1);
-  t_lm.lm_units = (unsigned long long)N * grid_of(vl);
+  TpLink t_lm = link(SIG_DOWN, A.L, u_dn, SIG_LM, 1);
   add_linear_ops(ops, &lm, lm_out, 1, EPI_LOGITS, d_hidden_, g_fin, -1, A.D, true, &t_lm);
+  ops.back().fl.tp.lm_units = units_of_last();
 }
 
 // ---- the decode step: forwardDecode (chpe_engine.zig:1663-1803) ------------
@@ -1183,9 +1200,9 @@ static void launch_tma(const Op& op, cudaStream_t s) {
   throw std::runtime_error("no TMA kernel for this format");
 }
 
-template <int FMT, int KIND>
+template <int FMT, int KIND, bool ALIGNED = false>
 static void launch_flat_t(const Op& op, cudaStream_t s) {
-  auto k = gemv_flat_tma_kernel<FMT, KIND>;
+  auto k = gemv_flat_tma_kernel<FMT, KIND, ALIGNED>;
   static bool configured = false;
   if (!configured) {
     CK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFlatSmemLimit));
@@ -1195,7 +1212,14 @@ static void launch_flat_t(const Op& op, cudaStream_t s) {
 }
 
 static void launch_flat(const Op& op, cudaStream_t s) {
-  if (op.kind == SRC_FLAT) {
+  if (op.kind == SRC_FLAT && op.fl.rc) {
+    switch (op.fmt) {
+      case FMT_W4G: return launch_flat_t<FMT_W4G, SRC_FLAT, true>(op, s);
+      case FMT_W4SB: return launch_flat_t<FMT_W4SB, SRC_FLAT, true>(op, s);
+      case FMT_W2G: return launch_flat_t<FMT_W2G, SRC_FLAT, true>(op, s);
+      case FMT_W2SB: return launch_flat_t<FMT_W2SB, SRC_FLAT, true>(op, s);
+    }
+  } else if (op.kind == SRC_FLAT) {
     switch (op.fmt) {
       case FMT_W4G: return launch_flat_t<FMT_W4G, SRC_FLAT>(op, s);
       case FMT_W4SB: return launch_flat_t<FMT_W4SB, SRC_FLAT>(op, s);
@@ -1221,12 +1245,18 @@ static const char* kind_name(int kind) {
   return kind >= 0 && kind <= 6 ? N[kind] : "?";
 }
 
+double Engine::step_weight_bytes() const {
+  double b = 0;
+  for (const Op& op : *ops_) b += op.alg_bytes;
+  return b;
+}
+
 std::string Engine::role_kernel_name(int role) const {
   for (const Op& op : *ops_) {
     if (op.role != role) continue;
     const std::string fk = std::string("<") + fmt_name(op.fmt) + "," + kind_name(op.kind) + ">";
     switch (op.type) {
-      case OP_FLAT_TMA: return "gemv_flat_tma_kernel" + fk;
+      case OP_FLAT_TMA: return std::string(op.fl.rc ? "gemv_flat_tma_kernel[aligned]" : "gemv_flat_tma_kernel") + fk;
       case OP_TMA: return "gemv_tma_kernel" + fk;
       case OP_GEMV: return "gemv_kernel" + fk;
       case OP_ATTN: return "attention_kernel<" + std::to_string(op.hd) + ">";

@@ -71,6 +71,7 @@ class Engine {
   // milliseconds per launch and the algorithmic weight bytes per launch.
   void bench_role(int role, int rounds, float* avg_ms, double* bytes_per_launch, int* launches);
   std::string role_kernel_name(int role) const;
+  double step_weight_bytes() const;  // algorithmic weight bytes of one step (this rank)
 
   // Test entry points that run one kernel family on host vectors.
   void debug_gemv_linear(uint64_t tile_start, uint64_t num_tiles, const float* x, uint64_t x_len,

@@ -96,6 +96,7 @@ struct TpLink {
   unsigned long long lm_units;    // LM head: arrivals per step of all ranks' CTAs
   int32_t bcast;               // 1: outputs lie in the region; write them on every rank
   int32_t pad_;
+  const int32_t* err;          // this rank's StepState::err: once set, waits give up at once
 };
 
 // Result of one forward step (chpe_engine.zig:803 ForwardResult).

@@ -20,8 +20,9 @@
 // the loop.  The first NST pieces are requested before the programmatic
 // dependent-launch wait.
 //
-// Consumers: 16 warps.  Warp w decodes chunks [w*CPWARP, (w+1)*CPWARP) of each
-// piece, lane L the chunks w*CPWARP + L + 32j.  A warp's run spans at most two
+// Consumers: 8 warps.  Warp w decodes chunks [w*CPWARP, (w+1)*CPWARP) of each
+// piece (4 chunks per lane for 16 KiB pieces), lane L the chunks
+// w*CPWARP + L + 32j, all of its code loads issued before the decode.  A warp's run spans at most two
 // rows (CPWARP*CW <= cols, checked by the host), so a lane keeps two partial
 // sums; the warp reduces them and lane 0 adds them to its own per-row slots
 // wacc[part][warp][row].  After the last piece the slots are summed over the
@@ -47,6 +48,7 @@ struct FlatTmaLaunch {
   uint32_t ncols;          // x length = columns of every segment
   uint32_t rpc;            // max rows per CTA (size of the per-warp row slots)
   uint32_t nst;            // stages in the ring (<= kFlatMaxStages)
+  uint32_t rc;             // aligned cells: rows per cell (32768 / cols); CTA rows are multiples
   const float* x;          // hidden when norm != 0, else the input vector
   const float* gamma;
   float eps;
@@ -63,7 +65,9 @@ struct FlatTmaLaunch {
 
 constexpr uint32_t kFlatStageBytes = 16384 + 896;  // codes + payload head (832) rounded to 128
 constexpr uint32_t kFlatMaxStages = 16;
-constexpr uint32_t kFlatThreads = 544;             // 16 consumer warps + 1 producer warp
+constexpr uint32_t kFlatConsumerWarps = 8;          // each decodes 1/8 of every piece
+constexpr uint32_t kFlatConsumers = kFlatConsumerWarps * 32;
+constexpr uint32_t kFlatThreads = kFlatConsumers + 32;  // + 1 producer warp
 constexpr uint32_t kFlatMaxRanges = 8;
 
 struct FlatRange {
@@ -88,7 +92,7 @@ __host__ __device__ inline FlatLayout flat_layout(uint32_t ncols, uint32_t cw, u
   l.x = nst * kFlatStageBytes;
   l.xs = l.x + slots * 32 * cw * 4;
   l.wacc = l.xs + slots * 32 * 4;
-  l.bars = (l.wacc + nparts * 16 * rpc * 4 + 15) & ~15u;
+  l.bars = (l.wacc + nparts * kFlatConsumerWarps * rpc * 4 + 15) & ~15u;
   l.ranges = l.bars + 2 * kFlatMaxStages * 8;
   l.total = l.ranges + kFlatMaxRanges * (uint32_t)sizeof(FlatRange);
   return l;
@@ -111,15 +115,21 @@ CHPE_DEV bool mbar_wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* b
 CHPE_DEV void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
-CHPE_DEV void consumer_sync() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
+CHPE_DEV void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kFlatConsumers) : "memory"); }
 
-template <int FMT, int KIND>
+// ALIGNED: flat cells whose rows start at cell boundaries (cols divides
+// 32768, as the 72B/9B hidden widths do).  Then every piece is a whole cell of
+// rc rows and consumer lane t always decodes the same column chunk t % (cols /
+// CW) of rows t / (cols / CW) + k * (256 / (cols / CW)): its x stays in
+// registers for the whole launch and shared memory carries only codes.
+template <int FMT, int KIND, bool ALIGNED = false>
 __global__ void __launch_bounds__(kFlatThreads, 1) gemv_flat_tma_kernel(const __grid_constant__ FlatTmaLaunch P) {
   using FI = FmtInfo<FMT>;
   constexpr uint32_t CW = FI::CW, QPC = CW / 4;
   constexpr uint32_t WPP = flat_wpp<FMT, KIND>();
   constexpr uint32_t NCH = WPP / CW;        // chunks in a full piece
-  constexpr uint32_t CPWARP = NCH / 16;     // chunks per consumer warp
+  constexpr uint32_t NW = kFlatConsumerWarps, NCT = kFlatConsumers;
+  constexpr uint32_t CPWARP = NCH / NW;     // chunks per consumer warp
   constexpr uint32_t CPL = CPWARP / 32;     // chunks per lane
   static_assert(CPL >= 1 && CPWARP % 32 == 0, "piece geometry");
   static_assert(NCH * 16 <= 16384, "a piece fits a stage");
@@ -136,16 +146,18 @@ __global__ void __launch_bounds__(kFlatThreads, 1) gemv_flat_tma_kernel(const __
   uint64_t* full = reinterpret_cast<uint64_t*>(fsm + lay.bars);
   uint64_t* empty = full + kFlatMaxStages;
   FlatRange* rg = reinterpret_cast<FlatRange*>(fsm + lay.ranges);
-  __shared__ float sred[16];
-  __shared__ unsigned long long kbest[16];
-  __shared__ uint32_t kfin[16];
+  __shared__ float sred[kFlatConsumerWarps];
+  __shared__ unsigned long long kbest[kFlatConsumerWarps];
+  __shared__ uint32_t kfin[kFlatConsumerWarps];
   __shared__ uint32_t s_npieces, s_nranges;
   __shared__ int s_abort, s_is_last;
   __shared__ volatile int s_bad;
 
   const uint32_t Rt = P.row_start[swig ? 1 : P.nseg];
-  const uint32_t R0 = (uint32_t)((uint64_t)Rt * blockIdx.x / gridDim.x);
-  const uint32_t R1 = (uint32_t)((uint64_t)Rt * (blockIdx.x + 1) / gridDim.x);
+  // rows split evenly over the CTAs, in whole cells when aligned
+  const uint32_t RU = ALIGNED ? P.rc : 1u, Ut = Rt / RU;
+  const uint32_t R0 = RU * (uint32_t)((uint64_t)Ut * blockIdx.x / gridDim.x);
+  const uint32_t R1 = RU * (uint32_t)((uint64_t)Ut * (blockIdx.x + 1) / gridDim.x);
 
   if (tid == 0) {
     // this CTA's flat ranges, gate pieces before up pieces for SwiGLU
@@ -163,6 +175,12 @@ __global__ void __launch_bounds__(kFlatThreads, 1) gemv_flat_tma_kernel(const __
         const uint32_t row0 = P.src[si].row0;  // tensor row of the call's row 0
         r.fa0 = (a - S0 + row0) * C;
         r.fb0 = (b - S0 + row0) * C;
+        // weights past the tiles the call has read as zero (chpe_engine.zig
+        // flat loops stop at the available tiles): no pieces there, and rows
+        // with nothing left keep a zero sum
+        const uint64_t lim = P.src[si].flat_limit;
+        if ((uint64_t)r.fb0 > lim) r.fb0 = (uint32_t)lim;
+        if (r.fb0 <= r.fa0) continue;
         r.k0 = r.fa0 / WPP;
         r.pstart = pieces;
         r.lrbase = (int32_t)S0 - (int32_t)R0 - (int32_t)row0;
@@ -177,7 +195,7 @@ __global__ void __launch_bounds__(kFlatThreads, 1) gemv_flat_tma_kernel(const __
     s_bad = 0;
     for (uint32_t i = 0; i < nst; i++) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], 16);
+      mbar_init(&empty[i], NW);
     }
     fence_mbar_init();
   }
@@ -194,7 +212,7 @@ __global__ void __launch_bounds__(kFlatThreads, 1) gemv_flat_tma_kernel(const __
   };
 
   // ---- producer warp ------------------------------------------------------
-  if (warp == 16) {
+  if (warp == NW) {
     uint32_t ri = 0, issued = 0;
     auto issue = [&](uint32_t i) {
       uint32_t k, fa, fb;
@@ -252,39 +270,40 @@ __global__ void __launch_bounds__(kFlatThreads, 1) gemv_flat_tma_kernel(const __
   const uint32_t nq = C / 4;
   const float4* x4 = reinterpret_cast<const float4*>(P.x);
   if (!stop) {
-    for (uint32_t i = tid; i < nparts * 16 * P.rpc; i += 512) wacc[i] = 0.f;
+    for (uint32_t i = tid; i < nparts * NW * P.rpc; i += NCT) wacc[i] = 0.f;
     if (!P.norm) {
       // all loads of a batch in flight before any is stored
-      for (uint32_t q0 = 0; q0 < nq; q0 += 512u * 8u) {
+      for (uint32_t q0 = 0; q0 < nq; q0 += NCT * 8u) {
         float4 v[8];
 #pragma unroll
         for (uint32_t u = 0; u < 8; u++) {
-          const uint32_t q = q0 + tid + 512u * u;
+          const uint32_t q = q0 + tid + NCT * u;
           if (q < nq) v[u] = x4[q];
         }
 #pragma unroll
         for (uint32_t u = 0; u < 8; u++) {
-          const uint32_t q = q0 + tid + 512u * u;
+          const uint32_t q = q0 + tid + NCT * u;
           if (q < nq) *reinterpret_cast<float4*>(&xsh[xpos<CW>(4 * q)]) = v[u];
         }
       }
     } else {
       // RMSNorm: x and gamma in one batch (the host sends cols <= 16384 here)
+      constexpr uint32_t XB = 16384u / 4u / NCT;
       const float4* g4 = reinterpret_cast<const float4*>(P.gamma);
-      float4 v[8], g[8];
+      float4 v[XB], g[XB];
       float ss = 0.f;
 #pragma unroll
-      for (uint32_t u = 0; u < 8; u++) {
-        const uint32_t q = tid + 512u * u;
+      for (uint32_t u = 0; u < XB; u++) {
+        const uint32_t q = tid + NCT * u;
         if (q < nq) { v[u] = x4[q]; g[u] = g4[q]; }
       }
 #pragma unroll
-      for (uint32_t u = 0; u < 8; u++)
-        if (tid + 512u * u < nq) ss += v[u].x * v[u].x + v[u].y * v[u].y + v[u].z * v[u].z + v[u].w * v[u].w;
+      for (uint32_t u = 0; u < XB; u++)
+        if (tid + NCT * u < nq) ss += v[u].x * v[u].x + v[u].y * v[u].y + v[u].z * v[u].z + v[u].w * v[u].w;
       ss = warp_sum(ss);
       if (L == 0) sred[warp] = ss;
       consumer_sync();
-      for (int w = 0; w < 16; w++) tot += sred[w];
+      for (uint32_t w = 0; w < NW; w++) tot += sred[w];
       if (P.check_layer >= 0) {
         // end-of-layer check of the reference's debug block (chpe_engine.zig:1753-1764)
         const int l = P.check_layer;
@@ -296,8 +315,8 @@ __global__ void __launch_bounds__(kFlatThreads, 1) gemv_flat_tma_kernel(const __
       }
       const float inv = 1.0f / sqrtf(tot / (float)C + P.eps);
 #pragma unroll
-      for (uint32_t u = 0; u < 8; u++) {
-        const uint32_t q = tid + 512u * u;
+      for (uint32_t u = 0; u < XB; u++) {
+        const uint32_t q = tid + NCT * u;
         if (q < nq) {
           float4 o;
           o.x = v[u].x * inv * g[u].x;
@@ -315,7 +334,7 @@ __global__ void __launch_bounds__(kFlatThreads, 1) gemv_flat_tma_kernel(const __
     if (tid == 0) tp_signal(P.tp, P.tp.signal_sig);  // every CTA arrives once per launch
     return;
   }
-  for (uint32_t cc = tid; cc < C / CW; cc += 512) {
+  for (uint32_t cc = tid; cc < C / CW; cc += NCT) {
     float s = 0.f;
 #pragma unroll
     for (uint32_t q = 0; q < QPC; q++) {
@@ -327,7 +346,76 @@ __global__ void __launch_bounds__(kFlatThreads, 1) gemv_flat_tma_kernel(const __
   consumer_sync();
   pdl_launch_dependents();
 
-  // ---- main loop ----------------------------------------------------------
+  // ---- main loop, aligned cells ---------------------------------------------
+  if constexpr (ALIGNED) {
+    const uint32_t NCPR = C / CW;         // column chunks per row (a multiple of 32, <= 256)
+    const uint32_t RG = NCT / NCPR;       // lanes groups over the rows of a cell
+    const uint32_t cc = tid % NCPR, rgp = tid / NCPR;
+    constexpr uint32_t SPAN = 32u / CPL;  // lanes per reduced row after the butterfly
+    f2x xr[CW / 2];
+#pragma unroll
+    for (uint32_t q = 0; q < QPC; q++) {
+      const float4 t = xquad<CW>(xsh, cc >> 5, q, cc & 31u);
+      xr[2 * q] = pack2(t.x, t.y);
+      xr[2 * q + 1] = pack2(t.z, t.w);
+    }
+    const float xsm = xsc[cc];
+    uint32_t ri = 0;
+    for (uint32_t i = 0; i < npieces; i++) {
+      const uint32_t s = i % nst;
+      if (!mbar_wait_or_abort(&full[s], (i / nst) & 1u, &s_bad)) {
+        if (L == 0) { atomicExch(&P.st->err, 1); s_bad = 1; }
+        break;
+      }
+      uint32_t k, fa, fb;
+      locate(i, ri, k, fa, fb);
+      const uint8_t* stg = fsm + s * kFlatStageBytes;
+      const uint8_t* pl = stg + 16384;
+      float psc = 1.f, pbi = 0.f;
+      if constexpr (FI::SB) { psc = ld_f32(pl + 32); pbi = ld_f32(pl + 36); }
+      uint4 vv[CPL];
+#pragma unroll
+      for (uint32_t kk = 0; kk < CPL; kk++)
+        vv[kk] = *reinterpret_cast<const uint4*>(stg + 16u * ((rgp + kk * RG) * NCPR + cc));
+      float v[CPL];
+#pragma unroll
+      for (uint32_t kk = 0; kk < CPL; kk++) {
+        const uint32_t ci = (rgp + kk * RG) * NCPR + cc;
+        f2x a0 = 0ull, a1 = 0ull;
+#pragma unroll
+        for (uint32_t q = 0; q < QPC; q++) quad_fma<FMT>(vv[kk], (int)q, xr[2 * q], xr[2 * q + 1], (q & 1) ? a1 : a0);
+        const float d = chunk_finish<FMT>(a0, a1, xsm);
+        if constexpr (FI::GROUPED) v[kk] = d * ld_f16(pl + 48 + 2 * ((ci * CW) >> 7));
+        else if constexpr (FI::SB) v[kk] = fmaf(pbi, xsm, d * psc);
+        else v[kk] = d;
+      }
+      // CPL row sums over the warp in one butterfly: after it, lane kk*SPAN
+      // holds the sum of row rgp + kk*RG
+      float b;
+      if constexpr (CPL == 4) {
+        const bool h16 = (L & 16u) != 0, h8 = (L & 8u) != 0;
+        const float a0 = (h16 ? v[2] : v[0]) + __shfl_xor_sync(0xffffffffu, h16 ? v[0] : v[2], 16);
+        const float a1 = (h16 ? v[3] : v[1]) + __shfl_xor_sync(0xffffffffu, h16 ? v[1] : v[3], 16);
+        b = (h8 ? a1 : a0) + __shfl_xor_sync(0xffffffffu, h8 ? a0 : a1, 8);
+      } else {
+        static_assert(CPL == 2, "aligned cells hold 4 (4-bit) or 2 (2-bit) chunks per lane");
+        const bool h16 = (L & 16u) != 0;
+        b = (h16 ? v[1] : v[0]) + __shfl_xor_sync(0xffffffffu, h16 ? v[0] : v[1], 16);
+        b += __shfl_xor_sync(0xffffffffu, b, 8);
+      }
+      b += __shfl_xor_sync(0xffffffffu, b, 4);
+      b += __shfl_xor_sync(0xffffffffu, b, 2);
+      b += __shfl_xor_sync(0xffffffffu, b, 1);
+      if ((L & (SPAN - 1u)) == 0u) {
+        const FlatRange& r = rg[ri];
+        const uint32_t row = (fa / C) + rgp + (L / SPAN) * RG;  // tensor row
+        wacc[(r.part * NW + warp) * P.rpc + (uint32_t)((int32_t)row + r.lrbase)] += b;
+      }
+      __syncwarp();
+      if (L == 0) mbar_arrive(&empty[s]);
+    }
+  } else {
+  // ---- main loop, any flat stream --------------------------------------------
   const uint32_t NCC = C / CW;  // chunks per row
   const float invC = 1.0f / (float)C;
   uint32_t ri = 0;
@@ -357,6 +445,12 @@ __global__ void __launch_bounds__(kFlatThreads, 1) gemv_flat_tma_kernel(const __
       float psc = 1.f, pbi = 0.f;
       if constexpr (FI::SB) { psc = ld_f32(pl + 32); pbi = ld_f32(pl + 36); }
       bool crossed = false;
+      uint4 vv[CPL];  // all of this lane's code loads first
+#pragma unroll
+      for (uint32_t j = 0; j < CPL; j++) {
+        const uint32_t ci = c0 + L + 32u * j;
+        vv[j] = ci < nch ? *reinterpret_cast<const uint4*>(stg + 16u * ci) : make_uint4(0u, 0u, 0u, 0u);
+      }
 #pragma unroll
       for (uint32_t j = 0; j < CPL; j++) {
         const uint32_t ci = c0 + L + 32u * j;
@@ -365,7 +459,7 @@ __global__ void __launch_bounds__(kFlatThreads, 1) gemv_flat_tma_kernel(const __
           const bool second = cc >= NCC;  // the run wraps into row rA + 1
           cc = second ? cc - NCC : cc;
           crossed |= second;
-          const uint4 v = *reinterpret_cast<const uint4*>(stg + 16u * ci);
+          const uint4 v = vv[j];
           const ulonglong2* xq = reinterpret_cast<const ulonglong2*>(xsh) + ((cc >> 5) * QPC * 32u + (cc & 31u));
           f2x a0 = 0ull, a1 = 0ull;
 #pragma unroll
@@ -391,13 +485,14 @@ __global__ void __launch_bounds__(kFlatThreads, 1) gemv_flat_tma_kernel(const __
       const bool any2 = __any_sync(0xffffffffu, crossed);
       if (L == 0 || (L == 16 && any2)) {
         const FlatRange& r = rg[ri];
-        wacc[(r.part * 16 + warp) * P.rpc + (uint32_t)((int32_t)rA + r.lrbase) + (L >> 4)] += keep;
+        wacc[(r.part * NW + warp) * P.rpc + (uint32_t)((int32_t)rA + r.lrbase) + (L >> 4)] += keep;
       }
     }
     __syncwarp();
     if (L == 0) mbar_arrive(&empty[s]);
   }
   (void)failed;
+  }  // any flat stream
   consumer_sync();
   if (s_bad) {
     if (tid == 0) tp_signal(P.tp, P.tp.signal_sig);
@@ -408,14 +503,14 @@ __global__ void __launch_bounds__(kFlatThreads, 1) gemv_flat_tma_kernel(const __
   unsigned long long lbest = 0ull;
   uint32_t lfin = 1u;
   const uint32_t nrows = R1 - R0;
-  for (uint32_t lr = tid; lr < nrows; lr += 512) {
+  for (uint32_t lr = tid; lr < nrows; lr += NCT) {
     float d0 = 0.f, d1 = 0.f;
 #pragma unroll
-    for (int w = 0; w < 16; w++) d0 += wacc[w * P.rpc + lr];
+    for (uint32_t w = 0; w < NW; w++) d0 += wacc[w * P.rpc + lr];
     if constexpr (FMT == FMT_I8RAW) d0 *= 0.00373708f;  // raw int8 dot scale (chpe_engine.zig:1236)
     if (swig) {
 #pragma unroll
-      for (int w = 0; w < 16; w++) d1 += wacc[(16 + w) * P.rpc + lr];
+      for (uint32_t w = 0; w < NW; w++) d1 += wacc[(NW + w) * P.rpc + lr];
       if constexpr (FMT == FMT_I8RAW) d1 *= 0.00373708f;
       tp_put(P.tp, P.out[0], R0 + lr, silu_ref(d0) * d1);
       continue;
@@ -457,7 +552,7 @@ __global__ void __launch_bounds__(kFlatThreads, 1) gemv_flat_tma_kernel(const __
     if (tid == 0) {
       unsigned long long b = 0ull;
       uint32_t f = 1u;
-      for (int w = 0; w < 16; w++) { b = kbest[w] > b ? kbest[w] : b; f &= kfin[w]; }
+      for (uint32_t w = 0; w < NW; w++) { b = kbest[w] > b ? kbest[w] : b; f &= kfin[w]; }
       const int nr = P.tp.world > 1 ? P.tp.world : 1;
       for (int rr = 0; rr < nr; rr++) {  // argmax and finiteness on every rank
         StepState* st = nr > 1 ? tp_at(P.st, P.tp, rr) : P.st;

@@ -95,6 +95,11 @@ void *chpe_init_tp_bytes(const void *bytes, uint64_t len, int arch, uint32_t max
                          int rank, int world);
 int chpe_tp_export_handle(void *ctx, uint8_t *handle64);
 int chpe_tp_connect(void *ctx, const uint8_t *handles, int world);
+/* The rows one rank owns (no GPU needed): ten uint32 values, query heads
+ * (count, first), kv heads (first, count), hidden rows (count, first), FFN
+ * rows (count, first), vocabulary rows (count, first).  0, or -1 when the
+ * architecture does not split evenly over `world`. */
+int chpe_tp_slice(int arch, int rank, int world, uint32_t out[10]);
 
 /* WeightArchive.validate (weight_archive.zig:152-172): 0 when valid, else the
  * error: 1 InvalidMagic, 2 UnsupportedVersion, 3 BadGeometry, 4 Truncated,
@@ -132,6 +137,11 @@ int chpe_bench_kernel(void *ctx, int role, int rounds, float *avg_ms, double *by
  * chpe_bench_kernel), e.g. "gemv_flat_tma_kernel<W4G,FLAT>"; "" when the
  * role has no op or ctx is NULL.  The string lives as long as ctx. */
 const char *chpe_role_kernel_name(void *ctx, int role);
+
+/* Algorithmic weight bytes one decode step of this context streams (codes
+ * and scales of the rows its projections use; with tensor parallelism, this
+ * rank's share).  0 for NULL. */
+double chpe_step_weight_bytes(void *ctx);
 
 /* all_finite of the last ForwardResult (1/0; 0 for NULL). */
 int chpe_get_last_all_finite(void *ctx);

@@ -110,11 +110,12 @@ def test_gemv_partial_spans_and_past_end():
 
 # (rows, cols) read from the 3B down-projection tiles (688 flat cells, or 2752
 # raw FP16 tiles): the widths of the 9B/72B tensors (4096, 8192, 12288,
-# 29568), widths just past one consumer warp's run, a handful of rows, a width
-# that is not a multiple of the chunk width, and a span longer than the tiles
-# given (not covered in full).
+# 29568; 4096 and 8192 take the aligned-cell path), widths just past one
+# consumer warp's run, a handful of rows, a width that is not a multiple of
+# the chunk width, and spans longer than the tiles given (not covered in
+# full, aligned and not).
 FLAT_SHAPES = [(2048, 8192), (700, 29568), (4000, 4096), (1500, 12288), (9000, 2112), (5, 8192),
-               (3, 29568), (1, 4096), (700, 30000), (770, 29568)]
+               (3, 29568), (1, 4096), (700, 30000), (770, 29568), (2800, 8192), (8, 4096)]
 
 
 @pytest.mark.parametrize("cfg", [chpe.SYNTH_3B_W4, chpe.SYNTH_3B_W2, chpe.SYNTH_3B_FP16_RAW])
