@@ -1,22 +1,25 @@
 #!/usr/bin/env python3
 """Benchmark: batch-1 greedy decode of chpe-qwen-engine's forwardDecode loop.
 
-Workload: Qwen2.5-3B in the repo's 4-bit dense-cell
-format (group-128 FP16 scales), random-init (seeded synthetic archive), a
-512-token prompt decoded token by token (untimed), then W warm-up and K timed
-greedy decode steps.  A step is one token through all 36 layers + LM head.
+Default workload (the configuration the metric is quoted on
+at 1/2/4/8 B200): Qwen2.5-72B in the 4-bit flat-cell format (group-128 FP16
+scales), random-init seeded synthetic archive, a 2048-token prompt decoded
+token by token (untimed), then W warm-up and K timed greedy steps.  A step is
+one token through all 80 layers + LM head.  With N > 1 (torchrun, one rank per
+GPU) the model is tensor parallel over the N GPUs (row-split projections,
+exchanges over NVLink peer memory); `value` is tokens of the one sequence per
+second (strong scaling).  --model picks another config (3b-w4 = config 2,
+9b-w4, 3b-w2, 3b-fp16); the 3B models run as independent replicas for N > 1.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--model M] [--impl ours|reference]
 
 value: tok/s with weights resident in HBM, device time (CUDA events on the
 engine stream) of K back-to-back greedy steps (each step's token is the
-previous argmax, fed back on the device).  e2e: the same steps through the C
-ABI with a pinned host->device copy of each token and a device->host copy of
-each step's logits and result, wall time.  With N > 1 (torchrun) every rank
-runs an independent replica on its own GPU (the 3B path does not shard) and
-value is the sum over ranks using the max over ranks of the time.
+previous argmax, fed back on the device), max over ranks.  e2e: the same steps
+through the C ABI with a pinned host->device copy of each token and a
+device->host copy of each step's logits and result, wall time, max over ranks.
 --impl reference times the CPU restatement of the reference engine (the Zig
-reference cannot be built here) on the host cores.
+reference cannot be built here) on all host cores, rank 0 only.
 """
 from __future__ import annotations
 
@@ -283,7 +286,23 @@ def run_ours(args, rank, world, local, dist):
                 "avg_launch_us": kms * 1000}
     else:
         # one role cannot run alone across ranks (its exchanges wait on the
-        # others): the roofline here is the whole step's weight stream per GPU
+        # others): per-role times come from steps launched op by op with CUDA
+        # events between the ops (all ranks together; max over ranks), and the
+        # roofline here is the whole step's weight stream per GPU
+        names = {chpe.ROLE_QKV: "qkv", chpe.ROLE_ATTN: "attention", chpe.ROLE_O: "o",
+                 chpe.ROLE_GATEUP: "gateup", chpe.ROLE_DOWN: "down", chpe.ROLE_LMHEAD: "lmhead"}
+        acc = {}
+        reps = 3
+        for _ in range(reps):
+            ms_ops, roles = eng.profile_step()
+            for m, r in zip(ms_ops, roles):
+                if int(r) in names:
+                    a = acc.setdefault(names[int(r)], [0.0, 0])
+                    a[0] += float(m)
+                    a[1] += 1
+        for name, (tot, cnt) in acc.items():
+            per_role[name] = {"avg_us": round(max_over_ranks(dist, tot / cnt) * 1000, 2),
+                              "launches_per_step": cnt // reps, "bytes_per_launch": None, "gbs": None}
         mine = eng.step_weight_bytes()
         step_bytes = sum_over_ranks(dist, mine)
         per_gpu = max_over_ranks(dist, mine) / (ms_max / args.steps / 1000.0) / 1e9
@@ -335,7 +354,7 @@ def main():
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--model", default="3b-w4", choices=sorted(MODELS))
+    ap.add_argument("--model", default="72b-w4", choices=sorted(MODELS))
     ap.add_argument("--prompt", type=int, default=None,
                     help="prompt tokens decoded before timing (default: the model's config)")
     ap.add_argument("--kernel-only", default=None,

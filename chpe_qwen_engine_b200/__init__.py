@@ -59,6 +59,8 @@ SYMBOLS = [
     ("chpe_tp_connect", _I, [_P, C.c_char_p, _I]),
     ("chpe_tp_slice", _I, [_I, _I, _I, _U32P]),
     ("chpe_step_weight_bytes", C.c_double, [_P]),
+    ("chpe_profile_step", _I, [_P, _FP, C.POINTER(C.c_int), _I]),
+    ("chpe_verify", _I, [_P, _U32P, C.c_size_t, C.c_uint32, _FP, _U32P]),
     ("chpe_get_last_all_finite", _I, [_P]),
     ("chpe_kernels_per_step", _I, [_P]),
     ("chpe_get_position", _U32, [_P]),
@@ -262,6 +264,15 @@ class Engine:
         assert n == self.vocab
         return out
 
+    def verify(self, tokens, pos: int) -> tuple[np.ndarray, np.ndarray]:
+        """chpe_verify: (logits [m, vocab], argmax [m]) of m candidates at pos.."""
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        lg = np.empty((t.size, self.vocab), np.float32)
+        am = np.empty(t.size, np.uint32)
+        if lib().chpe_verify(self.ctx, _u32p(t), t.size, pos, _fp(lg), _u32p(am)) != 0:
+            raise ChpeError(self._err() or "chpe_verify failed")
+        return lg, am
+
     def generate(self, prompt, n_gen: int) -> np.ndarray:
         p = np.ascontiguousarray(prompt, dtype=np.uint32)
         out = np.zeros(max(n_gen, 1), np.uint32)
@@ -293,6 +304,17 @@ class Engine:
     def op_kernel_name(self, role: int) -> str:
         """Kernel that runs the first op of `role`."""
         return (lib().chpe_role_kernel_name(self.ctx, role) or b"").decode()
+
+    def profile_step(self) -> tuple[np.ndarray, np.ndarray]:
+        """One greedy step op by op: (per-op ms, per-op role)."""
+        cap = 4096
+        ms = np.zeros(cap, np.float32)
+        roles = np.zeros(cap, np.int32)
+        n = lib().chpe_profile_step(self.ctx, _fp(ms), roles.ctypes.data_as(C.POINTER(C.c_int)), cap)
+        if n < 0:
+            raise ChpeError(self._err())
+        n = min(n, cap)
+        return ms[:n], roles[:n]
 
     def step_weight_bytes(self) -> float:
         """Algorithmic weight bytes one step streams on this rank."""

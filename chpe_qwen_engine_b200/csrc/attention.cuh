@@ -35,10 +35,18 @@ struct AttnLaunch {
 };
 
 constexpr int ATT_TT = 32;  // positions per staged tile
-// Splits of the positions per kv head.  The merge keeps one weight per split
-// in two registers per lane, so at most 64.
+// Splits of the positions per kv head: between 16 and 64, about one CTA per
+// SM over the kv heads a GPU holds.  The merge keeps one weight per split in
+// two registers per lane, so at most 64.
 constexpr int kAttnSplits = 16;
-static_assert(kAttnSplits <= 64, "attention merge holds at most 64 split weights");
+constexpr int kAttnMaxSplits = 64;
+static_assert(kAttnMaxSplits <= 64, "attention merge holds at most 64 split weights");
+inline int attn_splits(int num_sms, int kv_heads, int max_seq) {
+  int n = num_sms / (kv_heads > 0 ? kv_heads : 1);
+  const int tiles = (max_seq + ATT_TT - 1) / ATT_TT;  // more splits than tiles only idle
+  if (n > tiles) n = tiles;
+  return n < kAttnSplits ? kAttnSplits : (n > kAttnMaxSplits ? kAttnMaxSplits : n);
+}
 
 template <int HD>
 CHPE_DEV void attention_body(const AttnLaunch& P);
@@ -103,20 +111,28 @@ CHPE_DEV void attention_body(const AttnLaunch& P) {
   pdl_launch_dependents();
 
   const int n = pos + 1;
-  const int chunk = (n + P.nsplit - 1) / P.nsplit;
+  // at least one full tile per split: short contexts use fewer splits (the
+  // rest find an empty range and only report -inf to the merge)
+  int chunk = (n + P.nsplit - 1) / P.nsplit;
+  if (chunk < ATT_TT) chunk = ATT_TT;
   const int t0 = split * chunk, t1 = min(n, t0 + chunk);
   const float scale = 1.0f / sqrtf((float)HD);
   float m = -INFINITY, l = 0.f, acc[PER];
 #pragma unroll
   for (int e = 0; e < PER; e++) acc[e] = 0.f;
 
-  constexpr int VPR = HD / 8;  // 16-byte vectors per row
-  for (int tb = t0; tb < t1; tb += ATT_TT) {
+  constexpr int VPR = HD / 8;                 // 16-byte vectors per row
+  constexpr int MAXV = ATT_TT * VPR / 128;    // vectors per thread (launched with >= 128 threads)
+  // The next tile's K/V rows are loaded into registers while the current one
+  // is scored from shared memory.
+  uint4 kr[MAXV], vr[MAXV];
+  auto fetch = [&](int tb) {
     const int nt = min(ATT_TT, t1 - tb);
-    __syncthreads();  // previous tile consumed
-    for (int i = threadIdx.x; i < nt * VPR; i += blockDim.x) {
-      int r = i / VPR, c8 = (i % VPR) * 8, t = tb + r;
-      uint4 kv4, vv4;
+#pragma unroll
+    for (int u = 0; u < MAXV; u++) {
+      const int i = threadIdx.x + u * blockDim.x;
+      if (i >= nt * VPR) continue;
+      const int r = i / VPR, c8 = (i % VPR) * 8, t = tb + r;
       if (t == pos) {  // this step's entry, from the values just computed
         __half2 hk[4], hv[4];
 #pragma unroll
@@ -124,28 +140,43 @@ CHPE_DEV void attention_body(const AttnLaunch& P) {
           hk[e] = __floats2half2_rn(kn[c8 + 2 * e], kn[c8 + 2 * e + 1]);
           hv[e] = __floats2half2_rn(vn[c8 + 2 * e], vn[c8 + 2 * e + 1]);
         }
-        kv4 = *reinterpret_cast<uint4*>(hk);
-        vv4 = *reinterpret_cast<uint4*>(hv);
+        kr[u] = *reinterpret_cast<uint4*>(hk);
+        vr[u] = *reinterpret_cast<uint4*>(hv);
       } else {
-        size_t off = ((size_t)t * P.KV + kvh) * HD + c8;
-        kv4 = *reinterpret_cast<const uint4*>(P.kc + off);
-        vv4 = *reinterpret_cast<const uint4*>(P.vc + off);
+        const size_t off = ((size_t)t * P.KV + kvh) * HD + c8;
+        kr[u] = *reinterpret_cast<const uint4*>(P.kc + off);
+        vr[u] = *reinterpret_cast<const uint4*>(P.vc + off);
       }
-      *reinterpret_cast<uint4*>(&ks[r][c8]) = kv4;
-      *reinterpret_cast<uint4*>(&vs[r][c8]) = vv4;
     }
+  };
+  if (t0 < t1) fetch(t0);
+  for (int tb = t0; tb < t1; tb += ATT_TT) {
+    const int nt = min(ATT_TT, t1 - tb);
+    __syncthreads();  // previous tile consumed
+#pragma unroll
+    for (int u = 0; u < MAXV; u++) {
+      const int i = threadIdx.x + u * blockDim.x;
+      if (i >= nt * VPR) continue;
+      const int r = i / VPR, c8 = (i % VPR) * 8;
+      *reinterpret_cast<uint4*>(&ks[r][c8]) = kr[u];
+      *reinterpret_cast<uint4*>(&vs[r][c8]) = vr[u];
+    }
+    if (tb + ATT_TT < t1) fetch(tb + ATT_TT);
     __syncthreads();
     if (warp < G) {
       float sc = -INFINITY;  // lane = tile row
       if (L < nt) {
-        float d = 0.f;
-#pragma unroll 8
-        for (int e = 0; e < HD; e += 2) {
-          float2 kf = __half22float2(*reinterpret_cast<const __half2*>(&ks[L][e]));
-          d = fmaf(qs[warp][e], kf.x, d);
-          d = fmaf(qs[warp][e + 1], kf.y, d);
+        float d[4] = {0.f, 0.f, 0.f, 0.f};  // four independent chains
+#pragma unroll 4
+        for (int e = 0; e < HD; e += 8) {
+#pragma unroll
+          for (int h = 0; h < 4; h++) {
+            const float2 kf = __half22float2(*reinterpret_cast<const __half2*>(&ks[L][e + 2 * h]));
+            d[h] = fmaf(qs[warp][e + 2 * h], kf.x, d[h]);
+            d[h] = fmaf(qs[warp][e + 2 * h + 1], kf.y, d[h]);
+          }
         }
-        sc = d * scale;
+        sc = ((d[0] + d[1]) + (d[2] + d[3])) * scale;
       }
       const float tmax = warp_max(sc);
       const float mn = fmaxf(m, tmax);

@@ -111,6 +111,7 @@ extern "C" int chpe_attention_decode_noalloc(const float* q, const float* k, con
   P.max_seq = (int32_t)max_seq_len;
   int threads = (int)G * 32;
   if (threads < (int)head_dim / 2) threads = (int)head_dim / 2;
+  if (threads < 128) threads = 128;  // the kernel's tile loads assume at least 128 threads
   dim3 grid(nsplit, num_kv_heads);
   if (head_dim == 128) chpe::attention_kernel<128><<<grid, threads, 0, s>>>(P);
   else chpe::attention_kernel<256><<<grid, threads, 0, s>>>(P);

@@ -214,6 +214,20 @@ int chpe_decode_step(void* ctx, uint32_t token, uint32_t pos, float* out_logits)
   return (int)c->last_argmax;
 }
 
+int chpe_verify(void* ctx, const uint32_t* toks, size_t m, uint32_t pos, float* out_logits,
+                uint32_t* out_argmax) {
+  if (!ctx || !toks || m == 0) return -1;
+  Ctx* c = (Ctx*)ctx;
+  try {
+    c->engine->verify(toks, m, pos, out_logits, out_argmax);
+    store_result(c);
+  } catch (const std::exception& e) {
+    c->err = e.what();
+    return -1;
+  }
+  return 0;
+}
+
 int chpe_generate(void* ctx, const uint32_t* prompt, size_t n_prompt, size_t n_gen, uint32_t* out) {
   if (!ctx || !prompt || n_prompt == 0 || (n_gen > 0 && !out)) return -1;
   Ctx* c = (Ctx*)ctx;
@@ -263,6 +277,17 @@ int chpe_bench_kernel(void* ctx, int role, int rounds, float* avg_ms, double* by
     return -1;
   }
   return 0;
+}
+
+int chpe_profile_step(void* ctx, float* op_ms, int* op_roles, int cap) {
+  if (!ctx || cap < 0) return -1;
+  Ctx* c = (Ctx*)ctx;
+  try {
+    return c->engine->profile_step(op_ms, op_roles, cap);
+  } catch (const std::exception& e) {
+    c->err = e.what();
+    return -1;
+  }
 }
 
 double chpe_step_weight_bytes(void* ctx) {

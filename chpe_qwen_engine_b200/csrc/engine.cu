@@ -274,8 +274,8 @@ Engine::Engine(const uint8_t* bytes, uint64_t len, int arch, uint32_t max_seq, i
   d_tmp2_ = (float*)dalloc(maxproj * 4);
   d_xn_ = (float*)dalloc(maxproj * 4);
   const int G = A.H / A.KV;
-  nsplit_ = kAttnSplits;
-  d_part_ = (float*)dalloc((size_t)A.KV * nsplit_ * G * (A.HD + 2) * 4);
+  nsplit_ = attn_splits(num_sms_, (int)A.KV, (int)max_seq_);
+  d_part_ = (float*)dalloc((size_t)A.KV * kAttnMaxSplits * G * (A.HD + 2) * 4);
   d_counters_ = (uint32_t*)dalloc(A.KV * 4);
   size_t kv_elems = (size_t)A.L * max_seq_ * A.KV * A.HD;
   d_kc_ = (__half*)dalloc(kv_elems * 2);
@@ -305,6 +305,8 @@ Engine::Engine(const uint8_t* bytes, uint64_t len, int arch, uint32_t max_seq, i
 
 Engine::~Engine() {
   if (graph_) cudaGraphExecDestroy(graph_);
+  if (d_vlogits_) cudaFree(d_vlogits_);
+  if (d_vres_) cudaFree(d_vres_);
   for (void* p : ipc_open_) cudaIpcCloseMemHandle(p);
   if (d_region_) cudaFree(d_region_);
   for (void* p : allocs_) cudaFree(p);
@@ -619,7 +621,7 @@ void Engine::add_linear_ops(std::vector<Op>& ops, const GemvSrc* src, float* con
     else return false;
     const uint32_t cw = (uint32_t)fmt_cw(f);
     const uint64_t w = (uint64_t)(g.row0 + g.r_total) * g.c_total;
-    // a consumer warp's run of a piece (wpp/cw/8 chunks) spans at most two rows
+    // a consumer warp's run of a piece (wpp/cw/16 chunks) spans at most two rows
     if (gamma && ncols > 16384) return false;  // the fused RMSNorm loads x in one batch
     return g.c_total == ncols && ncols % cw == 0 && (wpp / cw / kFlatConsumerWarps) * cw <= ncols &&
            w < (1ull << 32) && g.r_total > 0;
@@ -941,7 +943,8 @@ void Engine::build_step_tp() {
   const uint32_t qd = A.H * A.HD, kvd = A.KV * A.HD;
   // arrivals per (step, layer) of each exchange: every rank launches the same
   // grids, so N x this rank's grid of the producing op
-  const unsigned long long u_att = (unsigned long long)N * nsplit_ * kvl;
+  const int nsp = attn_splits(num_sms_, (int)kvl, (int)max_seq_);
+  const unsigned long long u_att = (unsigned long long)N * nsp * kvl;
   unsigned long long u_o = 0, u_gu = 0, u_dn = 0;
   auto units_of_last = [&]() { return (unsigned long long)N * ops.back().grid.x; };
   TpLink base{};
@@ -1008,12 +1011,13 @@ void Engine::build_step_tp() {
       at.H = (int)hq;
       at.KV = (int)kvl;
       at.HD = (int)A.HD;
-      at.nsplit = nsplit_;
+      at.nsplit = nsp;
       at.max_seq = (int32_t)max_seq_;
       at.tp = link(-1, 0, 0, SIG_ATT, 1);
-      op.grid = dim3(nsplit_, kvl);
+      op.grid = dim3(nsp, kvl);
       op.threads = (int)(hq / kvl) * 32;
       if (op.threads < (int)A.HD / 2) op.threads = (int)A.HD / 2;
+      if (op.threads < 128) op.threads = 128;
       ops.push_back(op);
     }
     GemvSrc o = narrow(plan_linear(li.o_proj, li.o_tiles, A.D, A.D, A.D, 1, -1), d0, dl);
@@ -1087,6 +1091,7 @@ void Engine::build_step() {
       op.grid = dim3(nsplit_, A.KV);
       op.threads = (int)(A.H / A.KV) * 32;
       if (op.threads < (int)A.HD / 2) op.threads = (int)A.HD / 2;
+      if (op.threads < 128) op.threads = 128;
       ops.push_back(op);
     }
     GemvSrc o = plan_linear(li.o_proj, li.o_tiles, A.D, A.D, A.D, 1, -1);
@@ -1245,6 +1250,35 @@ static const char* kind_name(int kind) {
   return kind >= 0 && kind <= 6 ? N[kind] : "?";
 }
 
+int Engine::profile_step(float* op_ms, int* op_roles, int cap) {
+  if (!graph_) throw std::runtime_error("run forward() first");
+  if ((uint64_t)pos_ + 1 > max_seq_) throw std::runtime_error("sequence exceeds max_seq_len");
+  const std::vector<Op>& ops = *ops_;
+  const int n = (int)ops.size();
+  std::vector<cudaEvent_t> ev(n + 1);
+  for (auto& e : ev) CK(cudaEventCreate(&e));
+  int32_t one = 1, zero = 0;
+  CK(cudaMemcpyAsync(&d_st_->feed_argmax, &one, 4, cudaMemcpyHostToDevice, stream_));
+  CK(cudaMemcpyAsync(&d_st_->gather, &zero, 4, cudaMemcpyHostToDevice, stream_));
+  CK(cudaEventRecord(ev[0], stream_));
+  for (int i = 0; i < n; i++) {
+    launch(ops[i], stream_);
+    CK(cudaEventRecord(ev[i + 1], stream_));
+  }
+  CK(cudaMemcpyAsync(&d_st_->feed_argmax, &zero, 4, cudaMemcpyHostToDevice, stream_));
+  CK(cudaMemcpyAsync(&d_st_->gather, &one, 4, cudaMemcpyHostToDevice, stream_));
+  sync_result();
+  for (int i = 0; i < n && i < cap; i++) {
+    float ms = 0.f;
+    CK(cudaEventElapsedTime(&ms, ev[i], ev[i + 1]));
+    if (op_ms) op_ms[i] = ms;
+    if (op_roles) op_roles[i] = ops[i].role;
+  }
+  for (auto& e : ev) cudaEventDestroy(e);
+  pos_ += 1;
+  return n;
+}
+
 double Engine::step_weight_bytes() const {
   double b = 0;
   for (const Op& op : *ops_) b += op.alg_bytes;
@@ -1380,6 +1414,52 @@ void Engine::generate(const uint32_t* prompt, size_t n_prompt, size_t n_gen, uin
   sync_result();
   for (size_t i = 1; i < n_gen; i++) out_tokens[i] = (uint32_t)g[i - 1];
   pos_ = (uint32_t)(n_prompt + n_gen - 1);
+}
+
+void Engine::verify(const uint32_t* toks, size_t m, uint32_t pos, float* logits_out, uint32_t* argmax_out) {
+  if (m == 0) return;
+  if ((uint64_t)pos + m > max_seq_) throw std::runtime_error("sequence exceeds max_seq_len");
+  if (m + 1 > h_tok_cap_) throw std::runtime_error("too many candidates");
+  if (!graph_) {
+    // build the graph with a warm step at the first candidate's position (its
+    // cache entry is rewritten below)
+    forward(toks, 1, pos);
+  }
+  const size_t V = arch_->V;
+  if (m > vcap_) {
+    if (d_vlogits_) cudaFree(d_vlogits_);
+    if (d_vres_) cudaFree(d_vres_);
+    CK(cudaMalloc(&d_vlogits_, m * V * 4));
+    CK(cudaMalloc(&d_vres_, m * sizeof(StepResult)));
+    vcap_ = m;
+  }
+  h_st_->token = (int32_t)toks[0];
+  h_st_->pos = (int32_t)pos;
+  h_st_->feed_argmax = 0;
+  h_st_->stop = 0;
+  h_st_->best = 0;
+  h_st_->finite = 1;
+  h_st_->done_ctas = 0;
+  h_st_->n_gen = 0;
+  CK(cudaMemcpyAsync(d_st_, h_st_, sizeof(StepState), cudaMemcpyHostToDevice, stream_));
+  auto t0 = now_ns();
+  // m decode steps back to back on the device; each step's logits and result
+  // are copied aside before the next step reuses the buffers
+  for (size_t i = 0; i < m; i++) {
+    h_tok_[i] = toks[i];
+    if (i > 0) CK(cudaMemcpyAsync(&d_st_->token, &h_tok_[i], 4, cudaMemcpyHostToDevice, stream_));
+    CK(cudaGraphLaunch(graph_, stream_));
+    CK(cudaMemcpyAsync(d_vlogits_ + i * V, d_logits_, V * 4, cudaMemcpyDeviceToDevice, stream_));
+    CK(cudaMemcpyAsync(d_vres_ + i, d_res_, sizeof(StepResult), cudaMemcpyDeviceToDevice, stream_));
+  }
+  std::vector<StepResult> res(m);
+  CK(cudaMemcpyAsync(res.data(), d_vres_, m * sizeof(StepResult), cudaMemcpyDeviceToHost, stream_));
+  if (logits_out) CK(cudaMemcpyAsync(logits_out, d_vlogits_, m * V * 4, cudaMemcpyDeviceToHost, stream_));
+  sync_result();
+  last_ns_ = now_ns() - t0;
+  if (argmax_out)
+    for (size_t i = 0; i < m; i++) argmax_out[i] = res[i].argmax_token;
+  pos_ = pos + (uint32_t)m;
 }
 
 float Engine::timed_greedy_steps(size_t n) {

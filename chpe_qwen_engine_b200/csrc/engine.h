@@ -53,6 +53,11 @@ class Engine {
   // Greedy generation on the device: prompt (n_prompt) then n_gen steps
   // feeding each argmax back as the next token; out_tokens gets n_gen ids.
   void generate(const uint32_t* prompt, size_t n_prompt, size_t n_gen, uint32_t* out_tokens);
+  // Batch-M verification: logits of m candidate tokens scored at positions
+  // pos..pos+m-1, each seeing the KV entries of the ones before it (causal),
+  // i.e. m forwardDecode steps; logits_out [m][vocab], argmax_out [m] (either
+  // may be null).  The last step's result becomes last_result().
+  void verify(const uint32_t* toks, size_t m, uint32_t pos, float* logits_out, uint32_t* argmax_out);
   // n greedy steps from the current position, timed with CUDA events on the
   // engine stream; returns milliseconds.
   float timed_greedy_steps(size_t n);
@@ -71,6 +76,10 @@ class Engine {
   // milliseconds per launch and the algorithmic weight bytes per launch.
   void bench_role(int role, int rounds, float* avg_ms, double* bytes_per_launch, int* launches);
   std::string role_kernel_name(int role) const;
+  // One greedy step launched op by op with CUDA events between the ops (no
+  // graph); per-op milliseconds and roles.  With tensor parallelism every rank
+  // calls it together.  Advances the position like a decode step.
+  int profile_step(float* op_ms, int* op_roles, int cap);
   double step_weight_bytes() const;  // algorithmic weight bytes of one step (this rank)
 
   // Test entry points that run one kernel family on host vectors.
@@ -145,6 +154,10 @@ class Engine {
   TpShared* d_tpsh_ = nullptr;
   long long tp_delta_[kTpMax] = {};
   std::vector<void*> ipc_open_;
+  // verify(): per-candidate logits and results on the device
+  float* d_vlogits_ = nullptr;
+  StepResult* d_vres_ = nullptr;
+  size_t vcap_ = 0;
 };
 
 }  // namespace chpe

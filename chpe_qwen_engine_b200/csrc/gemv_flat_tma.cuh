@@ -20,8 +20,8 @@
 // the loop.  The first NST pieces are requested before the programmatic
 // dependent-launch wait.
 //
-// Consumers: 8 warps.  Warp w decodes chunks [w*CPWARP, (w+1)*CPWARP) of each
-// piece (4 chunks per lane for 16 KiB pieces), lane L the chunks
+// Consumers: 16 warps.  Warp w decodes chunks [w*CPWARP, (w+1)*CPWARP) of each
+// piece (2 chunks per lane for 16 KiB pieces), lane L the chunks
 // w*CPWARP + L + 32j, all of its code loads issued before the decode.  A warp's run spans at most two
 // rows (CPWARP*CW <= cols, checked by the host), so a lane keeps two partial
 // sums; the warp reduces them and lane 0 adds them to its own per-row slots
@@ -65,7 +65,7 @@ struct FlatTmaLaunch {
 
 constexpr uint32_t kFlatStageBytes = 16384 + 896;  // codes + payload head (832) rounded to 128
 constexpr uint32_t kFlatMaxStages = 16;
-constexpr uint32_t kFlatConsumerWarps = 8;          // each decodes 1/8 of every piece
+constexpr uint32_t kFlatConsumerWarps = 16;         // each decodes 1/16 of every piece
 constexpr uint32_t kFlatConsumers = kFlatConsumerWarps * 32;
 constexpr uint32_t kFlatThreads = kFlatConsumers + 32;  // + 1 producer warp
 constexpr uint32_t kFlatMaxRanges = 8;
@@ -348,10 +348,13 @@ __global__ void __launch_bounds__(kFlatThreads, 1) gemv_flat_tma_kernel(const __
 
   // ---- main loop, aligned cells ---------------------------------------------
   if constexpr (ALIGNED) {
-    const uint32_t NCPR = C / CW;         // column chunks per row (a multiple of 32, <= 256)
-    const uint32_t RG = NCT / NCPR;       // lanes groups over the rows of a cell
+    const uint32_t NCPR = C / CW;         // column chunks per row (a multiple of 32, <= NCT)
+    const uint32_t RG = NCT / NCPR;       // lane groups over the rows of a cell
     const uint32_t cc = tid % NCPR, rgp = tid / NCPR;
-    constexpr uint32_t SPAN = 32u / CPL;  // lanes per reduced row after the butterfly
+    const uint32_t RC = P.rc;             // rows per cell
+    constexpr uint32_t NV = 2 * CPL;      // values per lane per pair of cells
+    constexpr uint32_t SPAN = 32u / NV;   // lanes per reduced row after the butterfly
+    static_assert(NV == 2 || NV == 4, "two cells of 1 or 2 chunks per lane");
     f2x xr[CW / 2];
 #pragma unroll
     for (uint32_t q = 0; q < QPC; q++) {
@@ -360,59 +363,101 @@ __global__ void __launch_bounds__(kFlatThreads, 1) gemv_flat_tma_kernel(const __
       xr[2 * q + 1] = pack2(t.z, t.w);
     }
     const float xsm = xsc[cc];
-    uint32_t ri = 0;
-    for (uint32_t i = 0; i < npieces; i++) {
-      const uint32_t s = i % nst;
-      if (!mbar_wait_or_abort(&full[s], (i / nst) & 1u, &s_bad)) {
+    // this lane's chunks of a cell and their group-scale offsets are fixed
+    const uint32_t ci0 = rgp * NCPR + cc, cstep = RG * NCPR;
+    uint32_t soff[CPL];
+#pragma unroll
+    for (uint32_t kk = 0; kk < CPL; kk++) soff[kk] = 48u + 2u * (((ci0 + kk * cstep) * CW) >> 7);
+    // current range in registers; advanced when the piece index reaches the next one
+    uint32_t ri = 0, r_k0 = rg[0].k0, r_ps = rg[0].pstart, r_part = rg[0].part;
+    int32_t r_lrb = rg[0].lrbase;
+    uint32_t r_end = nranges > 1 ? rg[1].pstart : npieces;
+    auto cell_of = [&](uint32_t i, uint32_t& k, uint32_t& part, int32_t& lrb) {
+      if (i == r_end) {
+        ri++;
+        r_k0 = rg[ri].k0;
+        r_ps = rg[ri].pstart;
+        r_part = rg[ri].part;
+        r_lrb = rg[ri].lrbase;
+        r_end = ri + 1 < nranges ? rg[ri + 1].pstart : npieces;
+      }
+      k = r_k0 + (i - r_ps);
+      part = r_part;
+      lrb = r_lrb;
+    };
+    for (uint32_t i = 0; i < npieces; i += 2) {
+      const bool two = i + 1 < npieces;
+      const uint32_t sa = i % nst, sb = (i + 1) % nst;
+      bool ok = mbar_wait_or_abort(&full[sa], (i / nst) & 1u, &s_bad);
+      if (ok && two) ok = mbar_wait_or_abort(&full[sb], ((i + 1) / nst) & 1u, &s_bad);
+      if (!ok) {
         if (L == 0) { atomicExch(&P.st->err, 1); s_bad = 1; }
         break;
       }
-      uint32_t k, fa, fb;
-      locate(i, ri, k, fa, fb);
-      const uint8_t* stg = fsm + s * kFlatStageBytes;
-      const uint8_t* pl = stg + 16384;
-      float psc = 1.f, pbi = 0.f;
-      if constexpr (FI::SB) { psc = ld_f32(pl + 32); pbi = ld_f32(pl + 36); }
-      uint4 vv[CPL];
+      uint32_t ka, pa, kb = 0, pb = 0;
+      int32_t la, lb = 0;
+      cell_of(i, ka, pa, la);
+      if (two) cell_of(i + 1, kb, pb, lb);
+      const uint8_t* stg[2] = {fsm + sa * kFlatStageBytes, fsm + sb * kFlatStageBytes};
+      uint4 vv[NV];
+      float sc[NV];
 #pragma unroll
-      for (uint32_t kk = 0; kk < CPL; kk++)
-        vv[kk] = *reinterpret_cast<const uint4*>(stg + 16u * ((rgp + kk * RG) * NCPR + cc));
-      float v[CPL];
-#pragma unroll
-      for (uint32_t kk = 0; kk < CPL; kk++) {
-        const uint32_t ci = (rgp + kk * RG) * NCPR + cc;
-        f2x a0 = 0ull, a1 = 0ull;
-#pragma unroll
-        for (uint32_t q = 0; q < QPC; q++) quad_fma<FMT>(vv[kk], (int)q, xr[2 * q], xr[2 * q + 1], (q & 1) ? a1 : a0);
-        const float d = chunk_finish<FMT>(a0, a1, xsm);
-        if constexpr (FI::GROUPED) v[kk] = d * ld_f16(pl + 48 + 2 * ((ci * CW) >> 7));
-        else if constexpr (FI::SB) v[kk] = fmaf(pbi, xsm, d * psc);
-        else v[kk] = d;
+      for (uint32_t u = 0; u < NV; u++) {
+        const uint32_t c = u / CPL, kk = u % CPL;
+        const bool live = c == 0 || two;
+        vv[u] = live ? *reinterpret_cast<const uint4*>(stg[c] + 16u * (ci0 + kk * cstep)) : make_uint4(0u, 0u, 0u, 0u);
+        if constexpr (FI::GROUPED) sc[u] = live ? ld_f16(stg[c] + 16384 + soff[kk]) : 0.f;
+        else if constexpr (FI::SB) sc[u] = live ? ld_f32(stg[c] + 16384 + 32) : 0.f;
       }
-      // CPL row sums over the warp in one butterfly: after it, lane kk*SPAN
-      // holds the sum of row rgp + kk*RG
-      float b;
-      if constexpr (CPL == 4) {
+      float v[NV];
+#pragma unroll
+      for (uint32_t u = 0; u < NV; u++) {
+        f2x acc4[4] = {0ull, 0ull, 0ull, 0ull};  // four independent FMA chains per chunk
+#pragma unroll
+        for (uint32_t q = 0; q < QPC; q++) quad_fma<FMT>(vv[u], (int)q, xr[2 * q], xr[2 * q + 1], acc4[q & 3]);
+        if constexpr (QPC > 2) {
+          asm("add.rn.f32x2 %0, %0, %1;" : "+l"(acc4[0]) : "l"(acc4[2]));
+          asm("add.rn.f32x2 %0, %0, %1;" : "+l"(acc4[1]) : "l"(acc4[3]));
+        }
+        const float d = chunk_finish<FMT>(acc4[0], acc4[1], xsm);
+        if constexpr (FI::GROUPED) {
+          v[u] = d * sc[u];
+        } else if constexpr (FI::SB) {
+          const float bi = (u < CPL || two) ? ld_f32(stg[u / CPL] + 16384 + 36) : 0.f;
+          v[u] = fmaf(bi, xsm, d * sc[u]);
+        } else {
+          v[u] = d;
+        }
+      }
+      // NV row sums over the warp in one butterfly: afterwards lane u*SPAN
+      // holds the sum of value u (cell u / CPL, row rgp + (u % CPL) * RG)
+      float bsum;
+      if constexpr (NV == 4) {
         const bool h16 = (L & 16u) != 0, h8 = (L & 8u) != 0;
         const float a0 = (h16 ? v[2] : v[0]) + __shfl_xor_sync(0xffffffffu, h16 ? v[0] : v[2], 16);
         const float a1 = (h16 ? v[3] : v[1]) + __shfl_xor_sync(0xffffffffu, h16 ? v[1] : v[3], 16);
-        b = (h8 ? a1 : a0) + __shfl_xor_sync(0xffffffffu, h8 ? a0 : a1, 8);
+        bsum = (h8 ? a1 : a0) + __shfl_xor_sync(0xffffffffu, h8 ? a0 : a1, 8);
       } else {
-        static_assert(CPL == 2, "aligned cells hold 4 (4-bit) or 2 (2-bit) chunks per lane");
         const bool h16 = (L & 16u) != 0;
-        b = (h16 ? v[1] : v[0]) + __shfl_xor_sync(0xffffffffu, h16 ? v[0] : v[1], 16);
-        b += __shfl_xor_sync(0xffffffffu, b, 8);
+        bsum = (h16 ? v[1] : v[0]) + __shfl_xor_sync(0xffffffffu, h16 ? v[0] : v[1], 16);
+        bsum += __shfl_xor_sync(0xffffffffu, bsum, 8);
       }
-      b += __shfl_xor_sync(0xffffffffu, b, 4);
-      b += __shfl_xor_sync(0xffffffffu, b, 2);
-      b += __shfl_xor_sync(0xffffffffu, b, 1);
+      bsum += __shfl_xor_sync(0xffffffffu, bsum, 4);
+      bsum += __shfl_xor_sync(0xffffffffu, bsum, 2);
+      bsum += __shfl_xor_sync(0xffffffffu, bsum, 1);
       if ((L & (SPAN - 1u)) == 0u) {
-        const FlatRange& r = rg[ri];
-        const uint32_t row = (fa / C) + rgp + (L / SPAN) * RG;  // tensor row
-        wacc[(r.part * NW + warp) * P.rpc + (uint32_t)((int32_t)row + r.lrbase)] += b;
+        const uint32_t u = L / SPAN, c = u / CPL, kk = u % CPL;
+        if (c == 0 || two) {
+          const uint32_t row = (c ? kb : ka) * RC + rgp + kk * RG;  // tensor row
+          // each (warp, row) is written once per launch: a plain store
+          wacc[((c ? pb : pa) * NW + warp) * P.rpc + (uint32_t)((int32_t)row + (c ? lb : la))] = bsum;
+        }
       }
       __syncwarp();
-      if (L == 0) mbar_arrive(&empty[s]);
+      if (L == 0) {
+        mbar_arrive(&empty[sa]);
+        if (two) mbar_arrive(&empty[sb]);
+      }
     }
   } else {
   // ---- main loop, any flat stream --------------------------------------------

@@ -110,6 +110,16 @@ int chpe_validate_archive(const void *bytes, uint64_t len);
  * (the reference's ABI can only restart at 0).  Returns the argmax or -1. */
 int chpe_decode_step(void *ctx, uint32_t token, uint32_t pos, float *out_logits);
 
+/* Batch-M speculative verification (an extension; the reference has no such
+ * function): scores m candidate tokens at positions pos..pos+m-1 of the
+ * current sequence, candidate i seeing the KV entries of candidates < i
+ * (causal), which is exactly m forwardDecode steps.  out_logits gets
+ * [m][vocab] floats and out_argmax m ids (either may be NULL).  The cache
+ * keeps all m entries and the next position is pos+m (roll back by calling
+ * chpe_decode_step / chpe_verify at an earlier pos).  0, or -1 on error. */
+int chpe_verify(void *ctx, const uint32_t *toks, size_t m, uint32_t pos, float *out_logits,
+                uint32_t *out_argmax);
+
 /* Greedy generation on the device: runs the prompt from position 0, then
  * n_gen tokens, each the argmax of the step before, without host round
  * trips.  out_tokens receives n_gen ids.  0 on success, -1 on error. */
@@ -137,6 +147,13 @@ int chpe_bench_kernel(void *ctx, int role, int rounds, float *avg_ms, double *by
  * chpe_bench_kernel), e.g. "gemv_flat_tma_kernel<W4G,FLAT>"; "" when the
  * role has no op or ctx is NULL.  The string lives as long as ctx. */
 const char *chpe_role_kernel_name(void *ctx, int role);
+
+/* One greedy decode step launched op by op (not as the graph), with CUDA
+ * events between the ops: writes up to `cap` per-op milliseconds and roles
+ * (chpe_bench_kernel's numbering, 0 other) and returns the op count, -1 on
+ * error.  With tensor parallelism every rank calls it together.  Advances the
+ * position by one.  Needs a prior forward. */
+int chpe_profile_step(void *ctx, float *op_ms, int *op_roles, int cap);
 
 /* Algorithmic weight bytes one decode step of this context streams (codes
  * and scales of the rows its projections use; with tensor parallelism, this
