@@ -284,25 +284,27 @@ def run_ours(args, rank, world, local, dist):
                 "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                 "peak_kind": peak_kind, "traffic": traffic, "bytes_per_launch": kbytes,
                 "avg_launch_us": kms * 1000}
-    else:
+    # Per-role device time inside whole steps launched op by op with CUDA
+    # events between the ops (no graph, no overlap between kernels; with
+    # tensor parallelism every rank together, max over ranks).
+    names = {chpe.ROLE_QKV: "qkv", chpe.ROLE_ATTN: "attention", chpe.ROLE_O: "o",
+             chpe.ROLE_GATEUP: "gateup", chpe.ROLE_DOWN: "down", chpe.ROLE_LMHEAD: "lmhead"}
+    acc = {}
+    reps = 3
+    for _ in range(reps):
+        ms_ops, roles = eng.profile_step()
+        for m, r in zip(ms_ops, roles):
+            if int(r) in names:
+                a = acc.setdefault(names[int(r)], [0.0, 0])
+                a[0] += float(m)
+                a[1] += 1
+    per_role_step = {name: round(max_over_ranks(dist, tot / cnt) * 1000, 2) for name, (tot, cnt) in acc.items()}
+    if tp:
         # one role cannot run alone across ranks (its exchanges wait on the
-        # others): per-role times come from steps launched op by op with CUDA
-        # events between the ops (all ranks together; max over ranks), and the
-        # roofline here is the whole step's weight stream per GPU
-        names = {chpe.ROLE_QKV: "qkv", chpe.ROLE_ATTN: "attention", chpe.ROLE_O: "o",
-                 chpe.ROLE_GATEUP: "gateup", chpe.ROLE_DOWN: "down", chpe.ROLE_LMHEAD: "lmhead"}
-        acc = {}
-        reps = 3
-        for _ in range(reps):
-            ms_ops, roles = eng.profile_step()
-            for m, r in zip(ms_ops, roles):
-                if int(r) in names:
-                    a = acc.setdefault(names[int(r)], [0.0, 0])
-                    a[0] += float(m)
-                    a[1] += 1
-        for name, (tot, cnt) in acc.items():
-            per_role[name] = {"avg_us": round(max_over_ranks(dist, tot / cnt) * 1000, 2),
-                              "launches_per_step": cnt // reps, "bytes_per_launch": None, "gbs": None}
+        # others): the roofline here is the whole step's weight stream per GPU
+        for name, us in per_role_step.items():
+            per_role[name] = {"avg_us": us, "launches_per_step": acc[name][1] // reps,
+                              "bytes_per_launch": None, "gbs": None}
         mine = eng.step_weight_bytes()
         step_bytes = sum_over_ranks(dist, mine)
         per_gpu = max_over_ranks(dist, mine) / (ms_max / args.steps / 1000.0) / 1e9
@@ -337,7 +339,8 @@ def run_ours(args, rank, world, local, dist):
                    "algorithmic_bytes_per_token": step_bytes,
                    "weight_stream_gbs": step_bytes / (ms_step / 1000) / 1e9,
                    "weight_stream_frac_of_measured_hbm": step_bytes / (ms_step / 1000) / 1e9 / hbm,
-                   "per_role": per_role},
+                   "per_role": per_role,
+                   "per_role_in_step_us": per_role_step},
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": eng.vocab * 4 + 24},
         "roofline": roof,

@@ -689,6 +689,16 @@ void Engine::add_linear_ops(std::vector<Op>& ops, const GemvSrc* src, float* con
     const uint32_t budget = kFlatSmemLimit > fixed ? kFlatSmemLimit - fixed : 0u;
     uint32_t nst = budget / kFlatStageBytes;
     if (nst > kFlatStagesWanted) nst = kFlatStagesWanted;
+    // Column owners (rows that do not start at cell boundaries, no fused norm)
+    // are opt-in: measured slower than the stream mode on the down projections
+    // (two chunks per lane per row group do not amortise the group's bookkeeping).
+    t.mode = rc ? FLAT_ALIGNED : FLAT_STREAM;
+    {
+      const uint32_t cw = (uint32_t)fmt_cw(op.fmt), ncc = ncols / cw, sl = cw <= 32 ? 2u : 1u;
+      const char* co = getenv("CHPE_FLAT_COLOWN");
+      if (co && co[0] == '1' && !rc && !gamma && ncc >= 32 && ncc <= sl * kFlatConsumers && nst >= 4)
+        t.mode = FLAT_COLOWN;
+    }
     if (nst >= 2) {
       t.nst = nst;
       op.smem = flat_layout(ncols, cw, t.rpc, nparts, nst).total;
@@ -1205,9 +1215,9 @@ static void launch_tma(const Op& op, cudaStream_t s) {
   throw std::runtime_error("no TMA kernel for this format");
 }
 
-template <int FMT, int KIND, bool ALIGNED = false>
+template <int FMT, int KIND, int MODE = FLAT_STREAM>
 static void launch_flat_t(const Op& op, cudaStream_t s) {
-  auto k = gemv_flat_tma_kernel<FMT, KIND, ALIGNED>;
+  auto k = gemv_flat_tma_kernel<FMT, KIND, MODE>;
   static bool configured = false;
   if (!configured) {
     CK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFlatSmemLimit));
@@ -1217,12 +1227,25 @@ static void launch_flat_t(const Op& op, cudaStream_t s) {
 }
 
 static void launch_flat(const Op& op, cudaStream_t s) {
-  if (op.kind == SRC_FLAT && op.fl.rc) {
+  if (op.kind == SRC_FLAT && op.fl.mode == FLAT_ALIGNED) {
     switch (op.fmt) {
-      case FMT_W4G: return launch_flat_t<FMT_W4G, SRC_FLAT, true>(op, s);
-      case FMT_W4SB: return launch_flat_t<FMT_W4SB, SRC_FLAT, true>(op, s);
-      case FMT_W2G: return launch_flat_t<FMT_W2G, SRC_FLAT, true>(op, s);
-      case FMT_W2SB: return launch_flat_t<FMT_W2SB, SRC_FLAT, true>(op, s);
+      case FMT_W4G: return launch_flat_t<FMT_W4G, SRC_FLAT, FLAT_ALIGNED>(op, s);
+      case FMT_W4SB: return launch_flat_t<FMT_W4SB, SRC_FLAT, FLAT_ALIGNED>(op, s);
+      case FMT_W2G: return launch_flat_t<FMT_W2G, SRC_FLAT, FLAT_ALIGNED>(op, s);
+      case FMT_W2SB: return launch_flat_t<FMT_W2SB, SRC_FLAT, FLAT_ALIGNED>(op, s);
+    }
+  } else if (op.kind == SRC_FLAT && op.fl.mode == FLAT_COLOWN) {
+    switch (op.fmt) {
+      case FMT_W4G: return launch_flat_t<FMT_W4G, SRC_FLAT, FLAT_COLOWN>(op, s);
+      case FMT_W4SB: return launch_flat_t<FMT_W4SB, SRC_FLAT, FLAT_COLOWN>(op, s);
+      case FMT_W2G: return launch_flat_t<FMT_W2G, SRC_FLAT, FLAT_COLOWN>(op, s);
+      case FMT_W2SB: return launch_flat_t<FMT_W2SB, SRC_FLAT, FLAT_COLOWN>(op, s);
+    }
+  } else if (op.kind == SRC_RAW && op.fl.mode == FLAT_COLOWN) {
+    switch (op.fmt) {
+      case FMT_F16: return launch_flat_t<FMT_F16, SRC_RAW, FLAT_COLOWN>(op, s);
+      case FMT_BF16: return launch_flat_t<FMT_BF16, SRC_RAW, FLAT_COLOWN>(op, s);
+      case FMT_I8RAW: return launch_flat_t<FMT_I8RAW, SRC_RAW, FLAT_COLOWN>(op, s);
     }
   } else if (op.kind == SRC_FLAT) {
     switch (op.fmt) {
@@ -1290,7 +1313,10 @@ std::string Engine::role_kernel_name(int role) const {
     if (op.role != role) continue;
     const std::string fk = std::string("<") + fmt_name(op.fmt) + "," + kind_name(op.kind) + ">";
     switch (op.type) {
-      case OP_FLAT_TMA: return std::string(op.fl.rc ? "gemv_flat_tma_kernel[aligned]" : "gemv_flat_tma_kernel") + fk;
+      case OP_FLAT_TMA:
+        return std::string(op.fl.mode == FLAT_ALIGNED ? "gemv_flat_tma_kernel[aligned]"
+                           : op.fl.mode == FLAT_COLOWN ? "gemv_flat_tma_kernel[column owners]"
+                                                       : "gemv_flat_tma_kernel") + fk;
       case OP_TMA: return "gemv_tma_kernel" + fk;
       case OP_GEMV: return "gemv_kernel" + fk;
       case OP_ATTN: return "attention_kernel<" + std::to_string(op.hd) + ">";

@@ -49,6 +49,7 @@ struct FlatTmaLaunch {
   uint32_t rpc;            // max rows per CTA (size of the per-warp row slots)
   uint32_t nst;            // stages in the ring (<= kFlatMaxStages)
   uint32_t rc;             // aligned cells: rows per cell (32768 / cols); CTA rows are multiples
+  uint32_t mode;           // FlatMode the launch was planned for (host side)
   const float* x;          // hidden when norm != 0, else the input vector
   const float* gamma;
   float eps;
@@ -122,8 +123,17 @@ CHPE_DEV void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kFlatConsum
 // rc rows and consumer lane t always decodes the same column chunk t % (cols /
 // CW) of rows t / (cols / CW) + k * (256 / (cols / CW)): its x stays in
 // registers for the whole launch and shared memory carries only codes.
-template <int FMT, int KIND, bool ALIGNED = false>
+enum FlatMode : int { FLAT_STREAM = 0, FLAT_ALIGNED = 1, FLAT_COLOWN = 2 };
+
+// COLOWN ("column owner", any row width up to 1024 chunks, no fused norm):
+// consumer slot u = lane + 512*j owns column chunk u % (cols/CW) of row
+// u / (cols/CW) of every group of G = floor(slots / (cols/CW)) rows, keeps that
+// chunk's x in registers, and the CTA walks its rows group by group through
+// the ring (a group spans at most 2 tiles).  Used for the down projections
+// (29568, 12288, 11008 columns), whose rows do not start at cell boundaries.
+template <int FMT, int KIND, int MODE = FLAT_STREAM>
 __global__ void __launch_bounds__(kFlatThreads, 1) gemv_flat_tma_kernel(const __grid_constant__ FlatTmaLaunch P) {
+  constexpr bool ALIGNED = MODE == FLAT_ALIGNED;
   using FI = FmtInfo<FMT>;
   constexpr uint32_t CW = FI::CW, QPC = CW / 4;
   constexpr uint32_t WPP = flat_wpp<FMT, KIND>();
@@ -459,6 +469,112 @@ __global__ void __launch_bounds__(kFlatThreads, 1) gemv_flat_tma_kernel(const __
         if (two) mbar_arrive(&empty[sb]);
       }
     }
+  } else if constexpr (MODE == FLAT_COLOWN) {
+    // ---- main loop, column owners ------------------------------------------
+    const uint32_t NCC = C / CW;                         // chunks per row
+    constexpr uint32_t SL = CW <= 32 ? 2u : 1u;           // slots per lane
+    const uint32_t GR = (SL * NCT) / NCC;                // rows per group (host: >= 1)
+    const uint32_t active = GR * NCC;
+    uint32_t scc[SL], srow[SL];
+    f2x xr[SL][CW / 2];
+    float xs[SL];
+#pragma unroll
+    for (uint32_t j = 0; j < SL; j++) {
+      const uint32_t u = tid + NCT * j;
+      const uint32_t uu = u < active ? u : 0u;
+      scc[j] = uu % NCC;
+      srow[j] = u < active ? uu / NCC : 0xFFFFu;  // inactive slots never match a row
+#pragma unroll
+      for (uint32_t q = 0; q < QPC; q++) {
+        const float4 t = xquad<CW>(xsh, scc[j] >> 5, q, scc[j] & 31u);
+        xr[j][2 * q] = pack2(t.x, t.y);
+        xr[j][2 * q + 1] = pack2(t.z, t.w);
+      }
+      xs[j] = xsc[scc[j]];
+    }
+    // rows (within a group) of this warp's slots: at most two per slot
+    uint32_t wr0[SL];
+#pragma unroll
+    for (uint32_t j = 0; j < SL; j++) wr0[j] = (warp * 32u + NCT * j) / NCC;
+    uint32_t waited = 0, released = 0;  // pieces this warp waited for / released
+    bool bad = false;
+    for (uint32_t r = 0; r < nranges && !bad; r++) {
+      const FlatRange rgv = rg[r];
+      const uint32_t pend = r + 1 < nranges ? rg[r + 1].pstart : npieces;
+      const uint32_t ra = rgv.fa0 / C, rb = (rgv.fb0 + C - 1) / C;  // tensor rows touched
+      for (uint32_t g0 = ra; g0 < rb; g0 += GR) {
+        // pieces holding rows [g0, g0 + GR) of this range
+        const uint32_t fhi = min(rgv.fb0, (g0 + GR) * C);
+        const uint32_t p_hi = rgv.pstart + (fhi - 1u) / WPP - rgv.k0;
+        for (; waited <= p_hi; waited++)
+          if (!mbar_wait_or_abort(&full[waited % nst], (waited / nst) & 1u, &s_bad)) { bad = true; break; }
+        if (bad) break;
+        float v[2 * SL];
+#pragma unroll
+        for (uint32_t j = 0; j < SL; j++) {
+          const uint32_t row = g0 + srow[j];
+          const uint32_t f = row * C + scc[j] * CW;
+          const bool live = srow[j] < GR && row < rb && f >= rgv.fa0 && f < rgv.fb0;
+          float t = 0.f;
+          if (live) {
+            const uint32_t k = f / WPP, pi = rgv.pstart + k - rgv.k0;
+            const uint32_t fa_p = k * WPP > rgv.fa0 ? k * WPP : rgv.fa0;
+            const uint8_t* stg = fsm + (pi % nst) * kFlatStageBytes;
+            const uint4 cv = *reinterpret_cast<const uint4*>(stg + (f - fa_p) * FI::BITS / 8);
+            f2x acc4[4] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll
+            for (uint32_t q = 0; q < QPC; q++) quad_fma<FMT>(cv, (int)q, xr[j][2 * q], xr[j][2 * q + 1], acc4[q & 3]);
+            if constexpr (QPC > 2) {
+              asm("add.rn.f32x2 %0, %0, %1;" : "+l"(acc4[0]) : "l"(acc4[2]));
+              asm("add.rn.f32x2 %0, %0, %1;" : "+l"(acc4[1]) : "l"(acc4[3]));
+            }
+            const float d = chunk_finish<FMT>(acc4[0], acc4[1], xs[j]);
+            if constexpr (FI::GROUPED) t = d * ld_f16(stg + 16384 + 48 + 2 * ((f - k * WPP) >> 7));
+            else if constexpr (FI::SB) t = fmaf(ld_f32(stg + 16384 + 36), xs[j], d * ld_f32(stg + 16384 + 32));
+            else t = d;
+          }
+          // bin by the slot's row: first or second row of this warp's slots
+          const bool second = srow[j] != wr0[j];
+          v[2 * j] = second ? 0.f : t;
+          v[2 * j + 1] = second ? t : 0.f;
+        }
+        float bsum;
+        if constexpr (SL == 2) {
+          const bool h16 = (L & 16u) != 0, h8 = (L & 8u) != 0;
+          const float a0 = (h16 ? v[2] : v[0]) + __shfl_xor_sync(0xffffffffu, h16 ? v[0] : v[2], 16);
+          const float a1 = (h16 ? v[3] : v[1]) + __shfl_xor_sync(0xffffffffu, h16 ? v[1] : v[3], 16);
+          bsum = (h8 ? a1 : a0) + __shfl_xor_sync(0xffffffffu, h8 ? a0 : a1, 8);
+        } else {
+          const bool h16 = (L & 16u) != 0;
+          bsum = (h16 ? v[1] : v[0]) + __shfl_xor_sync(0xffffffffu, h16 ? v[0] : v[1], 16);
+          bsum += __shfl_xor_sync(0xffffffffu, bsum, 8);
+        }
+        bsum += __shfl_xor_sync(0xffffffffu, bsum, 4);
+        bsum += __shfl_xor_sync(0xffffffffu, bsum, 2);
+        bsum += __shfl_xor_sync(0xffffffffu, bsum, 1);
+        // lane 8b holds bin b (slot b/2, row wr0[slot] + b%2); lane 0 adds all
+        // bins in order (two bins may name the same row)
+        constexpr uint32_t NB = 2 * SL, SP = 32u / NB;
+        float bins[NB];
+#pragma unroll
+        for (uint32_t b = 0; b < NB; b++) bins[b] = __shfl_sync(0xffffffffu, bsum, b * SP);
+        if (L == 0) {
+          float* wrow = wacc + (rgv.part * NW + warp) * P.rpc;
+#pragma unroll
+          for (uint32_t b = 0; b < NB; b++) {
+            const uint32_t row = g0 + wr0[b / 2] + (b & 1u);
+            if (row < rb && wr0[b / 2] + (b & 1u) < GR) wrow[(uint32_t)((int32_t)row + rgv.lrbase)] += bins[b];
+          }
+        }
+        // release the pieces no later group of this warp needs
+        const uint32_t fnext = (g0 + GR) * C;
+        const uint32_t p_keep = (g0 + GR < rb && fnext < rgv.fb0) ? rgv.pstart + fnext / WPP - rgv.k0 : pend;
+        __syncwarp();
+        for (; released < p_keep; released++)
+          if (L == 0) mbar_arrive(&empty[released % nst]);
+      }
+    }
+    if (bad && L == 0) { atomicExch(&P.st->err, 1); s_bad = 1; }
   } else {
   // ---- main loop, any flat stream --------------------------------------------
   const uint32_t NCC = C / CW;  // chunks per row

@@ -118,8 +118,13 @@ FLAT_SHAPES = [(2048, 8192), (700, 29568), (4000, 4096), (1500, 12288), (9000, 2
                (3, 29568), (1, 4096), (700, 30000), (770, 29568), (2800, 8192), (8, 4096)]
 
 
+@pytest.mark.parametrize("colown", [False, True])
 @pytest.mark.parametrize("cfg", [chpe.SYNTH_3B_W4, chpe.SYNTH_3B_W2, chpe.SYNTH_3B_FP16_RAW])
-def test_gemv_flat_widths(cfg):
+def test_gemv_flat_widths(cfg, colown, monkeypatch):
+    # colown: the opt-in column-owner mode of the flat kernel for the widths
+    # whose rows do not start at cell boundaries (read when a call is planned)
+    if colown:
+        monkeypatch.setenv("CHPE_FLAT_COLOWN", "1")
     a, e, o = engines(cfg, 0)
     li = o.layer_info(4)
     rng = np.random.default_rng(17)
