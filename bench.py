@@ -370,6 +370,7 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    args.prompt_given = args.prompt is not None
     if args.prompt is None:
         args.prompt = MODELS[args.model]["prompt"]
     if args.kernel_only in ("flat-aligned", "flat-stream"):
@@ -389,8 +390,13 @@ def main():
         roles = {"qkv": chpe.ROLE_QKV, "attention": chpe.ROLE_ATTN, "o": chpe.ROLE_O,
                  "gateup": chpe.ROLE_GATEUP, "down": chpe.ROLE_DOWN, "lmhead": chpe.ROLE_LMHEAD}
         M = MODELS[args.model]
+        # --prompt given explicitly: decode that many tokens first, so the
+        # attention kernel runs at that context length
+        ctx = args.prompt if args.prompt_given else 0
         eng = chpe.Engine.from_bytes(chpe.synth_archive(getattr(chpe, M["synth"]), 0, seed=0),
-                                     getattr(chpe, M["arch"]), 64)
+                                     getattr(chpe, M["arch"]), ctx + 64)
+        if ctx:
+            eng.forward_tokens(np.random.default_rng(1).integers(0, 151936, ctx).astype(np.uint32))
         ms, b, n = eng.bench_kernel(roles[args.kernel_only], rounds=max(1, args.steps))
         print(json.dumps({"kernel": args.kernel_only, "avg_us": ms * 1000, "bytes_per_launch": b,
                           "gbs": b / (ms / 1000) / 1e9 if b else None, "launches": n}))

@@ -63,13 +63,16 @@ __global__ void __launch_bounds__(256) attention_kernel(const __grid_constant__ 
 template <int HD>
 CHPE_DEV void attention_body(const AttnLaunch& P) {
   constexpr int PER = HD / 32;     // head elements per lane
-  constexpr int KPAD = HD + 8;     // padded shared row (halves)
+  constexpr int KPAD = HD + 8;     // padded shared V row (halves, 16-byte rows)
+  // K rows are read lane-per-row: a 4-byte padding makes the row stride an
+  // odd number of words, so the 32 lanes of a score step hit 32 banks
+  constexpr int KPADK = HD + 2;
   const int G = P.H / P.KV;
   const int split = blockIdx.x, kvh = blockIdx.y;
   const int warp = threadIdx.x >> 5, L = threadIdx.x & 31;
   __shared__ float qs[8][HD];
   __shared__ float kn[HD], vn[HD];
-  __shared__ __align__(16) __half ks[ATT_TT][KPAD];
+  __shared__ __align__(16) __half ks[ATT_TT][KPADK];
   __shared__ __align__(16) __half vs[ATT_TT][KPAD];
   __shared__ float ps[8][ATT_TT];
   __shared__ int last_flag;
@@ -158,7 +161,13 @@ CHPE_DEV void attention_body(const AttnLaunch& P) {
       const int i = threadIdx.x + u * blockDim.x;
       if (i >= nt * VPR) continue;
       const int r = i / VPR, c8 = (i % VPR) * 8;
-      *reinterpret_cast<uint4*>(&ks[r][c8]) = kr[u];
+      {
+        uint32_t* kd = reinterpret_cast<uint32_t*>(&ks[r][c8]);  // 4-byte aligned rows
+        kd[0] = kr[u].x;
+        kd[1] = kr[u].y;
+        kd[2] = kr[u].z;
+        kd[3] = kr[u].w;
+      }
       *reinterpret_cast<uint4*>(&vs[r][c8]) = vr[u];
     }
     if (tb + ATT_TT < t1) fetch(tb + ATT_TT);
