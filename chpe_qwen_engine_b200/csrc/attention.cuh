@@ -25,7 +25,7 @@ struct AttnLaunch {
   __half* kc;           // this layer's K cache
   __half* vc;           // this layer's V cache
   float* out;           // [H*HD]
-  float* part;          // [KV][nsplit][G][HD + 2]
+  float* part;          // [KV][nsplit][G][HD + 4]: values, m, l, pad (16-byte records)
   uint32_t* counters;   // [KV], zero between steps
   const float* inv_freq;// [HD/2]
   StepState* st;
@@ -35,14 +35,15 @@ struct AttnLaunch {
 };
 
 constexpr int ATT_TT = 32;  // positions per staged tile
-// Splits of the positions per kv head: between 16 and 64, about one CTA per
-// SM over the kv heads a GPU holds.  The merge keeps one weight per split in
+// Splits of the positions per kv head: between 16 and 64, about two CTAs per
+// SM over the kv heads a GPU holds (a CTA needs 23-45 KB of shared memory and
+// 256 threads, so two are resident).  The merge keeps one weight per split in
 // two registers per lane, so at most 64.
 constexpr int kAttnSplits = 16;
 constexpr int kAttnMaxSplits = 64;
 static_assert(kAttnMaxSplits <= 64, "attention merge holds at most 64 split weights");
 inline int attn_splits(int num_sms, int kv_heads, int max_seq) {
-  int n = num_sms / (kv_heads > 0 ? kv_heads : 1);
+  int n = 2 * num_sms / (kv_heads > 0 ? kv_heads : 1);
   const int tiles = (max_seq + ATT_TT - 1) / ATT_TT;  // more splits than tiles only idle
   if (n > tiles) n = tiles;
   return n < kAttnSplits ? kAttnSplits : (n > kAttnMaxSplits ? kAttnMaxSplits : n);
@@ -52,7 +53,7 @@ template <int HD>
 CHPE_DEV void attention_body(const AttnLaunch& P);
 
 template <int HD>
-__global__ void __launch_bounds__(256) attention_kernel(const __grid_constant__ AttnLaunch P) {
+__global__ void __launch_bounds__(256, 2) attention_kernel(const __grid_constant__ AttnLaunch P) {
   attention_body<HD>(P);
   if (P.tp.world > 1) {  // every CTA arrives once, after any output it wrote
     __syncthreads();
@@ -198,18 +199,29 @@ CHPE_DEV void attention_body(const AttnLaunch& P) {
       for (int e = 0; e < PER; e++) acc[e] *= corr;
       for (int r = 0; r < nt; r++) {
         const float pr = ps[warp][r];
+        // this lane's PER contiguous dims: 8-byte shared loads of 4 halves
 #pragma unroll
-        for (int e = 0; e < PER; e++) acc[e] = fmaf(pr, __half2float(vs[r][L + 32 * e]), acc[e]);
+        for (int e4 = 0; e4 < PER; e4 += 4) {
+          const uint2 hv = *reinterpret_cast<const uint2*>(&vs[r][PER * L + e4]);
+          const float2 v01 = __half22float2(*reinterpret_cast<const __half2*>(&hv.x));
+          const float2 v23 = __half22float2(*reinterpret_cast<const __half2*>(&hv.y));
+          acc[e4] = fmaf(pr, v01.x, acc[e4]);
+          acc[e4 + 1] = fmaf(pr, v01.y, acc[e4 + 1]);
+          acc[e4 + 2] = fmaf(pr, v23.x, acc[e4 + 2]);
+          acc[e4 + 3] = fmaf(pr, v23.y, acc[e4 + 3]);
+        }
       }
       m = mn;
       __syncwarp();
     }
   }
+  constexpr int PS = HD + 4;  // partial record: HD values, m, l, pad (16-byte records)
   if (warp < G) {
-    float* dst = P.part + (((size_t)kvh * P.nsplit + split) * G + warp) * (HD + 2);
+    float* dst = P.part + (((size_t)kvh * P.nsplit + split) * G + warp) * PS;
 #pragma unroll
-    for (int e = 0; e < PER; e++) dst[L + 32 * e] = acc[e];
-    if (L == 0) { dst[HD] = m; dst[HD + 1] = l; }
+    for (int e4 = 0; e4 < PER; e4 += 4)
+      *reinterpret_cast<float4*>(dst + PER * L + e4) = make_float4(acc[e4], acc[e4 + 1], acc[e4 + 2], acc[e4 + 3]);
+    if (L == 0) *reinterpret_cast<float2*>(dst + HD) = make_float2(m, l);
   }
   __threadfence();
   __syncthreads();
@@ -221,49 +233,57 @@ CHPE_DEV void attention_body(const AttnLaunch& P) {
   if (!last_flag) return;
   __threadfence();
   if (warp < G) {
-    const float* src = P.part + ((size_t)kvh * P.nsplit * G + warp) * (HD + 2);
-    const size_t sstride = (size_t)G * (HD + 2);
-    float M = -INFINITY;
-    for (int s = L; s < P.nsplit; s += 32) M = fmaxf(M, __ldcg(src + s * sstride + HD));
-    M = warp_max(M);
-    float den = 0.f;
-    for (int s = L; s < P.nsplit; s += 32) {
-      float ms = __ldcg(src + s * sstride + HD);
-      if (ms != -INFINITY) den = fmaf(__ldcg(src + s * sstride + HD + 1), expf(ms - M), den);
-    }
-    den = warp_sum(den);
-    // weights of the splits, lanes over splits, then the values in batches of
-    // 8 splits whose loads are all issued before they are used
-    float wl[2];
+    const float* src = P.part + ((size_t)kvh * P.nsplit * G + warp) * PS;
+    const size_t sstride = (size_t)G * PS;
+    // (m, l) of splits L and L+32 in one round of loads
+    float2 ml[2];
 #pragma unroll
     for (int h = 0; h < 2; h++) {
       const int s = L + 32 * h;
-      const float ms = s < P.nsplit ? __ldcg(src + s * sstride + HD) : -INFINITY;
-      wl[h] = ms == -INFINITY ? 0.f : expf(ms - M);
+      ml[h] = s < P.nsplit ? __ldcg(reinterpret_cast<const float2*>(src + s * sstride + HD))
+                           : make_float2(-INFINITY, 0.f);
     }
+    const float M = warp_max(fmaxf(ml[0].x, ml[1].x));
+    float wl[2], den = 0.f;
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      wl[h] = ml[h].x == -INFINITY ? 0.f : expf(ml[h].x - M);
+      den = fmaf(ml[h].y, wl[h], den);
+    }
+    den = warp_sum(den);
+    // the values in batches of MB splits, every 16-byte load of a batch
+    // issued before any is used
+    constexpr int MB = PER == 4 ? 16 : 8;
     float o[PER];
 #pragma unroll
     for (int e = 0; e < PER; e++) o[e] = 0.f;
-    for (int s0 = 0; s0 < P.nsplit; s0 += 8) {
-      float a[8][PER];
+    for (int s0 = 0; s0 < P.nsplit; s0 += MB) {
+      float4 a[MB][PER / 4];
 #pragma unroll
-      for (int b = 0; b < 8; b++) {
+      for (int b = 0; b < MB; b++) {
         const int s = s0 + b;
 #pragma unroll
-        for (int e = 0; e < PER; e++) a[b][e] = s < P.nsplit ? __ldcg(src + s * sstride + L + 32 * e) : 0.f;
+        for (int e4 = 0; e4 < PER / 4; e4++)
+          a[b][e4] = s < P.nsplit ? __ldcg(reinterpret_cast<const float4*>(src + s * sstride + PER * L + 4 * e4))
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
       }
 #pragma unroll
-      for (int b = 0; b < 8; b++) {
+      for (int b = 0; b < MB; b++) {
         const int s = s0 + b;
         const float w = __shfl_sync(0xffffffffu, (s & 32) ? wl[1] : wl[0], s & 31);
 #pragma unroll
-        for (int e = 0; e < PER; e++) o[e] = fmaf(a[b][e], w, o[e]);
+        for (int e4 = 0; e4 < PER / 4; e4++) {
+          o[4 * e4] = fmaf(a[b][e4].x, w, o[4 * e4]);
+          o[4 * e4 + 1] = fmaf(a[b][e4].y, w, o[4 * e4 + 1]);
+          o[4 * e4 + 2] = fmaf(a[b][e4].z, w, o[4 * e4 + 2]);
+          o[4 * e4 + 3] = fmaf(a[b][e4].w, w, o[4 * e4 + 3]);
+        }
       }
     }
     const float inv = 1.0f / den;
     float* outp = P.out + (size_t)(kvh * G + warp) * HD;
 #pragma unroll
-    for (int e = 0; e < PER; e++) tp_put(P.tp, outp, L + 32 * e, o[e] * inv);
+    for (int e = 0; e < PER; e++) tp_put(P.tp, outp, PER * L + e, o[e] * inv);
   }
   if (threadIdx.x == 0) P.counters[kvh] = 0;
 }

@@ -58,7 +58,7 @@ extern "C" int chpe_attention_decode_noalloc(const float* q, const float* k, con
   if (head_dim != 128 && head_dim != 256) return fail(-1, "head_dim must be 128 or 256");
   if (pos >= max_seq_len) return fail(-1, "pos must be below max_seq_len");
   const uint32_t nsplit = chpe::kAttnSplits;
-  const size_t need = kPartOff + (size_t)num_kv_heads * nsplit * G * (head_dim + 2) * sizeof(float);
+  const size_t need = kPartOff + (size_t)num_kv_heads * nsplit * G * (head_dim + 4) * sizeof(float);
   if (need > kScratchBytes)
     return fail(-2, "needs " + std::to_string(need) + " bytes of scratch; the limit is " +
                         std::to_string(kScratchBytes));

@@ -275,7 +275,7 @@ Engine::Engine(const uint8_t* bytes, uint64_t len, int arch, uint32_t max_seq, i
   d_xn_ = (float*)dalloc(maxproj * 4);
   const int G = A.H / A.KV;
   nsplit_ = attn_splits(num_sms_, (int)A.KV, (int)max_seq_);
-  d_part_ = (float*)dalloc((size_t)A.KV * kAttnMaxSplits * G * (A.HD + 2) * 4);
+  d_part_ = (float*)dalloc((size_t)A.KV * kAttnMaxSplits * G * (A.HD + 4) * 4);
   d_counters_ = (uint32_t*)dalloc(A.KV * 4);
   size_t kv_elems = (size_t)A.L * max_seq_ * A.KV * A.HD;
   d_kc_ = (__half*)dalloc(kv_elems * 2);

@@ -375,9 +375,12 @@ __global__ void __launch_bounds__(kFlatThreads, 1) gemv_flat_tma_kernel(const __
     const float xsm = xsc[cc];
     // this lane's chunks of a cell and their group-scale offsets are fixed
     const uint32_t ci0 = rgp * NCPR + cc, cstep = RG * NCPR;
-    uint32_t soff[CPL];
+    uint32_t soff[CPL], coff[CPL];
 #pragma unroll
-    for (uint32_t kk = 0; kk < CPL; kk++) soff[kk] = 48u + 2u * (((ci0 + kk * cstep) * CW) >> 7);
+    for (uint32_t kk = 0; kk < CPL; kk++) {
+      coff[kk] = 16u * (ci0 + kk * cstep);                                 // code bytes in a stage
+      soff[kk] = 16384u + 48u + 2u * (((ci0 + kk * cstep) * CW) >> 7);    // its group scale
+    }
     // current range in registers; advanced when the piece index reaches the next one
     uint32_t ri = 0, r_k0 = rg[0].k0, r_ps = rg[0].pstart, r_part = rg[0].part;
     int32_t r_lrb = rg[0].lrbase;
@@ -408,16 +411,17 @@ __global__ void __launch_bounds__(kFlatThreads, 1) gemv_flat_tma_kernel(const __
       int32_t la, lb = 0;
       cell_of(i, ka, pa, la);
       if (two) cell_of(i + 1, kb, pb, lb);
-      const uint8_t* stg[2] = {fsm + sa * kFlatStageBytes, fsm + sb * kFlatStageBytes};
+      // an odd last cell is decoded twice (the second copy's sums are dropped):
+      // no branches around the loads
+      const uint8_t* stg[2] = {fsm + sa * kFlatStageBytes, fsm + (two ? sb : sa) * kFlatStageBytes};
       uint4 vv[NV];
       float sc[NV];
 #pragma unroll
       for (uint32_t u = 0; u < NV; u++) {
         const uint32_t c = u / CPL, kk = u % CPL;
-        const bool live = c == 0 || two;
-        vv[u] = live ? *reinterpret_cast<const uint4*>(stg[c] + 16u * (ci0 + kk * cstep)) : make_uint4(0u, 0u, 0u, 0u);
-        if constexpr (FI::GROUPED) sc[u] = live ? ld_f16(stg[c] + 16384 + soff[kk]) : 0.f;
-        else if constexpr (FI::SB) sc[u] = live ? ld_f32(stg[c] + 16384 + 32) : 0.f;
+        vv[u] = *reinterpret_cast<const uint4*>(stg[c] + coff[kk]);
+        if constexpr (FI::GROUPED) sc[u] = ld_f16(stg[c] + soff[kk]);
+        else if constexpr (FI::SB) sc[u] = ld_f32(stg[c] + 16384 + 32);
       }
       float v[NV];
 #pragma unroll
@@ -433,8 +437,7 @@ __global__ void __launch_bounds__(kFlatThreads, 1) gemv_flat_tma_kernel(const __
         if constexpr (FI::GROUPED) {
           v[u] = d * sc[u];
         } else if constexpr (FI::SB) {
-          const float bi = (u < CPL || two) ? ld_f32(stg[u / CPL] + 16384 + 36) : 0.f;
-          v[u] = fmaf(bi, xsm, d * sc[u]);
+          v[u] = fmaf(ld_f32(stg[u / CPL] + 16384 + 36), xsm, d * sc[u]);
         } else {
           v[u] = d;
         }
