@@ -61,6 +61,8 @@ SYMBOLS = [
     ("chpe_step_weight_bytes", C.c_double, [_P]),
     ("chpe_profile_step", _I, [_P, _FP, C.POINTER(C.c_int), _I]),
     ("chpe_verify", _I, [_P, _U32P, C.c_size_t, C.c_uint32, _FP, _U32P]),
+    ("chpe_deltanet_step", _I, [_P, _P, _P, _P, _P, _P, C.c_uint32, _P, _P, _P, _P, _P,
+                                C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_float, _P]),
     ("chpe_get_last_all_finite", _I, [_P]),
     ("chpe_kernels_per_step", _I, [_P]),
     ("chpe_get_position", _U32, [_P]),

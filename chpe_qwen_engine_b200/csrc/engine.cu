@@ -515,10 +515,37 @@ static double alg_bytes_of(const GemvSrc& s) {
   return 0.0;
 }
 
-void Engine::add_linear_ops(std::vector<Op>& ops, const GemvSrc* src, float* const* out, int nseg,
+void Engine::add_linear_ops(std::vector<Op>& ops, const GemvSrc* src_in, float* const* out, int nseg,
                             int epi, const float* x, const float* gamma, int check_layer,
                             uint32_t ncols, bool ignore_stop, const TpLink* tp) {
   const bool tp_on = tp && tp->world > 1;
+  // A row-tiled 2/4-bit cell of 16 rows x 2048 columns has the byte layout of
+  // a flat 32768-weight cell read at 2048 columns (codes row-major, group
+  // scale of (row, col) at 48 + 2*(row*16 + col/128)).  Without additive
+  // outliers and with every row covered, such tensors can take the flat
+  // kernel's aligned-cell mode; opt-in (CHPE_ROWTILE_AS_FLAT=1), as the
+  // row-block kernel measured faster on the 3B shapes.
+  GemvSrc srcv[3];
+  const char* raf = getenv("CHPE_ROWTILE_AS_FLAT");
+  bool as_flat = nseg <= 3 && raf && raf[0] == '1';
+  for (int i = 0; i < nseg && as_flat; i++) {
+    const GemvSrc& g = src_in[i];
+    as_flat = g.kind == SRC_ROWTILE &&
+              (g.fmt == FMT_W4G || g.fmt == FMT_W4SB || g.fmt == FMT_W2G || g.fmt == FMT_W2SB) &&
+              g.cell_rows == 16 && g.cell_cols == 2048 && g.c_total == 2048 && ncols == 2048 &&
+              g.outliers == OUTL_NONE && g.rows_covered == g.r_total && g.r_total % 16 == 0;
+  }
+  for (int i = 0; i < nseg && i < 3; i++) {
+    srcv[i] = src_in[i];
+    if (as_flat) {
+      srcv[i].kind = SRC_FLAT;
+      srcv[i].n_tiles = srcv[i].r_total / 16;
+      srcv[i].flat_limit = (uint64_t)srcv[i].n_tiles * 32768ull;
+      srcv[i].has_aux = 0;
+      srcv[i].row0 = 0;
+    }
+  }
+  const GemvSrc* src = nseg <= 3 ? srcv : src_in;
   const ChpeArch& A = *arch_;
   bool fused = true;
   for (int i = 0; i < nseg; i++) {

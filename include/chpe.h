@@ -110,6 +110,23 @@ int chpe_validate_archive(const void *bytes, uint64_t len);
  * (the reference's ABI can only restart at 0).  Returns the argmax or -1. */
 int chpe_decode_step(void *ctx, uint32_t token, uint32_t pos, float *out_logits);
 
+/* One decode step of a Qwen3.5 Gated DeltaNet (linear-attention) layer after
+ * its input projections, on the caller's device buffers (an extension: the
+ * reference runs these layers as GQA).  mixed_qkv [2*nk*128 + nv*128] (q|k|v
+ * before the conv), z [nv*128], a and b [nv]; conv_w [conv_dim][4] taps
+ * (oldest input first, 16-byte aligned); conv_hist [4][conv_dim] holds the
+ * inputs of position p in slot p % 4 (zero it at the start of a sequence);
+ * t is this token's position; A_log, dt_bias [nv]; norm_w [128]; state
+ * [nv][128][128] f32 per value head as [value j][key i], updated in place
+ * (16-byte aligned); out [nv*128] = gated-RMSNorm'ed output (the input of
+ * out_proj).  Head dims must be 128 and nv a multiple of nk.  Enqueued on
+ * `stream` (a cudaStream_t, or NULL); 0, or -1 for invalid arguments. */
+int chpe_deltanet_step(const float *mixed_qkv, const float *z, const float *a, const float *b,
+                       const float *conv_w, float *conv_hist, uint32_t t, const float *a_log,
+                       const float *dt_bias, const float *norm_w, float *state, float *out,
+                       uint32_t num_k_heads, uint32_t num_v_heads, uint32_t k_head_dim,
+                       uint32_t v_head_dim, float eps, void *stream);
+
 /* Batch-M speculative verification (an extension; the reference has no such
  * function): scores m candidate tokens at positions pos..pos+m-1 of the
  * current sequence, candidate i seeing the KV entries of candidates < i

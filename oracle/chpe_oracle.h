@@ -136,6 +136,13 @@ void oracle_gqa_attention(const float *q, const float *k_cache,
 /* Mock-archive path used by the reference's own engine tests
  * (chpe_engine.zig:1893-1933): the engine over `len` zero bytes. */
 
+/* One decode step of a Qwen3.5 Gated DeltaNet layer after its input
+ * projections (deltanet_oracle.c; no reference function exists). */
+void oracle_deltanet_step(const float *mixed_qkv, const float *z, const float *a, const float *b,
+                          const float *conv_w, float *conv_hist, uint32_t t, const float *a_log,
+                          const float *dt_bias, const float *norm_w, float *state, float *out,
+                          uint32_t nk, uint32_t nv, uint32_t dk, uint32_t dv, float eps);
+
 /* Tensor maps (as the reference tables give them). */
 void oracle_map_3b_cell_layer(size_t l, int64_t out[12]);
 void oracle_map_72b_layer(size_t l, int64_t out[12]);

@@ -62,6 +62,9 @@ def lib() -> C.CDLL:
         L = C.CDLL(LIB_PATH)
         P, F, S, I, U32, I64 = C.c_void_p, C.c_float, C.c_size_t, C.c_int, C.c_uint32, C.c_int64
         FP = C.POINTER(C.c_float)
+        L.oracle_deltanet_step.argtypes = [FP, FP, FP, FP, FP, FP, U32, FP, FP, FP, FP, FP,
+                                           U32, U32, U32, U32, F]
+        L.oracle_deltanet_step.restype = None
         L.oracle_validate.argtypes = [P, S, C.POINTER(Header)]
         L.oracle_validate.restype = I
         L.oracle_engine_new.argtypes = [P, S, I, S]
@@ -275,3 +278,19 @@ def map_72b_layer(l):
     o = (C.c_int64 * 12)()
     lib().oracle_map_72b_layer(l, o)
     return list(o)
+
+
+def deltanet_step(mixed, z, a, b, conv_w, conv_hist, t, a_log, dt_bias, norm_w, state,
+                  nk, nv, dk, dv, eps=1e-6):
+    """One Gated DeltaNet decode step (deltanet_oracle.c); conv_hist [4][conv_dim]
+    and state [nv][dv][dk] are updated in place.  Returns the output [nv*dv]."""
+    f = lambda x: np.ascontiguousarray(x, np.float32)
+    for arr in (conv_hist, state):
+        assert arr.dtype == np.float32 and arr.flags["C_CONTIGUOUS"]
+    ins = [f(mixed), f(z), f(a), f(b), f(conv_w)]
+    prm = [f(a_log), f(dt_bias), f(norm_w)]
+    out = np.zeros(nv * dv, np.float32)
+    lib().oracle_deltanet_step(fptr(ins[0]), fptr(ins[1]), fptr(ins[2]), fptr(ins[3]), fptr(ins[4]),
+                               fptr(conv_hist), t, fptr(prm[0]), fptr(prm[1]), fptr(prm[2]),
+                               fptr(state), fptr(out), nk, nv, dk, dv, eps)
+    return out

@@ -73,8 +73,13 @@ def _call_sites(o, l):
     ]
 
 
+@pytest.mark.parametrize("as_flat", [False, True])
 @pytest.mark.parametrize("cfg,flags", CELL_CONFIGS + [(chpe.SYNTH_3B_FP16_RAW, 0)])
-def test_gemv_linear_call_sites(cfg, flags):
+def test_gemv_linear_call_sites(cfg, flags, as_flat, monkeypatch):
+    # as_flat: the opt-in routing of 16x2048 row-tiled cells to the flat
+    # kernel's aligned-cell mode (read when a call is planned)
+    if as_flat:
+        monkeypatch.setenv("CHPE_ROWTILE_AS_FLAT", "1")
     a, e, o = engines(cfg, flags)
     rng = np.random.default_rng(11)
     for l in (0, 5, 21):

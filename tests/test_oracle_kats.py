@@ -207,3 +207,21 @@ def test_archive_validation_errors():
     assert O.validate(buf)[0] == 2
     buf[:64] = _hdr(header_bytes=8192)
     assert O.validate(buf)[0] == 10
+
+
+def test_deltanet_step_matches_transformers_golden():
+    """The Gated DeltaNet decode step (no reference function) against outputs
+    of the installed transformers package's Qwen3.5 functions
+    (tests/golden/gen_deltanet.py): three consecutive steps, outputs and the
+    final conv history and recurrent state."""
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "deltanet_step.npz"))
+    nk, nv, dk, dv, t0 = (int(g[k]) for k in ("nk", "nv", "dk", "dv", "t0"))
+    hist = g["hist0"].copy()
+    state = g["state0"].copy()
+    for s in range(g["mixed"].shape[0]):
+        out = O.deltanet_step(g["mixed"][s], g["z"][s], g["a"][s], g["b"][s], g["conv_w"], hist, t0 + s,
+                              g["a_log"], g["dt_bias"], g["norm_w"], state, nk, nv, dk, dv, float(g["eps"]))
+        ref = g["out"][s]
+        assert np.max(np.abs(out - ref)) <= 2e-5 * max(1.0, float(np.max(np.abs(ref)))), s
+    assert np.array_equal(hist, g["hist_end"])
+    assert np.max(np.abs(state - g["state_end"])) <= 1e-5 * max(1.0, float(np.max(np.abs(g["state_end"]))))
