@@ -33,6 +33,7 @@ enum OpType : int32_t {
 };
 constexpr int kTmaStages = 4;
 constexpr uint32_t kFlatSmemLimit = 227u * 1024u - 1024u;  // dynamic shared memory of one flat-TMA CTA
+constexpr uint32_t kFlatSmemHalf = 112u * 1024u;           // ... when two CTAs share an SM
 constexpr uint32_t kFlatStagesWanted = 12;
 
 // Roles of recorded ops (for per-kernel timing).
@@ -716,6 +717,21 @@ void Engine::add_linear_ops(std::vector<Op>& ops, const GemvSrc* src_in, float* 
     const uint32_t budget = kFlatSmemLimit > fixed ? kFlatSmemLimit - fixed : 0u;
     uint32_t nst = budget / kFlatStageBytes;
     if (nst > kFlatStagesWanted) nst = kFlatStagesWanted;
+    // Aligned launches whose shared memory fits twice per SM run 8 consumer
+    // warps per CTA and two CTAs per SM (grid up to twice the SMs).
+    uint32_t nw = 16, G8 = 0, rpc8 = 0, nst8 = 0;
+    {
+      const char* one = getenv("CHPE_FLAT_ONE_CTA");
+      if (rc && !(one && one[0] == '1') && (!gamma || ncols <= 8192)) {
+        G8 = Ut < 2u * (uint32_t)num_sms_ ? Ut : 2u * (uint32_t)num_sms_;
+        rpc8 = RU * ((Ut + G8 - 1) / G8);
+        const uint32_t f8 = flat_layout(ncols, cw, rpc8, nparts, 0, 8).total;
+        nst8 = kFlatSmemHalf > f8 ? (kFlatSmemHalf - f8) / kFlatStageBytes : 0u;
+        if (nst8 > kFlatStagesWanted) nst8 = kFlatStagesWanted;
+        if (nst8 >= 3) nw = 8;
+      }
+    }
+    t.nw = nw;
     // Column owners (rows that do not start at cell boundaries, no fused norm)
     // are opt-in: measured slower than the stream mode on the down projections
     // (two chunks per lane per row group do not amortise the group's bookkeeping).
@@ -725,6 +741,15 @@ void Engine::add_linear_ops(std::vector<Op>& ops, const GemvSrc* src_in, float* 
       const char* co = getenv("CHPE_FLAT_COLOWN");
       if (co && co[0] == '1' && !rc && !gamma && ncc >= 32 && ncc <= sl * kFlatConsumers && nst >= 4)
         t.mode = FLAT_COLOWN;
+    }
+    if (nw == 8) {
+      t.nst = nst8;
+      t.rpc = rpc8;
+      op.threads = (int)kFlatThreadsHalf;
+      op.smem = flat_layout(ncols, cw, rpc8, nparts, nst8, 8).total;
+      op.grid = dim3(G8);
+      ops.push_back(op);
+      return;
     }
     if (nst >= 2) {
       t.nst = nst;
@@ -1244,6 +1269,18 @@ static void launch_tma(const Op& op, cudaStream_t s) {
 
 template <int FMT, int KIND, int MODE = FLAT_STREAM>
 static void launch_flat_t(const Op& op, cudaStream_t s) {
+  if constexpr (MODE == FLAT_ALIGNED) {
+    if (op.fl.nw == 8) {
+      auto k8 = gemv_flat_tma_kernel<FMT, KIND, MODE, 8>;
+      static bool configured8 = false;
+      if (!configured8) {
+        CK(cudaFuncSetAttribute(k8, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFlatSmemHalf));
+        configured8 = true;
+      }
+      launch_pdl(k8, op.grid, dim3(kFlatThreadsHalf), op.smem, s, op.fl);
+      return;
+    }
+  }
   auto k = gemv_flat_tma_kernel<FMT, KIND, MODE>;
   static bool configured = false;
   if (!configured) {
@@ -1341,7 +1378,8 @@ std::string Engine::role_kernel_name(int role) const {
     const std::string fk = std::string("<") + fmt_name(op.fmt) + "," + kind_name(op.kind) + ">";
     switch (op.type) {
       case OP_FLAT_TMA:
-        return std::string(op.fl.mode == FLAT_ALIGNED ? "gemv_flat_tma_kernel[aligned]"
+        return std::string(op.fl.mode == FLAT_ALIGNED
+                               ? (op.fl.nw == 8 ? "gemv_flat_tma_kernel[aligned, 2 CTAs/SM]" : "gemv_flat_tma_kernel[aligned]")
                            : op.fl.mode == FLAT_COLOWN ? "gemv_flat_tma_kernel[column owners]"
                                                        : "gemv_flat_tma_kernel") + fk;
       case OP_TMA: return "gemv_tma_kernel" + fk;

@@ -50,6 +50,7 @@ struct FlatTmaLaunch {
   uint32_t nst;            // stages in the ring (<= kFlatMaxStages)
   uint32_t rc;             // aligned cells: rows per cell (32768 / cols); CTA rows are multiples
   uint32_t mode;           // FlatMode the launch was planned for (host side)
+  uint32_t nw;             // consumer warps the launch was planned for (16, or 8 for two CTAs per SM)
   const float* x;          // hidden when norm != 0, else the input vector
   const float* gamma;
   float eps;
@@ -66,9 +67,13 @@ struct FlatTmaLaunch {
 
 constexpr uint32_t kFlatStageBytes = 16384 + 896;  // codes + payload head (832) rounded to 128
 constexpr uint32_t kFlatMaxStages = 16;
+// Consumer warps per CTA: 16 (one CTA per SM), or 8 for aligned launches
+// whose shared memory fits twice per SM, so that the next launch's CTAs are
+// resident and streaming while this one's finish.
 constexpr uint32_t kFlatConsumerWarps = 16;         // each decodes 1/16 of every piece
 constexpr uint32_t kFlatConsumers = kFlatConsumerWarps * 32;
 constexpr uint32_t kFlatThreads = kFlatConsumers + 32;  // + 1 producer warp
+constexpr uint32_t kFlatThreadsHalf = 8 * 32 + 32;      // 8 consumer warps + 1 producer
 constexpr uint32_t kFlatMaxRanges = 8;
 
 struct FlatRange {
@@ -87,13 +92,13 @@ struct FlatLayout {
 
 // Shared-memory layout, shared by host (size) and kernel (offsets).
 __host__ __device__ inline FlatLayout flat_layout(uint32_t ncols, uint32_t cw, uint32_t rpc, uint32_t nparts,
-                                                  uint32_t nst) {
+                                                  uint32_t nst, uint32_t nw = kFlatConsumerWarps) {
   FlatLayout l;
   const uint32_t nchunks = ncols / cw, slots = (nchunks + 31) / 32;
   l.x = nst * kFlatStageBytes;
   l.xs = l.x + slots * 32 * cw * 4;
   l.wacc = l.xs + slots * 32 * 4;
-  l.bars = (l.wacc + nparts * kFlatConsumerWarps * rpc * 4 + 15) & ~15u;
+  l.bars = (l.wacc + nparts * nw * rpc * 4 + 15) & ~15u;
   l.ranges = l.bars + 2 * kFlatMaxStages * 8;
   l.total = l.ranges + kFlatMaxRanges * (uint32_t)sizeof(FlatRange);
   return l;
@@ -116,7 +121,8 @@ CHPE_DEV bool mbar_wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* b
 CHPE_DEV void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
-CHPE_DEV void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kFlatConsumers) : "memory"); }
+template <uint32_t NCT>
+CHPE_DEV void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(NCT) : "memory"); }
 
 // ALIGNED: flat cells whose rows start at cell boundaries (cols divides
 // 32768, as the 72B/9B hidden widths do).  Then every piece is a whole cell of
@@ -131,14 +137,16 @@ enum FlatMode : int { FLAT_STREAM = 0, FLAT_ALIGNED = 1, FLAT_COLOWN = 2 };
 // chunk's x in registers, and the CTA walks its rows group by group through
 // the ring (a group spans at most 2 tiles).  Used for the down projections
 // (29568, 12288, 11008 columns), whose rows do not start at cell boundaries.
-template <int FMT, int KIND, int MODE = FLAT_STREAM>
-__global__ void __launch_bounds__(kFlatThreads, 1) gemv_flat_tma_kernel(const __grid_constant__ FlatTmaLaunch P) {
+template <int FMT, int KIND, int MODE = FLAT_STREAM, int NWT = 16>
+__global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
+    gemv_flat_tma_kernel(const __grid_constant__ FlatTmaLaunch P) {
   constexpr bool ALIGNED = MODE == FLAT_ALIGNED;
   using FI = FmtInfo<FMT>;
   constexpr uint32_t CW = FI::CW, QPC = CW / 4;
   constexpr uint32_t WPP = flat_wpp<FMT, KIND>();
   constexpr uint32_t NCH = WPP / CW;        // chunks in a full piece
-  constexpr uint32_t NW = kFlatConsumerWarps, NCT = kFlatConsumers;
+  constexpr uint32_t NW = NWT, NCT = NWT * 32;
+  static_assert(NWT == 16 || (NWT == 8 && MODE == FLAT_ALIGNED), "8 consumer warps: aligned cells only");
   constexpr uint32_t CPWARP = NCH / NW;     // chunks per consumer warp
   constexpr uint32_t CPL = CPWARP / 32;     // chunks per lane
   static_assert(CPL >= 1 && CPWARP % 32 == 0, "piece geometry");
@@ -149,16 +157,16 @@ __global__ void __launch_bounds__(kFlatThreads, 1) gemv_flat_tma_kernel(const __
   const bool swig = P.epi == EPI_SWIGLU;
   const uint32_t nparts = swig ? 2u : 1u;
   const uint32_t C = P.ncols, nst = P.nst;
-  const FlatLayout lay = flat_layout(C, CW, P.rpc, nparts, nst);
+  const FlatLayout lay = flat_layout(C, CW, P.rpc, nparts, nst, NW);
   float* xsh = reinterpret_cast<float*>(fsm + lay.x);
   float* xsc = reinterpret_cast<float*>(fsm + lay.xs);
   float* wacc = reinterpret_cast<float*>(fsm + lay.wacc);
   uint64_t* full = reinterpret_cast<uint64_t*>(fsm + lay.bars);
   uint64_t* empty = full + kFlatMaxStages;
   FlatRange* rg = reinterpret_cast<FlatRange*>(fsm + lay.ranges);
-  __shared__ float sred[kFlatConsumerWarps];
-  __shared__ unsigned long long kbest[kFlatConsumerWarps];
-  __shared__ uint32_t kfin[kFlatConsumerWarps];
+  __shared__ float sred[NWT];
+  __shared__ unsigned long long kbest[NWT];
+  __shared__ uint32_t kfin[NWT];
   __shared__ uint32_t s_npieces, s_nranges;
   __shared__ int s_abort, s_is_last;
   __shared__ volatile int s_bad;
@@ -274,7 +282,7 @@ __global__ void __launch_bounds__(kFlatThreads, 1) gemv_flat_tma_kernel(const __
     }
     s_abort = ab;
   }
-  consumer_sync();
+  consumer_sync<NCT>();
   const bool stop = s_abort != 0;
   float tot = 0.f;
   const uint32_t nq = C / 4;
@@ -297,8 +305,9 @@ __global__ void __launch_bounds__(kFlatThreads, 1) gemv_flat_tma_kernel(const __
         }
       }
     } else {
-      // RMSNorm: x and gamma in one batch (the host sends cols <= 16384 here)
-      constexpr uint32_t XB = 16384u / 4u / NCT;
+      // RMSNorm: x and gamma in one batch (the host sends cols <= 16384 here,
+      // <= 8192 to the 8-warp variant)
+      constexpr uint32_t XB = (NWT == 8 ? 8192u : 16384u) / 4u / NCT;
       const float4* g4 = reinterpret_cast<const float4*>(P.gamma);
       float4 v[XB], g[XB];
       float ss = 0.f;
@@ -312,7 +321,7 @@ __global__ void __launch_bounds__(kFlatThreads, 1) gemv_flat_tma_kernel(const __
         if (tid + NCT * u < nq) ss += v[u].x * v[u].x + v[u].y * v[u].y + v[u].z * v[u].z + v[u].w * v[u].w;
       ss = warp_sum(ss);
       if (L == 0) sred[warp] = ss;
-      consumer_sync();
+      consumer_sync<NCT>();
       for (uint32_t w = 0; w < NW; w++) tot += sred[w];
       if (P.check_layer >= 0) {
         // end-of-layer check of the reference's debug block (chpe_engine.zig:1753-1764)
@@ -353,7 +362,7 @@ __global__ void __launch_bounds__(kFlatThreads, 1) gemv_flat_tma_kernel(const __
     }
     xsc[cc] = s;
   }
-  consumer_sync();
+  consumer_sync<NCT>();
   pdl_launch_dependents();
 
   // ---- main loop, aligned cells ---------------------------------------------
@@ -362,9 +371,10 @@ __global__ void __launch_bounds__(kFlatThreads, 1) gemv_flat_tma_kernel(const __
     const uint32_t RG = NCT / NCPR;       // lane groups over the rows of a cell
     const uint32_t cc = tid % NCPR, rgp = tid / NCPR;
     const uint32_t RC = P.rc;             // rows per cell
-    constexpr uint32_t NV = 2 * CPL;      // values per lane per pair of cells
+    constexpr uint32_t CPI = CPL >= 4 ? 1u : 2u;  // cells per iteration
+    constexpr uint32_t NV = CPI * CPL;    // values per lane per iteration
     constexpr uint32_t SPAN = 32u / NV;   // lanes per reduced row after the butterfly
-    static_assert(NV == 2 || NV == 4, "two cells of 1 or 2 chunks per lane");
+    static_assert(NV == 2 || NV == 4, "one or two cells of 1, 2 or 4 chunks per lane");
     f2x xr[CW / 2];
 #pragma unroll
     for (uint32_t q = 0; q < QPC; q++) {
@@ -398,8 +408,8 @@ __global__ void __launch_bounds__(kFlatThreads, 1) gemv_flat_tma_kernel(const __
       part = r_part;
       lrb = r_lrb;
     };
-    for (uint32_t i = 0; i < npieces; i += 2) {
-      const bool two = i + 1 < npieces;
+    for (uint32_t i = 0; i < npieces; i += CPI) {
+      const bool two = CPI == 2 && i + 1 < npieces;
       const uint32_t sa = i % nst, sb = (i + 1) % nst;
       bool ok = mbar_wait_or_abort(&full[sa], (i / nst) & 1u, &s_bad);
       if (ok && two) ok = mbar_wait_or_abort(&full[sb], ((i + 1) / nst) & 1u, &s_bad);
@@ -657,7 +667,7 @@ __global__ void __launch_bounds__(kFlatThreads, 1) gemv_flat_tma_kernel(const __
   }
   (void)failed;
   }  // any flat stream
-  consumer_sync();
+  consumer_sync<NCT>();
   if (s_bad) {
     if (tid == 0) tp_signal(P.tp, P.tp.signal_sig);
     return;
@@ -712,7 +722,7 @@ __global__ void __launch_bounds__(kFlatThreads, 1) gemv_flat_tma_kernel(const __
     }
     lfin = __all_sync(0xffffffffu, lfin != 0u) ? 1u : 0u;
     if (L == 0) { kbest[warp] = lbest; kfin[warp] = lfin; }
-    consumer_sync();
+    consumer_sync<NCT>();
     if (tid == 0) {
       unsigned long long b = 0ull;
       uint32_t f = 1u;
@@ -727,7 +737,7 @@ __global__ void __launch_bounds__(kFlatThreads, 1) gemv_flat_tma_kernel(const __
       __threadfence();
       s_is_last = atomicAdd(&P.st->done_ctas, 1u) == gridDim.x - 1;
     }
-    consumer_sync();
+    consumer_sync<NCT>();
     if (s_is_last && tid == 0) {
       float t0;
       if (P.tp.world > 1) {
@@ -743,7 +753,7 @@ __global__ void __launch_bounds__(kFlatThreads, 1) gemv_flat_tma_kernel(const __
     }
     return;
   }
-  consumer_sync();
+  consumer_sync<NCT>();
   if (tid == 0) tp_signal(P.tp, P.tp.signal_sig);
 }
 
