@@ -131,12 +131,11 @@ CHPE_DEV void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(NCT) : "mem
 // registers for the whole launch and shared memory carries only codes.
 enum FlatMode : int { FLAT_STREAM = 0, FLAT_ALIGNED = 1, FLAT_COLOWN = 2 };
 
-// COLOWN ("column owner", any row width up to 1024 chunks, no fused norm):
-// consumer slot u = lane + 512*j owns column chunk u % (cols/CW) of row
-// u / (cols/CW) of every group of G = floor(slots / (cols/CW)) rows, keeps that
-// chunk's x in registers, and the CTA walks its rows group by group through
-// the ring (a group spans at most 2 tiles).  Used for the down projections
-// (29568, 12288, 11008 columns), whose rows do not start at cell boundaries.
+// COLOWN ("column owner", rows of 513..1024 chunks, no fused norm): consumer
+// slot u = lane + 512*j owns column chunk u of every row, and the CTA walks its
+// rows four at a time through the ring, each x chunk read once per four rows.
+// Used for the 72B down projection (29568 columns), whose rows do not start
+// at cell boundaries.
 template <int FMT, int KIND, int MODE = FLAT_STREAM, int NWT = 16>
 __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
     gemv_flat_tma_kernel(const __grid_constant__ FlatTmaLaunch P) {
@@ -489,105 +488,89 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
     const uint32_t GR = (SL * NCT) / NCC;                // rows per group (host: >= 1)
     const uint32_t active = GR * NCC;
     uint32_t scc[SL], srow[SL];
-    f2x xr[SL][CW / 2];
-    float xs[SL];
 #pragma unroll
     for (uint32_t j = 0; j < SL; j++) {
       const uint32_t u = tid + NCT * j;
       const uint32_t uu = u < active ? u : 0u;
       scc[j] = uu % NCC;
       srow[j] = u < active ? uu / NCC : 0xFFFFu;  // inactive slots never match a row
-#pragma unroll
-      for (uint32_t q = 0; q < QPC; q++) {
-        const float4 t = xquad<CW>(xsh, scc[j] >> 5, q, scc[j] & 31u);
-        xr[j][2 * q] = pack2(t.x, t.y);
-        xr[j][2 * q + 1] = pack2(t.z, t.w);
-      }
-      xs[j] = xsc[scc[j]];
     }
-    // rows (within a group) of this warp's slots: at most two per slot
-    uint32_t wr0[SL];
+    {
+      // One row per group (rows longer than 512 chunks, the 72B down
+      // projection; the host sends no other width here): every active slot of
+      // a lane lies in the group's row, so four consecutive rows per
+      // iteration reuse each x load and share one 4-value butterfly.
+      constexpr uint32_t RI = 4;
+      uint32_t waited1 = 0, released1 = 0;
+      bool bad1 = false;
+      for (uint32_t r = 0; r < nranges && !bad1; r++) {
+        const FlatRange rgv = rg[r];
+        const uint32_t pend = r + 1 < nranges ? rg[r + 1].pstart : npieces;
+        const uint32_t ra = rgv.fa0 / C, rb = (rgv.fb0 + C - 1) / C;
+        for (uint32_t g0 = ra; g0 < rb; g0 += RI) {
+          const uint32_t g1 = g0 + RI < rb ? g0 + RI : rb;
+          const uint32_t fhi = min(rgv.fb0, g1 * C);
+          const uint32_t p_hi = rgv.pstart + (fhi - 1u) / WPP - rgv.k0;
+          for (; waited1 <= p_hi; waited1++)
+            if (!mbar_wait_or_abort(&full[waited1 % nst], (waited1 / nst) & 1u, &s_bad)) { bad1 = true; break; }
+          if (bad1) break;
+          float vrow[RI];
 #pragma unroll
-    for (uint32_t j = 0; j < SL; j++) wr0[j] = (warp * 32u + NCT * j) / NCC;
-    uint32_t waited = 0, released = 0;  // pieces this warp waited for / released
-    bool bad = false;
-    for (uint32_t r = 0; r < nranges && !bad; r++) {
-      const FlatRange rgv = rg[r];
-      const uint32_t pend = r + 1 < nranges ? rg[r + 1].pstart : npieces;
-      const uint32_t ra = rgv.fa0 / C, rb = (rgv.fb0 + C - 1) / C;  // tensor rows touched
-      for (uint32_t g0 = ra; g0 < rb; g0 += GR) {
-        // pieces holding rows [g0, g0 + GR) of this range
-        const uint32_t fhi = min(rgv.fb0, (g0 + GR) * C);
-        const uint32_t p_hi = rgv.pstart + (fhi - 1u) / WPP - rgv.k0;
-        for (; waited <= p_hi; waited++)
-          if (!mbar_wait_or_abort(&full[waited % nst], (waited / nst) & 1u, &s_bad)) { bad = true; break; }
-        if (bad) break;
-        float v[2 * SL];
+          for (uint32_t rr = 0; rr < RI; rr++) vrow[rr] = 0.f;
 #pragma unroll
-        for (uint32_t j = 0; j < SL; j++) {
-          const uint32_t row = g0 + srow[j];
-          const uint32_t f = row * C + scc[j] * CW;
-          const bool live = srow[j] < GR && row < rb && f >= rgv.fa0 && f < rgv.fb0;
-          float t = 0.f;
-          if (live) {
-            const uint32_t k = f / WPP, pi = rgv.pstart + k - rgv.k0;
-            const uint32_t fa_p = k * WPP > rgv.fa0 ? k * WPP : rgv.fa0;
-            const uint8_t* stg = fsm + (pi % nst) * kFlatStageBytes;
-            const uint4 cv = *reinterpret_cast<const uint4*>(stg + (f - fa_p) * FI::BITS / 8);
-            f2x acc4[4] = {0ull, 0ull, 0ull, 0ull};
+          for (uint32_t j = 0; j < SL; j++) {
+            // this slot's x: read once per iteration, used for its RI rows
+            f2x xq[CW / 2];
 #pragma unroll
-            for (uint32_t q = 0; q < QPC; q++) quad_fma<FMT>(cv, (int)q, xr[j][2 * q], xr[j][2 * q + 1], acc4[q & 3]);
-            if constexpr (QPC > 2) {
-              asm("add.rn.f32x2 %0, %0, %1;" : "+l"(acc4[0]) : "l"(acc4[2]));
-              asm("add.rn.f32x2 %0, %0, %1;" : "+l"(acc4[1]) : "l"(acc4[3]));
+            for (uint32_t q = 0; q < QPC; q++) {
+              const float4 t4 = xquad<CW>(xsh, scc[j] >> 5, q, scc[j] & 31u);
+              xq[2 * q] = pack2(t4.x, t4.y);
+              xq[2 * q + 1] = pack2(t4.z, t4.w);
             }
-            const float d = chunk_finish<FMT>(acc4[0], acc4[1], xs[j]);
-            if constexpr (FI::GROUPED) t = d * ld_f16(stg + 16384 + 48 + 2 * ((f - k * WPP) >> 7));
-            else if constexpr (FI::SB) t = fmaf(ld_f32(stg + 16384 + 36), xs[j], d * ld_f32(stg + 16384 + 32));
-            else t = d;
+            const float xsj = xsc[scc[j]];
+#pragma unroll
+            for (uint32_t rr = 0; rr < RI; rr++) {
+              const uint32_t row = g0 + rr;
+              const uint32_t f = row * C + scc[j] * CW;
+              if (srow[j] == 0u && row < g1 && f >= rgv.fa0 && f < rgv.fb0) {
+                const uint32_t k = f / WPP, pi = rgv.pstart + k - rgv.k0;
+                const uint32_t fa_p = k * WPP > rgv.fa0 ? k * WPP : rgv.fa0;
+                const uint8_t* stg = fsm + (pi % nst) * kFlatStageBytes;
+                const uint4 cv = *reinterpret_cast<const uint4*>(stg + (f - fa_p) * FI::BITS / 8);
+                f2x acc4[4] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll
+                for (uint32_t q = 0; q < QPC; q++) quad_fma<FMT>(cv, (int)q, xq[2 * q], xq[2 * q + 1], acc4[q & 3]);
+                if constexpr (QPC > 2) {
+                  asm("add.rn.f32x2 %0, %0, %1;" : "+l"(acc4[0]) : "l"(acc4[2]));
+                  asm("add.rn.f32x2 %0, %0, %1;" : "+l"(acc4[1]) : "l"(acc4[3]));
+                }
+                const float d = chunk_finish<FMT>(acc4[0], acc4[1], xsj);
+                if constexpr (FI::GROUPED) vrow[rr] += d * ld_f16(stg + 16384 + 48 + 2 * ((f - k * WPP) >> 7));
+                else if constexpr (FI::SB) vrow[rr] += fmaf(ld_f32(stg + 16384 + 36), xsj, d * ld_f32(stg + 16384 + 32));
+                else vrow[rr] += d;
+              }
+            }
           }
-          // bin by the slot's row: first or second row of this warp's slots
-          const bool second = srow[j] != wr0[j];
-          v[2 * j] = second ? 0.f : t;
-          v[2 * j + 1] = second ? t : 0.f;
-        }
-        float bsum;
-        if constexpr (SL == 2) {
           const bool h16 = (L & 16u) != 0, h8 = (L & 8u) != 0;
-          const float a0 = (h16 ? v[2] : v[0]) + __shfl_xor_sync(0xffffffffu, h16 ? v[0] : v[2], 16);
-          const float a1 = (h16 ? v[3] : v[1]) + __shfl_xor_sync(0xffffffffu, h16 ? v[1] : v[3], 16);
-          bsum = (h8 ? a1 : a0) + __shfl_xor_sync(0xffffffffu, h8 ? a0 : a1, 8);
-        } else {
-          const bool h16 = (L & 16u) != 0;
-          bsum = (h16 ? v[1] : v[0]) + __shfl_xor_sync(0xffffffffu, h16 ? v[0] : v[1], 16);
-          bsum += __shfl_xor_sync(0xffffffffu, bsum, 8);
-        }
-        bsum += __shfl_xor_sync(0xffffffffu, bsum, 4);
-        bsum += __shfl_xor_sync(0xffffffffu, bsum, 2);
-        bsum += __shfl_xor_sync(0xffffffffu, bsum, 1);
-        // lane 8b holds bin b (slot b/2, row wr0[slot] + b%2); lane 0 adds all
-        // bins in order (two bins may name the same row)
-        constexpr uint32_t NB = 2 * SL, SP = 32u / NB;
-        float bins[NB];
-#pragma unroll
-        for (uint32_t b = 0; b < NB; b++) bins[b] = __shfl_sync(0xffffffffu, bsum, b * SP);
-        if (L == 0) {
-          float* wrow = wacc + (rgv.part * NW + warp) * P.rpc;
-#pragma unroll
-          for (uint32_t b = 0; b < NB; b++) {
-            const uint32_t row = g0 + wr0[b / 2] + (b & 1u);
-            if (row < rb && wr0[b / 2] + (b & 1u) < GR) wrow[(uint32_t)((int32_t)row + rgv.lrbase)] += bins[b];
+          const float a0 = (h16 ? vrow[2] : vrow[0]) + __shfl_xor_sync(0xffffffffu, h16 ? vrow[0] : vrow[2], 16);
+          const float a1 = (h16 ? vrow[3] : vrow[1]) + __shfl_xor_sync(0xffffffffu, h16 ? vrow[1] : vrow[3], 16);
+          float bsum = (h8 ? a1 : a0) + __shfl_xor_sync(0xffffffffu, h8 ? a0 : a1, 8);
+          bsum += __shfl_xor_sync(0xffffffffu, bsum, 4);
+          bsum += __shfl_xor_sync(0xffffffffu, bsum, 2);
+          bsum += __shfl_xor_sync(0xffffffffu, bsum, 1);
+          if ((L & 7u) == 0u) {  // lane 8*rr holds row g0 + rr
+            const uint32_t row = g0 + (L >> 3);
+            if (row < g1) wacc[(rgv.part * NW + warp) * P.rpc + (uint32_t)((int32_t)row + rgv.lrbase)] += bsum;
           }
+          const uint32_t fnext = g1 * C;
+          const uint32_t p_keep = (g1 < rb && fnext < rgv.fb0) ? rgv.pstart + fnext / WPP - rgv.k0 : pend;
+          __syncwarp();
+          for (; released1 < p_keep; released1++)
+            if (L == 0) mbar_arrive(&empty[released1 % nst]);
         }
-        // release the pieces no later group of this warp needs
-        const uint32_t fnext = (g0 + GR) * C;
-        const uint32_t p_keep = (g0 + GR < rb && fnext < rgv.fb0) ? rgv.pstart + fnext / WPP - rgv.k0 : pend;
-        __syncwarp();
-        for (; released < p_keep; released++)
-          if (L == 0) mbar_arrive(&empty[released % nst]);
       }
+      if (bad1 && L == 0) { atomicExch(&P.st->err, 1); s_bad = 1; }
     }
-    if (bad && L == 0) { atomicExch(&P.st->err, 1); s_bad = 1; }
   } else {
   // ---- main loop, any flat stream --------------------------------------------
   const uint32_t NCC = C / CW;  // chunks per row
