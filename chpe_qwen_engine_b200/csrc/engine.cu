@@ -733,14 +733,15 @@ void Engine::add_linear_ops(std::vector<Op>& ops, const GemvSrc* src_in, float* 
     }
     t.nw = nw;
     // Column owners: rows of 513..1024 chunks that do not start at cell
-    // boundaries, no fused norm (the 72B down projection); CHPE_FLAT_COLOWN=0
-    // sends them to the stream mode instead.
+    // boundaries, no fused norm (the 72B down projection).  Opt-in with
+    // CHPE_FLAT_COLOWN=1: measured slower than the stream mode there (76.5 vs
+    // 65.6 us per 72B down launch).
     t.mode = rc ? FLAT_ALIGNED : FLAT_STREAM;
     {
       const uint32_t cw = (uint32_t)fmt_cw(op.fmt), ncc = ncols / cw, sl = cw <= 32 ? 2u : 1u;
       const char* co = getenv("CHPE_FLAT_COLOWN");
-      const bool off = co && co[0] == '0';
-      if (!off && !rc && !gamma && ncc > (sl * kFlatConsumers) / 2 && ncc <= sl * kFlatConsumers && nst >= 4)
+      const bool on = co && co[0] == '1';
+      if (on && !rc && !gamma && ncc > (sl * kFlatConsumers) / 2 && ncc <= sl * kFlatConsumers && nst >= 4)
         t.mode = FLAT_COLOWN;
     }
     if (nw == 8) {
