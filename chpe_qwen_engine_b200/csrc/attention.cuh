@@ -49,20 +49,23 @@ inline int attn_splits(int num_sms, int kv_heads, int max_seq) {
   return n < kAttnSplits ? kAttnSplits : (n > kAttnMaxSplits ? kAttnMaxSplits : n);
 }
 
+// Returns true on the CTA that reports this kv head to the other ranks: the
+// one that merged the splits (and wrote the head's outputs), or split 0 when
+// the step is skipped.
 template <int HD>
-CHPE_DEV void attention_body(const AttnLaunch& P);
+CHPE_DEV bool attention_body(const AttnLaunch& P);
 
 template <int HD>
 __global__ void __launch_bounds__(256, 2) attention_kernel(const __grid_constant__ AttnLaunch P) {
-  attention_body<HD>(P);
-  if (P.tp.world > 1) {  // every CTA arrives once, after any output it wrote
+  const bool reporter = attention_body<HD>(P);
+  if (P.tp.world > 1 && reporter) {  // one arrival per kv head, after its outputs
     __syncthreads();
     if (threadIdx.x == 0) tp_signal(P.tp, P.tp.signal_sig);
   }
 }
 
 template <int HD>
-CHPE_DEV void attention_body(const AttnLaunch& P) {
+CHPE_DEV bool attention_body(const AttnLaunch& P) {
   constexpr int PER = HD / 32;     // head elements per lane
   constexpr int KPAD = HD + 8;     // padded shared V row (halves, 16-byte rows)
   // K rows are read lane-per-row: a 4-byte padding makes the row stride an
@@ -79,9 +82,9 @@ CHPE_DEV void attention_body(const AttnLaunch& P) {
   __shared__ int last_flag;
 
   pdl_wait();
-  if (P.st->stop) return;
+  if (P.st->stop) return blockIdx.x == 0;
   const int pos = P.st->pos;
-  if (pos < 0 || pos >= P.max_seq) return;  // the host never schedules this
+  if (pos < 0 || pos >= P.max_seq) return blockIdx.x == 0;  // the host never schedules this
   const float pf = (float)pos;
 
   // RoPE on this warp's query head, on the new key; copy of the new value.
@@ -230,7 +233,7 @@ CHPE_DEV void attention_body(const AttnLaunch& P) {
     last_flag = (prev == (unsigned)P.nsplit - 1);
   }
   __syncthreads();
-  if (!last_flag) return;
+  if (!last_flag) return false;
   __threadfence();
   if (warp < G) {
     const float* src = P.part + ((size_t)kvh * P.nsplit * G + warp) * PS;
@@ -286,6 +289,7 @@ CHPE_DEV void attention_body(const AttnLaunch& P) {
     for (int e = 0; e < PER; e++) tp_put(P.tp, outp, PER * L + e, o[e] * inv);
   }
   if (threadIdx.x == 0) P.counters[kvh] = 0;
+  return true;
 }
 
 }  // namespace chpe

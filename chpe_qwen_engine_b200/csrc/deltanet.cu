@@ -51,7 +51,6 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_step_kernel(const DeltaN
   const uint32_t kh = h / (P.nv / P.nk);
   const uint32_t conv_dim = 2u * P.nk * kDk + P.nv * kDv;
   __shared__ float qs[kDk], ks[kDk], vs[kDv], os[kDv];
-  __shared__ float red[16];
   __shared__ float s_qn, s_kn, s_on;
 
   // ---- conv of this head's channels: q (0..127), k (128..255), v (256..383)
@@ -139,7 +138,6 @@ __global__ void __launch_bounds__(kThreads, 1) deltanet_step_kernel(const DeltaN
     const float zz = P.z[(size_t)h * kDv + tid];
     P.out[(size_t)h * kDv + tid] = os[tid] * s_on * P.norm_w[tid] * (zz * sigmoid_(zz));
   }
-  (void)red;
 }
 
 }  // namespace

@@ -526,7 +526,7 @@ void Engine::add_linear_ops(std::vector<Op>& ops, const GemvSrc* src_in, float* 
   // outliers and with every row covered, such tensors can take the flat
   // kernel's aligned-cell mode; opt-in (CHPE_ROWTILE_AS_FLAT=1), as the
   // row-block kernel measured faster on the 3B shapes.
-  GemvSrc srcv[3];
+  GemvSrc srcv[3] = {};
   const char* raf = getenv("CHPE_ROWTILE_AS_FLAT");
   bool as_flat = nseg <= 3 && raf && raf[0] == '1';
   for (int i = 0; i < nseg && as_flat; i++) {
@@ -1008,7 +1008,7 @@ void Engine::build_step_tp() {
   // arrivals per (step, layer) of each exchange: every rank launches the same
   // grids, so N x this rank's grid of the producing op
   const int nsp = attn_splits(num_sms_, (int)kvl, (int)max_seq_);
-  const unsigned long long u_att = (unsigned long long)N * nsp * kvl;
+  const unsigned long long u_att = (unsigned long long)N * kvl;  // one reporter CTA per kv head
   unsigned long long u_o = 0, u_gu = 0, u_dn = 0;
   auto units_of_last = [&]() { return (unsigned long long)N * ops.back().grid.x; };
   TpLink base{};
