@@ -732,17 +732,26 @@ void Engine::add_linear_ops(std::vector<Op>& ops, const GemvSrc* src_in, float* 
       }
     }
     t.nw = nw;
-    // Column owners: rows of 513..1024 chunks that do not start at cell
-    // boundaries, no fused norm (the 72B down projection).  Opt-in with
-    // CHPE_FLAT_COLOWN=1: measured slower than the stream mode there (76.5 vs
-    // 65.6 us per 72B down launch).
+    // Column owners: rows of 384..960 chunks (384..480 for 64-weight chunks,
+    // so that at least 4/5 of the first slots are busy) that do not start at
+    // cell boundaries, no fused norm (the down projections: 924 chunks on the
+    // 72B, 384 on the 9B; the 3B's 344 measured faster in the stream mode).
+    // x sits in registers, so the ring takes the shared memory x would have
+    // used.  CHPE_FLAT_COLOWN=0 keeps such calls on the stream mode.
     t.mode = rc ? FLAT_ALIGNED : FLAT_STREAM;
     {
-      const uint32_t cw = (uint32_t)fmt_cw(op.fmt), ncc = ncols / cw, sl = cw <= 32 ? 2u : 1u;
+      const uint32_t ncc = ncols / cw, sl = cw <= 32 ? 2u : 1u, lanes = kFlatColownWarps * 32u;
       const char* co = getenv("CHPE_FLAT_COLOWN");
-      const bool on = co && co[0] == '1';
-      if (on && !rc && !gamma && ncc > (sl * kFlatConsumers) / 2 && ncc <= sl * kFlatConsumers && nst >= 4)
+      const bool on = !(co && co[0] == '0');
+      const uint32_t fixed_co = flat_layout(ncols, cw, t.rpc, nparts, 0, kFlatColownWarps, false).total;
+      uint32_t nst_co = kFlatSmemLimit > fixed_co ? (kFlatSmemLimit - fixed_co) / kFlatStageBytes : 0u;
+      if (nst_co > kFlatStagesWanted) nst_co = kFlatStagesWanted;
+      if (on && !rc && !gamma && 5u * ncc >= 4u * lanes && ncc <= sl * lanes && nst_co >= 6) {
         t.mode = FLAT_COLOWN;
+        t.nw = kFlatColownWarps;
+        op.threads = (int)kFlatColownThreads;
+        nst = nst_co;
+      }
     }
     if (nw == 8) {
       t.nst = nst8;
@@ -755,7 +764,7 @@ void Engine::add_linear_ops(std::vector<Op>& ops, const GemvSrc* src_in, float* 
     }
     if (nst >= 2) {
       t.nst = nst;
-      op.smem = flat_layout(ncols, cw, t.rpc, nparts, nst).total;
+      op.smem = flat_layout(ncols, cw, t.rpc, nparts, nst, t.nw, t.mode != FLAT_COLOWN).total;
       op.grid = dim3(G);
       ops.push_back(op);
       for (int i = 0; i < nseg; i++) push_aux(src[i], epi == EPI_SWIGLU ? nullptr : out[i], gamma ? d_xn_ : x);
@@ -1283,13 +1292,14 @@ static void launch_flat_t(const Op& op, cudaStream_t s) {
       return;
     }
   }
-  auto k = gemv_flat_tma_kernel<FMT, KIND, MODE>;
+  constexpr int NWT = MODE == FLAT_COLOWN ? (int)kFlatColownWarps : 16;
+  auto k = gemv_flat_tma_kernel<FMT, KIND, MODE, NWT>;
   static bool configured = false;
   if (!configured) {
     CK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFlatSmemLimit));
     configured = true;
   }
-  launch_pdl(k, op.grid, dim3(kFlatThreads), op.smem, s, op.fl);
+  launch_pdl(k, op.grid, dim3(NWT * 32 + 32), op.smem, s, op.fl);
 }
 
 static void launch_flat(const Op& op, cudaStream_t s) {

@@ -74,6 +74,11 @@ constexpr uint32_t kFlatConsumerWarps = 16;         // each decodes 1/16 of ever
 constexpr uint32_t kFlatConsumers = kFlatConsumerWarps * 32;
 constexpr uint32_t kFlatThreads = kFlatConsumers + 32;  // + 1 producer warp
 constexpr uint32_t kFlatThreadsHalf = 8 * 32 + 32;      // 8 consumer warps + 1 producer
+// Column-owner launches run 15 consumer warps: 16 warps in all, four per
+// scheduler, which leaves each thread 128 registers (17 warps would cap it at
+// 96) for x in registers.
+constexpr uint32_t kFlatColownWarps = 15;
+constexpr uint32_t kFlatColownThreads = kFlatColownWarps * 32 + 32;
 constexpr uint32_t kFlatMaxRanges = 8;
 
 struct FlatRange {
@@ -90,11 +95,13 @@ struct FlatLayout {
   uint32_t x, xs, wacc, bars, ranges, total;
 };
 
-// Shared-memory layout, shared by host (size) and kernel (offsets).
+// Shared-memory layout, shared by host (size) and kernel (offsets).  xsm =
+// false (column owners: x lives in registers) leaves out x and its chunk sums.
 __host__ __device__ inline FlatLayout flat_layout(uint32_t ncols, uint32_t cw, uint32_t rpc, uint32_t nparts,
-                                                  uint32_t nst, uint32_t nw = kFlatConsumerWarps) {
+                                                  uint32_t nst, uint32_t nw = kFlatConsumerWarps,
+                                                  bool xsm = true) {
   FlatLayout l;
-  const uint32_t nchunks = ncols / cw, slots = (nchunks + 31) / 32;
+  const uint32_t nchunks = ncols / cw, slots = xsm ? (nchunks + 31) / 32 : 0u;
   l.x = nst * kFlatStageBytes;
   l.xs = l.x + slots * 32 * cw * 4;
   l.wacc = l.xs + slots * 32 * 4;
@@ -131,11 +138,12 @@ CHPE_DEV void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(NCT) : "mem
 // registers for the whole launch and shared memory carries only codes.
 enum FlatMode : int { FLAT_STREAM = 0, FLAT_ALIGNED = 1, FLAT_COLOWN = 2 };
 
-// COLOWN ("column owner", rows of 513..1024 chunks, no fused norm): consumer
-// slot u = lane + 512*j owns column chunk u of every row, and the CTA walks its
-// rows four at a time through the ring, each x chunk read once per four rows.
-// Used for the 72B down projection (29568 columns), whose rows do not start
-// at cell boundaries.
+// COLOWN ("column owner", rows of 384..960 chunks, no fused norm): consumer
+// slot u = lane + 480*j (15 consumer warps) owns column chunk u of every row, with that chunk of x
+// in registers for the whole launch (read once from global memory, so shared
+// memory holds only the ring), and the CTA walks its rows four at a time
+// through the ring.  For the 72B and 9B down projections (29568 and 12288
+// columns), whose rows do not start at cell boundaries.
 template <int FMT, int KIND, int MODE = FLAT_STREAM, int NWT = 16>
 __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
     gemv_flat_tma_kernel(const __grid_constant__ FlatTmaLaunch P) {
@@ -145,10 +153,11 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
   constexpr uint32_t WPP = flat_wpp<FMT, KIND>();
   constexpr uint32_t NCH = WPP / CW;        // chunks in a full piece
   constexpr uint32_t NW = NWT, NCT = NWT * 32;
-  static_assert(NWT == 16 || (NWT == 8 && MODE == FLAT_ALIGNED), "8 consumer warps: aligned cells only");
+  static_assert(MODE == FLAT_COLOWN ? NWT == (int)kFlatColownWarps : (NWT == 16 || (NWT == 8 && MODE == FLAT_ALIGNED)),
+                "consumer warps: 16; 8 for aligned cells at two CTAs per SM; 15 for column owners");
   constexpr uint32_t CPWARP = NCH / NW;     // chunks per consumer warp
   constexpr uint32_t CPL = CPWARP / 32;     // chunks per lane
-  static_assert(CPL >= 1 && CPWARP % 32 == 0, "piece geometry");
+  static_assert(MODE == FLAT_COLOWN || (CPL >= 1 && CPWARP % 32 == 0), "piece geometry");
   static_assert(NCH * 16 <= 16384, "a piece fits a stage");
 
   extern __shared__ __align__(128) uint8_t fsm[];
@@ -156,7 +165,8 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
   const bool swig = P.epi == EPI_SWIGLU;
   const uint32_t nparts = swig ? 2u : 1u;
   const uint32_t C = P.ncols, nst = P.nst;
-  const FlatLayout lay = flat_layout(C, CW, P.rpc, nparts, nst, NW);
+  constexpr bool XSM = MODE != FLAT_COLOWN;  // x staged in shared memory
+  const FlatLayout lay = flat_layout(C, CW, P.rpc, nparts, nst, NW, XSM);
   float* xsh = reinterpret_cast<float*>(fsm + lay.x);
   float* xsc = reinterpret_cast<float*>(fsm + lay.xs);
   float* wacc = reinterpret_cast<float*>(fsm + lay.wacc);
@@ -288,7 +298,9 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
   const float4* x4 = reinterpret_cast<const float4*>(P.x);
   if (!stop) {
     for (uint32_t i = tid; i < nparts * NW * P.rpc; i += NCT) wacc[i] = 0.f;
-    if (!P.norm) {
+    if (!XSM) {
+      // column owners load their x chunks into registers in the main loop
+    } else if (!P.norm) {
       // all loads of a batch in flight before any is stored
       for (uint32_t q0 = 0; q0 < nq; q0 += NCT * 8u) {
         float4 v[8];
@@ -306,7 +318,7 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
     } else {
       // RMSNorm: x and gamma in one batch (the host sends cols <= 16384 here,
       // <= 8192 to the 8-warp variant)
-      constexpr uint32_t XB = (NWT == 8 ? 8192u : 16384u) / 4u / NCT;
+      constexpr uint32_t XB = ((NWT == 8 ? 8192u : 16384u) / 4u + NCT - 1u) / NCT;
       const float4* g4 = reinterpret_cast<const float4*>(P.gamma);
       float4 v[XB], g[XB];
       float ss = 0.f;
@@ -352,7 +364,7 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
     if (tid == 0) tp_signal(P.tp, P.tp.signal_sig);  // every CTA arrives once per launch
     return;
   }
-  for (uint32_t cc = tid; cc < C / CW; cc += NCT) {
+  for (uint32_t cc = tid; XSM && cc < C / CW; cc += NCT) {
     float s = 0.f;
 #pragma unroll
     for (uint32_t q = 0; q < QPC; q++) {
@@ -483,94 +495,113 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
     }
   } else if constexpr (MODE == FLAT_COLOWN) {
     // ---- main loop, column owners ------------------------------------------
+    // One row per group (the host sends rows of 384..960 chunks for 16-byte
+    // chunks of 32 weights, 384..480 for 64): every active slot of a lane lies
+    // in the row, and four consecutive rows per iteration share one 4-value
+    // butterfly.
     const uint32_t NCC = C / CW;                         // chunks per row
     constexpr uint32_t SL = CW <= 32 ? 2u : 1u;           // slots per lane
-    const uint32_t GR = (SL * NCT) / NCC;                // rows per group (host: >= 1)
-    const uint32_t active = GR * NCC;
-    uint32_t scc[SL], srow[SL];
+    constexpr uint32_t RI = 4;                            // rows per iteration
+    f2x xr[SL][CW / 2];
+    float xsj[SL];
+    uint32_t scw[SL];                                     // first column of the slot
+    bool act[SL];
 #pragma unroll
     for (uint32_t j = 0; j < SL; j++) {
       const uint32_t u = tid + NCT * j;
-      const uint32_t uu = u < active ? u : 0u;
-      scc[j] = uu % NCC;
-      srow[j] = u < active ? uu / NCC : 0xFFFFu;  // inactive slots never match a row
-    }
-    {
-      // One row per group (rows longer than 512 chunks, the 72B down
-      // projection; the host sends no other width here): every active slot of
-      // a lane lies in the group's row, so four consecutive rows per
-      // iteration reuse each x load and share one 4-value butterfly.
-      constexpr uint32_t RI = 4;
-      uint32_t waited1 = 0, released1 = 0;
-      bool bad1 = false;
-      for (uint32_t r = 0; r < nranges && !bad1; r++) {
-        const FlatRange rgv = rg[r];
-        const uint32_t pend = r + 1 < nranges ? rg[r + 1].pstart : npieces;
-        const uint32_t ra = rgv.fa0 / C, rb = (rgv.fb0 + C - 1) / C;
-        for (uint32_t g0 = ra; g0 < rb; g0 += RI) {
-          const uint32_t g1 = g0 + RI < rb ? g0 + RI : rb;
-          const uint32_t fhi = min(rgv.fb0, g1 * C);
-          const uint32_t p_hi = rgv.pstart + (fhi - 1u) / WPP - rgv.k0;
-          for (; waited1 <= p_hi; waited1++)
-            if (!mbar_wait_or_abort(&full[waited1 % nst], (waited1 / nst) & 1u, &s_bad)) { bad1 = true; break; }
-          if (bad1) break;
-          float vrow[RI];
+      act[j] = u < NCC;
+      scw[j] = (act[j] ? u : 0u) * CW;
+      const float4* xp = reinterpret_cast<const float4*>(P.x + scw[j]);
+      float4 t4[QPC];
 #pragma unroll
-          for (uint32_t rr = 0; rr < RI; rr++) vrow[rr] = 0.f;
+      for (uint32_t q = 0; q < QPC; q++) t4[q] = act[j] ? xp[q] : make_float4(0.f, 0.f, 0.f, 0.f);
+      float sx = 0.f;
 #pragma unroll
-          for (uint32_t j = 0; j < SL; j++) {
-            // this slot's x: read once per iteration, used for its RI rows
-            f2x xq[CW / 2];
-#pragma unroll
-            for (uint32_t q = 0; q < QPC; q++) {
-              const float4 t4 = xquad<CW>(xsh, scc[j] >> 5, q, scc[j] & 31u);
-              xq[2 * q] = pack2(t4.x, t4.y);
-              xq[2 * q + 1] = pack2(t4.z, t4.w);
-            }
-            const float xsj = xsc[scc[j]];
-#pragma unroll
-            for (uint32_t rr = 0; rr < RI; rr++) {
-              const uint32_t row = g0 + rr;
-              const uint32_t f = row * C + scc[j] * CW;
-              if (srow[j] == 0u && row < g1 && f >= rgv.fa0 && f < rgv.fb0) {
-                const uint32_t k = f / WPP, pi = rgv.pstart + k - rgv.k0;
-                const uint32_t fa_p = k * WPP > rgv.fa0 ? k * WPP : rgv.fa0;
-                const uint8_t* stg = fsm + (pi % nst) * kFlatStageBytes;
-                const uint4 cv = *reinterpret_cast<const uint4*>(stg + (f - fa_p) * FI::BITS / 8);
-                f2x acc4[4] = {0ull, 0ull, 0ull, 0ull};
-#pragma unroll
-                for (uint32_t q = 0; q < QPC; q++) quad_fma<FMT>(cv, (int)q, xq[2 * q], xq[2 * q + 1], acc4[q & 3]);
-                if constexpr (QPC > 2) {
-                  asm("add.rn.f32x2 %0, %0, %1;" : "+l"(acc4[0]) : "l"(acc4[2]));
-                  asm("add.rn.f32x2 %0, %0, %1;" : "+l"(acc4[1]) : "l"(acc4[3]));
-                }
-                const float d = chunk_finish<FMT>(acc4[0], acc4[1], xsj);
-                if constexpr (FI::GROUPED) vrow[rr] += d * ld_f16(stg + 16384 + 48 + 2 * ((f - k * WPP) >> 7));
-                else if constexpr (FI::SB) vrow[rr] += fmaf(ld_f32(stg + 16384 + 36), xsj, d * ld_f32(stg + 16384 + 32));
-                else vrow[rr] += d;
-              }
-            }
-          }
-          const bool h16 = (L & 16u) != 0, h8 = (L & 8u) != 0;
-          const float a0 = (h16 ? vrow[2] : vrow[0]) + __shfl_xor_sync(0xffffffffu, h16 ? vrow[0] : vrow[2], 16);
-          const float a1 = (h16 ? vrow[3] : vrow[1]) + __shfl_xor_sync(0xffffffffu, h16 ? vrow[1] : vrow[3], 16);
-          float bsum = (h8 ? a1 : a0) + __shfl_xor_sync(0xffffffffu, h8 ? a0 : a1, 8);
-          bsum += __shfl_xor_sync(0xffffffffu, bsum, 4);
-          bsum += __shfl_xor_sync(0xffffffffu, bsum, 2);
-          bsum += __shfl_xor_sync(0xffffffffu, bsum, 1);
-          if ((L & 7u) == 0u) {  // lane 8*rr holds row g0 + rr
-            const uint32_t row = g0 + (L >> 3);
-            if (row < g1) wacc[(rgv.part * NW + warp) * P.rpc + (uint32_t)((int32_t)row + rgv.lrbase)] += bsum;
-          }
-          const uint32_t fnext = g1 * C;
-          const uint32_t p_keep = (g1 < rb && fnext < rgv.fb0) ? rgv.pstart + fnext / WPP - rgv.k0 : pend;
-          __syncwarp();
-          for (; released1 < p_keep; released1++)
-            if (L == 0) mbar_arrive(&empty[released1 % nst]);
-        }
+      for (uint32_t q = 0; q < QPC; q++) {
+        xr[j][2 * q] = pack2(t4[q].x, t4[q].y);
+        xr[j][2 * q + 1] = pack2(t4[q].z, t4[q].w);
+        sx += (t4[q].x + t4[q].y) + (t4[q].z + t4[q].w);
       }
-      if (bad1 && L == 0) { atomicExch(&P.st->err, 1); s_bad = 1; }
+      xsj[j] = sx;
     }
+    uint32_t waited = 0, released = 0;
+    bool bad = false;
+    for (uint32_t r = 0; r < nranges && !bad; r++) {
+      const FlatRange rgv = rg[r];
+      const uint32_t pend = r + 1 < nranges ? rg[r + 1].pstart : npieces;
+      const uint32_t pbase = rgv.pstart - rgv.k0;        // piece of tile k: pbase + k
+      const uint32_t ra = rgv.fa0 / C, rb = (rgv.fb0 + C - 1) / C;
+      for (uint32_t g0 = ra; g0 < rb; g0 += RI) {
+        const uint32_t g1 = g0 + RI < rb ? g0 + RI : rb;
+        const uint32_t flo = g0 * C > rgv.fa0 ? g0 * C : rgv.fa0;
+        const uint32_t fhi = g1 * C < rgv.fb0 ? g1 * C : rgv.fb0;
+        const uint32_t p_lo = pbase + flo / WPP, p_hi = pbase + (fhi - 1u) / WPP;
+        for (; waited <= p_hi; waited++)
+          if (!mbar_wait_or_abort(&full[waited % nst], (waited / nst) & 1u, &s_bad)) { bad = true; break; }
+        if (bad) break;
+        const uint32_t s_lo = p_lo % nst;                // ring slot of piece p_lo
+        float vrow[RI];
+#pragma unroll
+        for (uint32_t rr = 0; rr < RI; rr++) vrow[rr] = 0.f;
+#pragma unroll
+        for (uint32_t j = 0; j < SL; j++) {
+          if (warp * 32u + NCT * j >= NCC) continue;  // no active slot j in this warp
+          // the slot's chunk of RI rows: every load issued before the decode;
+          // a chunk outside the group reads the first piece's bytes and adds 0
+          uint4 cv[RI];
+          float sc[RI], bi[RI];
+          bool ok[RI];
+          uint32_t f = g0 * C + scw[j];
+#pragma unroll
+          for (uint32_t rr = 0; rr < RI; rr++, f += C) {
+            ok[rr] = act[j] && g0 + rr < g1 && f >= rgv.fa0 && f < rgv.fb0;
+            const uint32_t k = f / WPP, t0 = k * WPP;
+            uint32_t sidx = s_lo + (pbase + k - p_lo);
+            if (sidx >= nst) sidx -= nst;
+            const uint32_t fa_p = t0 > rgv.fa0 ? t0 : rgv.fa0;  // first weight of the piece
+            const uint8_t* stg = fsm + (ok[rr] ? sidx : s_lo) * kFlatStageBytes;
+            cv[rr] = *reinterpret_cast<const uint4*>(stg + (ok[rr] ? (f - fa_p) * FI::BITS / 8 : 0u));
+            if constexpr (FI::GROUPED) sc[rr] = ld_f16(stg + 16384 + 48 + (ok[rr] ? 2 * ((f - t0) >> 7) : 0u));
+            else if constexpr (FI::SB) { sc[rr] = ld_f32(stg + 16384 + 32); bi[rr] = ld_f32(stg + 16384 + 36); }
+          }
+#pragma unroll
+          for (uint32_t rr = 0; rr < RI; rr++) {
+            f2x acc4[4] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll
+            for (uint32_t q = 0; q < QPC; q++) quad_fma<FMT>(cv[rr], (int)q, xr[j][2 * q], xr[j][2 * q + 1], acc4[q & 3]);
+            if constexpr (QPC > 2) {
+              asm("add.rn.f32x2 %0, %0, %1;" : "+l"(acc4[0]) : "l"(acc4[2]));
+              asm("add.rn.f32x2 %0, %0, %1;" : "+l"(acc4[1]) : "l"(acc4[3]));
+            }
+            const float d = chunk_finish<FMT>(acc4[0], acc4[1], xsj[j]);
+            float t;
+            if constexpr (FI::GROUPED) t = d * sc[rr];
+            else if constexpr (FI::SB) t = fmaf(bi[rr], xsj[j], d * sc[rr]);
+            else t = d;
+            vrow[rr] += ok[rr] ? t : 0.f;
+          }
+          (void)bi;
+        }
+        const bool h16 = (L & 16u) != 0, h8 = (L & 8u) != 0;
+        const float a0 = (h16 ? vrow[2] : vrow[0]) + __shfl_xor_sync(0xffffffffu, h16 ? vrow[0] : vrow[2], 16);
+        const float a1 = (h16 ? vrow[3] : vrow[1]) + __shfl_xor_sync(0xffffffffu, h16 ? vrow[1] : vrow[3], 16);
+        float bsum = (h8 ? a1 : a0) + __shfl_xor_sync(0xffffffffu, h8 ? a0 : a1, 8);
+        bsum += __shfl_xor_sync(0xffffffffu, bsum, 4);
+        bsum += __shfl_xor_sync(0xffffffffu, bsum, 2);
+        bsum += __shfl_xor_sync(0xffffffffu, bsum, 1);
+        if ((L & 7u) == 0u) {  // lane 8*rr holds row g0 + rr
+          const uint32_t row = g0 + (L >> 3);
+          if (row < g1) wacc[(rgv.part * NW + warp) * P.rpc + (uint32_t)((int32_t)row + rgv.lrbase)] += bsum;
+        }
+        // pieces wholly before the next group's first weight are done
+        const uint32_t fnext = g1 * C;
+        const uint32_t p_keep = (g1 < rb && fnext < rgv.fb0) ? pbase + fnext / WPP : pend;
+        __syncwarp();
+        for (; released < p_keep; released++)
+          if (L == 0) mbar_arrive(&empty[released % nst]);
+      }
+    }
+    if (bad && L == 0) { atomicExch(&P.st->err, 1); s_bad = 1; }
   } else {
   // ---- main loop, any flat stream --------------------------------------------
   const uint32_t NCC = C / CW;  // chunks per row

@@ -126,10 +126,10 @@ FLAT_SHAPES = [(2048, 8192), (700, 29568), (4000, 4096), (1500, 12288), (9000, 2
 @pytest.mark.parametrize("colown", [False, True])
 @pytest.mark.parametrize("cfg", [chpe.SYNTH_3B_W4, chpe.SYNTH_3B_W2, chpe.SYNTH_3B_FP16_RAW])
 def test_gemv_flat_widths(cfg, colown, monkeypatch):
-    # colown: the opt-in column-owner mode for rows of 513..1024 chunks
-    # (e.g. 29568 4-bit columns); read when a call is planned
-    if colown:
-        monkeypatch.setenv("CHPE_FLAT_COLOWN", "1")
+    # colown: the column-owner mode (default for rows of 384..960 16-byte
+    # chunks, e.g. 29568 4-bit columns) or, with CHPE_FLAT_COLOWN=0, the
+    # stream mode for the same calls; read when a call is planned
+    monkeypatch.setenv("CHPE_FLAT_COLOWN", "1" if colown else "0")
     a, e, o = engines(cfg, 0)
     li = o.layer_info(4)
     rng = np.random.default_rng(17)
