@@ -690,7 +690,36 @@ void Engine::add_linear_ops(std::vector<Op>& ops, const GemvSrc* src_in, float* 
         al = src[i].r_total % cell_rows == 0 && src[i].row0 % cell_rows == 0;
       if (al) rc = cell_rows;
     }
-    const uint32_t RU = rc ? rc : 1u, Ut = Rt / RU;
+    // Tensor-core mode: aligned 4-bit group-scaled cells of 4096 or 8192
+    // columns, every segment whole 16-row blocks and fully present (no rows
+    // cut by the archive's end).  Taken for 8192 columns, and for 4096 when a
+    // CTA gets 32 blocks or more (the LM head): measured on B200, the FFMA
+    // decode of the two-CTA aligned mode is faster on the 9B's shorter
+    // 4096-column launches (QKV, O, gate/up).  CHPE_FLAT_MMA=0 keeps the
+    // FFMA decode everywhere, =1 takes the tensor cores wherever they apply.
+    bool mma = false;
+    {
+      const char* e = getenv("CHPE_FLAT_MMA");
+      const bool off = e && e[0] == '0', all = e && e[0] == '1';
+      const uint32_t blocks = Rt / kMmaRows;
+      const bool big = blocks >= 32u * (uint32_t)num_sms_;
+      mma = rc && op.fmt == FMT_W4G && op.kind == SRC_FLAT && (ncols == 4096 || ncols == 8192) && !off &&
+            (all || ncols == 8192 || big);
+      for (int i = 0; i < nseg && mma; i++)
+        mma = src[i].r_total % kMmaRows == 0 && src[i].row0 % kMmaRows == 0 &&
+              (uint64_t)(src[i].row0 + src[i].r_total) * ncols <= src[i].flat_limit;
+      if (mma) {
+        // two blocks in the ring at least; a partial slot for every block in flight
+        const uint32_t u = Rt / kMmaRows, g = u < (uint32_t)num_sms_ ? u : (uint32_t)num_sms_;
+        const uint32_t rpc = kMmaRows * ((u + g - 1) / g), np = epi == EPI_SWIGLU ? 2u : 1u;
+        const uint32_t f = flat_layout_mma(ncols, rpc, np, 0).total;
+        uint32_t n = kFlatSmemLimit > f ? (kFlatSmemLimit - f) / kFlatStageBytes : 0u;
+        if (n > kFlatStagesWanted) n = kFlatStagesWanted;
+        const uint32_t cpb = kMmaRows / rc;
+        if (n < 2 * cpb || (n + cpb - 1) / cpb + 1 > kMmaSlots) mma = false;
+      }
+    }
+    const uint32_t RU = mma ? kMmaRows : rc ? rc : 1u, Ut = Rt / RU;
     const uint32_t G = Ut < (uint32_t)num_sms_ ? Ut : (uint32_t)num_sms_;
     t.rc = rc;
     t.nseg = nseg;
@@ -713,10 +742,21 @@ void Engine::add_linear_ops(std::vector<Op>& ops, const GemvSrc* src_in, float* 
     if (tp_on) t.tp = *tp;
     const uint32_t nparts = epi == EPI_SWIGLU ? 2u : 1u;
     const uint32_t cw = (uint32_t)fmt_cw(op.fmt);
-    const uint32_t fixed = flat_layout(ncols, cw, t.rpc, nparts, 0).total;
+    const uint32_t fixed = mma ? flat_layout_mma(ncols, t.rpc, nparts, 0).total
+                               : flat_layout(ncols, cw, t.rpc, nparts, 0).total;
     const uint32_t budget = kFlatSmemLimit > fixed ? kFlatSmemLimit - fixed : 0u;
     uint32_t nst = budget / kFlatStageBytes;
     if (nst > kFlatStagesWanted) nst = kFlatStagesWanted;
+    if (mma) {
+      t.mode = FLAT_MMA;
+      t.nw = kFlatConsumerWarps;
+      t.nst = nst;
+      op.smem = flat_layout_mma(ncols, t.rpc, nparts, nst).total;
+      op.grid = dim3(G);
+      ops.push_back(op);
+      for (int i = 0; i < nseg; i++) push_aux(src[i], epi == EPI_SWIGLU ? nullptr : out[i], gamma ? d_xn_ : x);
+      return;
+    }
     // Aligned launches whose shared memory fits twice per SM run 8 consumer
     // warps per CTA and two CTAs per SM (grid up to twice the SMs).
     uint32_t nw = 16, G8 = 0, rpc8 = 0, nst8 = 0;
@@ -760,6 +800,7 @@ void Engine::add_linear_ops(std::vector<Op>& ops, const GemvSrc* src_in, float* 
       op.smem = flat_layout(ncols, cw, rpc8, nparts, nst8, 8).total;
       op.grid = dim3(G8);
       ops.push_back(op);
+      for (int i = 0; i < nseg; i++) push_aux(src[i], epi == EPI_SWIGLU ? nullptr : out[i], gamma ? d_xn_ : x);
       return;
     }
     if (nst >= 2) {
@@ -1303,6 +1344,8 @@ static void launch_flat_t(const Op& op, cudaStream_t s) {
 }
 
 static void launch_flat(const Op& op, cudaStream_t s) {
+  if (op.kind == SRC_FLAT && op.fl.mode == FLAT_MMA && op.fmt == FMT_W4G)
+    return launch_flat_t<FMT_W4G, SRC_FLAT, FLAT_MMA>(op, s);
   if (op.kind == SRC_FLAT && op.fl.mode == FLAT_ALIGNED) {
     switch (op.fmt) {
       case FMT_W4G: return launch_flat_t<FMT_W4G, SRC_FLAT, FLAT_ALIGNED>(op, s);
@@ -1390,6 +1433,7 @@ std::string Engine::role_kernel_name(int role) const {
     const std::string fk = std::string("<") + fmt_name(op.fmt) + "," + kind_name(op.kind) + ">";
     switch (op.type) {
       case OP_FLAT_TMA:
+        if (op.fl.mode == FLAT_MMA) return "gemv_flat_tma_kernel[mma]" + fk;
         return std::string(op.fl.mode == FLAT_ALIGNED
                                ? (op.fl.nw == 8 ? "gemv_flat_tma_kernel[aligned, 2 CTAs/SM]" : "gemv_flat_tma_kernel[aligned]")
                            : op.fl.mode == FLAT_COLOWN ? "gemv_flat_tma_kernel[column owners]"

@@ -162,6 +162,23 @@ CHPE_DEV void quad_fma(const uint4& v, int q, f2x x01, f2x x23, f2x& acc) {
   }
 }
 
+// D += A * B on the tensor cores, m16n8k32, u8 A, s8 B, s32 accumulate
+// (lane = 4g + t).  A registers (four k bytes each): (row g, k 4t..4t+3),
+// (row g+8, k 4t..4t+3), (row g, k 4t+16..4t+19), (row g+8, k 4t+16..4t+19);
+// B: (k 4t..4t+3, n g), (k 4t+16..4t+19, n g); D: (g, 2t), (g, 2t+1),
+// (g+8, 2t), (g+8, 2t+1).
+CHPE_DEV void mma_u8s8_16832(int d[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                             uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// An int32 of magnitude below 2^22 as a float, exactly: its bits added to
+// those of 1.5 * 2^23 give 1.5 * 2^23 + v, from which 1.5 * 2^23 is removed.
+CHPE_DEV float s32_exact(int v) { return __int_as_float(v + 0x4B400000) - 12582912.0f; }
+
 // Chunk sum of (weight code value) * x from the quad accumulators.
 template <int FMT>
 CHPE_DEV float chunk_finish(f2x a0, f2x a1, float xsum) {

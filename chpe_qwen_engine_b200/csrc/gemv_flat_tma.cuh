@@ -65,7 +65,10 @@ struct FlatTmaLaunch {
   TpLink tp;               // tensor-parallel wait / exchange / signal (world 1: none)
 };
 
-constexpr uint32_t kFlatStageBytes = 16384 + 896;  // codes + payload head (832) rounded to 128
+// codes + payload head (832) rounded to 128, + 64 so that consecutive stages
+// sit half a bank row apart (the MMA mode reads one row of each of two cells
+// per load)
+constexpr uint32_t kFlatStageBytes = 16384 + 896 + 64;
 constexpr uint32_t kFlatMaxStages = 16;
 // Consumer warps per CTA: 16 (one CTA per SM), or 8 for aligned launches
 // whose shared memory fits twice per SM, so that the next launch's CTAs are
@@ -93,7 +96,27 @@ struct FlatRange {
 
 struct FlatLayout {
   uint32_t x, xs, wacc, bars, ranges, total;
+  uint32_t bp, bc;  // MMA mode: per-block partial sums and their arrival counters
 };
+
+// MMA mode (FLAT_MMA): 16-row blocks, x as int8 B fragments (four pieces per
+// value, one power-of-two exponent per 128-column group).
+constexpr uint32_t kMmaRows = 16;
+constexpr uint32_t kMmaSlots = 8;   // per-block partial slots (host: >= ceil(nst / cells per block) + 1)
+constexpr uint32_t kMmaPieces = 4;  // int8 pieces of each B value: 7 + 3 x 7 bits under the group exponent
+__host__ __device__ inline FlatLayout flat_layout_mma(uint32_t ncols, uint32_t rpc, uint32_t nparts, uint32_t nst) {
+  FlatLayout l;
+  const uint32_t ng = ncols / 128u;
+  l.x = nst * kFlatStageBytes;                 // B fragments: [group][kstep][kind][t][piece] x 8 bytes
+  l.xs = l.x + ng * 2u * 2u * 4u * kMmaPieces * 8u;  // per group: 1 / exponent scale, x sum
+  l.wacc = l.xs + ng * 8u;                     // row sums [part][row]
+  l.bp = l.wacc + nparts * rpc * 4u;           // [slot][warp][16 rows]
+  l.bc = l.bp + kMmaSlots * kFlatConsumerWarps * kMmaRows * 4u;
+  l.bars = (l.bc + kMmaSlots * 4u + 15u) & ~15u;
+  l.ranges = l.bars + 2 * kFlatMaxStages * 8;
+  l.total = l.ranges + kFlatMaxRanges * (uint32_t)sizeof(FlatRange);
+  return l;
+}
 
 // Shared-memory layout, shared by host (size) and kernel (offsets).  xsm =
 // false (column owners: x lives in registers) leaves out x and its chunk sums.
@@ -136,7 +159,30 @@ CHPE_DEV void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(NCT) : "mem
 // rc rows and consumer lane t always decodes the same column chunk t % (cols /
 // CW) of rows t / (cols / CW) + k * (256 / (cols / CW)): its x stays in
 // registers for the whole launch and shared memory carries only codes.
-enum FlatMode : int { FLAT_STREAM = 0, FLAT_ALIGNED = 1, FLAT_COLOWN = 2 };
+enum FlatMode : int { FLAT_STREAM = 0, FLAT_ALIGNED = 1, FLAT_COLOWN = 2, FLAT_MMA = 3 };
+
+// MMA (aligned 4-bit group-scaled cells of 4096 or 8192 columns, every
+// segment a whole number of 16-row blocks): the products go through
+// mma.sync.m16n8k32 with the code bytes as the u8 A operand.  A byte
+// lo + 16 hi holds the codes of columns 2p and 2p + 1, so
+//   lo x0 + hi x1 = lo y + (16 hi) z,   y = x0, z = x1 / 16 (exact),
+// and the two MMAs of a k-step take A = the code words & 0x0F0F0F0F and
+// & 0xF0F0F0F0 (two LOP3 per 8 weights, the whole decode).  B holds y and z of
+// each 128-column group as int8 pieces: scaled by a power of two S_G so that
+// the group's largest |y|, |z| lands in [32, 64), then split into 4 pieces
+// of 7 bits (value = i0 + i1/128 + i2/128^2 + i3/128^3, columns n = 0..3 of
+// B), which keeps about 27 bits of the group's range.  The s32 accumulation
+// is exact (|D| < 2^21 by construction), converted with a magic-number add.
+// Per group and row: scale * (sum_n D_n 128^-n / S_G - 8 sum x) = scale *
+// sum (c - 8) x.  A non-finite x makes 1 / S_G NaN, so the group's rows are
+// NaN as the f32 dot product would be.
+//
+// A block is 16 consecutive rows (16 / rows-per-cell cells); warp w takes the
+// 128-column groups w, w + 16, ...; lane (g, t) (g = lane / 4, t = lane % 4)
+// loads 16-byte chunk t of the group for rows g and g + 8, whose four words
+// are the A registers of the group's two k-steps.  The 16 warps' partial row
+// sums of a block meet in a shared slot; the warp that arrives last adds them
+// in warp order, so results do not depend on timing.
 
 // COLOWN ("column owner", rows of 384..960 chunks, no fused norm): consumer
 // slot u = lane + 480*j (15 consumer warps) owns column chunk u of every row, with that chunk of x
@@ -155,9 +201,13 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
   constexpr uint32_t NW = NWT, NCT = NWT * 32;
   static_assert(MODE == FLAT_COLOWN ? NWT == (int)kFlatColownWarps : (NWT == 16 || (NWT == 8 && MODE == FLAT_ALIGNED)),
                 "consumer warps: 16; 8 for aligned cells at two CTAs per SM; 15 for column owners");
+  static_assert(MODE != FLAT_MMA || (FMT == FMT_W4G && KIND == SRC_FLAT && NWT == (int)kFlatConsumerWarps),
+                "MMA mode: 4-bit group-scaled flat cells, 16 consumer warps");
   constexpr uint32_t CPWARP = NCH / NW;     // chunks per consumer warp
   constexpr uint32_t CPL = CPWARP / 32;     // chunks per lane
   static_assert(MODE == FLAT_COLOWN || (CPL >= 1 && CPWARP % 32 == 0), "piece geometry");
+  constexpr bool MMA = MODE == FLAT_MMA;
+  constexpr uint32_t NWR = MMA ? 1u : NW;   // per-row partial slots in wacc
   static_assert(NCH * 16 <= 16384, "a piece fits a stage");
 
   extern __shared__ __align__(128) uint8_t fsm[];
@@ -165,8 +215,8 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
   const bool swig = P.epi == EPI_SWIGLU;
   const uint32_t nparts = swig ? 2u : 1u;
   const uint32_t C = P.ncols, nst = P.nst;
-  constexpr bool XSM = MODE != FLAT_COLOWN;  // x staged in shared memory
-  const FlatLayout lay = flat_layout(C, CW, P.rpc, nparts, nst, NW, XSM);
+  constexpr bool XSM = MODE != FLAT_COLOWN && !MMA;  // x staged in shared memory as f32
+  const FlatLayout lay = MMA ? flat_layout_mma(C, P.rpc, nparts, nst) : flat_layout(C, CW, P.rpc, nparts, nst, NW, XSM);
   float* xsh = reinterpret_cast<float*>(fsm + lay.x);
   float* xsc = reinterpret_cast<float*>(fsm + lay.xs);
   float* wacc = reinterpret_cast<float*>(fsm + lay.wacc);
@@ -181,8 +231,9 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
   __shared__ volatile int s_bad;
 
   const uint32_t Rt = P.row_start[swig ? 1 : P.nseg];
-  // rows split evenly over the CTAs, in whole cells when aligned
-  const uint32_t RU = ALIGNED ? P.rc : 1u, Ut = Rt / RU;
+  // rows split evenly over the CTAs, in whole cells when aligned, whole
+  // 16-row blocks in the MMA mode
+  const uint32_t RU = MMA ? kMmaRows : ALIGNED ? P.rc : 1u, Ut = Rt / RU;
   const uint32_t R0 = RU * (uint32_t)((uint64_t)Ut * blockIdx.x / gridDim.x);
   const uint32_t R1 = RU * (uint32_t)((uint64_t)Ut * (blockIdx.x + 1) / gridDim.x);
 
@@ -296,9 +347,61 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
   float tot = 0.f;
   const uint32_t nq = C / 4;
   const float4* x4 = reinterpret_cast<const float4*>(P.x);
+  // x quad q (columns 4q..4q+3) into shared memory: f32 at xpos, or (MMA)
+  // its three bf16 pieces into the B fragments and its group's x sum (the 32
+  // lanes of a warp hold the 32 quads of one 128-column group)
+  auto put4 = [&](uint32_t q, const float4& o) {
+    if constexpr (MMA) {
+      // columns 4q, 4q+1 are code byte 2q' of the group (q' = q % 32), 4q+2,
+      // 4q+3 byte 2q'+1: word q'/2, chunk t = q'/8, k-step s and half of the
+      // word within the chunk, bytes 2(q' % 2) and 2(q' % 2) + 1 of the register
+      const uint32_t G = q >> 5, qq = q & 31u, t = qq >> 3, wic = (qq >> 1) & 3u;
+      const uint32_t s_ = wic >> 1, up = wic & 1u, bi = 2u * (qq & 1u);
+      const float y0 = o.x, z0 = o.y * 0.0625f, y1 = o.z, z1 = o.w * 0.0625f;
+      float m = fmaxf(fmaxf(fabsf(y0), fabsf(z0)), fmaxf(fabsf(y1), fabsf(z1)));
+      if (!(m <= 3.402823466e38f)) m = __int_as_float(0x7f800000);  // NaN -> inf
+#pragma unroll
+      for (int sh = 16; sh > 0; sh >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, sh));
+      float S = 1.0f, invS = 1.0f;
+      if (!(m <= 3.402823466e38f)) {
+        S = 0.0f;  // pieces 0, rows NaN
+        invS = __int_as_float(0x7fc00000);
+      } else if (m > 0.0f) {
+        int ex;
+        frexpf(m, &ex);  // m in [2^(ex-1), 2^ex)
+        const int k = 6 - ex < 126 ? 6 - ex : 126;
+        S = ldexpf(1.0f, k);
+        invS = ldexpf(1.0f, -k);
+      }
+      uint8_t* bb = fsm + lay.x + (((G * 2u + s_) * 2u) * 4u + t) * kMmaPieces * 8u + up * 4u + bi;
+      float ry0 = y0 * S, ry1 = y1 * S, rz0 = z0 * S, rz1 = z1 * S;
+#pragma unroll
+      for (uint32_t n = 0; n < kMmaPieces; n++) {
+        const float iy0 = rintf(ry0), iy1 = rintf(ry1), iz0 = rintf(rz0), iz1 = rintf(rz1);
+        const uint16_t py = (uint16_t)((uint32_t)((int)iy0 & 0xff) | ((uint32_t)((int)iy1 & 0xff) << 8));
+        const uint16_t pz = (uint16_t)((uint32_t)((int)iz0 & 0xff) | ((uint32_t)((int)iz1 & 0xff) << 8));
+        *reinterpret_cast<uint16_t*>(bb + n * 8u) = py;                         // kind 0: y
+        *reinterpret_cast<uint16_t*>(bb + 4u * kMmaPieces * 8u + n * 8u) = pz;   // kind 1: z
+        ry0 = (ry0 - iy0) * 128.0f;
+        ry1 = (ry1 - iy1) * 128.0f;
+        rz0 = (rz0 - iz0) * 128.0f;
+        rz1 = (rz1 - iz1) * 128.0f;
+      }
+      const float sx = warp_sum((o.x + o.y) + (o.z + o.w));
+      if (L == 0) {
+        xsc[2 * G] = invS;
+        xsc[2 * G + 1] = sx;
+      }
+    } else {
+      *reinterpret_cast<float4*>(&xsh[xpos<CW>(4 * q)]) = o;
+    }
+  };
   if (!stop) {
-    for (uint32_t i = tid; i < nparts * NW * P.rpc; i += NCT) wacc[i] = 0.f;
-    if (!XSM) {
+    for (uint32_t i = tid; i < nparts * NWR * P.rpc; i += NCT) wacc[i] = 0.f;
+    if constexpr (MMA) {
+      for (uint32_t i = tid; i < kMmaSlots; i += NCT) reinterpret_cast<uint32_t*>(fsm + lay.bc)[i] = 0u;
+    }
+    if (MODE == FLAT_COLOWN) {
       // column owners load their x chunks into registers in the main loop
     } else if (!P.norm) {
       // all loads of a batch in flight before any is stored
@@ -312,7 +415,7 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
 #pragma unroll
         for (uint32_t u = 0; u < 8; u++) {
           const uint32_t q = q0 + tid + NCT * u;
-          if (q < nq) *reinterpret_cast<float4*>(&xsh[xpos<CW>(4 * q)]) = v[u];
+          if (q < nq) put4(q, v[u]);
         }
       }
     } else {
@@ -353,7 +456,7 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
           o.y = v[u].y * inv * g[u].y;
           o.z = v[u].z * inv * g[u].z;
           o.w = v[u].w * inv * g[u].w;
-          *reinterpret_cast<float4*>(&xsh[xpos<CW>(4 * q)]) = o;
+          put4(q, o);
           if (P.xn_out && blockIdx.x == 0) reinterpret_cast<float4*>(P.xn_out)[q] = o;
         }
       }
@@ -419,11 +522,17 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
       part = r_part;
       lrb = r_lrb;
     };
+    uint32_t ss = 0, sph = 0;  // ring slot and phase of piece i
     for (uint32_t i = 0; i < npieces; i += CPI) {
       const bool two = CPI == 2 && i + 1 < npieces;
-      const uint32_t sa = i % nst, sb = (i + 1) % nst;
-      bool ok = mbar_wait_or_abort(&full[sa], (i / nst) & 1u, &s_bad);
-      if (ok && two) ok = mbar_wait_or_abort(&full[sb], ((i + 1) / nst) & 1u, &s_bad);
+      const uint32_t sa = ss, sb = ss + 1 < nst ? ss + 1 : 0u, phb = ss + 1 < nst ? sph : sph ^ 1u;
+      bool ok = mbar_wait_or_abort(&full[sa], sph, &s_bad);
+      if (ok && two) ok = mbar_wait_or_abort(&full[sb], phb, &s_bad);
+      ss += CPI;
+      if (ss >= nst) {
+        ss -= nst;
+        sph ^= 1u;
+      }
       if (!ok) {
         if (L == 0) { atomicExch(&P.st->err, 1); s_bad = 1; }
         break;
@@ -493,6 +602,108 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
         if (two) mbar_arrive(&empty[sb]);
       }
     }
+  } else if constexpr (MMA) {
+    // ---- main loop, 16-row blocks on the tensor cores -------------------------
+    const uint32_t RC = P.rc;                  // rows per cell (4 or 8)
+    const uint32_t CPB = kMmaRows / RC;        // cells per block
+    const uint32_t NG = C >> 7;                // 128-column groups
+    const uint32_t g = L >> 2, t = L & 3u;
+    const uint32_t rowB = C >> 1;              // code bytes per row
+    const uint32_t c1 = g / RC, r1 = g % RC, c2 = (g + 8u) / RC, r2 = (g + 8u) % RC;
+    const uint32_t off1 = r1 * rowB + t * 16u, off2 = r2 * rowB + t * 16u;
+    const uint32_t soff1 = 16384u + 48u + 2u * r1 * NG, soff2 = 16384u + 48u + 2u * r2 * NG;
+    const uint2* bfr = reinterpret_cast<const uint2*>(fsm + lay.x) + t * kMmaPieces + (g < kMmaPieces ? g : 0u);
+    const bool bl = g < kMmaPieces;            // lanes that hold a B column (piece g)
+    // pieces 2t and 2t+1 sit in this lane's two D columns
+    const float pw0 = t == 0u ? 1.0f : t == 1u ? 6.103515625e-05f : 0.0f;          // 128^-(2t)
+    const float pw1 = t == 0u ? 7.8125e-03f : t == 1u ? 4.76837158203125e-07f : 0.0f;  // 128^-(2t+1)
+    const float corr = t == 0u ? 8.0f : 0.0f;  // the x-sum term, once per row (lane t = 0)
+    float* bpart = reinterpret_cast<float*>(fsm + lay.bp);
+    uint32_t* bcnt = reinterpret_cast<uint32_t*>(fsm + lay.bc);
+    uint32_t ri = 0, r_k0 = rg[0].k0, r_ps = rg[0].pstart, r_part = rg[0].part;
+    int32_t r_lrb = rg[0].lrbase;
+    uint32_t r_end = nranges > 1 ? rg[1].pstart : npieces;
+    const uint32_t nblk = npieces / CPB;       // the host sends whole blocks
+    uint32_t sb = 0, phb = 0;                  // ring slot and phase of the block's first piece
+    // slot of the block's piece c (CPB <= nst)
+    auto slot_of = [&](uint32_t c) { return sb + c < nst ? sb + c : sb + c - nst; };
+    for (uint32_t blk = 0; blk < nblk; blk++) {
+      const uint32_t i0 = blk * CPB;
+      bool ok = true;
+      for (uint32_t c = 0; c < CPB && ok; c++)
+        ok = mbar_wait_or_abort(&full[slot_of(c)], sb + c < nst ? phb : phb ^ 1u, &s_bad);
+      if (!ok) {
+        if (L == 0) { atomicExch(&P.st->err, 1); s_bad = 1; }
+        break;
+      }
+      if (i0 == r_end) {  // blocks never straddle ranges (whole blocks per segment)
+        ri++;
+        r_k0 = rg[ri].k0;
+        r_ps = rg[ri].pstart;
+        r_part = rg[ri].part;
+        r_lrb = rg[ri].lrbase;
+        r_end = ri + 1 < nranges ? rg[ri + 1].pstart : npieces;
+      }
+      const uint8_t* st1 = fsm + slot_of(c1) * kFlatStageBytes;
+      const uint8_t* st2 = fsm + slot_of(c2) * kFlatStageBytes;
+      float acc1 = 0.f, acc2 = 0.f;
+#pragma unroll 2
+      for (uint32_t G = warp; G < NG; G += NW) {
+        const uint4 w1 = *reinterpret_cast<const uint4*>(st1 + off1 + G * 64u);
+        const uint4 w2 = *reinterpret_cast<const uint4*>(st2 + off2 + G * 64u);
+        const float s1 = ld_f16(st1 + soff1 + 2u * G), s2 = ld_f16(st2 + soff2 + 2u * G);
+        const uint2* bg = bfr + G * (4u * 4u * kMmaPieces);  // [kstep][kind][t][piece]
+        int d[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (uint32_t ks = 0; ks < 2; ks++) {
+          const uint32_t a0 = word_of(w1, (int)(2 * ks)), a1 = word_of(w2, (int)(2 * ks));
+          const uint32_t a2 = word_of(w1, (int)(2 * ks + 1)), a3 = word_of(w2, (int)(2 * ks + 1));
+          const uint2 By = bl ? bg[(2u * ks) * 4u * kMmaPieces] : make_uint2(0u, 0u);
+          const uint2 Bz = bl ? bg[(2u * ks + 1u) * 4u * kMmaPieces] : make_uint2(0u, 0u);
+          mma_u8s8_16832(d, a0 & 0x0F0F0F0Fu, a1 & 0x0F0F0F0Fu, a2 & 0x0F0F0F0Fu, a3 & 0x0F0F0F0Fu, By.x, By.y);
+          mma_u8s8_16832(d, a0 & 0xF0F0F0F0u, a1 & 0xF0F0F0F0u, a2 & 0xF0F0F0F0u, a3 & 0xF0F0F0F0u, Bz.x, Bz.y);
+        }
+        const float invS = xsc[2 * G], xc = corr * xsc[2 * G + 1];
+        const float v1 = fmaf(s32_exact(d[1]), pw1, s32_exact(d[0]) * pw0);
+        const float v2 = fmaf(s32_exact(d[3]), pw1, s32_exact(d[2]) * pw0);
+        acc1 = fmaf(s1, fmaf(v1, invS, -xc), acc1);
+        acc2 = fmaf(s2, fmaf(v2, invS, -xc), acc2);
+      }
+      // lanes t = 0 and 1 hold the pieces n = 0,1 and n = 2,3; t = 2, 3 hold zeros
+      acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+      acc2 += __shfl_xor_sync(0xffffffffu, acc2, 1);
+      const uint32_t slot = blk % kMmaSlots;
+      float* bp = bpart + slot * (NW * kMmaRows);
+      if (t == 0u) {
+        bp[warp * kMmaRows + g] = acc1;
+        bp[warp * kMmaRows + g + 8u] = acc2;
+      }
+      __threadfence_block();
+      __syncwarp();
+      uint32_t last = 0;
+      if (L == 0) last = atomicAdd(&bcnt[slot], 1u) == NW - 1u ? 1u : 0u;
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (last) {
+        // every warp's partials of this block are in: add them in warp order
+        __threadfence_block();
+        if (L < kMmaRows) {
+          float sum = 0.f;
+#pragma unroll
+          for (uint32_t w = 0; w < NW; w++) sum += bp[w * kMmaRows + L];
+          const uint32_t k0 = r_k0 + (i0 - r_ps);  // first cell of the block
+          wacc[r_part * P.rpc + (uint32_t)((int32_t)(k0 * RC + L) + r_lrb)] = sum;
+        }
+        if (L == 0) bcnt[slot] = 0u;
+        __syncwarp();
+      }
+      if (L == 0)
+        for (uint32_t c = 0; c < CPB; c++) mbar_arrive(&empty[slot_of(c)]);
+      sb += CPB;
+      if (sb >= nst) {
+        sb -= nst;
+        phb ^= 1u;
+      }
+    }
   } else if constexpr (MODE == FLAT_COLOWN) {
     // ---- main loop, column owners ------------------------------------------
     // One row per group (the host sends rows of 384..960 chunks for 16-byte
@@ -524,7 +735,8 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
       }
       xsj[j] = sx;
     }
-    uint32_t waited = 0, released = 0;
+    // pieces waited for / released so far, with the ring slot (and phase) of the next one
+    uint32_t waited = 0, released = 0, wslot = 0, wph = 0, rslot = 0;
     bool bad = false;
     for (uint32_t r = 0; r < nranges && !bad; r++) {
       const FlatRange rgv = rg[r];
@@ -536,10 +748,16 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
         const uint32_t flo = g0 * C > rgv.fa0 ? g0 * C : rgv.fa0;
         const uint32_t fhi = g1 * C < rgv.fb0 ? g1 * C : rgv.fb0;
         const uint32_t p_lo = pbase + flo / WPP, p_hi = pbase + (fhi - 1u) / WPP;
-        for (; waited <= p_hi; waited++)
-          if (!mbar_wait_or_abort(&full[waited % nst], (waited / nst) & 1u, &s_bad)) { bad = true; break; }
+        for (; waited <= p_hi; waited++) {
+          if (!mbar_wait_or_abort(&full[wslot], wph, &s_bad)) { bad = true; break; }
+          if (++wslot == nst) {
+            wslot = 0;
+            wph ^= 1u;
+          }
+        }
         if (bad) break;
-        const uint32_t s_lo = p_lo % nst;                // ring slot of piece p_lo
+        // every piece before this group's first one has been released
+        const uint32_t s_lo = rslot;                     // ring slot of piece p_lo (== released)
         float vrow[RI];
 #pragma unroll
         for (uint32_t rr = 0; rr < RI; rr++) vrow[rr] = 0.f;
@@ -597,8 +815,10 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
         const uint32_t fnext = g1 * C;
         const uint32_t p_keep = (g1 < rb && fnext < rgv.fb0) ? pbase + fnext / WPP : pend;
         __syncwarp();
-        for (; released < p_keep; released++)
-          if (L == 0) mbar_arrive(&empty[released % nst]);
+        for (; released < p_keep; released++) {
+          if (L == 0) mbar_arrive(&empty[rslot]);
+          if (++rslot == nst) rslot = 0;
+        }
       }
     }
     if (bad && L == 0) { atomicExch(&P.st->err, 1); s_bad = 1; }
@@ -694,11 +914,11 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
   for (uint32_t lr = tid; lr < nrows; lr += NCT) {
     float d0 = 0.f, d1 = 0.f;
 #pragma unroll
-    for (uint32_t w = 0; w < NW; w++) d0 += wacc[w * P.rpc + lr];
+    for (uint32_t w = 0; w < NWR; w++) d0 += wacc[w * P.rpc + lr];
     if constexpr (FMT == FMT_I8RAW) d0 *= 0.00373708f;  // raw int8 dot scale (chpe_engine.zig:1236)
     if (swig) {
 #pragma unroll
-      for (uint32_t w = 0; w < NW; w++) d1 += wacc[(NW + w) * P.rpc + lr];
+      for (uint32_t w = 0; w < NWR; w++) d1 += wacc[(NWR + w) * P.rpc + lr];
       if constexpr (FMT == FMT_I8RAW) d1 *= 0.00373708f;
       tp_put(P.tp, P.out[0], R0 + lr, silu_ref(d0) * d1);
       continue;

@@ -142,6 +142,34 @@ def test_gemv_flat_widths(cfg, colown, monkeypatch):
             assert_close_vec(got, ref, 1e-4, f"{r}x{c} acc={acc}")
 
 
+# Aligned 4-bit shapes for the tensor-core decode: whole 16-row blocks of
+# 8192 / 4096 columns read from the 3B down-projection cells (688 cells), one
+# more than the cells hold (2800 x 8192: the FFMA decode takes it), and
+# single blocks.
+MMA_SHAPES = [(2048, 8192), (4000, 4096), (16, 8192), (32, 4096), (1600, 8192), (2800, 8192)]
+
+
+@pytest.mark.parametrize("mma", [False, True])
+@pytest.mark.parametrize("cfg,flags", [(chpe.SYNTH_3B_W4, 0), (chpe.SYNTH_3B_W4, chpe.SYNTH_OUTLIERS)])
+def test_gemv_flat_mma(cfg, flags, mma, monkeypatch):
+    """mma.sync decode (x as three bf16 pieces, f32 accumulate) of aligned
+    4-bit group-scaled cells against the oracle; with CHPE_FLAT_MMA=0 the FFMA
+    decode of the same calls.  x spans a wide range: a few entries 1e4 times
+    the rest."""
+    monkeypatch.setenv("CHPE_FLAT_MMA", "1" if mma else "0")
+    a, e, o = engines(cfg, flags)
+    li = o.layer_info(4)
+    rng = np.random.default_rng(29)
+    for r, c in MMA_SHAPES:
+        for acc in (False, True):
+            x = rng.standard_normal(c).astype(np.float32)
+            x[rng.integers(0, c, 4)] *= 1e4
+            y0 = rng.standard_normal(r).astype(np.float32)
+            ref = o.gemv_linear(li["down_proj"], li["down_tiles"], x, r, c, accumulate=acc, y=y0.copy())
+            got = e.probe_gemv_linear(li["down_proj"], li["down_tiles"], x, r, c, accumulate=acc, y=y0.copy())
+            assert_close_vec(got, ref, 1e-4, f"{r}x{c} acc={acc} mma={mma}")
+
+
 @pytest.mark.parametrize("arch", [chpe.ARCH_3B, chpe.ARCH_9B, chpe.ARCH_72B])
 def test_attention_against_oracle(arch):
     """RoPE + KV append + GQA softmax (chpe_engine.zig:1688-1734) over a
