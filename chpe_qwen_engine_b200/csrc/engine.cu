@@ -716,7 +716,8 @@ void Engine::add_linear_ops(std::vector<Op>& ops, const GemvSrc* src_in, float* 
         uint32_t n = kFlatSmemLimit > f ? (kFlatSmemLimit - f) / kFlatStageBytes : 0u;
         if (n > kFlatStagesWanted) n = kFlatStagesWanted;
         const uint32_t cpb = kMmaRows / rc;
-        if (n < 2 * cpb || (n + cpb - 1) / cpb + 1 > kMmaSlots) mma = false;
+        // two blocks in the ring, one of them outside the stages that stage B
+        if (n < 2 * cpb || n < flat_mma_b_stages(ncols) + cpb || (n + cpb - 1) / cpb + 1 > kMmaSlots) mma = false;
       }
     }
     const uint32_t RU = mma ? kMmaRows : rc ? rc : 1u, Ut = Rt / RU;

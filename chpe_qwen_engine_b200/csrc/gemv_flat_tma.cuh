@@ -104,11 +104,17 @@ struct FlatLayout {
 constexpr uint32_t kMmaRows = 16;
 constexpr uint32_t kMmaSlots = 8;   // per-block partial slots (host: >= ceil(nst / cells per block) + 1)
 constexpr uint32_t kMmaPieces = 4;  // int8 pieces of each B value: 7 + 3 x 7 bits under the group exponent
+// B fragments ([group][kstep][kind][t][piece] x 8 bytes) are staged in the
+// ring's last stages, which the producer fills only after every consumer warp
+// has copied its groups' fragments into registers.
+__host__ __device__ inline uint32_t flat_mma_b_stages(uint32_t ncols) {
+  return ((ncols / 128u) * 2u * 2u * 4u * kMmaPieces * 8u + kFlatStageBytes - 1u) / kFlatStageBytes;
+}
 __host__ __device__ inline FlatLayout flat_layout_mma(uint32_t ncols, uint32_t rpc, uint32_t nparts, uint32_t nst) {
   FlatLayout l;
-  const uint32_t ng = ncols / 128u;
-  l.x = nst * kFlatStageBytes;                 // B fragments: [group][kstep][kind][t][piece] x 8 bytes
-  l.xs = l.x + ng * 2u * 2u * 4u * kMmaPieces * 8u;  // per group: 1 / exponent scale, x sum
+  const uint32_t ng = ncols / 128u, nb = flat_mma_b_stages(ncols);
+  l.x = (nst >= nb ? nst - nb : 0u) * kFlatStageBytes;  // B staging, over the last nb stages
+  l.xs = nst * kFlatStageBytes;                // per group: 1 / exponent scale, x sum
   l.wacc = l.xs + ng * 8u;                     // row sums [part][row]
   l.bp = l.wacc + nparts * rpc * 4u;           // [slot][warp][16 rows]
   l.bc = l.bp + kMmaSlots * kFlatConsumerWarps * kMmaRows * 4u;
@@ -178,7 +184,8 @@ enum FlatMode : int { FLAT_STREAM = 0, FLAT_ALIGNED = 1, FLAT_COLOWN = 2, FLAT_M
 // NaN as the f32 dot product would be.
 //
 // A block is 16 consecutive rows (16 / rows-per-cell cells); warp w takes the
-// 128-column groups w, w + 16, ...; lane (g, t) (g = lane / 4, t = lane % 4)
+// 128-column groups w, w + 16, ... (at most four: 8192 columns), their B
+// fragments in registers; lane (g, t) (g = lane / 4, t = lane % 4)
 // loads 16-byte chunk t of the group for rows g and g + 8, whose four words
 // are the A registers of the group's two k-steps.  The 16 warps' partial row
 // sums of a block meet in a shared slot; the warp that arrives last adds them
@@ -312,7 +319,9 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
       for (uint32_t i = from; i < issued; i++) mbar_wait(&full[i % nst], (i / nst) & 1u);
     };
     if (L == 0) {
-      const uint32_t npre = npieces < nst ? npieces : nst;
+      // (MMA: the last stages hold the B fragments until the consumers' prologue ends)
+      const uint32_t nfree = MMA ? nst - flat_mma_b_stages(C) : nst;
+      const uint32_t npre = npieces < nfree ? npieces : nfree;
       for (; issued < npre; issued++) issue(issued);
     }
     __syncthreads();  // consumers' prologue done: s_abort is final
@@ -460,6 +469,23 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
           if (P.xn_out && blockIdx.x == 0) reinterpret_cast<float4*>(P.xn_out)[q] = o;
         }
       }
+    }
+  }
+  // MMA: each warp's B fragments (its 128-column groups warp + 16 j, lanes
+  // g < 4 hold piece g) into registers, before the producer may reuse the
+  // stages they were staged in
+  uint2 breg[4][4];
+  if constexpr (MMA) {
+    consumer_sync<NCT>();
+    const uint32_t g = L >> 2, t = L & 3u;
+    const uint2* bfr = reinterpret_cast<const uint2*>(fsm + lay.x) + t * kMmaPieces + (g < kMmaPieces ? g : 0u);
+#pragma unroll
+    for (uint32_t j = 0; j < 4; j++) {
+      const uint32_t G = warp + NW * j;
+#pragma unroll
+      for (uint32_t q = 0; q < 4; q++)
+        breg[j][q] = (!stop && g < kMmaPieces && G < (C >> 7)) ? bfr[G * (4u * 4u * kMmaPieces) + q * 4u * kMmaPieces]
+                                                               : make_uint2(0u, 0u);
     }
   }
   __syncthreads();  // with the producer: abort decision is final
@@ -612,8 +638,6 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
     const uint32_t c1 = g / RC, r1 = g % RC, c2 = (g + 8u) / RC, r2 = (g + 8u) % RC;
     const uint32_t off1 = r1 * rowB + t * 16u, off2 = r2 * rowB + t * 16u;
     const uint32_t soff1 = 16384u + 48u + 2u * r1 * NG, soff2 = 16384u + 48u + 2u * r2 * NG;
-    const uint2* bfr = reinterpret_cast<const uint2*>(fsm + lay.x) + t * kMmaPieces + (g < kMmaPieces ? g : 0u);
-    const bool bl = g < kMmaPieces;            // lanes that hold a B column (piece g)
     // pieces 2t and 2t+1 sit in this lane's two D columns
     const float pw0 = t == 0u ? 1.0f : t == 1u ? 6.103515625e-05f : 0.0f;          // 128^-(2t)
     const float pw1 = t == 0u ? 7.8125e-03f : t == 1u ? 4.76837158203125e-07f : 0.0f;  // 128^-(2t+1)
@@ -647,19 +671,19 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
       const uint8_t* st1 = fsm + slot_of(c1) * kFlatStageBytes;
       const uint8_t* st2 = fsm + slot_of(c2) * kFlatStageBytes;
       float acc1 = 0.f, acc2 = 0.f;
-#pragma unroll 2
-      for (uint32_t G = warp; G < NG; G += NW) {
+#pragma unroll
+      for (uint32_t j = 0; j < 4; j++) {
+        const uint32_t G = warp + NW * j;
+        if (G >= NG) break;
         const uint4 w1 = *reinterpret_cast<const uint4*>(st1 + off1 + G * 64u);
         const uint4 w2 = *reinterpret_cast<const uint4*>(st2 + off2 + G * 64u);
         const float s1 = ld_f16(st1 + soff1 + 2u * G), s2 = ld_f16(st2 + soff2 + 2u * G);
-        const uint2* bg = bfr + G * (4u * 4u * kMmaPieces);  // [kstep][kind][t][piece]
         int d[4] = {0, 0, 0, 0};
 #pragma unroll
         for (uint32_t ks = 0; ks < 2; ks++) {
           const uint32_t a0 = word_of(w1, (int)(2 * ks)), a1 = word_of(w2, (int)(2 * ks));
           const uint32_t a2 = word_of(w1, (int)(2 * ks + 1)), a3 = word_of(w2, (int)(2 * ks + 1));
-          const uint2 By = bl ? bg[(2u * ks) * 4u * kMmaPieces] : make_uint2(0u, 0u);
-          const uint2 Bz = bl ? bg[(2u * ks + 1u) * 4u * kMmaPieces] : make_uint2(0u, 0u);
+          const uint2 By = breg[j][2 * ks], Bz = breg[j][2 * ks + 1];
           mma_u8s8_16832(d, a0 & 0x0F0F0F0Fu, a1 & 0x0F0F0F0Fu, a2 & 0x0F0F0F0Fu, a3 & 0x0F0F0F0Fu, By.x, By.y);
           mma_u8s8_16832(d, a0 & 0xF0F0F0F0u, a1 & 0xF0F0F0F0u, a2 & 0xF0F0F0F0u, a3 & 0xF0F0F0F0u, Bz.x, Bz.y);
         }
