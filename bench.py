@@ -365,8 +365,10 @@ def main():
                     help="profiling case: build the engine (max_seq_len 64) and only launch this "
                          "op of every layer, --steps rounds after one warm-up round; flat-aligned / "
                          "flat-stream: one flat GEMV over 2064 contiguous 4-bit cells of the 3B "
-                         "archive (35 MB) read as 8192 columns (aligned cells) or 29568 columns "
-                         "(72B down width), --steps launches")
+                         "archive (35 MB) read as 8192 columns (aligned cells: the tensor-core mode, "
+                         "or with CHPE_FLAT_MMA=0 the FFMA aligned mode) or 29568 columns (the 72B "
+                         "down width: column owners, or with CHPE_FLAT_COLOWN=0 the stream mode), "
+                         "--steps launches")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
