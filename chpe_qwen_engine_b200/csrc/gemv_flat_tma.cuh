@@ -357,8 +357,9 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
   const uint32_t nq = C / 4;
   const float4* x4 = reinterpret_cast<const float4*>(P.x);
   // x quad q (columns 4q..4q+3) into shared memory: f32 at xpos, or (MMA)
-  // its three bf16 pieces into the B fragments and its group's x sum (the 32
-  // lanes of a warp hold the 32 quads of one 128-column group)
+  // the int8 pieces of y and z into the B fragment staging, with the group's
+  // exponent and x sum (the 32 lanes of a warp hold the 32 quads of one
+  // 128-column group)
   auto put4 = [&](uint32_t q, const float4& o) {
     if constexpr (MMA) {
       // columns 4q, 4q+1 are code byte 2q' of the group (q' = q % 32), 4q+2,

@@ -152,8 +152,10 @@ MMA_SHAPES = [(2048, 8192), (4000, 4096), (16, 8192), (32, 4096), (1600, 8192), 
 @pytest.mark.parametrize("mma", [False, True])
 @pytest.mark.parametrize("cfg,flags", [(chpe.SYNTH_3B_W4, 0), (chpe.SYNTH_3B_W4, chpe.SYNTH_OUTLIERS)])
 def test_gemv_flat_mma(cfg, flags, mma, monkeypatch):
-    """mma.sync decode (x as three bf16 pieces, f32 accumulate) of aligned
-    4-bit group-scaled cells against the oracle; with CHPE_FLAT_MMA=0 the FFMA
+    """mma.sync decode (code bytes as the u8 operand, x as int8 pieces under a
+    per-group exponent, exact s32 sums) of aligned 4-bit group-scaled cells
+    against the oracle, the tensor cores taken wherever they apply
+    (CHPE_FLAT_MMA=1); with CHPE_FLAT_MMA=0 the FFMA
     decode of the same calls.  x spans a wide range: a few entries 1e4 times
     the rest."""
     monkeypatch.setenv("CHPE_FLAT_MMA", "1" if mma else "0")
