@@ -6,12 +6,14 @@ at 1/2/4/8 B200): Qwen2.5-72B in the 4-bit flat-cell format (group-128 FP16
 scales), random-init seeded synthetic archive, a 2048-token prompt decoded
 token by token (untimed), then W warm-up and K timed greedy steps.  A step is
 one token through all 80 layers + LM head.  With N > 1 (torchrun, one rank per
-GPU) the model is tensor parallel over the N GPUs (row-split projections,
-exchanges over NVLink peer memory); `value` is tokens of the one sequence per
-second (strong scaling).  --model picks another config (3b-w4 = config 2,
-9b-w4, 3b-w2, 3b-fp16); the 3B models run as independent replicas for N > 1.
+GPU) the model is tensor parallel over the N GPUs; `value` is tokens of the
+one sequence per second (strong scaling).  --model picks another config
+(3b-fp16 = config 1, 3b-w4 / 3b-w2 = config 2, 9b-w4 = config 3, 72b-fp16 =
+the FP16 half of config 5); the 3B models run as independent replicas for
+N > 1.  --sweep prints config 2's isolated GEMV sweep instead.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--model M] [--impl ours|reference]
+  python bench.py --sweep [--model 3b-w4|3b-w2|3b-fp16]
 
 value: tok/s with weights resident in HBM, device time (CUDA events on the
 engine stream) of K back-to-back greedy steps (each step's token is the
@@ -19,7 +21,9 @@ previous argmax, fed back on the device), max over ranks.  e2e: the same steps
 through the C ABI with a pinned host->device copy of each token and a
 device->host copy of each step's logits and result, wall time, max over ranks.
 --impl reference times the CPU restatement of the reference engine (the Zig
-reference cannot be built here) on all host cores, rank 0 only.
+reference cannot be built here) on all host threads, rank 0 only, at the
+GPU arm's positions over a KV cache prefilled to the same context; both arms
+print the same `config`.
 """
 from __future__ import annotations
 
@@ -37,20 +41,28 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-PROMPT = 512
 METRIC = "batch-1 greedy decode tok/s (weight stream vs HBM roofline)"
 
 # Workloads: synthetic archive, architecture preset, prompt
 # length decoded before timing, and the layer count of the model.
 MODELS = {
-    "3b-w4": dict(synth="SYNTH_3B_W4", arch="ARCH_3B", prompt=512, name="qwen2.5-3b-w4-dense-cell"),
-    "3b-w2": dict(synth="SYNTH_3B_W2", arch="ARCH_3B", prompt=512, name="qwen2.5-3b-w2-dense-cell"),
-    "3b-fp16": dict(synth="SYNTH_3B_FP16_RAW", arch="ARCH_3B", prompt=32, name="qwen2.5-3b-fp16-raw"),
+    "3b-w4": dict(synth="SYNTH_3B_W4", arch="ARCH_3B", prompt=512, name="qwen2.5-3b-w4-dense-cell",
+                  dtype="u4->f32"),
+    "3b-w2": dict(synth="SYNTH_3B_W2", arch="ARCH_3B", prompt=512, name="qwen2.5-3b-w2-dense-cell",
+                  dtype="u2->f32"),
+    "3b-fp16": dict(synth="SYNTH_3B_FP16_RAW", arch="ARCH_3B", prompt=32, name="qwen2.5-3b-fp16-raw",
+                    dtype="f16->f32"),
     "9b-w4": dict(synth="SYNTH_9B_W4", arch="ARCH_9B", prompt=1024, name="qwen3.5-9b-w4-flat-cell",
-                  tp=True),
+                  tp=True, dtype="u4->f32"),
     "72b-w4": dict(synth="SYNTH_72B_W4", arch="ARCH_72B", prompt=2048, name="qwen2.5-72b-w4-flat-cell",
-                   tp=True),
+                   tp=True, dtype="u4->f32"),
+    # FP16 raw tiles laid out by the 72B tensor map, whose tile counts are
+    # sized for 4-bit cells: the reference reads a quarter of each projection
+    "72b-fp16": dict(synth="SYNTH_72B_FP16_RAW", arch="ARCH_72B", prompt=2048,
+                     name="qwen2.5-72b-fp16-raw-reference-map", tp=True, dtype="f16->f32"),
 }
+# layers, kv heads, head dim per architecture (KV bytes of a step)
+KV_GEOM = {0: (36, 2, 128), 1: (32, 4, 256), 2: (80, 8, 128)}
 
 
 def peaks():
@@ -153,19 +165,58 @@ def barrier(dist):
         dist.barrier()
 
 
-def oracle_cpu_baseline(archive, arch: int, steps: int, threads: int, toks) -> tuple[float, str]:
-    """The oracle (C restatement of the reference engine) decoding `steps`
-    tokens from position 0; returns tok/s."""
+def kv_bytes_per_step(arch: int, pos: float) -> float:
+    """FP16 K and V the attention of one step at position `pos` reads
+    (positions 0..pos of every layer and kv head)."""
+    L, KV, HD = KV_GEOM[arch]
+    return float(L * KV * HD * 2 * 2) * (pos + 1)
+
+
+def common_config(M, prompt: int, warmup: int, steps: int, world: int, tp: bool) -> dict:
+    """The workload both arms run (the same dict in both JSON lines)."""
+    p0 = prompt + warmup
+    return {"workload": M["name"], "prompt": prompt, "positions": f"{p0}..{p0 + steps - 1}",
+            "parallelism": f"tp{world}" if tp else f"replicas x{world}",
+            "kv": "paged FP16 (GPU), f32 (CPU); CPU context prefilled to the same length",
+            "l2": "inputs larger than L2 (the weights of a step exceed 126 MB)"}
+
+
+def prefilled_oracle(archive, arch: int, ctx: int, extra: int, threads: int):
+    """The oracle (C restatement of the reference engine) with its KV cache
+    filled at positions 0..ctx-1 by seeded rows, so its steps attend over
+    the same context length as the GPU arm's."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle_py as O
-    e = O.OracleEngine(archive, arch, steps + 8, threads=threads)
-    e.forward_decode(int(toks[0]), 0)  # warm (page-in)
+    e = O.OracleEngine(archive, arch, ctx + extra + 2, threads=threads)
+    L, KV, HD = KV_GEOM[arch]
+    rng = np.random.default_rng(5)
+    for l in range(L):
+        if ctx:
+            e.kv_load(l, 0, rng.standard_normal((ctx, KV * HD), dtype=np.float32),
+                      rng.standard_normal((ctx, KV * HD), dtype=np.float32))
+    return e
+
+
+def oracle_sample(archive, arch: int, pos0: int, warmup: int, max_steps: int, threads: int,
+                  budget_s: float) -> tuple[float, int, int]:
+    """Times oracle decode steps at positions pos0+warmup.. after `warmup`
+    untimed steps, stopping after max_steps or once budget_s has passed
+    (at least one step).  Returns (tok/s, steps timed, first timed position)."""
+    e = prefilled_oracle(archive, arch, pos0, warmup + max_steps, threads)
+    toks = np.random.default_rng(1).integers(0, 151936, warmup + max_steps + 1)
+    for i in range(warmup):
+        e.forward_decode(int(toks[i]), pos0 + i)
+    p = pos0 + warmup
+    n = 0
     t0 = time.perf_counter()
-    for i in range(steps):
-        e.forward_decode(int(toks[i + 1]), i + 1)
+    while n < max_steps:
+        e.forward_decode(int(toks[warmup + n]), p + n)
+        n += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
     dt = time.perf_counter() - t0
     e.close()
-    return steps / dt, f"{steps} decode steps of the full model at positions 1..{steps}"
+    return n / dt, n, p
 
 
 def run_reference(args, rank, world, dist):
@@ -173,36 +224,24 @@ def run_reference(args, rank, world, dist):
     if rank != 0:
         return
     M = MODELS[args.model]
+    tp = world > 1 and M.get("tp", False)
     archive = chpe.synth_archive(getattr(chpe, M["synth"]), 0, seed=0)
     arch = getattr(chpe, M["arch"])
     threads = os.cpu_count() or 1
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle_py as O
-    e = O.OracleEngine(archive, arch, args.steps + args.warmup + 4, threads=threads)
-    toks = np.random.default_rng(1).integers(0, 151936, args.steps + args.warmup + 2)
-    # bounded sample: at most ~60 s of timed CPU work
-    t0 = time.perf_counter()
-    e.forward_decode(int(toks[0]), 0)
-    per = time.perf_counter() - t0
-    warm = max(0, min(args.warmup, int(20.0 / max(per, 1e-3))) - 1)
-    steps = max(1, min(args.steps, int(60.0 / max(per, 1e-3))))
-    for i in range(warm):
-        e.forward_decode(int(toks[1 + i]), 1 + i)
-    p0 = 1 + warm
-    t0 = time.perf_counter()
-    for i in range(steps):
-        e.forward_decode(int(toks[p0 + i]), p0 + i)
-    dt = time.perf_counter() - t0
-    v = steps / dt
+    # the GPU arm's positions: the prompt, then its warm-up steps, then the
+    # timed steps; the CPU warms up on one step and times up to K within ~90 s
+    v, n, p = oracle_sample(archive, arch, args.prompt + args.warmup - 1, 1, args.steps, threads, 90.0)
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus,
-        "steps": steps, "warmup": warm + 1, "ms_per_step": dt * 1000 / steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u4->f32",
-        "data": "synthetic (seeded archive, random-init weights)",
-        "config": {"workload": M["name"], "archive_bytes": int(archive.size)},
+        "steps": n, "warmup": args.warmup, "ms_per_step": 1000.0 / v,
+        "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None,
+        "dtype": M["dtype"], "data": "synthetic (seeded archive, random-init weights)",
+        "config": common_config(M, args.prompt, args.warmup, args.steps, world, tp),
         "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": "port",
-                         "sample": f"{steps} decode steps at positions {p0}..{p0 + steps - 1} "
-                                   f"(short context); CPU restatement of src/chpe_engine.zig ({cpu_isa()})"},
+                         "sample": f"{n} decode steps at positions {p}..{p + n - 1} over a KV cache "
+                                   f"prefilled to the same context as the GPU arm; CPU restatement of "
+                                   f"src/chpe_engine.zig, rows split over {threads} threads "
+                                   f"(the reference itself is single-threaded) ({cpu_isa()})"},
         "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -299,6 +338,7 @@ def run_ours(args, rank, world, local, dist):
                 a[0] += float(m)
                 a[1] += 1
     per_role_step = {name: round(max_over_ranks(dist, tot / cnt) * 1000, 2) for name, (tot, cnt) in acc.items()}
+    ms_step = ms_max / args.steps
     if tp:
         # one role cannot run alone across ranks (its exchanges wait on the
         # others): the roofline here is the whole step's weight stream per GPU
@@ -307,48 +347,77 @@ def run_ours(args, rank, world, local, dist):
                               "bytes_per_launch": None, "gbs": None}
         mine = eng.step_weight_bytes()
         step_bytes = sum_over_ranks(dist, mine)
-        per_gpu = max_over_ranks(dist, mine) / (ms_max / args.steps / 1000.0) / 1e9
+        per_gpu = max_over_ranks(dist, mine) / (ms_step / 1000.0) / 1e9
         roof = {"kernel": "whole decode step per GPU (all kernels, exchanges included)", "bound": "hbm",
                 "achieved": per_gpu, "peak": hbm, "unit": "GB/s", "frac": per_gpu / hbm,
                 "peak_kind": peak_kind, "traffic": None, "bytes_per_launch": step_bytes / world,
-                "avg_launch_us": ms_max / args.steps * 1000}
+                "avg_launch_us": ms_step * 1000}
+    # KV read by the timed steps (their average position), FP16
+    p0 = args.prompt + args.warmup
+    kvb = kv_bytes_per_step(arch, p0 + (args.steps - 1) / 2.0)
     cpu = None
     if rank == 0 and archive is None:
         archive = np.memmap(path, dtype=np.uint8, mode="r")
     if rank == 0:
-        # ~10-30 s of single-thread CPU work: 3 steps of 3B, 1 of the larger models
-        big = archive.size > 4e9
-        sample_steps = int(os.environ.get("CHPE_CPU_SAMPLE_STEPS", "1" if big else "3"))
-        threads = (os.cpu_count() or 1) if archive.size > 20e9 else 1
-        v_cpu, sample = oracle_cpu_baseline(archive, arch, sample_steps, threads,
-                                            rng.integers(0, 151936, sample_steps + 2))
+        # a bounded sample (~25 s) of the same workload on the host: the oracle
+        # at the timed positions over a KV cache prefilled to the same context
+        threads = os.cpu_count() or 1
+        v_cpu, n_cpu, p_cpu = oracle_sample(archive, arch, p0 - 1, 1, 8, threads, 25.0)
         cpu = {"value": v_cpu, "unit": "tok/s", "cores": threads, "kind": "port",
-               "sample": sample + f"; CPU restatement of src/chpe_engine.zig, {threads} thread(s) ({cpu_isa()})"}
+               "sample": f"{n_cpu} decode steps at positions {p_cpu}..{p_cpu + n_cpu - 1} over a KV "
+                         f"cache prefilled to the same context; CPU restatement of src/chpe_engine.zig, "
+                         f"rows split over {threads} threads (the reference is single-threaded) "
+                         f"({cpu_isa()})"}
     if rank != 0:
         return
-    ms_step = ms_max / args.steps
+    total = step_bytes + kvb
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
-        "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "u4->f32",
+        "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": M["dtype"],
         "data": "synthetic (seeded archive, random-init weights)",
-        "config": {"workload": M["name"], "prompt": args.prompt,
-                   "positions": f"{args.prompt + args.warmup}..{args.prompt + args.warmup + args.steps - 1}",
-                   "parallelism": f"tp{world}" if tp else f"replicas x{world}",
-                   "l2": f"inputs larger than L2 ({step_bytes / 1e9:.2f} GB of weights per step)",
-                   "algorithmic_bytes_per_token": step_bytes,
-                   "weight_stream_gbs": step_bytes / (ms_step / 1000) / 1e9,
-                   "weight_stream_frac_of_measured_hbm": step_bytes / (ms_step / 1000) / 1e9 / hbm,
-                   "per_role": per_role,
-                   "per_role_in_step_us": per_role_step},
+        "config": common_config(M, args.prompt, args.warmup, args.steps, world, tp),
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": eng.vocab * 4 + 24},
         "roofline": roof,
         "cpu_baseline": cpu,
         "clocks": cs.summary(),
         "gpu_launches": eng.kernels_per_step() * args.steps,
+        "detail": {
+            "algorithmic_bytes_per_token": total,
+            "weight_bytes_per_token": step_bytes,
+            "kv_bytes_per_token": kvb,
+            "step_gbs": total / (ms_step / 1000) / 1e9,
+            "step_frac_of_measured_hbm": total / (ms_step / 1000) / 1e9 / hbm / (world if tp else 1),
+            "weight_stream_gbs": step_bytes / (ms_step / 1000) / 1e9,
+            "per_role": per_role,
+            "per_role_in_step_us": per_role_step,
+        },
     }
     print(json.dumps(line), flush=True)
+
+
+def run_sweep(args):
+    """Config 2's isolated GEMV sweep on the 3B dense-cell archive: every
+    launch of a role (one per layer) timed alone from a cold L2."""
+    import chpe_qwen_engine_b200 as chpe
+    M = MODELS[args.model]
+    arch = getattr(chpe, M["arch"])
+    eng = chpe.Engine.from_bytes(chpe.synth_archive(getattr(chpe, M["synth"]), 0, seed=0), arch, 64)
+    eng.forward_tokens(np.array([1, 2], np.uint32))
+    hbm, peak_kind = peaks()
+    shapes = [("o", chpe.ROLE_O, "2048x2048"), ("gateup", chpe.ROLE_GATEUP, "2048x(2x11008) fused SwiGLU"),
+              ("down", chpe.ROLE_DOWN, "11008x2048"), ("lmhead", chpe.ROLE_LMHEAD, "2048x151936 tied"),
+              ("qkv", chpe.ROLE_QKV, "2048x(2048+256+256) fused RMSNorm")]
+    rows = {}
+    for name, role, shape in shapes:
+        m, b, n = eng.bench_kernel_cold(role, rounds=max(1, args.steps // 8))
+        g = b / (m / 1000) / 1e9
+        rows[name] = {"shape_in_x_out": shape, "kernel": eng.op_kernel_name(role), "avg_us": round(m * 1000, 2),
+                      "bytes_per_launch": b, "gbs": round(g, 1), "frac": round(g / hbm, 3), "launches": n}
+    print(json.dumps({"sweep": M["name"], "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s",
+                      "timing": "CUDA events around each launch, a 256 MiB buffer written before it (cold L2)",
+                      "shapes": rows}), flush=True)
 
 
 def main():
@@ -358,6 +427,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--model", default="72b-w4", choices=sorted(MODELS))
+    ap.add_argument("--sweep", action="store_true",
+                    help="config 2's isolated GEMV sweep (3B archives): per-shape GB/s from a cold L2")
     ap.add_argument("--prompt", type=int, default=None,
                     help="prompt tokens decoded before timing (default: the model's config)")
     ap.add_argument("--kernel-only", default=None,
@@ -375,6 +446,11 @@ def main():
     args.prompt_given = args.prompt is not None
     if args.prompt is None:
         args.prompt = MODELS[args.model]["prompt"]
+    if args.sweep:
+        if args.model not in ("3b-w4", "3b-w2", "3b-fp16"):
+            args.model = "3b-w4"
+        run_sweep(args)
+        return
     if args.kernel_only in ("flat-aligned", "flat-stream"):
         import chpe_qwen_engine_b200 as chpe
         eng = chpe.Engine.from_bytes(chpe.synth_archive(chpe.SYNTH_3B_W4, 0, seed=0), chpe.ARCH_3B, 64)

@@ -53,6 +53,7 @@ SYMBOLS = [
     ("chpe_bench_host", _I, [_P, _U32P, _S, _FP, C.POINTER(C.c_double)]),
     ("chpe_bench_kernel", _I, [_P, _I, _I, _FP, C.POINTER(C.c_double), C.POINTER(C.c_int)]),
     ("chpe_role_kernel_name", C.c_char_p, [_P, _I]),
+    ("chpe_bench_kernel_cold", _I, [_P, _I, _I, _FP, C.POINTER(C.c_double), C.POINTER(C.c_int)]),
     ("chpe_init_tp", _P, [C.c_char_p, _I, C.c_uint32, _I, _I, _I]),
     ("chpe_init_tp_bytes", _P, [_P, C.c_uint64, _I, C.c_uint32, _I, _I, _I]),
     ("chpe_tp_export_handle", _I, [_P, C.c_char_p]),
@@ -67,10 +68,15 @@ SYMBOLS = [
     ("chpe_kernels_per_step", _I, [_P]),
     ("chpe_get_position", _U32, [_P]),
     ("chpe_last_error", C.c_char_p, [_P]),
+    ("chpe_kv_page_size", _U32, []),
+    ("chpe_kv_load", _I, [_P, _U32, _U32, _U32, _FP, _FP]),
+    ("chpe_kv_set_page_order", _I, [_P, _U32P, _U32]),
+    ("chpe_kv_page_table", _I, [_P, _U32P, _U32, _U32P]),
     ("chpe_probe_gemv_linear", _I, [_P, _U64, _U64, _FP, _U64, _FP, _U64, _U64, _I, _I64]),
     ("chpe_attention_decode_noalloc", _I, [_P, _P, _P, _P, _P, _P, _U32, _U32, _U32, _U32, _U32, _F, _P]),
     ("chpe_probe_attention", _I, [_P, _U32, _U32, _FP, _FP, _FP, _FP]),
     ("chpe_probe_embed", _I, [_P, _U32, _FP]),
+    ("chpe_probe_wait_timeout", _I, [_P, _U32]),
     ("chpe_probe_dequant_cell", _I, [_P, _U64, _I, _FP, _U64, C.POINTER(C.c_uint64)]),
 ]
 
@@ -303,6 +309,13 @@ class Engine:
             raise ChpeError(self._err())
         return ms.value, b.value, n.value
 
+    def bench_kernel_cold(self, role: int, rounds: int = 2) -> tuple[float, float, int]:
+        """bench_kernel with an L2 flush before every launch."""
+        ms, b, n = C.c_float(), C.c_double(), C.c_int()
+        if lib().chpe_bench_kernel_cold(self.ctx, role, rounds, C.byref(ms), C.byref(b), C.byref(n)) != 0:
+            raise ChpeError(self._err())
+        return ms.value, b.value, n.value
+
     def op_kernel_name(self, role: int) -> str:
         """Kernel that runs the first op of `role`."""
         return (lib().chpe_role_kernel_name(self.ctx, role) or b"").decode()
@@ -321,6 +334,30 @@ class Engine:
     def step_weight_bytes(self) -> float:
         """Algorithmic weight bytes one step streams on this rank."""
         return lib().chpe_step_weight_bytes(self.ctx)
+
+    # -- paged KV cache -------------------------------------------------------
+    def kv_load(self, layer: int, pos0: int, k, v):
+        """chpe_kv_load: K (rotated) / V rows [n][kv_heads*head_dim] at pos0.."""
+        k = np.ascontiguousarray(k, np.float32)
+        v = np.ascontiguousarray(v, np.float32)
+        n = k.shape[0] if k.ndim > 1 else 1
+        if lib().chpe_kv_load(self.ctx, layer, pos0, n, _fp(k), _fp(v)) != 0:
+            raise ChpeError(self._err())
+
+    def kv_set_page_order(self, order):
+        o = np.ascontiguousarray(order, np.uint32)
+        if lib().chpe_kv_set_page_order(self.ctx, _u32p(o), o.size) != 0:
+            raise ChpeError(self._err())
+
+    def kv_page_table(self) -> tuple[np.ndarray, int]:
+        """(physical page of each mapped logical page, pages in the pool)."""
+        npg = C.c_uint32()
+        n = lib().chpe_kv_page_table(self.ctx, None, 0, C.byref(npg))
+        out = np.zeros(max(n, 1), np.uint32)
+        n = lib().chpe_kv_page_table(self.ctx, _u32p(out), out.size, C.byref(npg))
+        if n < 0:
+            raise ChpeError(self._err())
+        return out[:n].copy(), int(npg.value)
 
     def kernels_per_step(self) -> int:
         return lib().chpe_kernels_per_step(self.ctx)

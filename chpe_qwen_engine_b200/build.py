@@ -2,6 +2,8 @@
 
 * libchpe.so        -- the product: C ABI + CUDA kernels for sm_100a (nvcc)
 * libchpe_synth.so  -- deterministic synthetic archive generator (gcc)
+* chpe_fwd          -- the command-line front end over libchpe.so (the
+                       reference's chpe_fwd contract)
 
 Usage: python -m chpe_qwen_engine_b200.build [--force]
 """
@@ -17,6 +19,7 @@ CSRC = os.path.join(PKG, "csrc")
 ROOT = os.path.dirname(PKG)
 LIBCHPE = os.path.join(PKG, "libchpe.so")
 LIBSYNTH = os.path.join(PKG, "libchpe_synth.so")
+CHPE_FWD = os.path.join(PKG, "chpe_fwd")
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -77,9 +80,20 @@ def build_engine(force: bool = False) -> str:
     return LIBCHPE
 
 
+def build_cli(force: bool = False) -> str:
+    """chpe_fwd, linked against the in-tree libchpe.so (found through $ORIGIN)."""
+    if force or _stale(CHPE_FWD, ["chpe_fwd.cpp", "../../include/chpe.h"]) or (
+            os.path.exists(CHPE_FWD) and os.path.getmtime(LIBCHPE) > os.path.getmtime(CHPE_FWD)):
+        cmd = [_nvcc(), "-O2", "-std=c++17", "-o", CHPE_FWD, os.path.join(CSRC, "chpe_fwd.cpp"),
+               "-I", os.path.join(ROOT, "include"), "-L", PKG, "-lchpe", "-Xlinker", "-rpath=$ORIGIN"]
+        subprocess.run(cmd, check=True)
+    return CHPE_FWD
+
+
 def build_all(force: bool = False) -> None:
     build_synth(force)
     build_engine(force)
+    build_cli(force)
 
 
 if __name__ == "__main__":

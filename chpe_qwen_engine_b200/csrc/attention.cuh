@@ -3,8 +3,7 @@
 // Restates the forwardDecode attention block (chpe_engine.zig:1688-1734):
 // NeoX rotate-half RoPE on q and k (applyRope, :195-216), append k/v at
 // `pos`, then per query head softmax(q.k * 1/sqrt(hd)) over t <= pos and the
-// weighted sum of v.  Cache layout: [max_seq][kv_heads][head_dim] FP16 per
-// layer.
+// weighted sum of v.  The cache holds FP16 K and V, paged (below).
 //
 // One CTA per (kv head, split of the positions).  A CTA stages its positions
 // in tiles of ATT_TT rows: every thread issues its 16-byte K and V loads of
@@ -31,8 +30,19 @@ struct AttnLaunch {
   StepState* st;
   int32_t H, KV, HD, nsplit;  // H, KV: this rank's heads (all of them on one GPU)
   int32_t max_seq;      // cache capacity; a step at pos >= max_seq is skipped
+  const uint32_t* pages;  // page table (logical page -> physical page), or nullptr: contiguous
+  int32_t page_shift;   // log2(positions per page)
+  uint32_t n_pages;     // physical pages in this layer's pool (entries beyond read page 0)
   TpLink tp;            // tensor parallel: out lies in the exchange region
 };
+
+// Cache row of position t: the physical row in the layer's pool.
+CHPE_DEV size_t kv_cache_row(const AttnLaunch& P, int t) {
+  if (!P.pages) return (size_t)t;
+  uint32_t pg = P.pages[t >> P.page_shift];
+  if (pg >= P.n_pages) pg = 0;  // an unmapped entry never addresses outside the pool
+  return ((size_t)pg << P.page_shift) + (size_t)(t & ((1 << P.page_shift) - 1));
+}
 
 constexpr int ATT_TT = 32;  // positions per staged tile
 // Splits of the positions per kv head: between 16 and 64, about two CTAs per
@@ -109,7 +119,7 @@ CHPE_DEV bool attention_body(const AttnLaunch& P) {
   for (int i = threadIdx.x; i < HD; i += blockDim.x) vn[i] = P.v[(size_t)kvh * HD + i];
   __syncthreads();
   if (split == 0) {
-    size_t base = ((size_t)pos * P.KV + kvh) * HD;
+    size_t base = (kv_cache_row(P, pos) * P.KV + kvh) * HD;
     for (int i = threadIdx.x; i < HD; i += blockDim.x) {
       P.kc[base + i] = __float2half_rn(kn[i]);
       P.vc[base + i] = __float2half_rn(vn[i]);
@@ -150,7 +160,7 @@ CHPE_DEV bool attention_body(const AttnLaunch& P) {
         kr[u] = *reinterpret_cast<uint4*>(hk);
         vr[u] = *reinterpret_cast<uint4*>(hv);
       } else {
-        const size_t off = ((size_t)t * P.KV + kvh) * HD + c8;
+        const size_t off = (kv_cache_row(P, t) * P.KV + kvh) * HD + c8;
         kr[u] = *reinterpret_cast<const uint4*>(P.kc + off);
         vr[u] = *reinterpret_cast<const uint4*>(P.vc + off);
       }

@@ -1,22 +1,26 @@
 // attention_noalloc.cu -- decode attention for callers that cannot allocate
 // device memory.
 //
-// Some callers of this library must not call cudaMalloc: code that records
-// work into a CUDA graph (allocation is not a capturable operation), runtimes
-// that hand out device memory only from their own fixed pools, and plugins
-// loaded into a host process that owns all allocation.  They have their
-// inputs, caches and outputs already, but the decode attention kernel also
-// needs scratch: the per-split softmax partials, the arrival counters of the
-// split merge, the RoPE inverse frequencies and the step's position.  Here
-// that scratch is a file-scope static device array of a fixed size, present on
-// every GPU that loads the library for as long as the library stays loaded.
+// Some callers of this library must not call cudaMalloc: serving runtimes
+// that hand out device memory only from their own pre-sized pools (an
+// allocation behind their back can exceed the budget they planned for the
+// KV cache and the weights, and cudaMalloc may synchronise the device in the
+// middle of their pipelined work), and plugins loaded into a host process that
+// owns all allocation on the GPU.  They have their inputs, caches and outputs
+// already, but the decode attention kernel also needs scratch: the per-split
+// softmax partials, the arrival counters of the split merge, the RoPE inverse
+// frequencies and the step's position.  Here that scratch is a file-scope
+// static device array of a fixed size (1 MiB), present on every GPU that
+// loads the library for as long as the library stays loaded.
 //
 // Set-up: the first call on a device (with that device current) resolves the
-// array's device address with cudaGetSymbolAddress and caches it; make that
-// first call before any stream capture.  Every call shares the array and
-// finds the previous call's contents there, so each call clears the counters
-// it relies on; calls whose kernels overlap on the GPU (different streams, no
-// ordering between them) race on the array and must not be issued.
+// array's device address with cudaGetSymbolAddress and caches it.  Every call
+// shares the array and finds the previous call's contents there, so each call
+// clears the counters it relies on and rewrites the position and frequencies;
+// calls whose kernels overlap on the GPU (different streams, no ordering
+// between them) race on the array and must not be issued.  Each call copies
+// its position and RoPE frequencies from host memory with cudaMemcpyAsync
+// (the source is staged before the call returns).
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -26,6 +30,7 @@
 
 #include "../../include/chpe.h"
 #include "attention.cuh"
+#include "engine.h"
 
 namespace {
 
@@ -41,7 +46,11 @@ constexpr int kMaxDevices = 64;
 std::mutex g_mu;
 void* g_scratch_ptr[kMaxDevices] = {};
 
-int fail(int code, const std::string&) { return code; }
+// The message is kept for chpe_last_error(NULL) on this thread.
+int fail(int code, const std::string& msg) {
+  chpe::set_thread_error("chpe_attention_decode_noalloc: " + msg);
+  return code;
+}
 
 }  // namespace
 
@@ -80,8 +89,8 @@ extern "C" int chpe_attention_decode_noalloc(const float* q, const float* k, con
   cudaStream_t s = static_cast<cudaStream_t>(stream);
 
   // step state (this position, no early exit) and RoPE frequencies, computed
-  // as applyRope does (chpe_engine.zig:200-202); both are copied from host
-  // values that outlive the copies (pageable sources are staged before return)
+  // as applyRope does (chpe_engine.zig:200-202); pageable sources are staged
+  // by cudaMemcpyAsync before it returns
   chpe::StepState st;
   memset(&st, 0, sizeof(st));
   st.pos = (int32_t)pos;
@@ -117,5 +126,6 @@ extern "C" int chpe_attention_decode_noalloc(const float* q, const float* k, con
   else chpe::attention_kernel<256><<<grid, threads, 0, s>>>(P);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(-3, std::string("launch: ") + cudaGetErrorString(e));
+  chpe::set_thread_error("");
   return 0;
 }

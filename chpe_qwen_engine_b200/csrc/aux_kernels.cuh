@@ -316,4 +316,19 @@ __global__ void dequant_kernel(const __grid_constant__ DequantLaunch P) {
   }
 }
 
+// Failure-detection probe: one thread waits, bounded by tp.wait_polls, for an
+// arrival on counter `kind` of this rank's exchange counters that nothing
+// sends (a slot no exchange uses), then records the timeout in StepState::err
+// exactly as a tensor-parallel wait that gave up does.
+struct WaitProbeLaunch {
+  TpLink tp;
+  StepState* st;
+  int32_t kind;
+};
+__global__ void wait_probe_kernel(const __grid_constant__ WaitProbeLaunch P) {
+  if (threadIdx.x != 0) return;
+  const unsigned long long target = ld_acquire_sys(&P.tp.sh->sig[P.kind]) + 1ull;
+  if (!tp_wait_count(P.tp, P.kind, target)) atomicExch(&P.st->err, 1);
+}
+
 }  // namespace chpe

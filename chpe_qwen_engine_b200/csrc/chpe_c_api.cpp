@@ -123,6 +123,8 @@ void store_result(Ctx* c) {
 
 }  // namespace
 
+void chpe::set_thread_error(const std::string& msg) { g_init_error = msg; }
+
 extern "C" {
 
 void* chpe_init(const char* archive_path) {
@@ -279,6 +281,19 @@ int chpe_bench_kernel(void* ctx, int role, int rounds, float* avg_ms, double* by
   return 0;
 }
 
+int chpe_bench_kernel_cold(void* ctx, int role, int rounds, float* avg_ms, double* bytes_per_launch,
+                           int* launches) {
+  if (!ctx || !avg_ms || !bytes_per_launch || !launches || rounds < 1) return -1;
+  Ctx* c = (Ctx*)ctx;
+  try {
+    c->engine->bench_role(role, rounds, avg_ms, bytes_per_launch, launches, true);
+  } catch (const std::exception& e) {
+    c->err = e.what();
+    return -1;
+  }
+  return 0;
+}
+
 int chpe_profile_step(void* ctx, float* op_ms, int* op_roles, int cap) {
   if (!ctx || cap < 0) return -1;
   Ctx* c = (Ctx*)ctx;
@@ -345,6 +360,39 @@ void chpe_free(void* ctx) {
   delete c;
 }
 
+int chpe_kv_load(void* ctx, uint32_t layer, uint32_t pos0, uint32_t n, const float* k, const float* v) {
+  if (!ctx || (n > 0 && (!k || !v))) return -1;
+  Ctx* c = (Ctx*)ctx;
+  try {
+    c->engine->kv_load(layer, pos0, n, k, v);
+  } catch (const std::exception& e) {
+    c->err = e.what();
+    return -1;
+  }
+  return 0;
+}
+
+int chpe_kv_set_page_order(void* ctx, const uint32_t* order, uint32_t n) {
+  if (!ctx || !order) return -1;
+  Ctx* c = (Ctx*)ctx;
+  try {
+    c->engine->kv_set_page_order(order, n);
+  } catch (const std::exception& e) {
+    c->err = e.what();
+    return -1;
+  }
+  return 0;
+}
+
+int chpe_kv_page_table(void* ctx, uint32_t* out, uint32_t cap, uint32_t* num_pages) {
+  if (!ctx) return -1;
+  Ctx* c = (Ctx*)ctx;
+  if (num_pages) *num_pages = c->engine->kv_pages();
+  return (int)c->engine->kv_page_table(out, out ? cap : 0);
+}
+
+uint32_t chpe_kv_page_size(void) { return chpe::Engine::kKvPage; }
+
 int chpe_probe_gemv_linear(void* ctx, uint64_t tile_start, uint64_t num_tiles, const float* x,
                            uint64_t x_len, float* y, uint64_t r_total, uint64_t c_total,
                            int accumulate, int64_t bias_tile) {
@@ -366,6 +414,18 @@ int chpe_probe_attention(void* ctx, uint32_t layer, uint32_t pos, const float* q
   Ctx* c = (Ctx*)ctx;
   try {
     c->engine->debug_attention(layer, pos, q, k, v, out);
+  } catch (const std::exception& e) {
+    c->err = e.what();
+    return -1;
+  }
+  return 0;
+}
+
+int chpe_probe_wait_timeout(void* ctx, uint32_t polls) {
+  if (!ctx) return -1;
+  Ctx* c = (Ctx*)ctx;
+  try {
+    c->engine->debug_wait_timeout(polls);
   } catch (const std::exception& e) {
     c->err = e.what();
     return -1;

@@ -21,13 +21,16 @@ extern "C" {
 #endif
 
 enum {
-  CHPE_SYNTH_3B_FP16_RAW = 0, /* 376853 raw tiles, FLAG_RAW_FP16 */
+  /* Benchmark configs are numbered from 1 in the order the benchmark
+   * definition lists them: 1 = 3B FP16, 2 = 3B 4/2-bit, 3 = 9B 4-bit,
+   * 4 = 9B verify, 5 = 72B 4-bit and FP16. */
+  CHPE_SYNTH_3B_FP16_RAW = 0, /* 376853 raw tiles, FLAG_RAW_FP16 (config 1) */
   CHPE_SYNTH_3B_BF16_RAW = 1, /* 376853 raw tiles, BF16 */
-  CHPE_SYNTH_3B_W4 = 2,       /* 94349 cells, 4-bit group-128 (config 1) */
-  CHPE_SYNTH_3B_W2 = 3,       /* 94349 cells, 2-bit group-128 (config 1) */
-  CHPE_SYNTH_9B_W4 = 4,       /* 546681 cells, 4-bit (config 2) */
-  CHPE_SYNTH_72B_W4 = 5,      /* 2219153 cells, 4-bit (config 4) */
-  CHPE_SYNTH_72B_FP16_RAW = 6,/* 2219153 raw tiles, reference map (config 4) */
+  CHPE_SYNTH_3B_W4 = 2,       /* 94349 cells, 4-bit group-128 (config 2) */
+  CHPE_SYNTH_3B_W2 = 3,       /* 94349 cells, 2-bit group-128 (config 2) */
+  CHPE_SYNTH_9B_W4 = 4,       /* 546681 cells, 4-bit (configs 3 and 4) */
+  CHPE_SYNTH_72B_W4 = 5,      /* 2219153 cells, 4-bit (config 5) */
+  CHPE_SYNTH_72B_FP16_RAW = 6,/* 2219153 raw tiles, reference map (config 5) */
   CHPE_SYNTH_9B_I8_RAW = 7,   /* 546681 raw tiles, INT8 (flags 0x08) */
   CHPE_SYNTH_NUM_CONFIGS = 8
 };

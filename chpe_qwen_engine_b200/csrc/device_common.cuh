@@ -105,9 +105,11 @@ CHPE_DEV unsigned long long ld_acquire_sys(const unsigned long long* p) {
 CHPE_DEV void red_add_relaxed_sys(unsigned long long* p, unsigned long long v) {
   asm volatile("red.relaxed.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
-// Bounded wait until this rank's counter `kind` reaches `target`.
+// Bounded wait until this rank's counter `kind` reaches `target`: at most
+// t.wait_polls polls (kMaxWaitPolls when 0), each followed by a short sleep.
 CHPE_DEV bool tp_wait_count(const chpe::TpLink& t, int kind, unsigned long long target) {
-  for (uint32_t i = 0; i < kMaxWaitPolls; i++) {
+  const uint32_t limit = t.wait_polls ? t.wait_polls : kMaxWaitPolls;
+  for (uint32_t i = 0; i < limit; i++) {
     if (ld_acquire_sys(&t.sh->sig[kind]) >= target) return true;
     if ((i & 1023u) == 0u && t.err && *reinterpret_cast<volatile const int32_t*>(t.err)) return false;
     __nanosleep(64);

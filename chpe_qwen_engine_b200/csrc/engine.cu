@@ -7,6 +7,7 @@
 #include <cmath>
 #include <cstdlib>
 #include <cstdio>
+#include <algorithm>
 #include <cstring>
 #include <stdexcept>
 #include <string>
@@ -203,6 +204,7 @@ Engine::Engine(const uint8_t* bytes, uint64_t len, int arch, uint32_t max_seq, i
     if (f_.record_count > avail) f_.record_count = avail;
   }
 
+  if (const char* wp = getenv("CHPE_WAIT_POLLS")) wait_polls_ = (uint32_t)strtoul(wp, nullptr, 10);
   CK(cudaSetDevice(device_));
   CK(cudaDeviceGetAttribute(&num_sms_, cudaDevAttrMultiProcessorCount, device_));
   CK(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
@@ -278,9 +280,27 @@ Engine::Engine(const uint8_t* bytes, uint64_t len, int arch, uint32_t max_seq, i
   nsplit_ = attn_splits(num_sms_, (int)A.KV, (int)max_seq_);
   d_part_ = (float*)dalloc((size_t)A.KV * kAttnMaxSplits * G * (A.HD + 4) * 4);
   d_counters_ = (uint32_t*)dalloc(A.KV * 4);
-  size_t kv_elems = (size_t)A.L * max_seq_ * A.KV * A.HD;
-  d_kc_ = (__half*)dalloc(kv_elems * 2);
-  d_vc_ = (__half*)dalloc(kv_elems * 2);
+  // Paged KV cache: per layer a pool of n_pages pages of kKvPage positions of
+  // this rank's kv heads; the page table starts all-zero (page 0) and the
+  // free list hands out pages 0, 1, 2, ... unless an order is set.
+  kv0_ = 0;
+  kvl_ = A.KV;
+  if (tp_world_ > 1) {
+    ChpeTpSlice sl;
+    if (chpe_tp_slice_of(arch_id_, tp_rank_, tp_world_, &sl) == 0) {
+      kv0_ = sl.kv0;
+      kvl_ = sl.kvl;
+    }
+  }
+  n_pages_ = (max_seq_ + kKvPage - 1) / kKvPage;
+  layer_kv_elems_ = (size_t)n_pages_ * kKvPage * kvl_ * A.HD;
+  d_kc_ = (__half*)dalloc((size_t)A.L * layer_kv_elems_ * 2);
+  d_vc_ = (__half*)dalloc((size_t)A.L * layer_kv_elems_ * 2);
+  d_pages_ = (uint32_t*)dalloc((size_t)n_pages_ * 4);
+  CK(cudaMallocHost(&h_pages_, (size_t)n_pages_ * 4));
+  memset(h_pages_, 0, (size_t)n_pages_ * 4);
+  free_pages_.clear();
+  for (uint32_t i = n_pages_; i-- > 0;) free_pages_.push_back(i);
   d_res_ = (StepResult*)dalloc(sizeof(StepResult));
   max_gen_ = max_seq_;
   d_gen_ = (int32_t*)dalloc((size_t)max_gen_ * 4);
@@ -315,6 +335,7 @@ Engine::~Engine() {
   if (h_st_) cudaFreeHost(h_st_);
   if (h_res_) cudaFreeHost(h_res_);
   if (h_tok_) cudaFreeHost(h_tok_);
+  if (h_pages_) cudaFreeHost(h_pages_);
   if (stream_) cudaStreamDestroy(stream_);
   delete ops_;
 }
@@ -1068,6 +1089,7 @@ void Engine::build_step_tp() {
   for (int r = 0; r < kTpMax; r++) base.delta[r] = tp_delta_[r];
   base.sh = d_tpsh_;
   base.err = &d_st_->err;
+  base.wait_polls = wait_polls_;
   base.wait_sig = -1;
   base.signal_sig = -1;
   base.wait_per_step = A.L;
@@ -1115,9 +1137,12 @@ void Engine::build_step_tp() {
       at.q = d_q_;
       at.k = d_k_;
       at.v = d_v_;
-      size_t lay = (size_t)l * max_seq_ * kvl * A.HD;  // this rank's kv heads only
-      at.kc = d_kc_ + lay;
-      at.vc = d_vc_ + lay;
+      if (kvl != kvl_) throw std::runtime_error("tensor parallel: kv heads differ from the cache layout");
+      at.kc = d_kc_ + (size_t)l * layer_kv_elems_;  // this rank's kv heads only
+      at.vc = d_vc_ + (size_t)l * layer_kv_elems_;
+      at.pages = d_pages_;
+      at.page_shift = kKvPageShift;
+      at.n_pages = n_pages_;
       at.out = d_attn_ + (size_t)h0 * A.HD;
       at.part = d_part_;
       at.counters = d_counters_;
@@ -1190,9 +1215,11 @@ void Engine::build_step() {
       at.q = d_q_;
       at.k = d_k_;
       at.v = d_v_;
-      size_t lay = (size_t)l * max_seq_ * A.KV * A.HD;
-      at.kc = d_kc_ + lay;
-      at.vc = d_vc_ + lay;
+      at.kc = d_kc_ + (size_t)l * layer_kv_elems_;
+      at.vc = d_vc_ + (size_t)l * layer_kv_elems_;
+      at.pages = d_pages_;
+      at.page_shift = kKvPageShift;
+      at.n_pages = n_pages_;
       at.out = d_attn_;
       at.part = d_part_;
       at.counters = d_counters_;
@@ -1396,6 +1423,7 @@ static const char* kind_name(int kind) {
 int Engine::profile_step(float* op_ms, int* op_roles, int cap) {
   if (!graph_) throw std::runtime_error("run forward() first");
   if ((uint64_t)pos_ + 1 > max_seq_) throw std::runtime_error("sequence exceeds max_seq_len");
+  kv_ensure((uint64_t)pos_ + 1);
   const std::vector<Op>& ops = *ops_;
   const int n = (int)ops.size();
   std::vector<cudaEvent_t> ev(n + 1);
@@ -1491,6 +1519,80 @@ void Engine::ensure_graph() {
   CK(cudaStreamDestroy(cs));
 }
 
+// ---- paged KV cache ---------------------------------------------------------
+// Host bookkeeping of the page table.  Every API call that runs steps ends by
+// synchronising the engine stream, so the pinned mirror is never rewritten
+// while an earlier copy of it is still pending.
+void Engine::kv_ensure(uint64_t end_pos) {
+  if (end_pos > max_seq_) throw std::runtime_error("sequence exceeds max_seq_len");
+  const uint32_t need = (uint32_t)((end_pos + kKvPage - 1) >> kKvPageShift);
+  if (need <= mapped_) return;
+  if (need > n_pages_) throw std::runtime_error("KV page pool exhausted");
+  for (uint32_t lp = mapped_; lp < need; lp++) {
+    if (free_pages_.empty()) throw std::runtime_error("KV page pool exhausted");
+    h_pages_[lp] = free_pages_.back();
+    free_pages_.pop_back();
+  }
+  CK(cudaMemcpyAsync(d_pages_ + mapped_, h_pages_ + mapped_, (size_t)(need - mapped_) * 4,
+                     cudaMemcpyHostToDevice, stream_));
+  mapped_ = need;
+}
+
+void Engine::kv_reset() {
+  // back onto the stack in reverse, so the same order comes out again
+  for (uint32_t lp = mapped_; lp-- > 0;) free_pages_.push_back(h_pages_[lp]);
+  mapped_ = 0;
+}
+
+void Engine::kv_set_page_order(const uint32_t* order, uint32_t n) {
+  if (n != n_pages_) throw std::runtime_error("page order must list every page of the pool once");
+  std::vector<char> seen(n_pages_, 0);
+  for (uint32_t i = 0; i < n; i++) {
+    if (order[i] >= n_pages_ || seen[order[i]]) throw std::runtime_error("page order is not a permutation");
+    seen[order[i]] = 1;
+  }
+  CK(cudaStreamSynchronize(stream_));
+  mapped_ = 0;
+  free_pages_.assign(order, order + n);
+  std::reverse(free_pages_.begin(), free_pages_.end());
+}
+
+uint32_t Engine::kv_page_table(uint32_t* out, uint32_t cap) const {
+  for (uint32_t i = 0; i < mapped_ && i < cap; i++) out[i] = h_pages_[i];
+  return mapped_;
+}
+
+void Engine::kv_load(uint32_t layer, uint32_t pos0, uint32_t n, const float* k, const float* v) {
+  const ChpeArch& A = *arch_;
+  if (layer >= A.L) throw std::runtime_error("layer out of range");
+  if ((uint64_t)pos0 + n > max_seq_) throw std::runtime_error("sequence exceeds max_seq_len");
+  if (n == 0) return;
+  CK(cudaSetDevice(device_));
+  kv_ensure((uint64_t)pos0 + n);
+  const size_t full = (size_t)A.KV * A.HD, mine = (size_t)kvl_ * A.HD;
+  std::vector<__half> hk((size_t)kKvPage * mine), hv((size_t)kKvPage * mine);
+  __half* kb = d_kc_ + (size_t)layer * layer_kv_elems_;
+  __half* vb = d_vc_ + (size_t)layer * layer_kv_elems_;
+  for (uint32_t p = pos0; p < pos0 + n;) {
+    const uint32_t lp = p >> kKvPageShift, in = p & (kKvPage - 1);
+    uint32_t run = kKvPage - in;
+    if (run > pos0 + n - p) run = pos0 + n - p;
+    for (uint32_t r = 0; r < run; r++) {
+      const float* ks = k + (size_t)(p - pos0 + r) * full + (size_t)kv0_ * A.HD;
+      const float* vs = v + (size_t)(p - pos0 + r) * full + (size_t)kv0_ * A.HD;
+      for (size_t i = 0; i < mine; i++) {
+        hk[r * mine + i] = __float2half_rn(ks[i]);
+        hv[r * mine + i] = __float2half_rn(vs[i]);
+      }
+    }
+    const size_t row = (size_t)h_pages_[lp] * kKvPage + in;
+    CK(cudaMemcpyAsync(kb + row * mine, hk.data(), run * mine * 2, cudaMemcpyHostToDevice, stream_));
+    CK(cudaMemcpyAsync(vb + row * mine, hv.data(), run * mine * 2, cudaMemcpyHostToDevice, stream_));
+    CK(cudaStreamSynchronize(stream_));  // the staging vectors are reused
+    p += run;
+  }
+}
+
 void Engine::run_steps(size_t n) {
   for (size_t i = 0; i < n; i++) CK(cudaGraphLaunch(graph_, stream_));
 }
@@ -1500,7 +1602,29 @@ void Engine::sync_result() {
   CK(cudaMemcpyAsync(&h_st_->err, &d_st_->err, 4, cudaMemcpyDeviceToHost, stream_));
   CK(cudaStreamSynchronize(stream_));
   last_ = *h_res_;
-  if (h_st_->err) throw std::runtime_error("a device wait timed out (bounded mbarrier wait)");
+  if (h_st_->err) {
+    // Every kernel returned (the waits are bounded); clear the flag so the
+    // next call starts clean, and report the timeout.
+    h_st_->err = 0;
+    CK(cudaMemcpyAsync(&d_st_->err, &h_st_->err, 4, cudaMemcpyHostToDevice, stream_));
+    CK(cudaStreamSynchronize(stream_));
+    throw std::runtime_error("a device wait timed out (bounded wait; the step's results are invalid)");
+  }
+}
+
+void Engine::debug_wait_timeout(uint32_t polls) {
+  CK(cudaSetDevice(device_));
+  WaitProbeLaunch P{};
+  P.tp.world = 2;  // a wait only reads this rank's own counters
+  P.tp.rank = 0;
+  P.tp.sh = d_tpsh_;
+  P.tp.err = &d_st_->err;
+  P.tp.wait_polls = polls ? polls : 1;
+  P.st = d_st_;
+  P.kind = 7;  // no exchange signals this slot
+  wait_probe_kernel<<<1, 32, 0, stream_>>>(P);
+  CK(cudaGetLastError());
+  sync_result();
 }
 
 // Positions start_pos.. for the given tokens (forwardDecode per token).
@@ -1508,6 +1632,8 @@ void Engine::forward(const uint32_t* toks, size_t n, uint32_t start_pos) {
   if (n == 0) return;
   if (ops_->empty()) throw std::runtime_error("tensor parallel engine: call tp_connect first");
   if ((uint64_t)start_pos + n > max_seq_) throw std::runtime_error("sequence exceeds max_seq_len");
+  if (start_pos == 0) kv_reset();  // a new sequence
+  kv_ensure((uint64_t)start_pos + n);
   if (!graph_) {
     // The warm-up launch inside ensure_graph runs one step on whatever state
     // is current; run it on a scratch position that is overwritten below.
@@ -1549,6 +1675,7 @@ void Engine::generate(const uint32_t* prompt, size_t n_prompt, size_t n_gen, uin
   if (n_prompt + n_gen > max_seq_) throw std::runtime_error("sequence exceeds max_seq_len");
   forward(prompt, n_prompt, 0);
   if (n_gen == 0) return;
+  kv_ensure(n_prompt + n_gen);
   // the last prompt step's argmax is the first generated token
   out_tokens[0] = last_.argmax_token;
   int32_t one = 1, zero = 0;
@@ -1568,6 +1695,8 @@ void Engine::verify(const uint32_t* toks, size_t m, uint32_t pos, float* logits_
   if (m == 0) return;
   if ((uint64_t)pos + m > max_seq_) throw std::runtime_error("sequence exceeds max_seq_len");
   if (m + 1 > h_tok_cap_) throw std::runtime_error("too many candidates");
+  if (pos == 0) kv_reset();
+  kv_ensure((uint64_t)pos + m);
   if (!graph_) {
     // build the graph with a warm step at the first candidate's position (its
     // cache entry is rewritten below)
@@ -1613,6 +1742,7 @@ void Engine::verify(const uint32_t* toks, size_t m, uint32_t pos, float* logits_
 float Engine::timed_greedy_steps(size_t n) {
   if (!graph_) throw std::runtime_error("run forward() first");
   if ((uint64_t)pos_ + n > max_seq_) throw std::runtime_error("sequence exceeds max_seq_len");
+  kv_ensure((uint64_t)pos_ + n);
   int32_t one = 1, zero = 0;
   CK(cudaMemcpyAsync(&d_st_->feed_argmax, &one, 4, cudaMemcpyHostToDevice, stream_));
   CK(cudaMemcpyAsync(&d_st_->n_gen, &zero, 4, cudaMemcpyHostToDevice, stream_));
@@ -1639,6 +1769,7 @@ float Engine::timed_greedy_steps(size_t n) {
 double Engine::timed_host_steps(const uint32_t* toks, size_t n, float* logits_host) {
   if (!graph_) throw std::runtime_error("run forward() first");
   if ((uint64_t)pos_ + n > max_seq_) throw std::runtime_error("sequence exceeds max_seq_len");
+  kv_ensure((uint64_t)pos_ + n);
   CK(cudaStreamSynchronize(stream_));
   uint64_t t0 = now_ns();
   for (size_t i = 0; i < n; i++) {
@@ -1659,7 +1790,8 @@ void Engine::copy_logits(float* out) const {
   CK(cudaMemcpy(out, d_logits_, (size_t)arch_->V * 4, cudaMemcpyDeviceToHost));
 }
 
-void Engine::bench_role(int role, int rounds, float* avg_ms, double* bytes_per_launch, int* launches) {
+void Engine::bench_role(int role, int rounds, float* avg_ms, double* bytes_per_launch, int* launches,
+                        bool flush_l2) {
   if (tp_world_ > 1)
     throw std::runtime_error("per-role timing launches one role alone; not available with tensor parallelism");
   std::vector<const Op*> sel;
@@ -1681,13 +1813,31 @@ void Engine::bench_role(int role, int rounds, float* avg_ms, double* bytes_per_l
   CK(cudaEventCreate(&a));
   CK(cudaEventCreate(&b));
   CK(cudaStreamSynchronize(stream_));
-  CK(cudaEventRecord(a, stream_));
-  for (int r = 0; r < rounds; r++)
-    for (const Op* op : sel) launch(*op, stream_);
-  CK(cudaEventRecord(b, stream_));
-  CK(cudaEventSynchronize(b));
   float ms = 0;
-  CK(cudaEventElapsedTime(&ms, a, b));
+  if (!flush_l2) {
+    CK(cudaEventRecord(a, stream_));
+    for (int r = 0; r < rounds; r++)
+      for (const Op* op : sel) launch(*op, stream_);
+    CK(cudaEventRecord(b, stream_));
+    CK(cudaEventSynchronize(b));
+    CK(cudaEventElapsedTime(&ms, a, b));
+  } else {
+    const size_t fb = 256ull << 20;  // twice the L2
+    void* flush = nullptr;
+    CK(cudaMalloc(&flush, fb));
+    for (int r = 0; r < rounds; r++)
+      for (const Op* op : sel) {
+        CK(cudaMemsetAsync(flush, r & 0xff, fb, stream_));
+        CK(cudaEventRecord(a, stream_));
+        launch(*op, stream_);
+        CK(cudaEventRecord(b, stream_));
+        CK(cudaEventSynchronize(b));
+        float one = 0.f;
+        CK(cudaEventElapsedTime(&one, a, b));
+        ms += one;
+      }
+    cudaFree(flush);
+  }
   cudaEventDestroy(a);
   cudaEventDestroy(b);
   *h_st_ = saved;
@@ -1728,6 +1878,7 @@ void Engine::debug_attention(uint32_t layer, uint32_t pos, const float* q, const
                              const float* v, float* out) {
   const ChpeArch& A = *arch_;
   if (layer >= A.L || pos >= max_seq_) throw std::runtime_error("layer or position out of range");
+  kv_ensure((uint64_t)pos + 1);
   const Op* att = nullptr;
   uint32_t seen = 0;
   for (const Op& op : *ops_)

@@ -19,6 +19,10 @@
 
 namespace chpe {
 
+// Records the calling thread's last error message, which chpe_last_error(NULL)
+// returns (failed inits and the context-free entry points).
+void set_thread_error(const std::string& msg);
+
 struct Op;  // one recorded kernel launch (engine.cu)
 
 struct EngineFacts {  // CHPEEngine fields after init sniffing (:862-918)
@@ -74,7 +78,10 @@ class Engine {
   // Times every recorded op of one role (ROLE_*) across all layers, `rounds`
   // times, with CUDA events on the engine stream; returns the average
   // milliseconds per launch and the algorithmic weight bytes per launch.
-  void bench_role(int role, int rounds, float* avg_ms, double* bytes_per_launch, int* launches);
+  // flush_l2: before every launch a 256 MiB buffer is written (evicting the
+  // weights from L2), and each launch is timed alone between its own events.
+  void bench_role(int role, int rounds, float* avg_ms, double* bytes_per_launch, int* launches,
+                  bool flush_l2 = false);
   std::string role_kernel_name(int role) const;
   // One greedy step launched op by op with CUDA events between the ops (no
   // graph); per-op milliseconds and roles.  With tensor parallelism every rank
@@ -93,6 +100,30 @@ class Engine {
   void debug_attention(uint32_t layer, uint32_t pos, const float* q, const float* k, const float* v,
                        float* out);
   void debug_dequant_cell(uint64_t tile, int flat, float* out, uint64_t cap, uint64_t* n_out);
+  // Runs a bounded device wait for an arrival that never comes, with `polls`
+  // polls at most; throws the device-timeout error the decode path raises and
+  // leaves the engine usable.
+  void debug_wait_timeout(uint32_t polls);
+
+  // ---- paged KV cache ------------------------------------------------------
+  // The cache of every layer is a pool of pages of kKvPage positions; the
+  // sequence's page table maps logical page p (positions p*kKvPage..) to a
+  // physical page, the same for every layer.  Pages are taken from a free
+  // list when a step first reaches them and all return to it when a new
+  // sequence starts at position 0.
+  static constexpr int kKvPageShift = 6;
+  static constexpr uint32_t kKvPage = 1u << kKvPageShift;
+  // Writes K (already rotated, as the cache holds it) and V rows
+  // [n][kv_heads*head_dim] for positions pos0..pos0+n-1 of one layer into the
+  // cache as FP16 (round to nearest), mapping pages as needed.  With tensor
+  // parallelism the rows hold every kv head; this rank keeps its own.
+  void kv_load(uint32_t layer, uint32_t pos0, uint32_t n, const float* k, const float* v);
+  // Sets the order in which free pages are handed out (a permutation of
+  // 0..n_pages-1); returns every mapped page first (a new sequence).
+  void kv_set_page_order(const uint32_t* order, uint32_t n);
+  // Mapped logical pages and their physical pages (up to cap entries).
+  uint32_t kv_page_table(uint32_t* out, uint32_t cap) const;
+  uint32_t kv_pages() const { return n_pages_; }
 
   cudaStream_t stream() const { return stream_; }
 
@@ -113,6 +144,8 @@ class Engine {
   void launch(const Op& op, cudaStream_t s) const;
   void record(cudaStream_t s) const;
   void run_steps(size_t n);
+  void kv_ensure(uint64_t end_pos);  // map pages for positions < end_pos
+  void kv_reset();                   // a new sequence: every page back to the free list
   void sync_result();
   void ensure_graph();
 
@@ -146,6 +179,14 @@ class Engine {
   uint32_t pos_ = 0;
   int num_sms_ = 148;
   int nsplit_ = 16;  // attention splits of the positions per kv head
+  uint32_t wait_polls_ = 0;  // tensor-parallel wait limit (0: the default; CHPE_WAIT_POLLS)
+  // paged KV cache
+  uint32_t n_pages_ = 0, mapped_ = 0;
+  uint32_t kv0_ = 0, kvl_ = 0;         // kv heads this rank holds (all of them on one GPU)
+  size_t layer_kv_elems_ = 0;          // halves per layer pool (n_pages * page * kv heads here * hd)
+  uint32_t* d_pages_ = nullptr;        // device page table [n_pages]
+  uint32_t* h_pages_ = nullptr;        // pinned mirror
+  std::vector<uint32_t> free_pages_;   // stack: back() is handed out next
 
   // tensor parallelism
   int tp_rank_ = 0, tp_world_ = 1;

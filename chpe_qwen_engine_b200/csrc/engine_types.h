@@ -95,7 +95,7 @@ struct TpLink {
   unsigned long long wait_units;  // arrivals per (step, layer) of the awaited kind
   unsigned long long lm_units;    // LM head: arrivals per step of all ranks' CTAs
   int32_t bcast;               // 1: outputs lie in the region; write them on every rank
-  int32_t pad_;
+  uint32_t wait_polls;         // polls before a wait gives up (0: the default limit)
   const int32_t* err;          // this rank's StepState::err: once set, waits give up at once
 };
 

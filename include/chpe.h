@@ -160,6 +160,13 @@ int chpe_bench_host(void *ctx, const uint32_t *tokens, size_t n_steps, float *lo
 int chpe_bench_kernel(void *ctx, int role, int rounds, float *avg_ms, double *bytes_per_launch,
                       int *launches);
 
+/* chpe_bench_kernel with every launch timed alone from a cold L2: before
+ * each launch a 256 MiB buffer (twice the L2) is written, so weights that a
+ * role's layers would otherwise keep in L2 between rounds (small tensors)
+ * come from HBM.  Same outputs; the average covers the launches only. */
+int chpe_bench_kernel_cold(void *ctx, int role, int rounds, float *avg_ms, double *bytes_per_launch,
+                           int *launches);
+
 /* Name of the kernel that runs the first op of a role (same role numbers as
  * chpe_bench_kernel), e.g. "gemv_flat_tma_kernel<W4G,FLAT>"; "" when the
  * role has no op or ctx is NULL.  The string lives as long as ctx. */
@@ -183,28 +190,52 @@ int chpe_get_last_all_finite(void *ctx);
 int chpe_kernels_per_step(void *ctx);
 /* Current sequence position (next step's pos). */
 uint32_t chpe_get_position(void *ctx);
-/* Last error message of ctx, or of the calling thread's last failed init
- * when ctx is NULL; "" when none. */
+/* Last error message of ctx, or, when ctx is NULL, of the calling thread's
+ * last failed init or chpe_attention_decode_noalloc call; "" when none. */
 const char *chpe_last_error(void *ctx);
 
-/* Decode attention for callers that cannot allocate device memory (code
- * recorded into a CUDA graph, runtimes that only hand out memory from their
- * own pools, plugins inside a host process that owns allocation).  No
+/* Paged KV cache (an extension; the reference keeps one contiguous f32
+ * cache, chpe_engine.zig:755-801).  Every layer's FP16 K and V live in a pool
+ * of pages of chpe_kv_page_size() positions; the sequence's page table maps
+ * logical page p (positions p*page ..) to a physical page, the same table for
+ * every layer.  A step maps the pages it reaches from a free list; a new
+ * sequence (any call that runs position 0) returns them all.
+ *
+ * chpe_kv_load writes K (rotated, as the cache holds it) and V rows
+ * k, v [n][kv_heads*head_dim] floats, rounded to FP16, at positions
+ * pos0..pos0+n-1 of one layer (restoring a saved prefix, or a test's
+ * prefilled context); with tensor parallelism each rank keeps its kv heads.
+ * It does not move the sequence position.
+ * chpe_kv_set_page_order sets the order free pages are handed out in (a
+ * permutation of all n pages) and starts a new sequence.
+ * chpe_kv_page_table writes up to cap entries of the mapped page table,
+ * stores the pool's page count in *num_pages (when non-NULL) and returns the
+ * mapped count.  0 / count on success, -1 on error (chpe_last_error). */
+uint32_t chpe_kv_page_size(void);
+int chpe_kv_load(void *ctx, uint32_t layer, uint32_t pos0, uint32_t n, const float *k,
+                 const float *v);
+int chpe_kv_set_page_order(void *ctx, const uint32_t *order, uint32_t n);
+int chpe_kv_page_table(void *ctx, uint32_t *out, uint32_t cap, uint32_t *num_pages);
+
+/* Decode attention for callers that cannot allocate device memory: serving
+ * runtimes that hand out device memory only from their own pre-sized pools,
+ * and plugins inside a host process that owns all allocation on the GPU.  No
  * counterpart in the reference.  It is the attention step of
  * chpe_probe_attention (RoPE on q and k with theta rope_theta, append k/v at
  * pos, GQA softmax over positions 0..pos) on device pointers the caller owns:
  * q [num_heads*head_dim] and k, v [num_kv_heads*head_dim] float; k_cache and
- * v_cache FP16 [max_seq_len][num_kv_heads][head_dim]; out
+ * v_cache FP16, contiguous [max_seq_len][num_kv_heads][head_dim]; out
  * [num_heads*head_dim] float; stream a cudaStream_t (NULL: default stream).
  * It allocates nothing: its scratch is a fixed 1 MiB static device array per
  * GPU, held until the library unloads.  The first call on a device resolves
- * that array's address (make it before any stream capture).  Calls share
- * the array, so calls that overlap on the GPU race; each call clears what it
- * needs.  Limits: head_dim 128 or 256, at most 8 query heads per kv head,
- * num_kv_heads * nsplit * (num_heads/num_kv_heads) * (head_dim+2) * 4 bytes of
- * partials + 4 KiB within 1 MiB (nsplit = max(16, 128/num_kv_heads)).
+ * that array's address (with the device current).  Calls share the array,
+ * so calls that overlap on the GPU race; each call clears what it needs.
+ * Limits: head_dim 128 or 256, at most 8 query heads per kv head, and
+ * 4096 + num_kv_heads * 16 * (num_heads/num_kv_heads) * (head_dim+4) * 4
+ * bytes (16 splits of the positions per kv head, one partial record of
+ * head_dim+4 floats per split and query head) within 1 MiB.
  * Returns 0, -1 for invalid arguments, -2 when the sizes exceed the scratch
- * limit, -3 for a CUDA error. */
+ * limit, -3 for a CUDA error; the reason is in chpe_last_error(NULL). */
 int chpe_attention_decode_noalloc(const float *q, const float *k, const float *v, void *k_cache,
                                   void *v_cache, float *out, uint32_t pos, uint32_t max_seq_len,
                                   uint32_t num_heads, uint32_t num_kv_heads, uint32_t head_dim,
@@ -225,6 +256,13 @@ int chpe_probe_gemv_linear(void *ctx, uint64_t tile_start, uint64_t num_tiles, c
  * earlier steps or calls left there.  0 on success. */
 int chpe_probe_attention(void *ctx, uint32_t layer, uint32_t pos, const float *q, const float *k,
                          const float *v, float *out);
+/* Failure detection without a GPU fault: a bounded device wait (the kind
+ * the tensor-parallel exchanges use) for an arrival nothing sends, limited to
+ * `polls` polls.  Returns -1 with the device-timeout error in
+ * chpe_last_error(ctx), exactly as a decode step whose exchange timed out
+ * does; the context stays usable.  (The decode path's limit is set with the
+ * environment variable CHPE_WAIT_POLLS when a context is created.) */
+int chpe_probe_wait_timeout(void *ctx, uint32_t polls);
 /* unpackEmbedRow (chpe_engine.zig:1491) for one token into out (hidden_dim
  * floats, read first: rows the reference leaves unwritten keep them). */
 int chpe_probe_embed(void *ctx, uint32_t token, float *out);

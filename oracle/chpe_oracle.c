@@ -236,6 +236,20 @@ void oracle_engine_free(OracleEngine *e) {
   free(e);
 }
 void oracle_set_threads(OracleEngine *e, int n) { e->threads = n < 1 ? 1 : n; }
+
+/* Writes K/V rows [n][KV*HD] at positions pos0.. of one layer of the cache
+ * (chpe_engine.zig:755-801 holds them as f32 [L][max_seq][KV*HD]); a test
+ * harness for prefilled long contexts, not a reference function.  Returns 0,
+ * or -1 when the rows do not fit. */
+int oracle_kv_load(OracleEngine *e, size_t layer, size_t pos0, size_t n, const float *k,
+                   const float *v) {
+  const Arch *A = &e->arch;
+  size_t kvd = A->KV * A->HD;
+  if (layer >= A->L || pos0 + n > e->max_seq) return -1;
+  memcpy(e->k_cache + (layer * e->max_seq + pos0) * kvd, k, n * kvd * 4);
+  memcpy(e->v_cache + (layer * e->max_seq + pos0) * kvd, v, n * kvd * 4);
+  return 0;
+}
 const float *oracle_logits(const OracleEngine *e) { return e->logits; }
 const float *oracle_hidden(const OracleEngine *e) { return e->hidden; }
 size_t oracle_vocab(const OracleEngine *e) { return e->arch.V; }

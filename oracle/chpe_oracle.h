@@ -80,6 +80,12 @@ void oracle_engine_free(OracleEngine *e);
  * accumulation order. */
 void oracle_set_threads(OracleEngine *e, int n);
 
+/* Test harness (no reference function): K/V rows [n][kv_heads*head_dim] at
+ * positions pos0.. of one layer's cache, for prefilled long contexts.  0, or
+ * -1 when they do not fit. */
+int oracle_kv_load(OracleEngine *e, size_t layer, size_t pos0, size_t n, const float *k,
+                   const float *v);
+
 /* chpe_engine.zig:1663 forwardDecode */
 void oracle_forward_decode(OracleEngine *e, uint32_t token, size_t pos,
                            OracleForwardResult *out);

@@ -72,6 +72,8 @@ def lib() -> C.CDLL:
         L.oracle_engine_free.argtypes = [P]
         L.oracle_set_threads.argtypes = [P, I]
         L.oracle_forward_decode.argtypes = [P, U32, S, C.POINTER(ForwardResult)]
+        L.oracle_kv_load.argtypes = [P, S, S, S, FP, FP]
+        L.oracle_kv_load.restype = I
         L.oracle_logits.argtypes = [P]
         L.oracle_logits.restype = FP
         L.oracle_hidden.argtypes = [P]
@@ -154,6 +156,13 @@ class OracleEngine:
         r = ForwardResult()
         lib().oracle_forward_decode(self.h, token, pos, C.byref(r))
         return r
+
+    def kv_load(self, layer: int, pos0: int, k: np.ndarray, v: np.ndarray):
+        """K/V rows [n][kv_heads*head_dim] at positions pos0.. of one layer."""
+        k = np.ascontiguousarray(k, np.float32)
+        v = np.ascontiguousarray(v, np.float32)
+        if lib().oracle_kv_load(self.h, layer, pos0, k.shape[0], fptr(k), fptr(v)) != 0:
+            raise ValueError("KV rows do not fit the cache")
 
     def logits(self) -> np.ndarray:
         p = lib().oracle_logits(self.h)

@@ -6,7 +6,11 @@ SwiGLU pair and the LM head run over flat cells, and the 9B geometry mixes
 full and linear-attention layer records (reference tensor maps).  Same gate
 as the 3B models: max-abs-err <= 2e-2, cosine >= 0.9999, identical argmax
 where the reference's top-1 margin exceeds 1e-3.  The archives are large
-(9-39 GB), so each test builds its own and frees it."""
+(9-39 GB), so each test builds its own and frees it.  The 72B FP16 archive
+lays raw FP16 tiles out by the 72B tensor map, whose tile counts are sized
+for 4-bit cells, so the reference reads a quarter of every projection
+(chpe_engine.zig:1396-1489 over qwen72b_tensor_map.zig:14-87); the GPU reads
+the same quarter."""
 import gc
 
 import numpy as np
@@ -22,6 +26,7 @@ LARGE = [
     (chpe.SYNTH_9B_W4, 3),
     (chpe.SYNTH_9B_I8_RAW, 2),
     (chpe.SYNTH_72B_W4, 2),
+    (chpe.SYNTH_72B_FP16_RAW, 2),  # FP16 raw tiles over the 4-bit-sized map (Q9)
 ]
 
 
