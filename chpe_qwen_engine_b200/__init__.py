@@ -47,8 +47,10 @@ SYMBOLS = [
     ("chpe_init_ex", _P, [C.c_char_p, _I, _U32, _I]),
     ("chpe_init_bytes", _P, [_P, _U64, _I, _U32, _I]),
     ("chpe_validate_archive", _I, [_P, _U64]),
+    ("chpe_convert_archive", _I, [C.c_char_p, C.c_char_p, _I, _I]),
     ("chpe_decode_step", _I, [_P, _U32, _U32, _FP]),
     ("chpe_generate", _I, [_P, _U32P, _S, _S, _U32P]),
+    ("chpe_speculative_generate", _I, [_P, _U32P, _S, _S, _U32, _U32, _U32P, C.POINTER(C.c_uint64)]),
     ("chpe_bench_greedy", _I, [_P, _S, _FP]),
     ("chpe_bench_host", _I, [_P, _U32P, _S, _FP, C.POINTER(C.c_double)]),
     ("chpe_bench_kernel", _I, [_P, _I, _I, _FP, C.POINTER(C.c_double), C.POINTER(C.c_int)]),
@@ -288,6 +290,17 @@ class Engine:
             raise ChpeError(self._err() or "chpe_generate failed")
         return out[:n_gen]
 
+    def speculative_generate(self, prompt, n_gen: int, draft_len: int = 4,
+                             ngram: int = 3) -> tuple[np.ndarray, dict]:
+        """chpe_speculative_generate: (tokens, {rounds, proposed, accepted})."""
+        p = np.ascontiguousarray(prompt, dtype=np.uint32)
+        out = np.zeros(max(n_gen, 1), np.uint32)
+        st = (C.c_uint64 * 3)()
+        if lib().chpe_speculative_generate(self.ctx, _u32p(p), p.size, n_gen, draft_len, ngram,
+                                           _u32p(out), st) != 0:
+            raise ChpeError(self._err() or "chpe_speculative_generate failed")
+        return out[:n_gen], {"rounds": st[0], "proposed": st[1], "accepted": st[2]}
+
     def bench_greedy(self, n_steps: int) -> float:
         ms = C.c_float()
         if lib().chpe_bench_greedy(self.ctx, n_steps, C.byref(ms)) != 0:
@@ -396,6 +409,16 @@ class Engine:
         if lib().chpe_probe_dequant_cell(self.ctx, tile, int(flat), _fp(out), out.size, C.byref(n)) != 0:
             raise ChpeError(self._err())
         return out[: n.value].copy()
+
+
+CONVERT_DENSE, CONVERT_RAW, CONVERT_RAW_FP16 = 0, 1, 2
+
+
+def convert_archive(src: str, dst: str, mode: int, device: int = 0) -> None:
+    """chpe_convert_archive: rewrite an archive as dense cells, raw tiles, or
+    raw FP16 tiles (BF16 -> FP16 on the GPU)."""
+    if lib().chpe_convert_archive(os.fsencode(src), os.fsencode(dst), mode, device) != 0:
+        raise ChpeError(lib().chpe_last_error(None).decode())
 
 
 def validate_archive(buf) -> int:

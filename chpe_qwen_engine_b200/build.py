@@ -29,7 +29,8 @@ NVCC_FLAGS = [
     "-I", CSRC, "-I", os.path.join(ROOT, "include"),
 ]
 
-ENGINE_SRCS = ["engine.cu", "attention_noalloc.cu", "deltanet.cu", "chpe_c_api.cpp", "chpe_maps.c"]
+ENGINE_SRCS = ["engine.cu", "attention_noalloc.cu", "deltanet.cu", "chpe_convert.cu", "chpe_c_api.cpp",
+               "chpe_maps.c"]
 ENGINE_DEPS = ENGINE_SRCS + ["engine.h", "engine_types.h", "gemv.cuh", "attention.cuh",
                              "aux_kernels.cuh", "gemv_tma.cuh", "gemv_flat_tma.cuh", "device_common.cuh", "chpe_maps.h",
                              "qwen3b_cell_map.inc", "../../include/chpe.h"]
@@ -84,7 +85,7 @@ def build_cli(force: bool = False) -> str:
     """chpe_fwd, linked against the in-tree libchpe.so (found through $ORIGIN)."""
     if force or _stale(CHPE_FWD, ["chpe_fwd.cpp", "../../include/chpe.h"]) or (
             os.path.exists(CHPE_FWD) and os.path.getmtime(LIBCHPE) > os.path.getmtime(CHPE_FWD)):
-        cmd = [_nvcc(), "-O2", "-std=c++17", "-o", CHPE_FWD, os.path.join(CSRC, "chpe_fwd.cpp"),
+        cmd = [_nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-O2", "-std=c++17", "-o", CHPE_FWD, os.path.join(CSRC, "chpe_fwd.cpp"),
                "-I", os.path.join(ROOT, "include"), "-L", PKG, "-lchpe", "-Xlinker", "-rpath=$ORIGIN"]
         subprocess.run(cmd, check=True)
     return CHPE_FWD

@@ -243,6 +243,20 @@ int chpe_generate(void* ctx, const uint32_t* prompt, size_t n_prompt, size_t n_g
   return 0;
 }
 
+int chpe_speculative_generate(void* ctx, const uint32_t* prompt, size_t n_prompt, size_t n_gen,
+                              uint32_t draft_len, uint32_t ngram, uint32_t* out, uint64_t* stats) {
+  if (!ctx || !prompt || n_prompt == 0 || (n_gen > 0 && !out)) return -1;
+  Ctx* c = (Ctx*)ctx;
+  try {
+    c->engine->speculative_generate(prompt, n_prompt, n_gen, draft_len, ngram, out, stats);
+    store_result(c);
+  } catch (const std::exception& e) {
+    c->err = e.what();
+    return -1;
+  }
+  return 0;
+}
+
 int chpe_bench_greedy(void* ctx, size_t n, float* ms) {
   if (!ctx || !ms) return -1;
   Ctx* c = (Ctx*)ctx;

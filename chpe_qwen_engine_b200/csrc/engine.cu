@@ -1739,6 +1739,69 @@ void Engine::verify(const uint32_t* toks, size_t m, uint32_t pos, float* logits_
   pos_ = pos + (uint32_t)m;
 }
 
+// Prompt-lookup draft: the up-to-m tokens that followed the latest earlier
+// occurrence of the sequence's last n tokens (n = ngram .. 1).
+static size_t lookup_draft(const std::vector<uint32_t>& h, uint32_t ngram, size_t m, uint32_t* d) {
+  const size_t H = h.size();
+  for (size_t n = ngram; n >= 1; n--) {
+    if (n >= H) continue;
+    for (size_t s = H - n; s-- > 0;) {  // candidate start of an earlier match
+      bool eq = true;
+      for (size_t j = 0; j < n && eq; j++) eq = h[s + j] == h[H - n + j];
+      if (!eq) continue;
+      size_t k = 0;
+      for (; k < m && s + n + k < H; k++) d[k] = h[s + n + k];
+      if (k > 0) return k;
+    }
+  }
+  return 0;
+}
+
+void Engine::speculative_generate(const uint32_t* prompt, size_t n_prompt, size_t n_gen, uint32_t draft,
+                                  uint32_t ngram, uint32_t* out, uint64_t* stats) {
+  if (n_prompt == 0) throw std::runtime_error("empty prompt");
+  if (n_prompt + n_gen > max_seq_) throw std::runtime_error("sequence exceeds max_seq_len");
+  if (draft + 1 > h_tok_cap_) throw std::runtime_error("draft longer than the token buffer");
+  uint64_t rounds = 0, proposed = 0, accepted = 0;
+  forward(prompt, n_prompt, 0);
+  if (n_gen == 0) return;
+  std::vector<uint32_t> hist(prompt, prompt + n_prompt);
+  uint32_t x = last_.argmax_token;  // emitted, not yet run through the model
+  size_t produced = 0;
+  out[produced++] = x;
+  hist.push_back(x);
+  uint32_t pos = (uint32_t)n_prompt;  // x's position
+  std::vector<uint32_t> chunk(draft + 1), am(draft + 1);
+  while (produced < n_gen) {
+    size_t m = draft;
+    if (m > n_gen - produced) m = n_gen - produced;
+    if ((uint64_t)pos + m + 1 > max_seq_) m = max_seq_ - pos - 1;
+    chunk[0] = x;
+    m = lookup_draft(hist, ngram ? ngram : 1, m, chunk.data() + 1);
+    verify(chunk.data(), m + 1, pos, nullptr, am.data());
+    rounds++;
+    proposed += m;
+    size_t k = 0;
+    while (k < m && am[k] == chunk[k + 1]) k++;
+    accepted += k;
+    for (size_t i = 0; i < k && produced < n_gen; i++) {
+      out[produced++] = chunk[i + 1];
+      hist.push_back(chunk[i + 1]);
+    }
+    if (produced < n_gen) {
+      out[produced++] = am[k];
+      hist.push_back(am[k]);
+    }
+    x = am[k];
+    pos += (uint32_t)(k + 1);
+  }
+  if (stats) {
+    stats[0] = rounds;
+    stats[1] = proposed;
+    stats[2] = accepted;
+  }
+}
+
 float Engine::timed_greedy_steps(size_t n) {
   if (!graph_) throw std::runtime_error("run forward() first");
   if ((uint64_t)pos_ + n > max_seq_) throw std::runtime_error("sequence exceeds max_seq_len");

@@ -62,6 +62,15 @@ class Engine {
   // i.e. m forwardDecode steps; logits_out [m][vocab], argmax_out [m] (either
   // may be null).  The last step's result becomes last_result().
   void verify(const uint32_t* toks, size_t m, uint32_t pos, float* logits_out, uint32_t* argmax_out);
+  // Greedy generation with speculative verification: drafts of up to
+  // `draft` tokens are proposed by prompt lookup (the tokens that followed the
+  // latest earlier occurrence of the last `ngram`.. 1 tokens of the sequence)
+  // and scored in one verify() call together with the pending token; the
+  // longest prefix matching the target's greedy tokens is kept, plus the
+  // target's own next token.  Output equals generate()'s.  stats (may be
+  // null): verify rounds, draft tokens proposed, draft tokens accepted.
+  void speculative_generate(const uint32_t* prompt, size_t n_prompt, size_t n_gen, uint32_t draft,
+                            uint32_t ngram, uint32_t* out_tokens, uint64_t* stats);
   // n greedy steps from the current position, timed with CUDA events on the
   // engine stream; returns milliseconds.
   float timed_greedy_steps(size_t n);

@@ -106,6 +106,23 @@ int chpe_tp_slice(int arch, int rank, int world, uint32_t out[10]);
  * 6 FileTooSmall, 10 MisalignedHeader. */
 int chpe_validate_archive(const void *bytes, uint64_t len);
 
+/* Archive converters (weight_archive.zig:617-776: convertToDensePosix,
+ * convertToRawContiguousPosix, convertToRawFp16ContiguousPosix), writing
+ * dst_path from the archive at src_path (validated first):
+ *   CHPE_CONVERT_DENSE     20480-byte records -> 17408-byte cells (the
+ *                          prefetch labels dropped; a raw source is refused);
+ *   CHPE_CONVERT_RAW       -> raw 16384-byte tiles (the code bytes only);
+ *   CHPE_CONVERT_RAW_FP16  -> raw tiles with every 2-D tile's BF16 weights
+ *                          rounded to FP16 on CUDA device `device`, 1-D tiles
+ *                          (the 3B raw layout's norm/bias positions, cells of
+ *                          quant_bits 32) copied verbatim, FLAG_RAW_FP16 set.
+ * The header keeps the source's fields with the new geometry.  0, or -1 with
+ * the reason in chpe_last_error(NULL). */
+#define CHPE_CONVERT_DENSE 0
+#define CHPE_CONVERT_RAW 1
+#define CHPE_CONVERT_RAW_FP16 2
+int chpe_convert_archive(const char *src_path, const char *dst_path, int mode, int device);
+
 /* One forwardDecode(token, pos) step that continues the current sequence
  * (the reference's ABI can only restart at 0).  Returns the argmax or -1. */
 int chpe_decode_step(void *ctx, uint32_t token, uint32_t pos, float *out_logits);
@@ -142,6 +159,21 @@ int chpe_verify(void *ctx, const uint32_t *toks, size_t m, uint32_t pos, float *
  * trips.  out_tokens receives n_gen ids.  0 on success, -1 on error. */
 int chpe_generate(void *ctx, const uint32_t *prompt, size_t n_prompt, size_t n_gen,
                   uint32_t *out_tokens);
+
+/* Speculative greedy generation (an extension; the reference has no
+ * speculative decoding): like chpe_generate, but after the prompt each round
+ * drafts up to draft_len tokens by prompt lookup (the tokens that followed
+ * the latest earlier occurrence of the sequence's last ngram .. 1 tokens),
+ * scores the pending token and the draft in one chpe_verify call, keeps the
+ * longest draft prefix equal to the model's greedy tokens plus the model's
+ * next token, and continues from there (the KV entries of rejected draft
+ * tokens are overwritten by the next round).  out_tokens receives exactly
+ * the n_gen tokens chpe_generate gives.  stats (may be NULL) receives three
+ * counts: verify rounds, draft tokens proposed, draft tokens accepted.
+ * 0 on success, -1 on error. */
+int chpe_speculative_generate(void *ctx, const uint32_t *prompt, size_t n_prompt, size_t n_gen,
+                              uint32_t draft_len, uint32_t ngram, uint32_t *out_tokens,
+                              uint64_t *stats);
 
 /* Benchmark helpers.  chpe_bench_greedy: n greedy steps from the current
  * position, device time by CUDA events on the engine stream.

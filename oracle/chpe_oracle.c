@@ -159,7 +159,10 @@ struct OracleEngine {
       *gate, *up, *mlp, *logits, *lm_row;
   float *k_cache, *v_cache; /* [L][max_seq][KV*HD] f32, zeroed (chpe_engine.zig:755-801) */
   size_t max_seq;
+  int kv_fp16; /* test option: round cached K/V to FP16 as a half-precision cache does */
 };
+
+static float round_f16(float f) { return (float)(_Float16)f; }
 
 /* chpe_engine.zig:854-974 CHPEEngine.init format sniffing and sizing. */
 OracleEngine *oracle_engine_new(const uint8_t *a, size_t len, int arch_id, size_t max_seq) {
@@ -236,6 +239,7 @@ void oracle_engine_free(OracleEngine *e) {
   free(e);
 }
 void oracle_set_threads(OracleEngine *e, int n) { e->threads = n < 1 ? 1 : n; }
+void oracle_set_kv_fp16(OracleEngine *e, int on) { e->kv_fp16 = on != 0; }
 
 /* Writes K/V rows [n][KV*HD] at positions pos0.. of one layer of the cache
  * (chpe_engine.zig:755-801 holds them as f32 [L][max_seq][KV*HD]); a test
@@ -1168,6 +1172,11 @@ void oracle_forward_decode(OracleEngine *e, uint32_t tok, size_t pos, OracleForw
     if (pos * kvd + kvd <= e->max_seq * kvd) {
       memcpy(kc + pos * kvd, e->k, kvd * 4);
       memcpy(vc + pos * kvd, e->v, kvd * 4);
+      if (e->kv_fp16)
+        for (size_t i = 0; i < kvd; i++) {
+          kc[pos * kvd + i] = round_f16(kc[pos * kvd + i]);
+          vc[pos * kvd + i] = round_f16(vc[pos * kvd + i]);
+        }
     }
     float scale = 1.0f / sqrtf((float)A->HD);
     AttnCtx ac = {e->q, kc, vc, pos, kvd, gqa, A->HD, scale, e->attn_out};
@@ -1205,4 +1214,67 @@ void oracle_forward_decode(OracleEngine *e, uint32_t tok, size_t pos, OracleForw
   res->elapsed_ns = now_ns() - t0;
   res->hidden_norm = sqrtf(hs);
   res->all_finite = fin;
+}
+
+
+/* ---- archive converters (weight_archive.zig:617-776) -------------------- */
+
+/* f32 -> f16 as Zig's @floatCast rounds it (nearest, ties to even); a NaN
+ * keeps its sign, gets the quiet bit and the top payload bits. */
+static uint16_t f32_to_f16_bits(float f) {
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  if (((u >> 23) & 0xFF) == 0xFF && (u & 0x7FFFFF))
+    return (uint16_t)(((u >> 16) & 0x8000) | 0x7E00 | ((u & 0x7FFFFF) >> 13));
+  _Float16 h = (_Float16)f;
+  uint16_t b;
+  memcpy(&b, &h, 2);
+  return b;
+}
+
+/* Output header (4096 bytes) of a conversion (`mode` 0 dense, 1 raw, 2 raw FP16). */
+void oracle_convert_header(const uint8_t *src, int mode, uint8_t *out) {
+  memset(out, 0, 4096);
+  memcpy(out, src, 64);
+  uint64_t v;
+  if (mode == 0) {
+    v = CELL_BYTES; memcpy(out + 32, &v, 8);
+    v = 0; memcpy(out + 48, &v, 8);
+  } else {
+    v = TILE_CODE_BYTES; memcpy(out + 32, &v, 8); memcpy(out + 40, &v, 8);
+    v = 0; memcpy(out + 48, &v, 8);
+    if (mode == 2) { v = rd64(src + 56) | FLAG_RAW_FP16; memcpy(out + 56, &v, 8); }
+  }
+}
+
+/* Output record `i` of a conversion: a 17408-byte cell (mode 0) or a 16384-byte
+ * tile (modes 1, 2).  Returns the bytes written. */
+size_t oracle_convert_record(const uint8_t *src, int mode, size_t i, uint8_t *out) {
+  uint64_t count = rd64(src + 16), rb = rd64(src + 32), pb = rd64(src + 48);
+  int raw = rb == TILE_CODE_BYTES && pb == 0, dense = pb == 0;
+  const uint8_t *cell = src + 4096 + i * rb + pb; /* getCellDirect */
+  const uint8_t *tile = raw ? src + 4096 + i * TILE_CODE_BYTES
+                        : dense ? src + 4096 + i * CELL_BYTES + 64
+                                : src + 4096 + i * RECORD_BYTES + PREFETCH_LABEL_BYTES + 64;
+  if (mode == 0) { memcpy(out, cell, CELL_BYTES); return CELL_BYTES; }
+  if (mode == 1) { memcpy(out, tile, TILE_CODE_BYTES); return TILE_CODE_BYTES; }
+  int one_d = 0, decided = 0;
+  if (count == 376853) {
+    if (i == 376852) { one_d = 1; decided = 1; }
+    else if (i < 37984) { one_d = 0; decided = 1; }
+    else {
+      size_t rel = (i - 37984) % 9413;
+      if (rel == 0 || rel == 513 || rel == 578 || rel == 643 || rel == 1156) { one_d = 1; decided = 1; }
+    }
+  }
+  if (!decided && !raw) one_d = cell[PAYLOAD_OFF + 20] == 32;
+  if (one_d) { memcpy(out, tile, TILE_CODE_BYTES); return TILE_CODE_BYTES; }
+  for (size_t k = 0; k < 8192; k++) {
+    uint32_t b = (uint32_t)rd16(tile + 2 * k) << 16;
+    float f;
+    memcpy(&f, &b, 4);
+    uint16_t h = f32_to_f16_bits(f);
+    memcpy(out + 2 * k, &h, 2);
+  }
+  return TILE_CODE_BYTES;
 }

@@ -79,6 +79,10 @@ void oracle_engine_free(OracleEngine *e);
  * depend on the thread count: every output element keeps the reference's
  * accumulation order. */
 void oracle_set_threads(OracleEngine *e, int n);
+/* Test option, not reference behaviour (the reference caches f32): round each
+ * cached K/V row to FP16 when a step stores it, as a half-precision KV cache
+ * does, so a comparison can separate the cache's rounding from the rest. */
+void oracle_set_kv_fp16(OracleEngine *e, int on);
 
 /* Test harness (no reference function): K/V rows [n][kv_heads*head_dim] at
  * positions pos0.. of one layer's cache, for prefilled long contexts.  0, or
@@ -148,6 +152,12 @@ void oracle_deltanet_step(const float *mixed_qkv, const float *z, const float *a
                           const float *conv_w, float *conv_hist, uint32_t t, const float *a_log,
                           const float *dt_bias, const float *norm_w, float *state, float *out,
                           uint32_t nk, uint32_t nv, uint32_t dk, uint32_t dv, float eps);
+
+/* Archive converters (weight_archive.zig:617-776): the output header of a
+ * conversion (mode 0 dense, 1 raw, 2 raw FP16; 4096 bytes) and output record
+ * i (returns its size).  `src` is a validated archive. */
+void oracle_convert_header(const uint8_t *src, int mode, uint8_t *out);
+size_t oracle_convert_record(const uint8_t *src, int mode, size_t i, uint8_t *out);
 
 /* Tensor maps (as the reference tables give them). */
 void oracle_map_3b_cell_layer(size_t l, int64_t out[12]);

@@ -71,6 +71,7 @@ def lib() -> C.CDLL:
         L.oracle_engine_new.restype = P
         L.oracle_engine_free.argtypes = [P]
         L.oracle_set_threads.argtypes = [P, I]
+        L.oracle_set_kv_fp16.argtypes = [P, I]
         L.oracle_forward_decode.argtypes = [P, U32, S, C.POINTER(ForwardResult)]
         L.oracle_kv_load.argtypes = [P, S, S, S, FP, FP]
         L.oracle_kv_load.restype = I
@@ -101,6 +102,9 @@ def lib() -> C.CDLL:
         L.oracle_rms_norm.argtypes = [FP, FP, FP, S, F]
         L.oracle_apply_rope.argtypes = [FP, S, S, S, F]
         L.oracle_gqa_attention.argtypes = [FP, FP, FP, S, S, S, S, FP]
+        L.oracle_convert_header.argtypes = [P, I, P]
+        L.oracle_convert_record.argtypes = [P, I, S, P]
+        L.oracle_convert_record.restype = S
         L.oracle_map_3b_cell_layer.argtypes = [S, C.POINTER(C.c_int64)]
         L.oracle_map_72b_layer.argtypes = [S, C.POINTER(C.c_int64)]
         _lib = L
@@ -151,6 +155,10 @@ class OracleEngine:
 
     def set_threads(self, n: int):
         lib().oracle_set_threads(self.h, n)
+
+    def set_kv_fp16(self, on: bool = True):
+        """Test option: round cached K/V rows to FP16 (the reference keeps f32)."""
+        lib().oracle_set_kv_fp16(self.h, int(on))
 
     def forward_decode(self, token: int, pos: int) -> ForwardResult:
         r = ForwardResult()
@@ -303,3 +311,15 @@ def deltanet_step(mixed, z, a, b, conv_w, conv_hist, t, a_log, dt_bias, norm_w, 
                                fptr(conv_hist), t, fptr(prm[0]), fptr(prm[1]), fptr(prm[2]),
                                fptr(state), fptr(out), nk, nv, dk, dv, eps)
     return out
+
+
+def convert_header(src: np.ndarray, mode: int) -> np.ndarray:
+    out = np.zeros(4096, np.uint8)
+    lib().oracle_convert_header(src.ctypes.data, mode, out.ctypes.data)
+    return out
+
+
+def convert_record(src: np.ndarray, mode: int, i: int) -> np.ndarray:
+    out = np.zeros(17408, np.uint8)
+    n = lib().oracle_convert_record(src.ctypes.data, mode, i, out.ctypes.data)
+    return out[:n].copy()

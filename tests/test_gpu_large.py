@@ -18,7 +18,7 @@ import pytest
 
 import chpe_qwen_engine_b200 as chpe
 import oracle_py as O
-from _util import assert_logits_match, oracle_threads
+from _util import assert_logits_match, cosine, oracle_threads
 
 pytestmark = pytest.mark.gpu
 
@@ -34,18 +34,40 @@ LARGE = [
 def test_large_decode_matches_oracle(cfg, steps):
     a = chpe.synth_archive(cfg)
     arch = chpe.SYNTH_ARCH[cfg]
+    fp16_kv_bound = cfg == chpe.SYNTH_72B_FP16_RAW
     try:
         e = chpe.Engine.from_bytes(a, arch, 64)
         o = O.OracleEngine(a, arch, 64, threads=oracle_threads())
+        if fp16_kv_bound:
+            # The GPU caches K/V in FP16, the reference in f32.  On this
+            # 80-layer FP16 model the cache's rounding alone moves the logits
+            # by about 0.025 from the second position on (it moves the 3B FP16
+            # model's by about 0.005).  A second oracle that rounds its cached
+            # K/V to FP16 separates that from the kernels' arithmetic: the GPU
+            # must meet the full gate against it, and the reference-semantics
+            # oracle's cosine and greedy-token gates.
+            o16 = O.OracleEngine(a, arch, 64, threads=oracle_threads())
+            o16.set_kv_fp16(True)
         rng = np.random.default_rng(2)
         toks = rng.integers(0, e.vocab, steps).astype(np.uint32)
         for pos, t in enumerate(toks):
             r_ref = o.forward_decode(int(t), pos)
             r_got = e.forward_decode(int(t), pos)
             ref, got = o.logits(), e.logits()
-            assert_logits_match(got, ref, f"cfg {cfg} pos {pos}")
+            if fp16_kv_bound:
+                r_ref = o16.forward_decode(int(t), pos)
+                assert_logits_match(got, o16.logits(), f"cfg {cfg} pos {pos} (oracle with FP16 KV)")
+                cos = cosine(got, ref)
+                assert cos >= 0.9999, f"cfg {cfg} pos {pos}: cosine {cos}"
+                top2 = np.partition(ref, -2)[-2:]
+                if top2[1] - top2[0] > 1e-3:
+                    assert int(np.argmax(got)) == int(np.argmax(ref))
+            else:
+                assert_logits_match(got, ref, f"cfg {cfg} pos {pos}")
             assert r_got.all_finite == bool(r_ref.all_finite)
             assert abs(r_got.hidden_norm - r_ref.hidden_norm) <= 1e-3 * max(1.0, r_ref.hidden_norm)
+        if fp16_kv_bound:
+            o16.close()
         o.close()
         e.close()
     finally:
