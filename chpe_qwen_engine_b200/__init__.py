@@ -64,6 +64,8 @@ SYMBOLS = [
     ("chpe_step_weight_bytes", C.c_double, [_P]),
     ("chpe_profile_step", _I, [_P, _FP, C.POINTER(C.c_int), _I]),
     ("chpe_verify", _I, [_P, _U32P, C.c_size_t, C.c_uint32, _FP, _U32P]),
+    ("chpe_last_verify_batched", _I, [_P]),
+    ("chpe_verify_batched_unavailable", C.c_char_p, [_P, _I]),
     ("chpe_deltanet_step", _I, [_P, _P, _P, _P, _P, _P, C.c_uint32, _P, _P, _P, _P, _P,
                                 C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_float, _P]),
     ("chpe_get_last_all_finite", _I, [_P]),
@@ -79,6 +81,8 @@ SYMBOLS = [
     ("chpe_probe_attention", _I, [_P, _U32, _U32, _FP, _FP, _FP, _FP]),
     ("chpe_probe_embed", _I, [_P, _U32, _FP]),
     ("chpe_probe_wait_timeout", _I, [_P, _U32]),
+    ("chpe_probe_tc_i8", _I, [_P, _P, _I, _P, _I]),
+    ("chpe_probe_bgemm", _I, [_P, _U64, _U64, _FP, _I, _FP, _U64, _U64, _I]),
     ("chpe_probe_dequant_cell", _I, [_P, _U64, _I, _FP, _U64, C.POINTER(C.c_uint64)]),
 ]
 
@@ -283,6 +287,12 @@ class Engine:
             raise ChpeError(self._err() or "chpe_verify failed")
         return lg, am
 
+    def last_verify_batched(self) -> bool:
+        return bool(lib().chpe_last_verify_batched(self.ctx))
+
+    def verify_batched_unavailable(self, m: int) -> str:
+        return (lib().chpe_verify_batched_unavailable(self.ctx, m) or b"").decode()
+
     def generate(self, prompt, n_gen: int) -> np.ndarray:
         p = np.ascontiguousarray(prompt, dtype=np.uint32)
         out = np.zeros(max(n_gen, 1), np.uint32)
@@ -385,6 +395,16 @@ class Engine:
         y = np.zeros(r_total, np.float32) if y is None else np.ascontiguousarray(y, np.float32).copy()
         if lib().chpe_probe_gemv_linear(self.ctx, tile_start, num_tiles, _fp(x), x.size, _fp(y), r_total,
                                         c_total, int(accumulate), bias_tile) != 0:
+            raise ChpeError(self._err())
+        return y
+
+    def probe_bgemm(self, tile_start, num_tiles, x, r_total, c_total, accumulate=False, y=None):
+        """chpe_probe_bgemm: x [nt][c_total] -> y [nt][r_total] on the tensor cores."""
+        x = np.ascontiguousarray(x, np.float32)
+        nt = x.shape[0]
+        y = np.zeros((nt, r_total), np.float32) if y is None else np.ascontiguousarray(y, np.float32).copy()
+        if lib().chpe_probe_bgemm(self.ctx, tile_start, num_tiles, _fp(x), nt, _fp(y), r_total, c_total,
+                                  int(accumulate)) != 0:
             raise ChpeError(self._err())
         return y
 

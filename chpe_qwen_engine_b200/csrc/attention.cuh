@@ -33,6 +33,12 @@ struct AttnLaunch {
   const uint32_t* pages;  // page table (logical page -> physical page), or nullptr: contiguous
   int32_t page_shift;   // log2(positions per page)
   uint32_t n_pages;     // physical pages in this layer's pool (entries beyond read page 0)
+  // Batched steps: token z = blockIdx.z sits at position st->pos + z, its
+  // q / out / partials / counters offset by these strides, and the K/V rows
+  // of every position it attends to (its own included) are already in the
+  // cache (rope_append_kernel), so nothing is appended here.
+  int32_t batched;
+  uint32_t q_tok, out_tok, part_tok;
   TpLink tp;            // tensor parallel: out lies in the exchange region
 };
 
@@ -93,13 +99,16 @@ CHPE_DEV bool attention_body(const AttnLaunch& P) {
 
   pdl_wait();
   if (P.st->stop) return blockIdx.x == 0;
-  const int pos = P.st->pos;
+  const int tok = P.batched ? (int)blockIdx.z : 0;
+  const int pos = P.st->pos + tok;
   if (pos < 0 || pos >= P.max_seq) return blockIdx.x == 0;  // the host never schedules this
   const float pf = (float)pos;
+  float* const part_base = P.part + (size_t)tok * P.part_tok;
+  uint32_t* const counters = P.counters + (size_t)tok * P.KV;
 
   // RoPE on this warp's query head, on the new key; copy of the new value.
   if (warp < G) {
-    const float* qh = P.q + (size_t)(kvh * G + warp) * HD;
+    const float* qh = P.q + (size_t)tok * P.q_tok + (size_t)(kvh * G + warp) * HD;
     for (int i = L; i < HD / 2; i += 32) {
       float th = pf * P.inv_freq[i];
       float c = cosf(th), s = sinf(th);
@@ -108,7 +117,7 @@ CHPE_DEV bool attention_body(const AttnLaunch& P) {
       qs[warp][i + HD / 2] = x0 * s + x1 * c;
     }
   }
-  for (int i = threadIdx.x; i < HD / 2; i += blockDim.x) {
+  for (int i = threadIdx.x; i < HD / 2 && !P.batched; i += blockDim.x) {
     const float* kh = P.k + (size_t)kvh * HD;
     float th = pf * P.inv_freq[i];
     float c = cosf(th), s = sinf(th);
@@ -116,9 +125,9 @@ CHPE_DEV bool attention_body(const AttnLaunch& P) {
     kn[i] = x0 * c - x1 * s;
     kn[i + HD / 2] = x0 * s + x1 * c;
   }
-  for (int i = threadIdx.x; i < HD; i += blockDim.x) vn[i] = P.v[(size_t)kvh * HD + i];
+  for (int i = threadIdx.x; i < HD && !P.batched; i += blockDim.x) vn[i] = P.v[(size_t)kvh * HD + i];
   __syncthreads();
-  if (split == 0) {
+  if (split == 0 && !P.batched) {
     size_t base = (kv_cache_row(P, pos) * P.KV + kvh) * HD;
     for (int i = threadIdx.x; i < HD; i += blockDim.x) {
       P.kc[base + i] = __float2half_rn(kn[i]);
@@ -150,7 +159,7 @@ CHPE_DEV bool attention_body(const AttnLaunch& P) {
       const int i = threadIdx.x + u * blockDim.x;
       if (i >= nt * VPR) continue;
       const int r = i / VPR, c8 = (i % VPR) * 8, t = tb + r;
-      if (t == pos) {  // this step's entry, from the values just computed
+      if (t == pos && !P.batched) {  // this step's entry, from the values just computed
         __half2 hk[4], hv[4];
 #pragma unroll
         for (int e = 0; e < 4; e++) {
@@ -230,7 +239,7 @@ CHPE_DEV bool attention_body(const AttnLaunch& P) {
   }
   constexpr int PS = HD + 4;  // partial record: HD values, m, l, pad (16-byte records)
   if (warp < G) {
-    float* dst = P.part + (((size_t)kvh * P.nsplit + split) * G + warp) * PS;
+    float* dst = part_base + (((size_t)kvh * P.nsplit + split) * G + warp) * PS;
 #pragma unroll
     for (int e4 = 0; e4 < PER; e4 += 4)
       *reinterpret_cast<float4*>(dst + PER * L + e4) = make_float4(acc[e4], acc[e4 + 1], acc[e4 + 2], acc[e4 + 3]);
@@ -239,14 +248,14 @@ CHPE_DEV bool attention_body(const AttnLaunch& P) {
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
-    unsigned prev = atomicAdd(&P.counters[kvh], 1u);
+    unsigned prev = atomicAdd(&counters[kvh], 1u);
     last_flag = (prev == (unsigned)P.nsplit - 1);
   }
   __syncthreads();
   if (!last_flag) return false;
   __threadfence();
   if (warp < G) {
-    const float* src = P.part + ((size_t)kvh * P.nsplit * G + warp) * PS;
+    const float* src = part_base + ((size_t)kvh * P.nsplit * G + warp) * PS;
     const size_t sstride = (size_t)G * PS;
     // (m, l) of splits L and L+32 in one round of loads
     float2 ml[2];
@@ -294,11 +303,11 @@ CHPE_DEV bool attention_body(const AttnLaunch& P) {
       }
     }
     const float inv = 1.0f / den;
-    float* outp = P.out + (size_t)(kvh * G + warp) * HD;
+    float* outp = P.out + (size_t)tok * P.out_tok + (size_t)(kvh * G + warp) * HD;
 #pragma unroll
     for (int e = 0; e < PER; e++) tp_put(P.tp, outp, PER * L + e, o[e] * inv);
   }
-  if (threadIdx.x == 0) P.counters[kvh] = 0;
+  if (threadIdx.x == 0) counters[kvh] = 0;
   return true;
 }
 

@@ -1,5 +1,7 @@
 // aux_kernels.cuh -- embedding lookup, stand-alone RMSNorm / SwiGLU / argmax
 // for decomposed plans, the synthetic-pattern GEMV and the dequant probe.
+// The kernels here and in gemv.cuh have internal linkage: every translation
+// unit that launches one holds its own copy.
 #pragma once
 #include "device_common.cuh"
 #include "gemv.cuh"
@@ -18,8 +20,10 @@ struct EmbedLaunch {
   float* hidden;
   StepState* st;
   const StepResult* res;
-  int32_t use_state;    // 0: token comes from `token` (probe), 1: from the step state
+  int32_t use_state;    // 0: token comes from `token` (probe), 1: from the step state,
+                        // 2: from tokens[blockIdx.y] into row blockIdx.y of hidden ([y][D])
   uint32_t token;
+  const int32_t* tokens;
 };
 
 CHPE_DEV float embed_pattern(uint32_t i, uint32_t tok) {
@@ -28,12 +32,14 @@ CHPE_DEV float embed_pattern(uint32_t i, uint32_t tok) {
 
 // unpackEmbedRow (chpe_engine.zig:1491-1552) and unpackEmbedRowCell
 // (:1288-1394); each CTA owns blockDim.x columns of the hidden vector.
-__global__ void embed_kernel(const __grid_constant__ EmbedLaunch P) {
+static __global__ void embed_kernel(const __grid_constant__ EmbedLaunch P) {
   pdl_wait();
-  const uint32_t tok = P.use_state ? (P.st->feed_argmax ? P.res->argmax_token : (uint32_t)P.st->token)
-                                   : P.token;
-  if (P.use_state && blockIdx.x == 0 && threadIdx.x == 0) P.st->stop = 0;
+  const uint32_t tok = P.use_state == 2 ? (uint32_t)P.tokens[blockIdx.y]
+                       : P.use_state ? (P.st->feed_argmax ? P.res->argmax_token : (uint32_t)P.st->token)
+                                     : P.token;
+  if (P.use_state == 1 && blockIdx.x == 0 && threadIdx.x == 0) P.st->stop = 0;
   const uint32_t D = P.D;
+  float* const hidden = P.hidden + (P.use_state == 2 ? (size_t)blockIdx.y * D : 0);
   const uint32_t c0 = blockIdx.x * blockDim.x, c = c0 + threadIdx.x;
   int mode = P.mode;
   uint64_t tile = 0, row = 0;
@@ -47,19 +53,19 @@ __global__ void embed_kernel(const __grid_constant__ EmbedLaunch P) {
   }
   const uint8_t* code = P.arc + 4096 + tile * P.stride + P.prefix;
   if (mode == EMB_PATTERN) {
-    if (c < D) P.hidden[c] = embed_pattern(c, tok);
+    if (c < D) hidden[c] = embed_pattern(c, tok);
     return;
   }
   if (mode == EMB_RAW_F16) {
-    if (c < D) P.hidden[c] = ld_f16(code + 2 * (row * D + c));
+    if (c < D) hidden[c] = ld_f16(code + 2 * (row * D + c));
     return;
   }
   if (mode == EMB_RAW_BF16) {
-    if (c < D) P.hidden[c] = bf2f(ld_u16(code + 2 * (row * D + c)));
+    if (c < D) hidden[c] = bf2f(ld_u16(code + 2 * (row * D + c)));
     return;
   }
   if (mode == EMB_RAW_I8) {
-    if (c < D) P.hidden[c] = (float)(int8_t)code[row * D + c] * 0.00373708f;
+    if (c < D) hidden[c] = (float)(int8_t)code[row * D + c] * 0.00373708f;
     return;
   }
   const uint8_t* pl = code + 16384;
@@ -71,14 +77,14 @@ __global__ void embed_kernel(const __grid_constant__ EmbedLaunch P) {
   if (qb == 8) {
     if (row >= 8) return;  // the row is left as it was
     if (c < ng * 128)
-      P.hidden[c] = (float)(int8_t)code[row * D + c] * ld_f16(pl + 48 + 2 * (row * ng + c / 128));
+      hidden[c] = (float)(int8_t)code[row * D + c] * ld_f16(pl + 48 + 2 * (row * ng + c / 128));
     return;
   } else if (qb == 2) {
     if (row >= 16) return;
     const float CB[4] = {0.f, 1.f, -2.f, -1.f};
     if (c < ng * 128) {
       uint8_t b = code[row * (D / 4) + c / 4];
-      P.hidden[c] = CB[(b >> (2 * (c & 3))) & 3] * ld_f16(pl + 48 + 2 * (row * ng + c / 128));
+      hidden[c] = CB[(b >> (2 * (c & 3))) & 3] * ld_f16(pl + 48 + 2 * (row * ng + c / 128));
     }
     replace = g128;
   } else if (g128 || qb == 4) {
@@ -86,14 +92,14 @@ __global__ void embed_kernel(const __grid_constant__ EmbedLaunch P) {
     if (c < ng * 128) {
       uint8_t b = code[row * (D / 2) + c / 2];
       float q = (float)((c & 1) ? (b >> 4) & 15 : b & 15);
-      P.hidden[c] = (q - 8.0f) * ld_f16(pl + 48 + 2 * (row * ng + c / 128));
+      hidden[c] = (q - 8.0f) * ld_f16(pl + 48 + 2 * (row * ng + c / 128));
     }
     replace = g128;
   } else {
     if (c < D) {
       uint8_t b = code[row * (D / 2) + c / 2];
       float q = (float)((c & 1) ? (b >> 4) & 15 : b & 15);
-      P.hidden[c] = __fadd_rn(__fmul_rn(q - 8.0f, ld_f32(pl + 32)), ld_f32(pl + 36));
+      hidden[c] = __fadd_rn(__fmul_rn(q - 8.0f, ld_f32(pl + 32)), ld_f32(pl + 36));
     }
     return;
   }
@@ -103,7 +109,7 @@ __global__ void embed_kernel(const __grid_constant__ EmbedLaunch P) {
       for (int k = 0; k < 8; k++) {
         uint32_t col = ld_u16(pl + 816 + 2 * k);
         if (col < D && col >= c0 && col < c0 + blockDim.x)
-          P.hidden[col] = ld_f16(pl + 560 + 2 * (row * 8 + k));
+          hidden[col] = ld_f16(pl + 560 + 2 * (row * 8 + k));
       }
     }
   }
@@ -121,7 +127,7 @@ struct NormLaunch {
   StepState* st;
   int32_t ignore_stop;
 };
-__global__ void __launch_bounds__(256) rmsnorm_kernel(const __grid_constant__ NormLaunch P) {
+static __global__ void __launch_bounds__(256) rmsnorm_kernel(const __grid_constant__ NormLaunch P) {
   __shared__ float red[8];
   pdl_wait();
   if (!P.ignore_stop && P.st->stop) return;
@@ -153,7 +159,7 @@ struct SwigluLaunch {
   uint32_t n;
   StepState* st;
 };
-__global__ void swiglu_kernel(const __grid_constant__ SwigluLaunch P) {
+static __global__ void swiglu_kernel(const __grid_constant__ SwigluLaunch P) {
   pdl_wait();
   if (P.st->stop) return;
   uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -167,7 +173,7 @@ struct PatternLaunch {
   uint32_t n;
   StepState* st;
 };
-__global__ void pattern_kernel(const __grid_constant__ PatternLaunch P) {
+static __global__ void pattern_kernel(const __grid_constant__ PatternLaunch P) {
   pdl_wait();
   if (P.st && P.st->stop) return;
   uint32_t r = blockIdx.x * blockDim.x + threadIdx.x;
@@ -186,7 +192,7 @@ struct ArgmaxLaunch {
   int32_t* gen_tokens;
   int32_t max_gen;
 };
-__global__ void __launch_bounds__(256) argmax_kernel(const __grid_constant__ ArgmaxLaunch P) {
+static __global__ void __launch_bounds__(256) argmax_kernel(const __grid_constant__ ArgmaxLaunch P) {
   __shared__ unsigned long long kb[8];
   __shared__ uint32_t kf[8];
   __shared__ int is_last;
@@ -258,7 +264,7 @@ struct DequantLaunch {
   float* out;
   uint32_t cap;
 };
-__global__ void dequant_kernel(const __grid_constant__ DequantLaunch P) {
+static __global__ void dequant_kernel(const __grid_constant__ DequantLaunch P) {
   const uint8_t* code = P.cell_code;
   const uint8_t* pl = code + 16384;
   const uint32_t qb = pl[20];
@@ -325,7 +331,7 @@ struct WaitProbeLaunch {
   StepState* st;
   int32_t kind;
 };
-__global__ void wait_probe_kernel(const __grid_constant__ WaitProbeLaunch P) {
+static __global__ void wait_probe_kernel(const __grid_constant__ WaitProbeLaunch P) {
   if (threadIdx.x != 0) return;
   const unsigned long long target = ld_acquire_sys(&P.tp.sh->sig[P.kind]) + 1ull;
   if (!tp_wait_count(P.tp, P.kind, target)) atomicExch(&P.st->err, 1);

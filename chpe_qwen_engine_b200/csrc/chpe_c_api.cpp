@@ -230,6 +230,21 @@ int chpe_verify(void* ctx, const uint32_t* toks, size_t m, uint32_t pos, float* 
   return 0;
 }
 
+int chpe_last_verify_batched(void* ctx) {
+  return ctx ? ((Ctx*)ctx)->engine->last_verify_batched() : 0;
+}
+
+const char* chpe_verify_batched_unavailable(void* ctx, int m) {
+  if (!ctx) return "null context";
+  Ctx* c = (Ctx*)ctx;
+  try {
+    c->name = c->engine->batch_unavailable_reason(m <= 4 ? 4 : 8);
+  } catch (const std::exception& e) {
+    c->name = e.what();
+  }
+  return c->name.c_str();
+}
+
 int chpe_generate(void* ctx, const uint32_t* prompt, size_t n_prompt, size_t n_gen, uint32_t* out) {
   if (!ctx || !prompt || n_prompt == 0 || (n_gen > 0 && !out)) return -1;
   Ctx* c = (Ctx*)ctx;
@@ -428,6 +443,19 @@ int chpe_probe_attention(void* ctx, uint32_t layer, uint32_t pos, const float* q
   Ctx* c = (Ctx*)ctx;
   try {
     c->engine->debug_attention(layer, pos, q, k, v, out);
+  } catch (const std::exception& e) {
+    c->err = e.what();
+    return -1;
+  }
+  return 0;
+}
+
+int chpe_probe_bgemm(void* ctx, uint64_t tile_start, uint64_t num_tiles, const float* x, int nt, float* y,
+                     uint64_t r_total, uint64_t c_total, int accumulate) {
+  if (!ctx || !x || !y) return -1;
+  Ctx* c = (Ctx*)ctx;
+  try {
+    c->engine->debug_bgemm(tile_start, num_tiles, x, nt, y, r_total, c_total, accumulate);
   } catch (const std::exception& e) {
     c->err = e.what();
     return -1;

@@ -325,6 +325,7 @@ Engine::Engine(const uint8_t* bytes, uint64_t len, int arch, uint32_t max_seq, i
 }
 
 Engine::~Engine() {
+  free_batch_steps();
   if (graph_) cudaGraphExecDestroy(graph_);
   if (d_vlogits_) cudaFree(d_vlogits_);
   if (d_vres_) cudaFree(d_vres_);
@@ -1693,6 +1694,11 @@ void Engine::generate(const uint32_t* prompt, size_t n_prompt, size_t n_gen, uin
 
 void Engine::verify(const uint32_t* toks, size_t m, uint32_t pos, float* logits_out, uint32_t* argmax_out) {
   if (m == 0) return;
+  last_verify_batched_ = 0;
+  if (verify_batched(toks, m, pos, logits_out, argmax_out)) {
+    last_verify_batched_ = 1;
+    return;
+  }
   if ((uint64_t)pos + m > max_seq_) throw std::runtime_error("sequence exceeds max_seq_len");
   if (m + 1 > h_tok_cap_) throw std::runtime_error("too many candidates");
   if (pos == 0) kv_reset();

@@ -23,7 +23,8 @@ namespace chpe {
 // returns (failed inits and the context-free entry points).
 void set_thread_error(const std::string& msg);
 
-struct Op;  // one recorded kernel launch (engine.cu)
+struct Op;         // one recorded kernel launch (engine.cu)
+struct BatchStep;  // the batched decode step of NT tokens (engine_verify.cu)
 
 struct EngineFacts {  // CHPEEngine fields after init sniffing (:862-918)
   int archive_valid = 0, is_raw = 0, is_raw_fp16 = 0, is_dense = 0;
@@ -62,6 +63,10 @@ class Engine {
   // i.e. m forwardDecode steps; logits_out [m][vocab], argmax_out [m] (either
   // may be null).  The last step's result becomes last_result().
   void verify(const uint32_t* toks, size_t m, uint32_t pos, float* logits_out, uint32_t* argmax_out);
+  // How the last verify() ran: 1 batched tensor-core step, 0 sequential
+  // steps; and why the batched step does not apply ("" when it does).
+  int last_verify_batched() const { return last_verify_batched_; }
+  std::string batch_unavailable_reason(int nt);
   // Greedy generation with speculative verification: drafts of up to
   // `draft` tokens are proposed by prompt lookup (the tokens that followed the
   // latest earlier occurrence of the last `ngram`.. 1 tokens of the sequence)
@@ -109,6 +114,10 @@ class Engine {
   void debug_attention(uint32_t layer, uint32_t pos, const float* q, const float* k, const float* v,
                        float* out);
   void debug_dequant_cell(uint64_t tile, int flat, float* out, uint64_t cap, uint64_t* n_out);
+  // The batched tensor-core GEMM of NT (4 or 8) tokens over one gemvLinear
+  // call site: x [nt][c_total], y [nt][r_total] (read for accumulate).
+  void debug_bgemm(uint64_t tile_start, uint64_t num_tiles, const float* x, int nt, float* y,
+                   uint64_t r_total, uint64_t c_total, int accumulate);
   // Runs a bounded device wait for an arrival that never comes, with `polls`
   // polls at most; throws the device-timeout error the decode path raises and
   // leaves the engine usable.
@@ -189,6 +198,7 @@ class Engine {
   int num_sms_ = 148;
   int nsplit_ = 16;  // attention splits of the positions per kv head
   uint32_t wait_polls_ = 0;  // tensor-parallel wait limit (0: the default; CHPE_WAIT_POLLS)
+  int last_verify_batched_ = 0;
   // paged KV cache
   uint32_t n_pages_ = 0, mapped_ = 0;
   uint32_t kv0_ = 0, kvl_ = 0;         // kv heads this rank holds (all of them on one GPU)
@@ -204,6 +214,16 @@ class Engine {
   TpShared* d_tpsh_ = nullptr;
   long long tp_delta_[kTpMax] = {};
   std::vector<void*> ipc_open_;
+  // The batched step of nt (4 or 8) tokens, built on first use; null when
+  // the archive cannot take it (then verify() runs sequential steps).
+  BatchStep* batch_step(int nt);
+  // verify() through the batched step; false when it does not apply (the
+  // caller then runs the sequential steps).
+  bool verify_batched(const uint32_t* toks, size_t m, uint32_t pos, float* logits_out, uint32_t* argmax_out);
+  void free_batch_steps();
+  BatchStep* bsteps_[2] = {nullptr, nullptr};
+  int bstep_state_[2] = {0, 0};  // 0 not tried, 1 built, -1 not applicable
+  std::string bstep_why_[2];
   // verify(): per-candidate logits and results on the device
   float* d_vlogits_ = nullptr;
   StepResult* d_vres_ = nullptr;

@@ -596,7 +596,7 @@ struct GenLaunch {
 };
 
 // Row-tiled cells of any format: one warp per row.
-__global__ void __launch_bounds__(256) gemv_generic_rowtile(const __grid_constant__ GenLaunch P) {
+static __global__ void __launch_bounds__(256) gemv_generic_rowtile(const __grid_constant__ GenLaunch P) {
   pdl_wait();
   if (P.st && P.st->stop) return;
   const GemvSrc& s = P.src;
@@ -648,7 +648,7 @@ __global__ void __launch_bounds__(256) gemv_generic_rowtile(const __grid_constan
 }
 
 // Flat cells of any format: one warp per row, per-chunk tile dispatch.
-__global__ void __launch_bounds__(256) gemv_generic_flat(const __grid_constant__ GenLaunch P) {
+static __global__ void __launch_bounds__(256) gemv_generic_flat(const __grid_constant__ GenLaunch P) {
   pdl_wait();
   if (P.st && P.st->stop) return;
   const GemvSrc& s = P.src;
@@ -705,7 +705,7 @@ struct AuxLaunch {
   const float* x;
   StepState* st;
 };
-__global__ void flat_aux_fix(const __grid_constant__ AuxLaunch P) {
+static __global__ void flat_aux_fix(const __grid_constant__ AuxLaunch P) {
   pdl_wait();
   if (P.st && P.st->stop) return;
   const GemvSrc& s = P.src;

@@ -153,6 +153,18 @@ int chpe_deltanet_step(const float *mixed_qkv, const float *z, const float *a, c
  * chpe_decode_step / chpe_verify at an earlier pos).  0, or -1 on error. */
 int chpe_verify(void *ctx, const uint32_t *toks, size_t m, uint32_t pos, float *out_logits,
                 uint32_t *out_argmax);
+/* How chpe_verify runs: for m <= 8 candidates on an archive whose
+ * projections and LM head are 4-bit group-scaled flat cells in whole 128-row
+ * blocks (the 9B and 72B archives) it runs one batched step of 4 or 8 tokens
+ * whose GEMMs read every weight once for all candidates on the tcgen05 tensor
+ * cores (results equal m decode steps up to f32 rounding); otherwise m
+ * sequential decode steps (bit-identical to chpe_decode_step).  The
+ * environment variable CHPE_VERIFY_BATCHED=0 forces the sequential steps.
+ * chpe_last_verify_batched: 1 when the last chpe_verify ran the batched
+ * step.  chpe_verify_batched_unavailable: "" when m candidates can take the
+ * batched step, else the reason (valid until the next call on ctx). */
+int chpe_last_verify_batched(void *ctx);
+const char *chpe_verify_batched_unavailable(void *ctx, int m);
 
 /* Greedy generation on the device: runs the prompt from position 0, then
  * n_gen tokens, each the argmax of the step before, without host round
@@ -295,6 +307,19 @@ int chpe_probe_attention(void *ctx, uint32_t layer, uint32_t pos, const float *q
  * does; the context stays usable.  (The decode path's limit is set with the
  * environment variable CHPE_WAIT_POLLS when a context is created.) */
 int chpe_probe_wait_timeout(void *ctx, uint32_t polls);
+/* The batched GEMM of chpe_verify on one gemvLinear call site of 4-bit
+ * group-scaled flat cells (tcgen05 tensor cores): y[t] (= or +=) W x[t] for
+ * nt (4 or 8) tokens; x [nt][c_total], y [nt][r_total] host buffers; rows a
+ * multiple of 128, columns of 128.  0, or -1 (chpe_last_error) when the call
+ * cannot take that path. */
+int chpe_probe_bgemm(void *ctx, uint64_t tile_start, uint64_t num_tiles, const float *x, int nt,
+                     float *y, uint64_t r_total, uint64_t c_total, int accumulate);
+/* The tensor-core path of the batched GEMMs on its own: D [128][n] (s32) =
+ * A [128][64] (unsigned bytes) x B [n][64] (signed bytes)^T through
+ * tcgen05.mma kind::i8 with A in tensor memory and B in shared memory
+ * (n 16 or 32), on CUDA device `device`, host buffers.  0, or -1 with the
+ * reason in chpe_last_error(NULL). */
+int chpe_probe_tc_i8(const uint8_t *a, const int8_t *b, int n, int32_t *d, int device);
 /* unpackEmbedRow (chpe_engine.zig:1491) for one token into out (hidden_dim
  * floats, read first: rows the reference leaves unwritten keep them). */
 int chpe_probe_embed(void *ctx, uint32_t token, float *out);

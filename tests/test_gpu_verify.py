@@ -59,3 +59,58 @@ def test_verify_rejects_bad_arguments():
     assert L.chpe_verify(e.ctx, None, 4, 0, None, None) == -1
     t = np.array([1], np.uint32)
     assert L.chpe_verify(e.ctx, t.ctypes.data_as(chpe._U32P), 0, 0, None, None) == -1
+
+
+def _prefill(e, oracles, L, KV, HD, ctx, rng):
+    for l in range(L):
+        k = (rng.standard_normal((ctx, KV * HD)) * 1.5).astype(np.float16).astype(np.float32)
+        v = rng.standard_normal((ctx, KV * HD)).astype(np.float16).astype(np.float32)
+        e.kv_load(l, 0, k, v)
+        for o in oracles:
+            o.kv_load(l, 0, k, v)
+
+
+@pytest.mark.parametrize("ctx", [5, 2048])
+def test_batched_verify_9b(ctx, monkeypatch):
+    """Config 4: Qwen3.5-9B 4-bit, batch-4/8 verification through the batched
+    tcgen05 step, against the same candidates run as sequential decode steps
+    (CHPE_VERIFY_BATCHED=0) and against the oracle; at ctx 5 after a real
+    prompt, at ctx 2048 over a prefilled KV cache.  m = 3 pads the batch of 4;
+    a second candidate set at the same position checks the rollback."""
+    import gc
+    a = chpe.synth_archive(chpe.SYNTH_9B_W4)
+    try:
+        e = chpe.Engine.from_bytes(a, chpe.ARCH_9B, ctx + 16)
+        assert e.verify_batched_unavailable(8) == ""
+        o = O.OracleEngine(a, O.ARCH_9B, ctx + 16, threads=oracle_threads())
+        o16 = O.OracleEngine(a, O.ARCH_9B, ctx + 16, threads=oracle_threads())
+        o16.set_kv_fp16(True)
+        rng = np.random.default_rng(ctx)
+        if ctx == 5:
+            e.forward_tokens(PROMPT)
+            for p, t in enumerate(PROMPT):
+                o.forward_decode(int(t), p)
+                o16.forward_decode(int(t), p)
+        else:
+            _prefill(e, (o, o16), 32, 4, 256, ctx, rng)
+        for m in (4, 8, 3):
+            cand = rng.integers(0, e.vocab, m).astype(np.uint32)
+            lg, am = e.verify(cand, ctx)
+            assert e.last_verify_batched(), e.verify_batched_unavailable(m)
+            monkeypatch.setenv("CHPE_VERIFY_BATCHED", "0")
+            lg_seq, am_seq = e.verify(cand, ctx)  # rollback to the same position
+            assert not e.last_verify_batched()
+            monkeypatch.delenv("CHPE_VERIFY_BATCHED")
+            for i, t in enumerate(cand):
+                assert_logits_match(lg[i], lg_seq[i], f"ctx {ctx} m {m} cand {i} vs sequential")
+                assert int(am[i]) == int(np.argmax(lg[i]))
+                o.forward_decode(int(t), ctx + i)
+                o16.forward_decode(int(t), ctx + i)
+                assert_logits_match(lg[i], o.logits(), f"ctx {ctx} m {m} cand {i} vs oracle")
+                assert_logits_match(lg[i], o16.logits(), f"ctx {ctx} m {m} cand {i} vs oracle, FP16 KV")
+        o.close()
+        o16.close()
+        e.close()
+    finally:
+        del a
+        gc.collect()
