@@ -399,6 +399,49 @@ def run_ours(args, rank, world, local, dist):
     print(json.dumps(line), flush=True)
 
 
+def run_verify(args):
+    """Config 4: Qwen3.5-9B 4-bit batch-M speculative verification against a
+    2048-token context (the prompt decoded first).  Each timed call scores M
+    candidates at the same position (rolling back between calls), through the
+    batched tcgen05 step and, for comparison, as M sequential decode steps;
+    one greedy decode step is timed at the same position."""
+    import chpe_qwen_engine_b200 as chpe
+    M = args.verify
+    ctx = args.prompt if args.prompt_given else 2048
+    a = chpe.synth_archive(chpe.SYNTH_9B_W4, 0, seed=0)
+    eng = chpe.Engine.from_bytes(a, chpe.ARCH_9B, ctx + 2 * args.steps + 64)
+    rng = np.random.default_rng(1)
+    eng.forward_tokens(rng.integers(0, 151936, ctx).astype(np.uint32))
+    cand = rng.integers(0, 151936, M).astype(np.uint32)
+
+    def timed(n):
+        for _ in range(args.warmup):
+            eng.verify(cand, ctx)
+        t0 = time.perf_counter()
+        for _ in range(n):
+            eng.verify(cand, ctx)
+        return (time.perf_counter() - t0) / n
+
+    with ClockSampler(0) as cs:
+        t_batched = timed(args.steps)
+        batched = eng.last_verify_batched()
+        os.environ["CHPE_VERIFY_BATCHED"] = "0"
+        t_seq = timed(max(1, args.steps // 2))
+        del os.environ["CHPE_VERIFY_BATCHED"]
+    eng.forward_decode(int(cand[0]), ctx)  # sets the graph position
+    ms1 = eng.bench_greedy(args.steps) / args.steps
+    print(json.dumps({
+        "metric": f"batch-{M} speculative verify: candidate tokens scored per second", "unit": "tok/s",
+        "value": M / t_batched, "impl": "ours", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "higher_is_better": True, "batched_tensor_core_path": batched,
+        "why_not_batched": "" if batched else eng.verify_batched_unavailable(M),
+        "ms_per_verify": t_batched * 1000, "ms_per_verify_sequential": t_seq * 1000,
+        "ms_per_decode_step": ms1, "verify_over_decode_step": t_batched * 1000 / ms1,
+        "timing": "wall time of chpe_verify calls (host round trip included); decode step: CUDA events",
+        "config": {"workload": "qwen3.5-9b-w4-flat-cell", "context": ctx, "candidates": M},
+        "clocks": cs.summary()}), flush=True)
+
+
 def run_sweep(args):
     """Config 2's isolated GEMV sweep on the 3B dense-cell archive: every
     launch of a role (one per layer) timed alone from a cold L2."""
@@ -429,6 +472,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--model", default="72b-w4", choices=sorted(MODELS))
+    ap.add_argument("--verify", type=int, default=0, choices=[0, 4, 8],
+                    help="config 4: batch-M speculative verification on the 9B archive at a 2048 context")
     ap.add_argument("--sweep", action="store_true",
                     help="config 2's isolated GEMV sweep (3B archives): per-shape GB/s from a cold L2")
     ap.add_argument("--prompt", type=int, default=None,
@@ -448,6 +493,9 @@ def main():
     args.prompt_given = args.prompt is not None
     if args.prompt is None:
         args.prompt = MODELS[args.model]["prompt"]
+    if args.verify:
+        run_verify(args)
+        return
     if args.sweep:
         if args.model not in ("3b-w4", "3b-w2", "3b-fp16"):
             args.model = "3b-w4"

@@ -25,7 +25,7 @@ def test_tcgen05_i8_product_exact(n):
 # (rows, cols) read from the 3B down-projection cells (688 flat 4-bit cells):
 # the 9B/72B widths, rows that straddle cells (29568, 12288 columns), split-K
 # ranges of one and several groups
-BG_SHAPES = [(2048, 8192), (1024, 4096), (640, 29568), (512, 12288), (128, 128 * 40), (256, 2048)]
+BG_SHAPES = [(2048, 8192), (1024, 4096), (640, 29568), (512, 12288), (128, 128 * 40), (256, 2176)]
 
 
 @pytest.mark.parametrize("nt", [4, 8])
