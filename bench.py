@@ -479,7 +479,8 @@ def main():
     ap.add_argument("--prompt", type=int, default=None,
                     help="prompt tokens decoded before timing (default: the model's config)")
     ap.add_argument("--kernel-only", default=None,
-                    choices=["qkv", "attention", "o", "gateup", "down", "lmhead", "flat-aligned", "flat-stream"],
+                    choices=["qkv", "attention", "o", "gateup", "down", "lmhead", "flat-aligned", "flat-stream",
+                             "bgemm4", "bgemm8"],
                     help="profiling case: build the engine (max_seq_len 64) and only launch this "
                          "op of every layer, --steps rounds after one warm-up round; flat-aligned / "
                          "flat-stream: one flat GEMV over 2064 contiguous 4-bit cells of the 3B "
@@ -500,6 +501,20 @@ def main():
         if args.model not in ("3b-w4", "3b-w2", "3b-fp16"):
             args.model = "3b-w4"
         run_sweep(args)
+        return
+    if args.kernel_only in ("bgemm4", "bgemm8"):
+        # the batched tcgen05 GEMM alone: 60000 contiguous 4-bit cells of the
+        # 3B archive (about 1 GB, beyond L2) read as a 480000 x 4096 tensor,
+        # NT tokens, --steps launches through the probe entry point
+        import chpe_qwen_engine_b200 as chpe
+        nt = 4 if args.kernel_only == "bgemm4" else 8
+        eng = chpe.Engine.from_bytes(chpe.synth_archive(chpe.SYNTH_3B_W4, 0, seed=0), chpe.ARCH_3B, 64)
+        rows, cols = 480000, 4096
+        x = np.random.default_rng(3).standard_normal((nt, cols)).astype(np.float32)
+        for _ in range(max(1, args.steps)):
+            y = eng.probe_bgemm(0, 60000, x, rows, cols)
+        print(json.dumps({"kernel": "bgemm_w4_kernel", "nt": nt, "rows": rows, "cols": cols,
+                          "y00": float(y[0][0])}))
         return
     if args.kernel_only in ("flat-aligned", "flat-stream"):
         import chpe_qwen_engine_b200 as chpe
