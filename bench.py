@@ -428,6 +428,14 @@ def run_verify(args):
         os.environ["CHPE_VERIFY_BATCHED"] = "0"
         t_seq = timed(max(1, args.steps // 2))
         del os.environ["CHPE_VERIFY_BATCHED"]
+    # per-role device time of the batched step, ops launched one by one
+    ms_role, by_role = eng.profile_verify(M, ctx)
+    hbm, _ = peaks()
+    names = ["other", "qkv", "attention", "o", "gateup", "down", "lmhead", "embed"]
+    roles = {names[i]: {"ms": round(float(ms_role[i]), 4),
+                        "gbs": round(by_role[i] / (ms_role[i] / 1000) / 1e9, 1) if by_role[i] else None}
+             for i in range(8) if ms_role[i] > 0}
+    wbytes = float(by_role.sum())
     eng.forward_decode(int(cand[0]), ctx)  # sets the graph position
     ms1 = eng.bench_greedy(args.steps) / args.steps
     print(json.dumps({
@@ -438,6 +446,9 @@ def run_verify(args):
         "ms_per_verify": t_batched * 1000, "ms_per_verify_sequential": t_seq * 1000,
         "ms_per_decode_step": ms1, "verify_over_decode_step": t_batched * 1000 / ms1,
         "timing": "wall time of chpe_verify calls (host round trip included); decode step: CUDA events",
+        "batched_step_per_role": roles, "batched_step_weight_bytes": wbytes,
+        "batched_step_ops_ms": float(ms_role.sum()),
+        "batched_step_weight_frac_of_measured_hbm": wbytes / (float(ms_role.sum()) / 1000) / 1e9 / hbm,
         "config": {"workload": "qwen3.5-9b-w4-flat-cell", "context": ctx, "candidates": M},
         "clocks": cs.summary()}), flush=True)
 
@@ -503,16 +514,16 @@ def main():
         run_sweep(args)
         return
     if args.kernel_only in ("bgemm4", "bgemm8"):
-        # the batched tcgen05 GEMM alone: 60000 contiguous 4-bit cells of the
-        # 3B archive (about 1 GB, beyond L2) read as a 480000 x 4096 tensor,
-        # NT tokens, --steps launches through the probe entry point
+        # the batched tcgen05 GEMM alone: the 9472 embedding cells of the 3B
+        # archive (165 MB, beyond L2) read as a 75776 x 4096 tensor, NT
+        # tokens, --steps launches through the probe entry point
         import chpe_qwen_engine_b200 as chpe
         nt = 4 if args.kernel_only == "bgemm4" else 8
         eng = chpe.Engine.from_bytes(chpe.synth_archive(chpe.SYNTH_3B_W4, 0, seed=0), chpe.ARCH_3B, 64)
-        rows, cols = 480000, 4096
+        rows, cols = 75776, 4096
         x = np.random.default_rng(3).standard_normal((nt, cols)).astype(np.float32)
         for _ in range(max(1, args.steps)):
-            y = eng.probe_bgemm(0, 60000, x, rows, cols)
+            y = eng.probe_bgemm(0, 9472, x, rows, cols)
         print(json.dumps({"kernel": "bgemm_w4_kernel", "nt": nt, "rows": rows, "cols": cols,
                           "y00": float(y[0][0])}))
         return

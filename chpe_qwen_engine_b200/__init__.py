@@ -65,6 +65,7 @@ SYMBOLS = [
     ("chpe_profile_step", _I, [_P, _FP, C.POINTER(C.c_int), _I]),
     ("chpe_verify", _I, [_P, _U32P, C.c_size_t, C.c_uint32, _FP, _U32P]),
     ("chpe_last_verify_batched", _I, [_P]),
+    ("chpe_profile_verify", _I, [_P, C.c_size_t, _U32, _FP, C.POINTER(C.c_double), _I]),
     ("chpe_verify_batched_unavailable", C.c_char_p, [_P, _I]),
     ("chpe_deltanet_step", _I, [_P, _P, _P, _P, _P, _P, C.c_uint32, _P, _P, _P, _P, _P,
                                 C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_float, _P]),
@@ -286,6 +287,14 @@ class Engine:
         if lib().chpe_verify(self.ctx, _u32p(t), t.size, pos, _fp(lg), _u32p(am)) != 0:
             raise ChpeError(self._err() or "chpe_verify failed")
         return lg, am
+
+    def profile_verify(self, m: int, pos: int) -> tuple[np.ndarray, np.ndarray]:
+        """(milliseconds, algorithmic bytes) per role of the batched step."""
+        ms = np.zeros(8, np.float32)
+        by = np.zeros(8, np.float64)
+        if lib().chpe_profile_verify(self.ctx, m, pos, _fp(ms), by.ctypes.data_as(C.POINTER(C.c_double)), 8) < 0:
+            raise ChpeError(self._err())
+        return ms, by
 
     def last_verify_batched(self) -> bool:
         return bool(lib().chpe_last_verify_batched(self.ctx))

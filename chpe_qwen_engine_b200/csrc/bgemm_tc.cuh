@@ -68,6 +68,13 @@ struct BgemmLaunch {
   uint32_t* finite;        // EPI_LOGITS: [NT] finiteness flags
   int32_t* bad;            // EPI_ACCUM: set when a residual leaves [-1e18, 1e18] or is not finite
   int32_t* err;            // set when a bounded wait gave up
+  // RMSNorm factors without re-reading x: an EPI_ACCUM launch writes, per
+  // 128-row block, each token's sum of squares of the new rows to
+  // ssq_out[block][NT]; a normalising launch with ssq_in sums its ssq_n
+  // slots per token in block order (null: it reads x itself).
+  float* ssq_out;
+  const float* ssq_in;
+  uint32_t ssq_n;
 };
 
 struct BgSmem {  // dynamic shared memory layout (bytes)
@@ -99,6 +106,7 @@ __global__ void __launch_bounds__(kBgThreads, 1) bgemm_w4_kernel(const __grid_co
   __shared__ __align__(8) uint64_t dfull[2][kBgStages];
   __shared__ uint32_t s_taddr;
   __shared__ float s_inv[NT];
+  __shared__ float s_red[4 * NT];
   __shared__ int s_last;
   const uint32_t tid = threadIdx.x, warp = tid >> 5, L = tid & 31u;
   const uint32_t wg = tid >> 7, row = tid & 127u;
@@ -148,7 +156,14 @@ __global__ void __launch_bounds__(kBgThreads, 1) bgemm_w4_kernel(const __grid_co
   pdl_wait();
 
   // RMSNorm factors of the tokens (warp t: token t)
-  if (P.gamma) {
+  if (P.gamma && P.ssq_in) {
+    if (tid < (uint32_t)NT) {
+      float ss = 0.f;
+      for (uint32_t b = 0; b < P.ssq_n; b++) ss += P.ssq_in[b * NT + tid];
+      s_inv[tid] = 1.0f / sqrtf(ss / (float)P.C + P.eps);
+    }
+    __syncthreads();
+  } else if (P.gamma) {
     if (warp < (uint32_t)NT) {
       const float* xr = P.x + (size_t)warp * P.x_stride;
       float ss = 0.f;
@@ -404,8 +419,20 @@ __global__ void __launch_bounds__(kBgThreads, 1) bgemm_w4_kernel(const __grid_co
       const float v = o[(size_t)t * P.out_stride + lr] + y[t];
       o[(size_t)t * P.out_stride + lr] = v;
       ok = ok && fabsf(v) <= 1e18f;
+      y[t] = v;
     }
     if (!ok) atomicExch(P.bad, 1);
+    if (P.ssq_out) {  // the block's sums of squares per token, in a fixed order
+      float* red = s_red;  // [4 warps][NT]
+#pragma unroll
+      for (int t = 0; t < NT; t++) {
+        const float q = warp_sum(y[t] * y[t]);
+        if (L == 0) red[(warp & 3u) * NT + t] = q;
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (row < (uint32_t)NT)
+        P.ssq_out[blk * NT + row] = ((red[row] + red[NT + row]) + red[2 * NT + row]) + red[3 * NT + row];
+    }
   } else {  // EPI_LOGITS
 #pragma unroll
     for (int t = 0; t < NT; t++) {

@@ -230,6 +230,17 @@ int chpe_verify(void* ctx, const uint32_t* toks, size_t m, uint32_t pos, float* 
   return 0;
 }
 
+int chpe_profile_verify(void* ctx, size_t m, uint32_t pos, float* role_ms, double* role_bytes, int cap) {
+  if (!ctx || !role_ms || !role_bytes || cap < 1) return -1;
+  Ctx* c = (Ctx*)ctx;
+  try {
+    return c->engine->profile_verify(m, pos, role_ms, role_bytes, cap);
+  } catch (const std::exception& e) {
+    c->err = e.what();
+    return -1;
+  }
+}
+
 int chpe_last_verify_batched(void* ctx) {
   return ctx ? ((Ctx*)ctx)->engine->last_verify_batched() : 0;
 }

@@ -1635,6 +1635,26 @@ void Engine::forward(const uint32_t* toks, size_t n, uint32_t start_pos) {
   if ((uint64_t)start_pos + n > max_seq_) throw std::runtime_error("sequence exceeds max_seq_len");
   if (start_pos == 0) kv_reset();  // a new sequence
   kv_ensure((uint64_t)start_pos + n);
+  {
+    // Batched prefill: whole chunks of 8 tokens through the batched step
+    // (each weight read once per chunk on the tensor cores); the rest, and
+    // archives that cannot take it, token by token.  CHPE_PREFILL_BATCHED=0
+    // keeps every token on the single-token step.
+    const char* pb = getenv("CHPE_PREFILL_BATCHED");
+    size_t done = 0;
+    const auto tb = now_ns();
+    if (n >= 8 && !(pb && pb[0] == '0') && tp_world_ == 1) {
+      while (n - done >= 8 && verify_batched(toks + done, 8, start_pos + (uint32_t)done, nullptr, nullptr))
+        done += 8;
+    }
+    if (done == n) {
+      last_ns_ = now_ns() - tb;
+      return;
+    }
+    toks += done;
+    n -= done;
+    start_pos += (uint32_t)done;
+  }
   if (!graph_) {
     // The warm-up launch inside ensure_graph runs one step on whatever state
     // is current; run it on a scratch position that is overwritten below.

@@ -66,6 +66,12 @@ class Engine {
   // How the last verify() ran: 1 batched tensor-core step, 0 sequential
   // steps; and why the batched step does not apply ("" when it does).
   int last_verify_batched() const { return last_verify_batched_; }
+  // The batched step of m candidates at pos launched op by op with CUDA
+  // events between the ops (scratch candidates; the KV entries at
+  // pos.. are overwritten): per role (chpe_bench_kernel's numbering, 0
+  // other) the summed milliseconds and algorithmic weight bytes.  Returns
+  // the op count.
+  int profile_verify(size_t m, uint32_t pos, float* role_ms, double* role_bytes, int cap);
   std::string batch_unavailable_reason(int nt);
   // Greedy generation with speculative verification: drafts of up to
   // `draft` tokens are proposed by prompt lookup (the tokens that followed the

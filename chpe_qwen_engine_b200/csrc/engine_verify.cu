@@ -221,6 +221,8 @@ enum BOpType : int32_t { BOP_EMBED = 0, BOP_GEMM, BOP_ROPE, BOP_ATTN, BOP_FINAL 
 
 struct BOp {
   int32_t type = 0, hd = 128;
+  int32_t role = 0;       // chpe_bench_kernel's role numbers (0: other)
+  double alg_bytes = 0;   // algorithmic weight bytes (codes + scales of the rows used)
   dim3 grid{1, 1, 1}, block{256, 1, 1};
   uint32_t smem = 0;
   BgemmLaunch bg{};
@@ -264,8 +266,14 @@ static void launch_v(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_t
   CKV(cudaLaunchKernelEx(&cfg, kern, a));
 }
 
+static void run_bop(const BatchStep& B, const BOp& op, cudaStream_t s);
+
 static void run_bops(const BatchStep& B, cudaStream_t s) {
-  for (const BOp& op : B.ops) {
+  for (const BOp& op : B.ops) run_bop(B, op, s);
+}
+
+static void run_bop(const BatchStep& B, const BOp& op, cudaStream_t s) {
+  {
     switch (op.type) {
       case BOP_EMBED: launch_v(embed_kernel, op.grid, op.block, 0, s, op.em); break;
       case BOP_GEMM: launch_bgemm(B.nt, op.bg, op.smem, s, true); break;
@@ -343,6 +351,10 @@ BatchStep* Engine::batch_step(int nt) {
   B->res = (StepResult*)dalloc(8 * sizeof(StepResult));
   const int G = (int)(A.H / A.KV);
   B->apart = (float*)dalloc((size_t)nt * A.KV * nsplit_ * G * (A.HD + 4) * 4);
+  float* ssq[2] = {(float*)dalloc((size_t)(A.D / kBgRows + 1) * nt * 4),
+                   (float*)dalloc((size_t)(A.D / kBgRows + 1) * nt * 4)};
+  const float* ssq_prev = nullptr;  // sums of squares the last residual update wrote
+  int ssq_next = 0;
   B->acnt = (uint32_t*)dalloc((size_t)nt * A.KV * 4);
   {
     std::vector<uint32_t> ones(8, 1u);
@@ -355,16 +367,29 @@ BatchStep* Engine::batch_step(int nt) {
   size_t part_max = 0, cnt_max = 0;
   std::string why;
   auto gemm = [&](const GemvSrc* src, int nseg, int epi, uint32_t C, const float* x, uint32_t xs,
-                  const float* gamma, float* const* out, uint32_t os) -> bool {
+                  const float* gamma, float* const* out, uint32_t os, int role) -> bool {
     BOp op;
     op.type = BOP_GEMM;
+    op.role = role;
     if (!plan_bgemm(src, nseg, epi, C, nt, num_sms_, op.bg, op.smem)) return false;
+    for (int i = 0; i < nseg; i++)
+      op.alg_bytes += (double)(op.bg.rows_avail[i] > src[i].row0 ? op.bg.rows_avail[i] - src[i].row0 : 0u) *
+                      C * (0.5 + 2.0 / 128.0);
     op.bg.x = x;
     op.bg.x_stride = xs;
     op.bg.gamma = gamma;
     op.bg.eps = A.eps;
     for (int i = 0; i < nseg; i++) op.bg.out[i] = out[i];
     op.bg.out_stride = os;
+    if (gamma) {
+      op.bg.ssq_in = ssq_prev;
+      op.bg.ssq_n = A.D / kBgRows;
+    }
+    if (epi == EPI_ACCUM) {
+      op.bg.ssq_out = ssq[ssq_next];
+      ssq_next ^= 1;
+      ssq_prev = op.bg.ssq_out;
+    }
     const size_t pm = (size_t)op.bg.ksplit * nt * op.bg.rows_total;
     if (pm > part_max) part_max = pm;
     if (op.bg.rows_total / kBgRows > cnt_max) cnt_max = op.bg.rows_total / kBgRows;
@@ -375,6 +400,7 @@ BatchStep* Engine::batch_step(int nt) {
     {  // embedding of every token
       BOp op;
       op.type = BOP_EMBED;
+      op.role = 7;
       EmbedLaunch& e = op.em;
       e.arc = d_arc_;
       e.record_count = f_.record_count;
@@ -402,7 +428,7 @@ BatchStep* Engine::batch_step(int nt) {
                         plan_linear(li.k_proj, li.k_tiles, kvd, A.D, A.D, 0, li.k_bias),
                         plan_linear(li.v_proj, li.v_tiles, kvd, A.D, A.D, 0, li.v_bias)};
       float* qkv_out[3] = {B->qkv, B->qkv + qd, B->qkv + qd + kvd};
-      if (!gemm(qkv, 3, EPI_STORE, A.D, B->h, A.D, g_in, qkv_out, qkvs)) {
+      if (!gemm(qkv, 3, EPI_STORE, A.D, B->h, A.D, g_in, qkv_out, qkvs, 1)) {
         why = "layer " + std::to_string(l) + " QKV is not 4-bit group-scaled flat cells in 128-row blocks";
         break;
       }
@@ -430,6 +456,7 @@ BatchStep* Engine::batch_step(int nt) {
       {
         BOp op;
         op.type = BOP_ATTN;
+        op.role = 2;
         op.hd = (int)A.HD;
         AttnLaunch& at = op.at;
         at.q = B->qkv;
@@ -463,20 +490,20 @@ BatchStep* Engine::batch_step(int nt) {
       }
       GemvSrc o = plan_linear(li.o_proj, li.o_tiles, A.D, A.D, A.D, 1, -1);
       float* o_out[1] = {B->h};
-      if (!gemm(&o, 1, EPI_ACCUM, A.D, B->attn, qd, nullptr, o_out, A.D)) {
+      if (!gemm(&o, 1, EPI_ACCUM, A.D, B->attn, qd, nullptr, o_out, A.D, 3)) {
         why = "layer " + std::to_string(l) + " O is not 4-bit group-scaled flat cells in 128-row blocks";
         break;
       }
       GemvSrc gu[2] = {plan_linear(li.gate_proj, li.gate_tiles, A.F, A.D, A.D, 0, -1),
                        plan_linear(li.up_proj, li.up_tiles, A.F, A.D, A.D, 0, -1)};
       float* gu_out[2] = {B->mlp, nullptr};
-      if (!gemm(gu, 2, EPI_SWIGLU, A.D, B->h, A.D, g_post, gu_out, A.F)) {
+      if (!gemm(gu, 2, EPI_SWIGLU, A.D, B->h, A.D, g_post, gu_out, A.F, 4)) {
         why = "layer " + std::to_string(l) + " gate/up is not 4-bit group-scaled flat cells in 128-row blocks";
         break;
       }
       GemvSrc dn = plan_linear(li.down_proj, li.down_tiles, A.D, A.F, A.F, 1, -1);
       float* dn_out[1] = {B->h};
-      if (!gemm(&dn, 1, EPI_ACCUM, A.F, B->mlp, A.F, nullptr, dn_out, A.D)) {
+      if (!gemm(&dn, 1, EPI_ACCUM, A.F, B->mlp, A.F, nullptr, dn_out, A.D, 5)) {
         why = "layer " + std::to_string(l) + " down is not 4-bit group-scaled flat cells in 128-row blocks";
         break;
       }
@@ -486,7 +513,7 @@ BatchStep* Engine::batch_step(int nt) {
       const float* g_fin = upload_floats(gam);
       GemvSrc lm = plan_lm_head();
       float* lm_out[1] = {B->logits};
-      if (!gemm(&lm, 1, EPI_LOGITS, A.D, B->h, A.D, g_fin, lm_out, A.V))
+      if (!gemm(&lm, 1, EPI_LOGITS, A.D, B->h, A.D, g_fin, lm_out, A.V, 6))
         why = "the LM head is not 4-bit group-scaled flat cells in 128-row blocks";
     }
     if (!why.empty()) {
@@ -524,6 +551,45 @@ BatchStep* Engine::batch_step(int nt) {
   bsteps_[idx] = B;
   bstep_state_[idx] = 1;
   return B;
+}
+
+int Engine::profile_verify(size_t m, uint32_t pos, float* role_ms, double* role_bytes, int cap) {
+  const int nt = m <= 4 ? 4 : 8;
+  BatchStep* B = batch_step(nt);
+  if (!B) throw std::runtime_error("the batched step does not apply: " + bstep_why_[nt == 4 ? 0 : 1]);
+  if ((uint64_t)pos + nt > max_seq_) throw std::runtime_error("sequence exceeds max_seq_len");
+  CKV(cudaSetDevice(device_));
+  kv_ensure((uint64_t)pos + nt);
+  for (int i = 0; i < nt; i++) B->h_toks[i] = (int32_t)(1000 + i);
+  memset(B->h_st, 0, sizeof(StepState));
+  B->h_st->pos = (int32_t)pos;
+  B->h_st->finite = 1;
+  CKV(cudaMemcpyAsync(B->toks, B->h_toks, 8 * 4, cudaMemcpyHostToDevice, stream_));
+  CKV(cudaMemcpyAsync(B->st, B->h_st, sizeof(StepState), cudaMemcpyHostToDevice, stream_));
+  const size_t n = B->ops.size();
+  std::vector<cudaEvent_t> ev(n + 1);
+  for (auto& e : ev) CKV(cudaEventCreate(&e));
+  CKV(cudaEventRecord(ev[0], stream_));
+  for (size_t i = 0; i < n; i++) {
+    run_bop(*B, B->ops[i], stream_);
+    CKV(cudaEventRecord(ev[i + 1], stream_));
+  }
+  CKV(cudaStreamSynchronize(stream_));
+  for (int r = 0; r < cap; r++) {
+    role_ms[r] = 0.f;
+    role_bytes[r] = 0.0;
+  }
+  for (size_t i = 0; i < n; i++) {
+    float ms = 0.f;
+    CKV(cudaEventElapsedTime(&ms, ev[i], ev[i + 1]));
+    const int r = B->ops[i].role;
+    if (r >= 0 && r < cap) {
+      role_ms[r] += ms;
+      role_bytes[r] += B->ops[i].alg_bytes;
+    }
+  }
+  for (auto& e : ev) cudaEventDestroy(e);
+  return (int)n;
 }
 
 bool Engine::verify_batched(const uint32_t* toks, size_t m, uint32_t pos, float* logits_out, uint32_t* argmax_out) {

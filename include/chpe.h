@@ -223,6 +223,13 @@ const char *chpe_role_kernel_name(void *ctx, int role);
  * position by one.  Needs a prior forward. */
 int chpe_profile_step(void *ctx, float *op_ms, int *op_roles, int cap);
 
+/* The batched verification step of m (<= 8) scratch candidates at pos,
+ * launched op by op with CUDA events between the ops: per role (numbers as
+ * chpe_bench_kernel; 0 other) the summed milliseconds and algorithmic weight
+ * bytes, `cap` entries each.  The KV entries at pos.. are overwritten.
+ * Returns the op count, -1 on error. */
+int chpe_profile_verify(void *ctx, size_t m, uint32_t pos, float *role_ms, double *role_bytes, int cap);
+
 /* Algorithmic weight bytes one decode step of this context streams (codes
  * and scales of the rows its projections use; with tensor parallelism, this
  * rank's share).  0 for NULL. */

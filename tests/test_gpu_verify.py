@@ -70,16 +70,47 @@ def _prefill(e, oracles, L, KV, HD, ctx, rng):
             o.kv_load(l, 0, k, v)
 
 
+@pytest.fixture(scope="module")
+def archive_9b():
+    import gc
+    a = chpe.synth_archive(chpe.SYNTH_9B_W4)
+    yield a
+    del a
+    gc.collect()
+
+
+def test_batched_prefill_9b(archive_9b, monkeypatch):
+    """Batched prefill: a 21-token prompt through chpe_forward_tokens runs two
+    chunks of 8 through the batched tcgen05 step and 5 tokens one by one; the
+    last logits match the same prompt on the single-token step and the oracle."""
+    a = archive_9b
+    prompt = np.random.default_rng(4).integers(0, 248320, 21).astype(np.uint32)
+    e = chpe.Engine.from_bytes(a, chpe.ARCH_9B, 64)
+    got = np.empty(e.vocab, np.float32)
+    e.forward_tokens(prompt, got)
+    assert e.position() == 21
+    monkeypatch.setenv("CHPE_PREFILL_BATCHED", "0")
+    seq = np.empty(e.vocab, np.float32)
+    e.forward_tokens(prompt, seq)
+    monkeypatch.delenv("CHPE_PREFILL_BATCHED")
+    assert_logits_match(got, seq, "batched prefill vs single-token steps")
+    o = O.OracleEngine(a, O.ARCH_9B, 64, threads=oracle_threads())
+    for p, t in enumerate(prompt):
+        o.forward_decode(int(t), p)
+    assert_logits_match(got, o.logits(), "batched prefill vs oracle")
+    o.close()
+    e.close()
+
+
 @pytest.mark.parametrize("ctx", [5, 2048])
-def test_batched_verify_9b(ctx, monkeypatch):
+def test_batched_verify_9b(ctx, monkeypatch, archive_9b):
     """Config 4: Qwen3.5-9B 4-bit, batch-4/8 verification through the batched
     tcgen05 step, against the same candidates run as sequential decode steps
     (CHPE_VERIFY_BATCHED=0) and against the oracle; at ctx 5 after a real
     prompt, at ctx 2048 over a prefilled KV cache.  m = 3 pads the batch of 4;
     a second candidate set at the same position checks the rollback."""
-    import gc
-    a = chpe.synth_archive(chpe.SYNTH_9B_W4)
-    try:
+    a = archive_9b
+    if True:
         e = chpe.Engine.from_bytes(a, chpe.ARCH_9B, ctx + 16)
         assert e.verify_batched_unavailable(8) == ""
         o = O.OracleEngine(a, O.ARCH_9B, ctx + 16, threads=oracle_threads())
@@ -111,6 +142,3 @@ def test_batched_verify_9b(ctx, monkeypatch):
         o.close()
         o16.close()
         e.close()
-    finally:
-        del a
-        gc.collect()
