@@ -22,7 +22,9 @@
 // scale * sum (c - 8) x from a tcgen05.ld of the row's D columns.
 //
 // Work split: a CTA takes one block of 128 rows and one range of at most
-// kBgMaxGroups groups (split-K).  Its 256 threads are two warpgroups; each
+// kBgMaxGroups groups (split-K); two CTAs share an SM (256 TMEM columns and
+// at most 128 registers per thread each), so one's prologue and epilogue
+// overlap the other's stream.  Its 256 threads are two warpgroups; each
 // processes alternate groups with its own two TMEM stages (A 32 columns,
 // D 32 columns each).  Thread r of a warpgroup owns row r: it loads the row's
 // 64 code bytes and scale of a group kBgAhead groups ahead (registers), masks
@@ -100,7 +102,7 @@ __host__ __device__ inline uint32_t bg_b_off(uint32_t n, uint32_t k, uint32_t N)
 }
 
 template <int NT>
-__global__ void __launch_bounds__(kBgThreads, 1) bgemm_w4_kernel(const __grid_constant__ BgemmLaunch P) {
+__global__ void __launch_bounds__(kBgThreads, 2) bgemm_w4_kernel(const __grid_constant__ BgemmLaunch P) {
   constexpr uint32_t N = 4u * NT;
   extern __shared__ __align__(1024) uint8_t bsm[];
   __shared__ __align__(8) uint64_t dfull[2][kBgStages];
@@ -180,14 +182,31 @@ __global__ void __launch_bounds__(kBgThreads, 1) bgemm_w4_kernel(const __grid_co
     __syncthreads();
   }
   // B pieces: warp w builds (token, group) pairs w, w + 8, ...; lane L holds
-  // columns 4L..4L+3 of the group (code bytes 2L and 2L + 1)
+  // columns 4L..4L+3 of the group (code bytes 2L and 2L + 1).  The x (and
+  // gain) loads of kBgBatch pairs are issued together, then the pairs built.
   float* xsc = reinterpret_cast<float*>(bsm + lay.xsc);
-  for (uint32_t q = warp; q < (uint32_t)NT * ng; q += kBgThreads / 32u) {
-    const uint32_t t = q / ng, gl = q % ng, c = (g0 + gl) * 128u + 4u * L;
-    float4 o = *reinterpret_cast<const float4*>(P.x + (size_t)t * P.x_stride + c);
+  constexpr uint32_t kBgBatch = 6;
+  const uint32_t npairs = (uint32_t)NT * ng;
+  for (uint32_t q0 = warp; q0 < npairs; q0 += kBgBatch * (kBgThreads / 32u)) {
+    float4 xv[kBgBatch], gv[kBgBatch];
+#pragma unroll
+    for (uint32_t b = 0; b < kBgBatch; b++) {
+      const uint32_t q = q0 + b * (kBgThreads / 32u);
+      if (q < npairs) {
+        const uint32_t t = q / ng, c = (g0 + q % ng) * 128u + 4u * L;
+        xv[b] = *reinterpret_cast<const float4*>(P.x + (size_t)t * P.x_stride + c);
+        gv[b] = P.gamma ? *reinterpret_cast<const float4*>(P.gamma + c) : make_float4(1.f, 1.f, 1.f, 1.f);
+      }
+    }
+#pragma unroll
+    for (uint32_t b = 0; b < kBgBatch; b++) {
+    const uint32_t q = q0 + b * (kBgThreads / 32u);
+    if (q >= npairs) break;
+    const uint32_t t = q / ng, gl = q % ng;
+    float4 o = xv[b];
     if (P.gamma) {
       const float iv = s_inv[t];
-      const float4 gm = *reinterpret_cast<const float4*>(P.gamma + c);
+      const float4 gm = gv[b];
       o.x = o.x * iv * gm.x;
       o.y = o.y * iv * gm.y;
       o.z = o.z * iv * gm.z;
@@ -227,6 +246,7 @@ __global__ void __launch_bounds__(kBgThreads, 1) bgemm_w4_kernel(const __grid_co
     if (L == 0) {
       xsc[2u * (t * ng + gl)] = invS;
       xsc[2u * (t * ng + gl) + 1u] = sx;
+    }
     }
   }
   fence_proxy_async_smem();  // B written by threads, read by the tensor core
@@ -355,6 +375,9 @@ __global__ void __launch_bounds__(kBgThreads, 1) bgemm_w4_kernel(const __grid_co
     tc::fence_after_sync();
     tc::tmem_dealloc(taddr, kBgTmemCols);
   }
+  // the next launch's CTAs allocate tensor memory before their dependency
+  // wait: release it before letting them start
+  __syncthreads();
   pdl_launch_dependents();
   if (wg == 0) {
 #pragma unroll

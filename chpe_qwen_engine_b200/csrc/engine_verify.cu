@@ -49,7 +49,7 @@ bool plan_bgemm(const GemvSrc* src, int nseg, int epi, uint32_t C, int nt, int n
   if (epi == EPI_SWIGLU && (nseg != 2 || src[0].r_total != src[1].r_total)) return false;
   const uint32_t G = C / 128u, nb = rows / kBgRows;
   uint32_t ks = (G + kBgMaxGroups - 1) / kBgMaxGroups;
-  const uint32_t fill = ((uint32_t)num_sms + nb - 1) / nb;  // about one CTA per SM at least
+  const uint32_t fill = (2u * (uint32_t)num_sms + nb - 1) / nb;  // two CTAs per SM at least
   if (fill > ks) ks = fill;
   if (ks > G) ks = G;
   B.nseg = nseg;
