@@ -21,6 +21,10 @@
 // and row the epilogue forms scale * (sum_n D_n 128^-n / S - 8 sum x) =
 // scale * sum (c - 8) x from a tcgen05.ld of the row's D columns.
 //
+// B is built once per launch by bgemm_prep_kernel (into global memory, in
+// the shared-memory layout) and every CTA copies its groups in with one bulk
+// copy.
+//
 // Work split: a CTA takes one block of 128 rows and one range of at most
 // kBgMaxGroups groups (split-K); two CTAs share an SM (256 TMEM columns and
 // at most 128 registers per thread each), so one's prologue and epilogue
@@ -77,7 +81,22 @@ struct BgemmLaunch {
   float* ssq_out;
   const float* ssq_in;
   uint32_t ssq_n;
+  // B pieces and per-(group, token) (1/S, sum x) of every group, written by
+  // bgemm_prep_kernel: [G][128 N] bytes in the shared-memory layout of B, and
+  // [G][NT][2] floats
+  uint8_t* pieces;
+  float* pxsc;
+  // Timing trace (measurement only; null in the decode paths): per CTA the
+  // global timer at entry, after the prologue, after the main loop and at
+  // the end, as 4 consecutive u64.
+  unsigned long long* trace;
 };
+
+CHPE_DEV unsigned long long bg_now() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
 struct BgSmem {  // dynamic shared memory layout (bytes)
   uint32_t b, xsc, ycomb, total;
@@ -101,17 +120,93 @@ __host__ __device__ inline uint32_t bg_b_off(uint32_t n, uint32_t k, uint32_t N)
   return j * N * 32u + (n >> 3) * 256u + (kk >> 4) * 128u + (n & 7u) * 16u + (kk & 15u);
 }
 
+// B pieces of one 128-column group for every token, once per launch: CTA g
+// = group g, warp t = token t (lane L: columns 4L..4L+3, code bytes 2L and
+// 2L + 1).  RMSNorm factors from the sums of squares the last residual
+// update left (ssq_in), or from x itself.  It lets the GEMM's CTAs start (and
+// prefetch their weights into L2) before it has finished.
+template <int NT>
+__global__ void __launch_bounds__(NT * 32) bgemm_prep_kernel(const __grid_constant__ BgemmLaunch P) {
+  constexpr uint32_t N = 4u * NT;
+  pdl_launch_dependents();
+  pdl_wait();
+  const uint32_t g = blockIdx.x, t = threadIdx.x >> 5, L = threadIdx.x & 31u;
+  float inv = 1.0f;
+  if (P.gamma) {
+    float ss = 0.f;
+    if (P.ssq_in) {
+      for (uint32_t b = 0; b < P.ssq_n; b++) ss += P.ssq_in[b * NT + t];
+    } else {
+      const float* xr = P.x + (size_t)t * P.x_stride;
+      for (uint32_t c = 4u * L; c < P.C; c += 128u) {
+        const float4 v = *reinterpret_cast<const float4*>(xr + c);
+        ss = fmaf(v.x, v.x, ss);
+        ss = fmaf(v.y, v.y, ss);
+        ss = fmaf(v.z, v.z, ss);
+        ss = fmaf(v.w, v.w, ss);
+      }
+      ss = warp_sum(ss);
+    }
+    inv = 1.0f / sqrtf(ss / (float)P.C + P.eps);
+  }
+  const uint32_t c = g * 128u + 4u * L;
+  float4 o = *reinterpret_cast<const float4*>(P.x + (size_t)t * P.x_stride + c);
+  if (P.gamma) {
+    const float4 gm = *reinterpret_cast<const float4*>(P.gamma + c);
+    o.x = o.x * inv * gm.x;
+    o.y = o.y * inv * gm.y;
+    o.z = o.z * inv * gm.z;
+    o.w = o.w * inv * gm.w;
+  }
+  const float y0 = o.x, z0 = o.y * 0.0625f, y1 = o.z, z1 = o.w * 0.0625f;
+  float m = fmaxf(fmaxf(fabsf(y0), fabsf(z0)), fmaxf(fabsf(y1), fabsf(z1)));
+  if (!(m <= 3.402823466e38f)) m = __int_as_float(0x7f800000);  // NaN -> inf
+  m = warp_max(m);
+  float Sc = 1.0f, invS = 1.0f;
+  if (!(m <= 3.402823466e38f)) {
+    Sc = 0.0f;  // pieces 0, rows NaN
+    invS = __int_as_float(0x7fc00000);
+  } else if (m > 0.0f) {
+    int ex;
+    frexpf(m, &ex);  // m in [2^(ex-1), 2^ex)
+    const int k = 6 - ex < 126 ? 6 - ex : 126;
+    Sc = ldexpf(1.0f, k);
+    invS = ldexpf(1.0f, -k);
+  }
+  uint8_t* gb = P.pieces + (size_t)g * 128u * N;  // lo half, then hi half at + 64 N
+  float ry0 = y0 * Sc, ry1 = y1 * Sc, rz0 = z0 * Sc, rz1 = z1 * Sc;
+#pragma unroll
+  for (uint32_t n = 0; n < 4u; n++) {
+    const float iy0 = rintf(ry0), iy1 = rintf(ry1), iz0 = rintf(rz0), iz1 = rintf(rz1);
+    const uint16_t py = (uint16_t)((uint32_t)((int)iy0 & 0xff) | ((uint32_t)((int)iy1 & 0xff) << 8));
+    const uint16_t pz = (uint16_t)((uint32_t)((int)iz0 & 0xff) | ((uint32_t)((int)iz1 & 0xff) << 8));
+    const uint32_t off = bg_b_off(4u * t + n, 2u * L, N);
+    *reinterpret_cast<uint16_t*>(gb + off) = py;
+    *reinterpret_cast<uint16_t*>(gb + 64u * N + off) = pz;
+    ry0 = (ry0 - iy0) * 128.0f;
+    ry1 = (ry1 - iy1) * 128.0f;
+    rz0 = (rz0 - iz0) * 128.0f;
+    rz1 = (rz1 - iz1) * 128.0f;
+  }
+  const float sx = warp_sum((o.x + o.y) + (o.z + o.w));
+  if (L == 0) {
+    P.pxsc[2u * (g * NT + t)] = invS;
+    P.pxsc[2u * (g * NT + t) + 1u] = sx;
+  }
+}
+
 template <int NT>
 __global__ void __launch_bounds__(kBgThreads, 2) bgemm_w4_kernel(const __grid_constant__ BgemmLaunch P) {
   constexpr uint32_t N = 4u * NT;
   extern __shared__ __align__(1024) uint8_t bsm[];
   __shared__ __align__(8) uint64_t dfull[2][kBgStages];
+  __shared__ __align__(8) uint64_t bfull;
   __shared__ uint32_t s_taddr;
-  __shared__ float s_inv[NT];
   __shared__ float s_red[4 * NT];
   __shared__ int s_last;
   const uint32_t tid = threadIdx.x, warp = tid >> 5, L = tid & 31u;
   const uint32_t wg = tid >> 7, row = tid & 127u;
+  if (P.trace && tid == 0) P.trace[4 * blockIdx.x] = bg_now();
 
   // this CTA's block and column range
   const uint32_t split = blockIdx.x % P.ksplit, blk = blockIdx.x / P.ksplit;
@@ -131,6 +226,7 @@ __global__ void __launch_bounds__(kBgThreads, 2) bgemm_w4_kernel(const __grid_co
   if (tid == 0) {
     for (int w = 0; w < 2; w++)
       for (uint32_t s = 0; s < kBgStages; s++) mbar_init(&dfull[w][s], 1);
+    mbar_init(&bfull, 1);
     fence_mbar_init();
   }
   // where row `row` of this block keeps the codes of group g (64 bytes) and
@@ -156,97 +252,20 @@ __global__ void __launch_bounds__(kBgThreads, 2) bgemm_w4_kernel(const __grid_co
     }
   }
   pdl_wait();
+  __syncthreads();  // the barriers initialised above are visible to every thread
 
-  // RMSNorm factors of the tokens (warp t: token t)
-  if (P.gamma && P.ssq_in) {
-    if (tid < (uint32_t)NT) {
-      float ss = 0.f;
-      for (uint32_t b = 0; b < P.ssq_n; b++) ss += P.ssq_in[b * NT + tid];
-      s_inv[tid] = 1.0f / sqrtf(ss / (float)P.C + P.eps);
-    }
-    __syncthreads();
-  } else if (P.gamma) {
-    if (warp < (uint32_t)NT) {
-      const float* xr = P.x + (size_t)warp * P.x_stride;
-      float ss = 0.f;
-      for (uint32_t c = 4u * L; c < P.C; c += 128u) {
-        const float4 v = *reinterpret_cast<const float4*>(xr + c);
-        ss = fmaf(v.x, v.x, ss);
-        ss = fmaf(v.y, v.y, ss);
-        ss = fmaf(v.z, v.z, ss);
-        ss = fmaf(v.w, v.w, ss);
-      }
-      ss = warp_sum(ss);
-      if (L == 0) s_inv[warp] = 1.0f / sqrtf(ss / (float)P.C + P.eps);
-    }
-    __syncthreads();
-  }
-  // B pieces: warp w builds (token, group) pairs w, w + 8, ...; lane L holds
-  // columns 4L..4L+3 of the group (code bytes 2L and 2L + 1).  The x (and
-  // gain) loads of kBgBatch pairs are issued together, then the pairs built.
+  // this CTA's groups of B and their (1/S, sum x), prepared by
+  // bgemm_prep_kernel, copied in with two bulk copies
   float* xsc = reinterpret_cast<float*>(bsm + lay.xsc);
-  constexpr uint32_t kBgBatch = 6;
-  const uint32_t npairs = (uint32_t)NT * ng;
-  for (uint32_t q0 = warp; q0 < npairs; q0 += kBgBatch * (kBgThreads / 32u)) {
-    float4 xv[kBgBatch], gv[kBgBatch];
-#pragma unroll
-    for (uint32_t b = 0; b < kBgBatch; b++) {
-      const uint32_t q = q0 + b * (kBgThreads / 32u);
-      if (q < npairs) {
-        const uint32_t t = q / ng, c = (g0 + q % ng) * 128u + 4u * L;
-        xv[b] = *reinterpret_cast<const float4*>(P.x + (size_t)t * P.x_stride + c);
-        gv[b] = P.gamma ? *reinterpret_cast<const float4*>(P.gamma + c) : make_float4(1.f, 1.f, 1.f, 1.f);
-      }
+  {
+    const uint32_t nb = ng * 128u * N, nx = ng * (uint32_t)NT * 8u;
+    if (tid == 0) {
+      mbar_expect_tx(&bfull, nb + nx);
+      bulk_g2s(bsm + lay.b, P.pieces + (size_t)g0 * 128u * N, nb, &bfull);
+      bulk_g2s(xsc, P.pxsc + (size_t)g0 * NT * 2u, nx, &bfull);
     }
-#pragma unroll
-    for (uint32_t b = 0; b < kBgBatch; b++) {
-    const uint32_t q = q0 + b * (kBgThreads / 32u);
-    if (q >= npairs) break;
-    const uint32_t t = q / ng, gl = q % ng;
-    float4 o = xv[b];
-    if (P.gamma) {
-      const float iv = s_inv[t];
-      const float4 gm = gv[b];
-      o.x = o.x * iv * gm.x;
-      o.y = o.y * iv * gm.y;
-      o.z = o.z * iv * gm.z;
-      o.w = o.w * iv * gm.w;
-    }
-    const float y0 = o.x, z0 = o.y * 0.0625f, y1 = o.z, z1 = o.w * 0.0625f;
-    float m = fmaxf(fmaxf(fabsf(y0), fabsf(z0)), fmaxf(fabsf(y1), fabsf(z1)));
-    if (!(m <= 3.402823466e38f)) m = __int_as_float(0x7f800000);  // NaN -> inf
-    m = warp_max(m);
-    float Sc = 1.0f, invS = 1.0f;
-    if (!(m <= 3.402823466e38f)) {
-      Sc = 0.0f;  // pieces 0, rows NaN
-      invS = __int_as_float(0x7fc00000);
-    } else if (m > 0.0f) {
-      int ex;
-      frexpf(m, &ex);  // m in [2^(ex-1), 2^ex)
-      const int k = 6 - ex < 126 ? 6 - ex : 126;
-      Sc = ldexpf(1.0f, k);
-      invS = ldexpf(1.0f, -k);
-    }
-    uint8_t* gb = bsm + lay.b + gl * 128u * N;  // lo half, then hi half at + 64 N
-    float ry0 = y0 * Sc, ry1 = y1 * Sc, rz0 = z0 * Sc, rz1 = z1 * Sc;
-#pragma unroll
-    for (uint32_t n = 0; n < 4u; n++) {
-      const float iy0 = rintf(ry0), iy1 = rintf(ry1), iz0 = rintf(rz0), iz1 = rintf(rz1);
-      const uint16_t py = (uint16_t)((uint32_t)((int)iy0 & 0xff) | ((uint32_t)((int)iy1 & 0xff) << 8));
-      const uint16_t pz = (uint16_t)((uint32_t)((int)iz0 & 0xff) | ((uint32_t)((int)iz1 & 0xff) << 8));
-      const uint32_t off = bg_b_off(4u * t + n, 2u * L, N);
-      *reinterpret_cast<uint16_t*>(gb + off) = py;
-      *reinterpret_cast<uint16_t*>(gb + 64u * N + off) = pz;
-      ry0 = (ry0 - iy0) * 128.0f;
-      ry1 = (ry1 - iy1) * 128.0f;
-      rz0 = (rz0 - iz0) * 128.0f;
-      rz1 = (rz1 - iz1) * 128.0f;
-    }
-    const float sx = warp_sum((o.x + o.y) + (o.z + o.w));
-    if (L == 0) {
-      xsc[2u * (t * ng + gl)] = invS;
-      xsc[2u * (t * ng + gl) + 1u] = sx;
-    }
+    if (!mbar_wait(&bfull, 0)) {
+      if (tid == 0) atomicExch(P.err, 1);
     }
   }
   fence_proxy_async_smem();  // B written by threads, read by the tensor core
@@ -256,6 +275,7 @@ __global__ void __launch_bounds__(kBgThreads, 2) bgemm_w4_kernel(const __grid_co
   const uint32_t taddr = s_taddr;
   const uint32_t lane_base = (uint32_t)((warp & 3u) * 32u) << 16;
 
+  if (P.trace && tid == 0) P.trace[4 * blockIdx.x + 1] = bg_now();
   // ---- main loop: this warpgroup's groups gl = wg, wg + 2, ... ----------
   float y[NT];
 #pragma unroll
@@ -305,7 +325,7 @@ __global__ void __launch_bounds__(kBgThreads, 2) bgemm_w4_kernel(const __grid_co
       const float d0 = (float)(int32_t)d[4 * t], d1 = (float)(int32_t)d[4 * t + 1];
       const float d2 = (float)(int32_t)d[4 * t + 2], d3 = (float)(int32_t)d[4 * t + 3];
       const float sum = (d0 + d1 * 0.0078125f) + (d2 * 6.103515625e-05f + d3 * 4.76837158203125e-07f);
-      const float invS = xsc[2u * (t * ng + gl)], sx = xsc[2u * (t * ng + gl) + 1u];
+      const float invS = xsc[2u * (gl * NT + t)], sx = xsc[2u * (gl * NT + t) + 1u];
       y[t] = fmaf(scale, fmaf(sum, invS, -8.0f * sx), y[t]);
     }
   };
@@ -363,6 +383,7 @@ __global__ void __launch_bounds__(kBgThreads, 2) bgemm_w4_kernel(const __grid_co
     epilogue(0, q0);
   }
 
+  if (P.trace && tid == 0) P.trace[4 * blockIdx.x + 2] = bg_now();
   // ---- the two warpgroups' sums, in a fixed order ------------------------
   float* ycomb = reinterpret_cast<float*>(bsm + lay.ycomb);
   if (wg == 1) {
@@ -402,9 +423,13 @@ __global__ void __launch_bounds__(kBgThreads, 2) bgemm_w4_kernel(const __grid_co
       if (s_last) P.counters[ci] = 0u;
     }
     __syncthreads();
-    if (!s_last) return;
+    if (!s_last) {
+      if (P.trace && tid == 0) P.trace[4 * blockIdx.x + 3] = bg_now();
+      return;
+    }
     __threadfence();
   }
+  if (P.trace && tid == 0) P.trace[4 * blockIdx.x + 3] = bg_now();
   if (wg != 0) return;
   // ---- epilogue of the block's rows (thread = row) -----------------------
   if (swig) {

@@ -5,6 +5,8 @@
 // candidates < i) and prompt chunks.  The result equals NT forwardDecode
 // steps (chpe_engine.zig:1663-1803) up to f32 rounding.
 #include <algorithm>
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <stdexcept>
 #include <string>
@@ -73,12 +75,17 @@ void launch_bgemm(int nt, const BgemmLaunch& B, uint32_t smem, cudaStream_t s, b
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
+  cudaLaunchConfig_t pc = cfg;  // the B-piece preparation: one CTA per group, a warp per token
+  pc.gridDim = dim3(B.C / 128u);
+  pc.blockDim = dim3(32u * (uint32_t)nt);
+  pc.dynamicSmemBytes = 0;
   if (nt == 4) {
     static bool set4 = false;
     if (!set4) {
       CKV(cudaFuncSetAttribute(bgemm_w4_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
       set4 = true;
     }
+    CKV(cudaLaunchKernelEx(&pc, bgemm_prep_kernel<4>, B));
     CKV(cudaLaunchKernelEx(&cfg, bgemm_w4_kernel<4>, B));
   } else {
     static bool set8 = false;
@@ -86,6 +93,7 @@ void launch_bgemm(int nt, const BgemmLaunch& B, uint32_t smem, cudaStream_t s, b
       CKV(cudaFuncSetAttribute(bgemm_w4_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
       set8 = true;
     }
+    CKV(cudaLaunchKernelEx(&pc, bgemm_prep_kernel<8>, B));
     CKV(cudaLaunchKernelEx(&cfg, bgemm_w4_kernel<8>, B));
   }
 }
@@ -109,6 +117,12 @@ void Engine::debug_bgemm(uint64_t tile_start, uint64_t num_tiles, const float* x
   CKV(cudaMalloc(&dp, npart * 4));
   CKV(cudaMalloc(&dc, nblk * 4));
   CKV(cudaMalloc(&flags, 8));
+  uint8_t* dpieces = nullptr;
+  float* dpxsc = nullptr;
+  CKV(cudaMalloc(&dpieces, (size_t)(c_total / 128) * 128 * 4 * nt));
+  CKV(cudaMalloc(&dpxsc, (size_t)(c_total / 128) * nt * 8));
+  B.pieces = dpieces;
+  B.pxsc = dpxsc;
   CKV(cudaMemcpy(dx, x, nx * 4, cudaMemcpyHostToDevice));
   CKV(cudaMemcpy(dy, y, ny * 4, cudaMemcpyHostToDevice));
   CKV(cudaMemset(dc, 0, nblk * 4));
@@ -121,9 +135,27 @@ void Engine::debug_bgemm(uint64_t tile_start, uint64_t num_tiles, const float* x
   B.counters = dc;
   B.bad = flags;
   B.err = flags + 1;
+  // CHPE_BGEMM_TRACE=<file>: per-CTA timer samples of this launch are
+  // written there (entry, prologue end, main loop end, exit), as u64
+  const char* trace_path = getenv("CHPE_BGEMM_TRACE");
+  unsigned long long* dtrace = nullptr;
+  if (trace_path) {
+    CKV(cudaMalloc(&dtrace, (size_t)B.nunits * 32));
+    CKV(cudaMemset(dtrace, 0, (size_t)B.nunits * 32));
+    B.trace = dtrace;
+  }
   launch_bgemm(nt, B, smem, stream_, false);
   CKV(cudaGetLastError());
   CKV(cudaStreamSynchronize(stream_));
+  if (dtrace) {
+    std::vector<unsigned long long> h((size_t)B.nunits * 4);
+    CKV(cudaMemcpy(h.data(), dtrace, h.size() * 8, cudaMemcpyDeviceToHost));
+    cudaFree(dtrace);
+    if (FILE* f = fopen(trace_path, "wb")) {
+      fwrite(h.data(), 8, h.size(), f);
+      fclose(f);
+    }
+  }
   int32_t h[2] = {0, 0};
   CKV(cudaMemcpy(y, dy, ny * 4, cudaMemcpyDeviceToHost));
   CKV(cudaMemcpy(h, flags, 8, cudaMemcpyDeviceToHost));
@@ -132,6 +164,8 @@ void Engine::debug_bgemm(uint64_t tile_start, uint64_t num_tiles, const float* x
   cudaFree(dp);
   cudaFree(dc);
   cudaFree(flags);
+  cudaFree(dpieces);
+  cudaFree(dpxsc);
   if (h[1]) throw std::runtime_error("a device wait timed out in the batched GEMM");
 }
 
@@ -534,8 +568,13 @@ BatchStep* Engine::batch_step(int nt) {
     }
     B->part = (float*)dalloc(part_max * 4);
     B->cnt = (uint32_t*)dalloc(cnt_max * 4);
+    const uint32_t gmax = (A.F > A.D ? A.F : A.D) / 128u + 1u;
+    uint8_t* pieces = (uint8_t*)dalloc((size_t)gmax * 128u * 4u * nt);
+    float* pxsc = (float*)dalloc((size_t)gmax * nt * 8u);
     for (BOp& op : B->ops) {
       if (op.type != BOP_GEMM) continue;
+      op.bg.pieces = pieces;
+      op.bg.pxsc = pxsc;
       op.bg.part = B->part;
       op.bg.counters = B->cnt;
       op.bg.best = B->best;
