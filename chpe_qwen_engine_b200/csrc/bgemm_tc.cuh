@@ -88,7 +88,10 @@ struct BgemmLaunch {
   float* pxsc;
   // Timing trace (measurement only; null in the decode paths): per CTA the
   // global timer at entry, after the prologue, after the main loop and at
-  // the end, as 4 consecutive u64.
+  // the end, as 4 consecutive u64; then, for CTA 0's first thread, 6 stamps
+  // per main-loop iteration for the first 8 iterations (iteration start,
+  // epilogue wait done, D read, A stored, warpgroup barrier passed, MMAs
+  // issued).
   unsigned long long* trace;
 };
 
@@ -306,12 +309,18 @@ __global__ void __launch_bounds__(kBgThreads, 2) bgemm_w4_kernel(const __grid_co
   load(2, c2, s2);
   bool failed = false;
   const uint32_t idesc = tc::idesc_i8_u8s8(kBgRows, N);
+  unsigned long long* tr = (P.trace && blockIdx.x == 0 && tid == 0) ? P.trace + 4u * gridDim.x : nullptr;
+  uint32_t it_now = 0;
+  auto stamp = [&](uint32_t k) {
+    if (tr && it_now < 8u) tr[it_now * 6u + k] = bg_now();
+  };
   auto epilogue = [&](uint32_t k, float scale) {
     const uint32_t s = k % kBgStages, gl = wg + 2u * k;
     if (!failed && !mbar_wait(&dfull[wg][s], (k / kBgStages) & 1u)) {
       failed = true;
       if (row == 0) atomicExch(P.err, 1);
     }
+    stamp(1);
     tc::fence_after_sync();
     if (failed) return;
     const uint32_t dcol = (wg * kBgStages + s) * 64u + 32u;
@@ -320,6 +329,7 @@ __global__ void __launch_bounds__(kBgThreads, 2) bgemm_w4_kernel(const __grid_co
     for (uint32_t cc = 0; cc < N; cc += 16u)
       tc::ld16(taddr + lane_base + dcol + cc, *reinterpret_cast<uint32_t(*)[16]>(&d[cc]));
     tc::ld_wait();
+    stamp(2);
 #pragma unroll
     for (int t = 0; t < NT; t++) {
       const float d0 = (float)(int32_t)d[4 * t], d1 = (float)(int32_t)d[4 * t + 1];
@@ -331,6 +341,8 @@ __global__ void __launch_bounds__(kBgThreads, 2) bgemm_w4_kernel(const __grid_co
   };
   for (uint32_t i = 0; i < nmy; i++) {
     const uint32_t s = i % kBgStages, gl = wg + 2u * i;
+    it_now = i;
+    stamp(0);
     if (i >= kBgStages) {  // frees stage s
       epilogue(i - kBgStages, q0);
       q0 = q1;
@@ -359,8 +371,10 @@ __global__ void __launch_bounds__(kBgThreads, 2) bgemm_w4_kernel(const __grid_co
     tc::st16(taddr + lane_base + acol, lo);
     tc::st16(taddr + lane_base + acol + 16u, hi);
     tc::st_wait();
+    stamp(3);
     tc::fence_before_sync();
     asm volatile("bar.sync %0, 128;" ::"r"(1u + wg) : "memory");  // this warpgroup's A is complete
+    stamp(4);
     if (row == 0) {
       tc::fence_after_sync();
       const uint8_t* gb = bsm + lay.b + gl * 128u * N;
@@ -373,6 +387,7 @@ __global__ void __launch_bounds__(kBgThreads, 2) bgemm_w4_kernel(const __grid_co
         tc::mma_i8_ts(dt, taddr + acol + 16u + 8u * j,
                       tc::smem_desc_kmajor(gb + 64u * N + j * N * 32u, 128u, 256u), idesc, 1u);
       tc::commit(&dfull[wg][s]);
+      stamp(5);
     }
   }
   // the groups still in the stages (at most two): oldest first

@@ -140,15 +140,15 @@ void Engine::debug_bgemm(uint64_t tile_start, uint64_t num_tiles, const float* x
   const char* trace_path = getenv("CHPE_BGEMM_TRACE");
   unsigned long long* dtrace = nullptr;
   if (trace_path) {
-    CKV(cudaMalloc(&dtrace, (size_t)B.nunits * 32));
-    CKV(cudaMemset(dtrace, 0, (size_t)B.nunits * 32));
+    CKV(cudaMalloc(&dtrace, (size_t)B.nunits * 32 + 48 * 8));
+    CKV(cudaMemset(dtrace, 0, (size_t)B.nunits * 32 + 48 * 8));
     B.trace = dtrace;
   }
   launch_bgemm(nt, B, smem, stream_, false);
   CKV(cudaGetLastError());
   CKV(cudaStreamSynchronize(stream_));
   if (dtrace) {
-    std::vector<unsigned long long> h((size_t)B.nunits * 4);
+    std::vector<unsigned long long> h((size_t)B.nunits * 4 + 48);
     CKV(cudaMemcpy(h.data(), dtrace, h.size() * 8, cudaMemcpyDeviceToHost));
     cudaFree(dtrace);
     if (FILE* f = fopen(trace_path, "wb")) {
