@@ -72,6 +72,7 @@ SYMBOLS = [
     ("chpe_get_last_all_finite", _I, [_P]),
     ("chpe_kernels_per_step", _I, [_P]),
     ("chpe_get_position", _U32, [_P]),
+    ("chpe_device_archive_bytes", _U64, [_P]),
     ("chpe_last_error", C.c_char_p, [_P]),
     ("chpe_kv_page_size", _U32, []),
     ("chpe_kv_load", _I, [_P, _U32, _U32, _U32, _FP, _FP]),
@@ -396,6 +397,9 @@ class Engine:
 
     def position(self) -> int:
         return lib().chpe_get_position(self.ctx)
+
+    def device_archive_bytes(self) -> int:
+        return lib().chpe_device_archive_bytes(self.ctx)
 
     # -- probes used by the parity suite ------------------------------------
     def probe_gemv_linear(self, tile_start, num_tiles, x, r_total, c_total, accumulate=False,

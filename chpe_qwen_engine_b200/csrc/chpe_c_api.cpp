@@ -387,6 +387,7 @@ float chpe_get_last_hidden_norm(void* ctx) { return ctx ? ((Ctx*)ctx)->last_hidd
 int chpe_get_last_all_finite(void* ctx) { return ctx ? ((Ctx*)ctx)->last_finite : 0; }
 int chpe_kernels_per_step(void* ctx) { return ctx ? ((Ctx*)ctx)->engine->kernels_per_step() : 0; }
 uint32_t chpe_get_position(void* ctx) { return ctx ? ((Ctx*)ctx)->engine->current_pos() : 0; }
+uint64_t chpe_device_archive_bytes(void* ctx) { return ctx ? ((Ctx*)ctx)->engine->device_archive_bytes() : 0; }
 
 const char* chpe_last_error(void* ctx) {
   return ctx ? ((Ctx*)ctx)->err.c_str() : g_init_error.c_str();

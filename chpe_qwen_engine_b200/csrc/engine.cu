@@ -159,6 +159,117 @@ const float* Engine::upload_floats(const std::vector<float>& v) {
   return d;
 }
 
+// Copies archive bytes [src_off, src_off + n) to device memory at dst
+// through two pinned staging buffers.
+static void stage_upload(uint8_t* dst, const uint8_t* bytes, uint64_t src_off, uint64_t n, cudaStream_t s) {
+  const uint64_t chunk = 64ull << 20;
+  uint8_t* stage[2] = {nullptr, nullptr};
+  cudaEvent_t ev[2];
+  CK(cudaMallocHost(&stage[0], chunk));
+  CK(cudaMallocHost(&stage[1], chunk));
+  CK(cudaEventCreateWithFlags(&ev[0], cudaEventDisableTiming));
+  CK(cudaEventCreateWithFlags(&ev[1], cudaEventDisableTiming));
+  int i = 0;
+  for (uint64_t off = 0; off < n; off += chunk, i ^= 1) {
+    const uint64_t m = n - off < chunk ? n - off : chunk;
+    CK(cudaEventSynchronize(ev[i]));
+    memcpy(stage[i], bytes + src_off + off, m);
+    CK(cudaMemcpyAsync(dst + off, stage[i], m, cudaMemcpyHostToDevice, s));
+    CK(cudaEventRecord(ev[i], s));
+  }
+  CK(cudaStreamSynchronize(s));
+  cudaFreeHost(stage[0]);
+  cudaFreeHost(stage[1]);
+  cudaEventDestroy(ev[0]);
+  cudaEventDestroy(ev[1]);
+}
+
+// The whole archive verbatim, plus a zeroed tail so reads past the last
+// record stay inside the allocation.
+void Engine::upload_archive(const uint8_t* bytes, uint64_t len) {
+  const uint64_t pad = 1ull << 20;
+  CK(cudaMalloc(&d_arc_, len + pad));
+  CK(cudaMemsetAsync(d_arc_ + len, 0, pad, stream_));
+  stage_upload(d_arc_, bytes, 0, len, stream_);
+  dev_arc_bytes_ = len;
+}
+
+// Tensor parallelism: the tiles this rank's kernels read.  The embedding
+// lookups read the record tok/16 (or tok/rows-per-tile of a raw archive)
+// and a little past it (the reference's over-reads), so the embedding
+// records and two more are taken whole; each projection contributes the
+// tiles of its row slice.  Norms and biases are read on the host.
+void Engine::upload_shards(const uint8_t* bytes, uint64_t len) {
+  const ChpeArch& A = *arch_;
+  ChpeTpSlice sl;
+  if (chpe_tp_slice_of(arch_id_, tp_rank_, tp_world_, &sl) != 0) {
+    upload_archive(bytes, len);  // the step builder reports the unsplittable shape
+    return;
+  }
+  const uint64_t rc = f_.record_count, wpt = f_.is_raw ? f_.wpt : 32768ull;
+  std::vector<std::pair<uint64_t, uint64_t>> want;
+  auto add = [&](uint64_t lo, uint64_t hi) {
+    if (lo >= rc) return;
+    if (hi > rc) hi = rc;
+    if (hi > lo) want.push_back({lo, hi});
+  };
+  {
+    const uint64_t rows_per_tile = f_.is_raw ? (wpt / A.D ? wpt / A.D : 1) : 16;
+    add(0, (A.V + rows_per_tile - 1) / rows_per_tile + 2);
+  }
+  auto slice = [&](int64_t start, int64_t tiles, uint32_t r0, uint32_t n, uint32_t C) {
+    if (start < 0) return;
+    const uint64_t lo = (uint64_t)start + (uint64_t)r0 * C / wpt;
+    const uint64_t hi = (uint64_t)start + ((uint64_t)(r0 + n) * C + wpt - 1) / wpt;
+    const uint64_t end = (uint64_t)start + (uint64_t)tiles;
+    add(lo, hi < end ? hi : end);
+  };
+  for (uint32_t l = 0; l < A.L; l++) {
+    ChpeLayerInfo li;
+    chpe_layer_info(arch_id_, f_.is_raw, l, &li);
+    slice(li.q_proj, li.q_tiles, sl.h0 * A.HD, sl.hq * A.HD, A.D);
+    slice(li.k_proj, li.k_tiles, sl.kv0 * A.HD, sl.kvl * A.HD, A.D);
+    slice(li.v_proj, li.v_tiles, sl.kv0 * A.HD, sl.kvl * A.HD, A.D);
+    slice(li.o_proj, li.o_tiles, sl.d0, sl.dl, A.D);
+    slice(li.gate_proj, li.gate_tiles, sl.f0, sl.fl, A.D);
+    slice(li.up_proj, li.up_tiles, sl.f0, sl.fl, A.D);
+    slice(li.down_proj, li.down_tiles, sl.d0, sl.dl, A.F);
+  }
+  {
+    int64_t lhs, lht;
+    chpe_lm_head_span(arch_id_, &lhs, &lht);
+    slice(lhs, lht, sl.v0, sl.vl, A.D);
+  }
+  std::sort(want.begin(), want.end());
+  std::vector<std::pair<uint64_t, uint64_t>> runs;
+  for (const auto& w : want) {
+    if (!runs.empty() && w.first <= runs.back().second) {
+      if (w.second > runs.back().second) runs.back().second = w.second;
+    } else {
+      runs.push_back(w);
+    }
+  }
+  const uint64_t pad = 1ull << 20;
+  for (const auto& r : runs) {
+    const uint64_t off = 4096 + r.first * f_.stride;
+    uint64_t n = (r.second - r.first) * f_.stride;
+    if (off + n > len) n = len > off ? len - off : 0;
+    Shard sh{r.first, r.second, nullptr};
+    CK(cudaMalloc(&sh.dev, n + pad));
+    CK(cudaMemsetAsync(sh.dev + n, 0, pad, stream_));
+    stage_upload(sh.dev, bytes, off, n, stream_);
+    dev_arc_bytes_ += n;
+    shards_.push_back(sh);
+  }
+}
+
+const uint8_t* Engine::arc_for(uint64_t tile) const {
+  if (shards_.empty()) return d_arc_;
+  for (const Shard& sh : shards_)
+    if (tile >= sh.lo && tile < sh.hi) return sh.dev - (4096 + sh.lo * f_.stride);
+  throw std::runtime_error("tensor parallel: a kernel would read a tile this rank did not upload");
+}
+
 // ---- construction: CHPEEngine.init (chpe_engine.zig:854-974) ---------------
 Engine::Engine(const uint8_t* bytes, uint64_t len, int arch, uint32_t max_seq, int device, int tp_rank,
                int tp_world)
@@ -209,33 +320,8 @@ Engine::Engine(const uint8_t* bytes, uint64_t len, int arch, uint32_t max_seq, i
   CK(cudaDeviceGetAttribute(&num_sms_, cudaDevAttrMultiProcessorCount, device_));
   CK(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
 
-  // Archive bytes to HBM verbatim, through pinned staging buffers, plus a
-  // zeroed tail so reads past the last record stay inside the allocation.
-  const uint64_t pad = 1ull << 20;
-  CK(cudaMalloc(&d_arc_, len + pad));
-  CK(cudaMemsetAsync(d_arc_ + len, 0, pad, stream_));
-  {
-    const uint64_t chunk = 64ull << 20;
-    uint8_t* stage[2] = {nullptr, nullptr};
-    cudaEvent_t ev[2];
-    CK(cudaMallocHost(&stage[0], chunk));
-    CK(cudaMallocHost(&stage[1], chunk));
-    CK(cudaEventCreateWithFlags(&ev[0], cudaEventDisableTiming));
-    CK(cudaEventCreateWithFlags(&ev[1], cudaEventDisableTiming));
-    int i = 0;
-    for (uint64_t off = 0; off < len; off += chunk, i ^= 1) {
-      uint64_t n = len - off < chunk ? len - off : chunk;
-      CK(cudaEventSynchronize(ev[i]));
-      memcpy(stage[i], bytes + off, n);
-      CK(cudaMemcpyAsync(d_arc_ + off, stage[i], n, cudaMemcpyHostToDevice, stream_));
-      CK(cudaEventRecord(ev[i], stream_));
-    }
-    CK(cudaStreamSynchronize(stream_));
-    cudaFreeHost(stage[0]);
-    cudaFreeHost(stage[1]);
-    cudaEventDestroy(ev[0]);
-    cudaEventDestroy(ev[1]);
-  }
+  if (tp_world_ > 1 && f_.archive_valid && f_.record_count > 0) upload_shards(bytes, len);
+  else upload_archive(bytes, len);
 
   const ChpeArch& A = *arch_;
   auto dalloc = [&](size_t bytes_) -> void* {
@@ -333,6 +419,7 @@ Engine::~Engine() {
   if (d_region_) cudaFree(d_region_);
   for (void* p : allocs_) cudaFree(p);
   if (d_arc_) cudaFree(d_arc_);
+  for (const Shard& sh : shards_) cudaFree(sh.dev);
   if (h_st_) cudaFreeHost(h_st_);
   if (h_res_) cudaFreeHost(h_res_);
   if (h_tok_) cudaFreeHost(h_tok_);
@@ -951,7 +1038,7 @@ void Engine::push_embed(std::vector<Op>& ops) {
   op.type = OP_EMBED;
   op.role = ROLE_EMBED;
   EmbedLaunch& e = op.em;
-  e.arc = d_arc_;
+  e.arc = arc_for(0);
   e.record_count = f_.record_count;
   e.stride = f_.stride;
   e.prefix = f_.is_raw ? 0 : (f_.is_dense ? 64 : 3072 + 64);
@@ -1110,6 +1197,14 @@ void Engine::build_step_tp() {
     s.row0 = r0;
     s.r_total = n;
     if (s.bias) s.bias += r0;
+    // the slice's tiles lie in one uploaded run: address it there
+    const uint64_t wpt = s.kind == SRC_RAW ? f_.wpt : 32768ull;
+    const uint64_t t0 = (s.tile0 - 4096) / f_.stride;
+    const uint64_t ta = t0 + (uint64_t)r0 * s.c_total / wpt;
+    const uint64_t tb = t0 + ((uint64_t)(r0 + n) * s.c_total - 1) / wpt;
+    s.arc = arc_for(ta);
+    if (arc_for(tb < t0 + s.n_tiles ? tb : t0 + s.n_tiles - 1) != s.arc)
+      throw std::runtime_error("tensor parallel: a slice spans two uploaded runs");
     return s;
   };
 

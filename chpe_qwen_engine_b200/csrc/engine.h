@@ -93,6 +93,9 @@ class Engine {
   uint64_t last_elapsed_ns() const { return last_ns_; }
   void copy_logits(float* out) const;  // last step's logits (vocab floats)
   uint32_t current_pos() const { return pos_; }
+  // Bytes of archive held in device memory: the whole archive on one GPU, this
+  // rank's shards with tensor parallelism.
+  uint64_t device_archive_bytes() const { return dev_arc_bytes_; }
   int kernels_per_step() const;
 
   // Times every recorded op of one role (ROLE_*) across all layers, `rounds`
@@ -205,6 +208,20 @@ class Engine {
   int nsplit_ = 16;  // attention splits of the positions per kv head
   uint32_t wait_polls_ = 0;  // tensor-parallel wait limit (0: the default; CHPE_WAIT_POLLS)
   int last_verify_batched_ = 0;
+  // Tensor parallelism uploads only the archive tiles this rank reads: the
+  // embedding records and its row slice of every projection, each merged
+  // run of tiles in its own allocation.  arc_for(tile) is the base pointer
+  // that addresses byte offsets of the original archive inside the run that
+  // holds `tile` (the whole archive's allocation without sharding).
+  struct Shard {
+    uint64_t lo, hi;  // tiles [lo, hi)
+    uint8_t* dev;     // bytes of record lo onward (+ zero padding)
+  };
+  std::vector<Shard> shards_;
+  uint64_t dev_arc_bytes_ = 0;
+  void upload_archive(const uint8_t* bytes, uint64_t len);
+  void upload_shards(const uint8_t* bytes, uint64_t len);
+  const uint8_t* arc_for(uint64_t tile) const;
   // paged KV cache
   uint32_t n_pages_ = 0, mapped_ = 0;
   uint32_t kv0_ = 0, kvl_ = 0;         // kv heads this rank holds (all of them on one GPU)

@@ -87,6 +87,7 @@ void *chpe_init_bytes(const void *bytes, uint64_t len, int arch, uint32_t max_se
  * that every rank calls the same forward / generate / bench functions in
  * lockstep.  Heads, hidden, FFN rows and vocabulary must divide by world; all
  * projections must be flat cells or raw streams (the 9B and 72B archives).
+ * Each rank uploads only the archive tiles it reads.
  * Results equal the single-GPU engine's: each output element is computed
  * whole on one rank.  Returns NULL / -1 on failure (chpe_last_error). */
 void *chpe_init_tp(const char *archive_path, int arch, uint32_t max_seq_len, int device, int rank,
@@ -241,6 +242,11 @@ int chpe_get_last_all_finite(void *ctx);
 int chpe_kernels_per_step(void *ctx);
 /* Current sequence position (next step's pos). */
 uint32_t chpe_get_position(void *ctx);
+/* Archive bytes held in this context's device memory: the whole archive on
+ * one GPU; with tensor parallelism only the tiles the rank reads (the
+ * embedding records and its row slice of every projection), about
+ * 1/world of the weights. */
+uint64_t chpe_device_archive_bytes(void *ctx);
 /* Last error message of ctx, or, when ctx is NULL, of the calling thread's
  * last failed init or chpe_attention_decode_noalloc call; "" when none. */
 const char *chpe_last_error(void *ctx);

@@ -61,6 +61,8 @@ def _rank_body(rank, world, port, cfg, q):
             out.append((r.argmax_token, r.max_logit, r.token0_logit, r.hidden_norm, r.all_finite,
                         e.logits().copy()))
         gen = e.generate(np.array([11, 2222, 33333], np.uint32), 4)
+        # the rank holds only the tiles it reads: its slices and the embedding
+        assert e.device_archive_bytes() < 0.6 * a.size, (e.device_archive_bytes(), a.size)
         q.put((rank, out, [int(x) for x in gen]))
         e.close()
     finally:
