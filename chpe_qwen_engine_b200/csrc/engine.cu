@@ -1202,6 +1202,10 @@ void Engine::build_step_tp() {
     const uint64_t t0 = (s.tile0 - 4096) / f_.stride;
     const uint64_t ta = t0 + (uint64_t)r0 * s.c_total / wpt;
     const uint64_t tb = t0 + ((uint64_t)(r0 + n) * s.c_total - 1) / wpt;
+    if (ta >= t0 + s.n_tiles) {  // rows past the tensor's tiles: the kernel reads none of them
+      s.arc = arc_for(0);
+      return s;
+    }
     s.arc = arc_for(ta);
     if (arc_for(tb < t0 + s.n_tiles ? tb : t0 + s.n_tiles - 1) != s.arc)
       throw std::runtime_error("tensor parallel: a slice spans two uploaded runs");
