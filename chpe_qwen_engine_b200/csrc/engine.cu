@@ -1734,6 +1734,22 @@ void Engine::forward(const uint32_t* toks, size_t n, uint32_t start_pos) {
   if ((uint64_t)start_pos + n > max_seq_) throw std::runtime_error("sequence exceeds max_seq_len");
   if (start_pos == 0) kv_reset();  // a new sequence
   kv_ensure((uint64_t)start_pos + n);
+  if (!graph_) {
+    // The single-token step graph (later steps and the benchmarks need it,
+    // even when the whole prompt goes through the batched step).  The
+    // warm-up launch inside ensure_graph runs one step on whatever state is
+    // current; run it at start_pos, whose KV rows are overwritten below.
+    h_st_->token = (int32_t)toks[0];
+    h_st_->pos = (int32_t)start_pos;
+    h_st_->feed_argmax = 0;
+    h_st_->stop = 0;
+    h_st_->best = 0;
+    h_st_->finite = 1;
+    h_st_->done_ctas = 0;
+    h_st_->n_gen = 0;
+    CK(cudaMemcpyAsync(d_st_, h_st_, sizeof(StepState), cudaMemcpyHostToDevice, stream_));
+    ensure_graph();
+  }
   {
     // Batched prefill: whole chunks of 8 tokens through the batched step
     // (each weight read once per chunk on the tensor cores); the rest, and
@@ -1753,20 +1769,6 @@ void Engine::forward(const uint32_t* toks, size_t n, uint32_t start_pos) {
     toks += done;
     n -= done;
     start_pos += (uint32_t)done;
-  }
-  if (!graph_) {
-    // The warm-up launch inside ensure_graph runs one step on whatever state
-    // is current; run it on a scratch position that is overwritten below.
-    h_st_->token = (int32_t)toks[0];
-    h_st_->pos = (int32_t)start_pos;
-    h_st_->feed_argmax = 0;
-    h_st_->stop = 0;
-    h_st_->best = 0;
-    h_st_->finite = 1;
-    h_st_->done_ctas = 0;
-    h_st_->n_gen = 0;
-    CK(cudaMemcpyAsync(d_st_, h_st_, sizeof(StepState), cudaMemcpyHostToDevice, stream_));
-    ensure_graph();
   }
   auto t0 = now_ns();
   h_st_->token = (int32_t)toks[0];

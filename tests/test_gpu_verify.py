@@ -142,3 +142,27 @@ def test_batched_verify_9b(ctx, monkeypatch, archive_9b):
         o.close()
         o16.close()
         e.close()
+
+
+def test_all_batched_prompt_then_single_token_steps(monkeypatch):
+    """A prompt whose every token goes through the batched step (a multiple
+    of 8) leaves the engine ready for single-token steps: greedy steps on the
+    device and host-driven steps run, and their results equal those after
+    the same prompt decoded token by token (within f32 summation order)."""
+    a = archive(chpe.SYNTH_3B_W4)
+    prompt = np.random.default_rng(4).integers(0, 151936, 16).astype(np.uint32)
+    res = []
+    for batched in ("1", "0"):
+        monkeypatch.setenv("CHPE_PREFILL_BATCHED", batched)
+        e = chpe.Engine.from_bytes(a, chpe.ARCH_3B, 64)
+        e.forward_tokens(prompt)
+        first = e.logits().copy()
+        e.bench_greedy(3)
+        r = e.last_result()
+        _, lg = e.bench_host(np.array([5, 77], np.uint32))
+        res.append((first, r.argmax_token, lg))
+        e.close()
+    (f1, t1, l1), (f0, t0, l0) = res
+    assert_logits_match(f1, f0, "batched vs sequential prompt")
+    assert t1 == t0
+    assert_logits_match(l1, l0, "host steps after the prompt")
