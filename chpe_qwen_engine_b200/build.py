@@ -32,7 +32,7 @@ NVCC_FLAGS = [
 ENGINE_SRCS = ["engine.cu", "engine_verify.cu", "attention_noalloc.cu", "deltanet.cu", "chpe_convert.cu", "tc_probe.cu",
                "chpe_c_api.cpp", "chpe_maps.c"]
 ENGINE_DEPS = ENGINE_SRCS + ["engine.h", "engine_types.h", "gemv.cuh", "attention.cuh",
-                             "aux_kernels.cuh", "gemv_tma.cuh", "gemv_flat_tma.cuh", "device_common.cuh", "chpe_maps.h",
+                             "aux_kernels.cuh", "gemv_tma.cuh", "gemv_flat_tma.cuh", "gemv_rowblk.cuh", "device_common.cuh", "chpe_maps.h",
                              "tc_common.cuh", "bgemm_tc.cuh",
                              "qwen3b_cell_map.inc", "../../include/chpe.h"]
 SYNTH_SRCS = ["chpe_synth.c", "chpe_maps.c"]

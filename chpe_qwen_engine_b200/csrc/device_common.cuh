@@ -132,6 +132,12 @@ CHPE_DEV void tp_signal(const chpe::TpLink& t, int kind) {
   asm volatile("fence.acq_rel.sys;" ::: "memory");
   for (int r = 0; r < t.world; r++) red_add_relaxed_sys(&tp_at(t.sh, t, r)->sig[kind], 1ull);
 }
+// n arrivals at once (a CTA that writes the outputs of n CTAs)
+CHPE_DEV void tp_signal_n(const chpe::TpLink& t, int kind, uint32_t n) {
+  if (t.world <= 1 || kind < 0) return;
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+  for (int r = 0; r < t.world; r++) red_add_relaxed_sys(&tp_at(t.sh, t, r)->sig[kind], (unsigned long long)n);
+}
 // Store v at y[i] on this rank, or on every rank when the output is exchanged.
 CHPE_DEV void tp_put(const chpe::TpLink& t, float* y, uint32_t i, float v) {
   if (t.bcast && t.world > 1) {

@@ -18,6 +18,7 @@
 #include "gemv.cuh"
 #include "gemv_tma.cuh"
 #include "gemv_flat_tma.cuh"
+#include "gemv_rowblk.cuh"
 
 namespace chpe {
 
@@ -366,6 +367,11 @@ Engine::Engine(const uint8_t* bytes, uint64_t len, int arch, uint32_t max_seq, i
   nsplit_ = attn_splits(num_sms_, (int)A.KV, (int)max_seq_);
   d_part_ = (float*)dalloc((size_t)A.KV * kAttnMaxSplits * G * (A.HD + 4) * 4);
   d_counters_ = (uint32_t*)dalloc(A.KV * 4);
+  // row sums of the column parts of the row-block GEMV, and its arrival
+  // counters and abort flags (two per row range)
+  rb_part_cap_ = (uint64_t)kRbMaxParts * maxproj;
+  d_rb_part_ = (float*)dalloc(rb_part_cap_ * 4);
+  d_rb_cnt_ = (uint32_t*)dalloc(2u * 1024u * 4u);
   // Paged KV cache: per layer a pool of n_pages pages of kKvPage positions of
   // this rank's kv heads; the page table starts all-zero (page 0) and the
   // free list hands out pages 0, 1, 2, ... unless an order is set.
@@ -850,6 +856,48 @@ void Engine::add_linear_ops(std::vector<Op>& ops, const GemvSrc* src_in, float* 
     for (int i = 0; i < nseg; i++)
       if (src[i].has_aux) t.xn_out = d_xn_;
     if (tp_on) t.tp = *tp;
+    // Row blocks on the tensor cores (gemv_rowblk.cuh): 4-bit group-scaled
+    // flat cells whose rows do not start at cell boundaries (the down
+    // projections), one segment, no fused norm, no down_aux fix-ups, rows in
+    // whole 8-row units and present in the tiles.  Taken for rows of more
+    // than one column part (the 72B's 231 groups: measured on B200 50.0 us
+    // against 51.7 us for the column-owner FFMA decode); for the 9B's 96
+    // groups the column owners are faster (16.5 against 19.3 us).
+    // CHPE_FLAT_ROWBLK=0 keeps every call on the FFMA decode, =1 takes the
+    // tensor cores wherever they apply.
+    {
+      const char* e = getenv("CHPE_FLAT_ROWBLK");
+      const uint32_t G = ncols / 128u, ncp = (G + kRbPartGroups - 1) / kRbPartGroups;
+      const bool want = e ? e[0] == '1' : ncp > 1;
+      const bool rb = want && !rc && op.kind == SRC_FLAT && op.fmt == FMT_W4G && nseg == 1 &&
+                      !gamma && (epi == EPI_ACCUM || epi == EPI_STORE) && ncols % 128u == 0 &&
+                      src[0].r_total % kRbUnit == 0 && !src[0].has_aux && ncp <= kRbMaxParts &&
+                      (uint64_t)ncp * src[0].r_total <= rb_part_cap_ &&
+                      (uint64_t)(src[0].row0 + src[0].r_total) * ncols <= src[0].flat_limit;
+      if (rb) {
+        const uint32_t gpn = (G + ncp - 1) / ncp, Ut = src[0].r_total / kRbUnit;
+        const uint32_t nrr = Ut < (uint32_t)num_sms_ / ncp ? Ut : (uint32_t)num_sms_ / ncp;
+        const uint32_t rpc = kRbUnit * ((Ut + nrr - 1) / nrr);
+        const RbLayout l0 = rowblk_layout(gpn, rpc, 0);
+        uint32_t n = kFlatSmemLimit > l0.total ? (kFlatSmemLimit - l0.total) / l0.stage : 0u;
+        if (n > kRbMaxStages) n = kRbMaxStages;
+        // two 8-row blocks in the ring, one of them outside the B staging
+        if (nrr >= 1 && n >= 2 * kRbUnit && n >= l0.nb + kRbUnit) {
+          t.mode = FLAT_ROWBLK;
+          t.rc = ncp;
+          t.nw = gpn;
+          t.nst = n;
+          t.rpc = rpc;
+          t.part_buf = d_rb_part_;
+          t.part_cnt = d_rb_cnt_;
+          op.threads = (int)kRbThreads;
+          op.smem = rowblk_layout(gpn, rpc, n).total;
+          op.grid = dim3(nrr * ncp);
+          ops.push_back(op);
+          return;
+        }
+      }
+    }
     const uint32_t nparts = epi == EPI_SWIGLU ? 2u : 1u;
     const uint32_t cw = (uint32_t)fmt_cw(op.fmt);
     const uint32_t fixed = mma ? flat_layout_mma(ncols, t.rpc, nparts, 0).total
@@ -1471,7 +1519,25 @@ static void launch_flat_t(const Op& op, cudaStream_t s) {
   launch_pdl(k, op.grid, dim3(NWT * 32 + 32), op.smem, s, op.fl);
 }
 
+template <int NGW>
+static void launch_rowblk_t(const Op& op, cudaStream_t s) {
+  static bool configured = false;
+  if (!configured) {
+    CK(cudaFuncSetAttribute(gemv_rowblk_kernel<NGW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFlatSmemLimit));
+    configured = true;
+  }
+  launch_pdl(gemv_rowblk_kernel<NGW>, op.grid, dim3(kRbThreads), op.smem, s, op.fl);
+}
+
 static void launch_flat(const Op& op, cudaStream_t s) {
+  if (op.fl.mode == FLAT_ROWBLK) {
+    switch ((op.fl.nw + kRbWarps - 1) / kRbWarps) {  // groups per warp, rounded up to even
+      case 1: case 2: return launch_rowblk_t<2>(op, s);
+      case 3: case 4: return launch_rowblk_t<4>(op, s);
+      case 5: case 6: return launch_rowblk_t<6>(op, s);
+      default: return launch_rowblk_t<8>(op, s);
+    }
+  }
   if (op.kind == SRC_FLAT && op.fl.mode == FLAT_MMA && op.fmt == FMT_W4G)
     return launch_flat_t<FMT_W4G, SRC_FLAT, FLAT_MMA>(op, s);
   if (op.kind == SRC_FLAT && op.fl.mode == FLAT_ALIGNED) {
@@ -1563,6 +1629,7 @@ std::string Engine::role_kernel_name(int role) const {
     switch (op.type) {
       case OP_FLAT_TMA:
         if (op.fl.mode == FLAT_MMA) return "gemv_flat_tma_kernel[mma]" + fk;
+        if (op.fl.mode == FLAT_ROWBLK) return "gemv_rowblk_kernel[mma]" + fk;
         return std::string(op.fl.mode == FLAT_ALIGNED
                                ? (op.fl.nw == 8 ? "gemv_flat_tma_kernel[aligned, 2 CTAs/SM]" : "gemv_flat_tma_kernel[aligned]")
                            : op.fl.mode == FLAT_COLOWN ? "gemv_flat_tma_kernel[column owners]"

@@ -191,6 +191,9 @@ class Engine {
   float *d_hidden_, *d_q_, *d_k_, *d_v_, *d_attn_, *d_mlp_, *d_logits_, *d_xn_, *d_tmp_, *d_tmp2_;
   float *d_part_, *d_invfreq_;
   uint32_t* d_counters_;
+  float* d_rb_part_ = nullptr;    // row-block GEMV: [part][rows] row sums
+  uint32_t* d_rb_cnt_ = nullptr;  // row-block GEMV: arrival counters and abort flags
+  uint64_t rb_part_cap_ = 0;      // floats in d_rb_part_
   __half *d_kc_, *d_vc_;
   StepState* d_st_;
   StepResult* d_res_;

@@ -175,6 +175,60 @@ CHPE_DEV void mma_u8s8_16832(int d[4], uint32_t a0, uint32_t a1, uint32_t a2, ui
       : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
+// B operand of the m16n8k32 integer decode: x quad q (columns 4q..4q+3; the
+// 32 lanes of a warp hold the 32 quads of one 128-column group) as int8
+// pieces.  A code byte lo + 16 hi holds the codes of columns 2p and 2p + 1,
+// and lo x0 + hi x1 = lo y + (16 hi) z with y = x0, z = x1 / 16 (exact); y
+// and z of the group are scaled by a power of two S that puts the largest
+// |y|, |z| in [32, 64) and split into four 7-bit pieces (value = i0 + i1/128
+// + i2/128^2 + i3/128^3, B columns n = 0..3).  Staging layout
+// [group][k-step][kind y|z][t][piece] x 8 bytes: columns 4q, 4q+1 are code
+// byte 2q' of the group (q' = q % 32), 4q+2, 4q+3 byte 2q'+1: word q'/2,
+// chunk t = q'/8, k-step and half of the word within the chunk, bytes
+// 2(q' % 2) and 2(q' % 2) + 1 of the register.  xsc[2 group] = 1 / S (NaN
+// when x holds a non-finite value, whose rows are then NaN as the f32 dot
+// product would be), xsc[2 group + 1] = the group's x sum.
+constexpr uint32_t kMmaPieces = 4;
+CHPE_DEV void mma_b_put_quad(uint8_t* bstage, float* xsc, uint32_t q, const float4& o, uint32_t L) {
+  const uint32_t G = q >> 5, qq = q & 31u, t = qq >> 3, wic = (qq >> 1) & 3u;
+  const uint32_t s_ = wic >> 1, up = wic & 1u, bi = 2u * (qq & 1u);
+  const float y0 = o.x, z0 = o.y * 0.0625f, y1 = o.z, z1 = o.w * 0.0625f;
+  float m = fmaxf(fmaxf(fabsf(y0), fabsf(z0)), fmaxf(fabsf(y1), fabsf(z1)));
+  if (!(m <= 3.402823466e38f)) m = __int_as_float(0x7f800000);  // NaN -> inf
+#pragma unroll
+  for (int sh = 16; sh > 0; sh >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, sh));
+  float S = 1.0f, invS = 1.0f;
+  if (!(m <= 3.402823466e38f)) {
+    S = 0.0f;  // pieces 0, rows NaN
+    invS = __int_as_float(0x7fc00000);
+  } else if (m > 0.0f) {
+    int ex;
+    frexpf(m, &ex);  // m in [2^(ex-1), 2^ex)
+    const int k = 6 - ex < 126 ? 6 - ex : 126;
+    S = ldexpf(1.0f, k);
+    invS = ldexpf(1.0f, -k);
+  }
+  uint8_t* bb = bstage + (((G * 2u + s_) * 2u) * 4u + t) * kMmaPieces * 8u + up * 4u + bi;
+  float ry0 = y0 * S, ry1 = y1 * S, rz0 = z0 * S, rz1 = z1 * S;
+#pragma unroll
+  for (uint32_t n = 0; n < kMmaPieces; n++) {
+    const float iy0 = rintf(ry0), iy1 = rintf(ry1), iz0 = rintf(rz0), iz1 = rintf(rz1);
+    const uint16_t py = (uint16_t)((uint32_t)((int)iy0 & 0xff) | ((uint32_t)((int)iy1 & 0xff) << 8));
+    const uint16_t pz = (uint16_t)((uint32_t)((int)iz0 & 0xff) | ((uint32_t)((int)iz1 & 0xff) << 8));
+    *reinterpret_cast<uint16_t*>(bb + n * 8u) = py;                         // kind 0: y
+    *reinterpret_cast<uint16_t*>(bb + 4u * kMmaPieces * 8u + n * 8u) = pz;   // kind 1: z
+    ry0 = (ry0 - iy0) * 128.0f;
+    ry1 = (ry1 - iy1) * 128.0f;
+    rz0 = (rz0 - iz0) * 128.0f;
+    rz1 = (rz1 - iz1) * 128.0f;
+  }
+  const float sx = warp_sum((o.x + o.y) + (o.z + o.w));
+  if (L == 0) {
+    xsc[2 * G] = invS;
+    xsc[2 * G + 1] = sx;
+  }
+}
+
 // An int32 of magnitude below 2^22 as a float, exactly: its bits added to
 // those of 1.5 * 2^23 give 1.5 * 2^23 + v, from which 1.5 * 2^23 is removed.
 CHPE_DEV float s32_exact(int v) { return __int_as_float(v + 0x4B400000) - 12582912.0f; }

@@ -63,6 +63,8 @@ struct FlatTmaLaunch {
   int32_t max_gen;
   float* xn_out;           // normalised x for the down_aux fix-up op (or null)
   TpLink tp;               // tensor-parallel wait / exchange / signal (world 1: none)
+  float* part_buf;         // ROWBLK with column parts: [part][rows] row sums
+  uint32_t* part_cnt;      // ROWBLK with column parts: arrival counters and abort flags per row range
 };
 
 // codes + payload head (832) rounded to 128, + 64 so that consecutive stages
@@ -103,7 +105,6 @@ struct FlatLayout {
 // value, one power-of-two exponent per 128-column group).
 constexpr uint32_t kMmaRows = 16;
 constexpr uint32_t kMmaSlots = 8;   // per-block partial slots (host: >= ceil(nst / cells per block) + 1)
-constexpr uint32_t kMmaPieces = 4;  // int8 pieces of each B value: 7 + 3 x 7 bits under the group exponent
 // B fragments ([group][kstep][kind][t][piece] x 8 bytes) are staged in the
 // ring's last stages, which the producer fills only after every consumer warp
 // has copied its groups' fragments into registers.
@@ -165,7 +166,8 @@ CHPE_DEV void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(NCT) : "mem
 // rc rows and consumer lane t always decodes the same column chunk t % (cols /
 // CW) of rows t / (cols / CW) + k * (256 / (cols / CW)): its x stays in
 // registers for the whole launch and shared memory carries only codes.
-enum FlatMode : int { FLAT_STREAM = 0, FLAT_ALIGNED = 1, FLAT_COLOWN = 2, FLAT_MMA = 3 };
+// ROWBLK: the tensor-core kernel of gemv_rowblk.cuh (same launch record).
+enum FlatMode : int { FLAT_STREAM = 0, FLAT_ALIGNED = 1, FLAT_COLOWN = 2, FLAT_MMA = 3, FLAT_ROWBLK = 4 };
 
 // MMA (aligned 4-bit group-scaled cells of 4096 or 8192 columns, every
 // segment a whole number of 16-row blocks): the products go through
@@ -362,46 +364,7 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
   // 128-column group)
   auto put4 = [&](uint32_t q, const float4& o) {
     if constexpr (MMA) {
-      // columns 4q, 4q+1 are code byte 2q' of the group (q' = q % 32), 4q+2,
-      // 4q+3 byte 2q'+1: word q'/2, chunk t = q'/8, k-step s and half of the
-      // word within the chunk, bytes 2(q' % 2) and 2(q' % 2) + 1 of the register
-      const uint32_t G = q >> 5, qq = q & 31u, t = qq >> 3, wic = (qq >> 1) & 3u;
-      const uint32_t s_ = wic >> 1, up = wic & 1u, bi = 2u * (qq & 1u);
-      const float y0 = o.x, z0 = o.y * 0.0625f, y1 = o.z, z1 = o.w * 0.0625f;
-      float m = fmaxf(fmaxf(fabsf(y0), fabsf(z0)), fmaxf(fabsf(y1), fabsf(z1)));
-      if (!(m <= 3.402823466e38f)) m = __int_as_float(0x7f800000);  // NaN -> inf
-#pragma unroll
-      for (int sh = 16; sh > 0; sh >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, sh));
-      float S = 1.0f, invS = 1.0f;
-      if (!(m <= 3.402823466e38f)) {
-        S = 0.0f;  // pieces 0, rows NaN
-        invS = __int_as_float(0x7fc00000);
-      } else if (m > 0.0f) {
-        int ex;
-        frexpf(m, &ex);  // m in [2^(ex-1), 2^ex)
-        const int k = 6 - ex < 126 ? 6 - ex : 126;
-        S = ldexpf(1.0f, k);
-        invS = ldexpf(1.0f, -k);
-      }
-      uint8_t* bb = fsm + lay.x + (((G * 2u + s_) * 2u) * 4u + t) * kMmaPieces * 8u + up * 4u + bi;
-      float ry0 = y0 * S, ry1 = y1 * S, rz0 = z0 * S, rz1 = z1 * S;
-#pragma unroll
-      for (uint32_t n = 0; n < kMmaPieces; n++) {
-        const float iy0 = rintf(ry0), iy1 = rintf(ry1), iz0 = rintf(rz0), iz1 = rintf(rz1);
-        const uint16_t py = (uint16_t)((uint32_t)((int)iy0 & 0xff) | ((uint32_t)((int)iy1 & 0xff) << 8));
-        const uint16_t pz = (uint16_t)((uint32_t)((int)iz0 & 0xff) | ((uint32_t)((int)iz1 & 0xff) << 8));
-        *reinterpret_cast<uint16_t*>(bb + n * 8u) = py;                         // kind 0: y
-        *reinterpret_cast<uint16_t*>(bb + 4u * kMmaPieces * 8u + n * 8u) = pz;   // kind 1: z
-        ry0 = (ry0 - iy0) * 128.0f;
-        ry1 = (ry1 - iy1) * 128.0f;
-        rz0 = (rz0 - iz0) * 128.0f;
-        rz1 = (rz1 - iz1) * 128.0f;
-      }
-      const float sx = warp_sum((o.x + o.y) + (o.z + o.w));
-      if (L == 0) {
-        xsc[2 * G] = invS;
-        xsc[2 * G + 1] = sx;
-      }
+      mma_b_put_quad(fsm + lay.x, xsc, q, o, L);
     } else {
       *reinterpret_cast<float4*>(&xsh[xpos<CW>(4 * q)]) = o;
     }

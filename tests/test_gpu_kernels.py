@@ -172,6 +172,36 @@ def test_gemv_flat_mma(cfg, flags, mma, monkeypatch):
             assert_close_vec(got, ref, 1e-4, f"{r}x{c} acc={acc} mma={mma}")
 
 
+# Row-block shapes for the tensor-core decode of rows that do not start at
+# cell boundaries (rows in whole 8-row units, every row in the 688 cells):
+# CTAs of 16-row blocks with an 8-row tail (5320 x 4224: 33 groups, a
+# two-group last chunk), the 9B / 72B down widths, a single 8-row block, and
+# rows that give one or two 8-row units per CTA.
+ROWBLK_SHAPES = [(5320, 4224), (1824, 12288), (752, 29568), (8, 29568), (24, 11008), (2000, 11008),
+                 (16, 4224), (2960, 6272)]
+
+
+@pytest.mark.parametrize("rowblk", [True, False])
+def test_gemv_rowblk(rowblk, monkeypatch):
+    """Row-block tensor-core decode (gemv_rowblk_kernel: per-row bulk copies
+    of 16-group chunks, the int8-piece B of every group in shared memory)
+    against the oracle; with CHPE_FLAT_ROWBLK=0 the FFMA decode of the same
+    calls (CHPE_FLAT_ROWBLK=1 takes the tensor cores wherever they apply).  x
+    spans a wide range: a few entries 1e4 times the rest."""
+    monkeypatch.setenv("CHPE_FLAT_ROWBLK", "1" if rowblk else "0")
+    a, e, o = engines(chpe.SYNTH_3B_W4, 0)
+    li = o.layer_info(4)
+    rng = np.random.default_rng(31)
+    for r, c in ROWBLK_SHAPES:
+        for acc in (False, True):
+            x = rng.standard_normal(c).astype(np.float32)
+            x[rng.integers(0, c, 4)] *= 1e4
+            y0 = rng.standard_normal(r).astype(np.float32)
+            ref = o.gemv_linear(li["down_proj"], li["down_tiles"], x, r, c, accumulate=acc, y=y0.copy())
+            got = e.probe_gemv_linear(li["down_proj"], li["down_tiles"], x, r, c, accumulate=acc, y=y0.copy())
+            assert_close_vec(got, ref, 1e-4, f"{r}x{c} acc={acc} rowblk={rowblk}")
+
+
 @pytest.mark.parametrize("arch", [chpe.ARCH_3B, chpe.ARCH_9B, chpe.ARCH_72B])
 def test_attention_against_oracle(arch):
     """RoPE + KV append + GQA softmax (chpe_engine.zig:1688-1734) over a

@@ -71,8 +71,12 @@ def _rank_body(rank, world, port, cfg, q):
 
 
 @pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
-def test_tp2_decode_matches_oracle_and_single_gpu():
+@pytest.mark.parametrize("rowblk", ["0", "1"])
+def test_tp2_decode_matches_oracle_and_single_gpu(rowblk, monkeypatch):
+    """rowblk "1": the down projections on the row-block tensor-core kernel
+    (its exchange: outputs broadcast to both ranks, one arrival per CTA)."""
     import torch.multiprocessing as mp
+    monkeypatch.setenv("CHPE_FLAT_ROWBLK", rowblk)  # inherited by the spawned ranks
     cfg, world = chpe.SYNTH_9B_W4, 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
