@@ -491,14 +491,15 @@ def main():
                     help="prompt tokens decoded before timing (default: the model's config)")
     ap.add_argument("--kernel-only", default=None,
                     choices=["qkv", "attention", "o", "gateup", "down", "lmhead", "flat-aligned", "flat-stream",
-                             "bgemm4", "bgemm8"],
+                             "flat-rowblk", "bgemm4", "bgemm8"],
                     help="profiling case: build the engine (max_seq_len 64) and only launch this "
                          "op of every layer, --steps rounds after one warm-up round; flat-aligned / "
                          "flat-stream: one flat GEMV over 2064 contiguous 4-bit cells of the 3B "
                          "archive (35 MB) read as 8192 columns (aligned cells: the tensor-core mode, "
                          "or with CHPE_FLAT_MMA=0 the FFMA aligned mode) or 29568 columns (the 72B "
-                         "down width: column owners, or with CHPE_FLAT_COLOWN=0 the stream mode), "
-                         "--steps launches")
+                         "down width: column owners, or with CHPE_FLAT_COLOWN=0 the stream mode); "
+                         "flat-rowblk: the same cells as 2280 rows x 29568 columns (the row-block "
+                         "tensor-core kernel); --steps launches")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -527,17 +528,20 @@ def main():
         print(json.dumps({"kernel": "bgemm_w4_kernel", "nt": nt, "rows": rows, "cols": cols,
                           "y00": float(y[0][0])}))
         return
-    if args.kernel_only in ("flat-aligned", "flat-stream"):
+    if args.kernel_only in ("flat-aligned", "flat-stream", "flat-rowblk"):
         import chpe_qwen_engine_b200 as chpe
         eng = chpe.Engine.from_bytes(chpe.synth_archive(chpe.SYNTH_3B_W4, 0, seed=0), chpe.ARCH_3B, 64)
         tile0, ntiles = 9497, 2064  # layer 0 down, gate, up: contiguous 4-bit cells
         cols = 8192 if args.kernel_only == "flat-aligned" else 29568
         rows = ntiles * 32768 // cols
+        if args.kernel_only == "flat-rowblk":
+            rows -= rows % 8  # whole 8-row units: the row-block tensor-core kernel
         x = np.random.default_rng(3).standard_normal(cols).astype(np.float32)
         for _ in range(max(1, args.steps)):
             y = eng.probe_gemv_linear(tile0, ntiles, x, rows, cols)
         print(json.dumps({"kernel": args.kernel_only, "rows": rows, "cols": cols,
-                          "kernel_name": "gemv_flat_tma_kernel", "y0": float(y[0])}))
+                          "kernel_name": "gemv_rowblk_kernel" if args.kernel_only == "flat-rowblk"
+                          else "gemv_flat_tma_kernel", "y0": float(y[0])}))
         return
     if args.kernel_only:
         import chpe_qwen_engine_b200 as chpe

@@ -859,16 +859,17 @@ void Engine::add_linear_ops(std::vector<Op>& ops, const GemvSrc* src_in, float* 
     // Row blocks on the tensor cores (gemv_rowblk.cuh): 4-bit group-scaled
     // flat cells whose rows do not start at cell boundaries (the down
     // projections), one segment, no fused norm, no down_aux fix-ups, rows in
-    // whole 8-row units and present in the tiles.  Taken for rows of more
-    // than one column part (the 72B's 231 groups: measured on B200 50.0 us
-    // against 51.7 us for the column-owner FFMA decode); for the 9B's 96
-    // groups the column owners are faster (16.5 against 19.3 us).
-    // CHPE_FLAT_ROWBLK=0 keeps every call on the FFMA decode, =1 takes the
-    // tensor cores wherever they apply.
+    // whole 8-row units and present in the tiles.  Taken on one GPU for rows
+    // of more than one column part (the 72B's 231 groups: measured on B200
+    // 50.0 us against 51.7 us for the column-owner FFMA decode); for the
+    // 9B's 96 groups the column owners are faster (16.5 against 19.3 us),
+    // and so they are for the 72B's tensor-parallel slices (46.1 against
+    // 49.5 us per layer at 2 GPUs).  CHPE_FLAT_ROWBLK=0 keeps every call on
+    // the FFMA decode, =1 takes the tensor cores wherever they apply.
     {
       const char* e = getenv("CHPE_FLAT_ROWBLK");
       const uint32_t G = ncols / 128u, ncp = (G + kRbPartGroups - 1) / kRbPartGroups;
-      const bool want = e ? e[0] == '1' : ncp > 1;
+      const bool want = e ? e[0] == '1' : (ncp > 1 && !tp_on);
       const bool rb = want && !rc && op.kind == SRC_FLAT && op.fmt == FMT_W4G && nseg == 1 &&
                       !gamma && (epi == EPI_ACCUM || epi == EPI_STORE) && ncols % 128u == 0 &&
                       src[0].r_total % kRbUnit == 0 && !src[0].has_aux && ncp <= kRbMaxParts &&
