@@ -97,31 +97,85 @@ CHPE_DEV bool attention_body(const AttnLaunch& P) {
   __shared__ float ps[8][ATT_TT];
   __shared__ int last_flag;
 
-  pdl_wait();
-  if (P.st->stop) return blockIdx.x == 0;
+  // Single-token steps start before the dependency wait: the step's position
+  // is set before the step begins, and the rows of the positions before it
+  // are in the cache from earlier steps (the page table from the host), so
+  // the first tile's K/V loads are in flight while the QKV projection
+  // finishes.  Batched steps wait first: their candidates' rows come from the
+  // preceding rope_append_kernel.
+  if (P.batched) pdl_wait();
   const int tok = P.batched ? (int)blockIdx.z : 0;
   const int pos = P.st->pos + tok;
-  if (pos < 0 || pos >= P.max_seq) return blockIdx.x == 0;  // the host never schedules this
+  if (pos < 0 || pos >= P.max_seq) {  // the host never schedules this
+    if (!P.batched) pdl_wait();
+    return blockIdx.x == 0;
+  }
   const float pf = (float)pos;
   float* const part_base = P.part + (size_t)tok * P.part_tok;
   uint32_t* const counters = P.counters + (size_t)tok * P.KV;
+  const int n = pos + 1;
+  // at least one full tile per split: short contexts use fewer splits (the
+  // rest find an empty range and only report -inf to the merge)
+  int chunk = (n + P.nsplit - 1) / P.nsplit;
+  if (chunk < ATT_TT) chunk = ATT_TT;
+  const int t0 = split * chunk, t1 = min(n, t0 + chunk);
+
+  constexpr int VPR = HD / 8;                 // 16-byte vectors per row
+  constexpr int MAXV = ATT_TT * VPR / 128;    // vectors per thread (launched with >= 128 threads)
+  // The next tile's K/V rows are loaded into registers while the current one
+  // is scored from shared memory.  This step's own row (single-token steps)
+  // comes from the values computed below, filled in by `own`.
+  uint4 kr[MAXV], vr[MAXV];
+  auto fetch = [&](int tb) {
+    const int nt = min(ATT_TT, t1 - tb);
+#pragma unroll
+    for (int u = 0; u < MAXV; u++) {
+      const int i = threadIdx.x + u * blockDim.x;
+      if (i >= nt * VPR) continue;
+      const int r = i / VPR, c8 = (i % VPR) * 8, t = tb + r;
+      if (t == pos && !P.batched) continue;
+      const size_t off = (kv_cache_row(P, t) * P.KV + kvh) * HD + c8;
+      kr[u] = *reinterpret_cast<const uint4*>(P.kc + off);
+      vr[u] = *reinterpret_cast<const uint4*>(P.vc + off);
+    }
+  };
+  if (t0 < t1) fetch(t0);
+  // RoPE angles of this lane's pairs i = L + 32 j (applyRope: cos/sin of pos * inv_freq[i])
+  constexpr int NJ = (HD / 2 + 31) / 32;
+  float rc[NJ], rs[NJ];
+#pragma unroll
+  for (int j = 0; j < NJ; j++) {
+    const int i = L + 32 * j;
+    const float th = i < HD / 2 ? pf * P.inv_freq[i] : 0.f;
+    rc[j] = cosf(th);
+    rs[j] = sinf(th);
+  }
+  if (!P.batched) pdl_wait();
+  if (P.st->stop) return blockIdx.x == 0;
 
   // RoPE on this warp's query head, on the new key; copy of the new value.
   if (warp < G) {
     const float* qh = P.q + (size_t)tok * P.q_tok + (size_t)(kvh * G + warp) * HD;
-    for (int i = L; i < HD / 2; i += 32) {
-      float th = pf * P.inv_freq[i];
-      float c = cosf(th), s = sinf(th);
-      float x0 = qh[i], x1 = qh[i + HD / 2];
-      qs[warp][i] = x0 * c - x1 * s;
-      qs[warp][i + HD / 2] = x0 * s + x1 * c;
+#pragma unroll
+    for (int j = 0; j < NJ; j++) {
+      const int i = L + 32 * j;
+      if (i >= HD / 2) break;
+      const float x0 = qh[i], x1 = qh[i + HD / 2];
+      qs[warp][i] = x0 * rc[j] - x1 * rs[j];
+      qs[warp][i + HD / 2] = x0 * rs[j] + x1 * rc[j];
     }
   }
-  for (int i = threadIdx.x; i < HD / 2 && !P.batched; i += blockDim.x) {
+  if (!P.batched && (int)threadIdx.x < HD / 2) {  // pair i = threadIdx.x = L + 32 warp
     const float* kh = P.k + (size_t)kvh * HD;
-    float th = pf * P.inv_freq[i];
-    float c = cosf(th), s = sinf(th);
-    float x0 = kh[i], x1 = kh[i + HD / 2];
+    float c = 0.f, s = 0.f;
+#pragma unroll
+    for (int j = 0; j < NJ; j++)
+      if (j == warp) {
+        c = rc[j];
+        s = rs[j];
+      }
+    const int i = threadIdx.x;
+    const float x0 = kh[i], x1 = kh[i + HD / 2];
     kn[i] = x0 * c - x1 * s;
     kn[i + HD / 2] = x0 * s + x1 * c;
   }
@@ -136,46 +190,30 @@ CHPE_DEV bool attention_body(const AttnLaunch& P) {
   }
   pdl_launch_dependents();
 
-  const int n = pos + 1;
-  // at least one full tile per split: short contexts use fewer splits (the
-  // rest find an empty range and only report -inf to the merge)
-  int chunk = (n + P.nsplit - 1) / P.nsplit;
-  if (chunk < ATT_TT) chunk = ATT_TT;
-  const int t0 = split * chunk, t1 = min(n, t0 + chunk);
   const float scale = 1.0f / sqrtf((float)HD);
   float m = -INFINITY, l = 0.f, acc[PER];
 #pragma unroll
   for (int e = 0; e < PER; e++) acc[e] = 0.f;
-
-  constexpr int VPR = HD / 8;                 // 16-byte vectors per row
-  constexpr int MAXV = ATT_TT * VPR / 128;    // vectors per thread (launched with >= 128 threads)
-  // The next tile's K/V rows are loaded into registers while the current one
-  // is scored from shared memory.
-  uint4 kr[MAXV], vr[MAXV];
-  auto fetch = [&](int tb) {
+  // this step's entry, from the values just computed (rounded as the cache holds them)
+  auto own = [&](int tb) {
     const int nt = min(ATT_TT, t1 - tb);
 #pragma unroll
     for (int u = 0; u < MAXV; u++) {
       const int i = threadIdx.x + u * blockDim.x;
       if (i >= nt * VPR) continue;
       const int r = i / VPR, c8 = (i % VPR) * 8, t = tb + r;
-      if (t == pos && !P.batched) {  // this step's entry, from the values just computed
-        __half2 hk[4], hv[4];
+      if (t != pos || P.batched) continue;
+      __half2 hk[4], hv[4];
 #pragma unroll
-        for (int e = 0; e < 4; e++) {
-          hk[e] = __floats2half2_rn(kn[c8 + 2 * e], kn[c8 + 2 * e + 1]);
-          hv[e] = __floats2half2_rn(vn[c8 + 2 * e], vn[c8 + 2 * e + 1]);
-        }
-        kr[u] = *reinterpret_cast<uint4*>(hk);
-        vr[u] = *reinterpret_cast<uint4*>(hv);
-      } else {
-        const size_t off = (kv_cache_row(P, t) * P.KV + kvh) * HD + c8;
-        kr[u] = *reinterpret_cast<const uint4*>(P.kc + off);
-        vr[u] = *reinterpret_cast<const uint4*>(P.vc + off);
+      for (int e = 0; e < 4; e++) {
+        hk[e] = __floats2half2_rn(kn[c8 + 2 * e], kn[c8 + 2 * e + 1]);
+        hv[e] = __floats2half2_rn(vn[c8 + 2 * e], vn[c8 + 2 * e + 1]);
       }
+      kr[u] = *reinterpret_cast<uint4*>(hk);
+      vr[u] = *reinterpret_cast<uint4*>(hv);
     }
   };
-  if (t0 < t1) fetch(t0);
+  if (t0 < t1) own(t0);
   for (int tb = t0; tb < t1; tb += ATT_TT) {
     const int nt = min(ATT_TT, t1 - tb);
     __syncthreads();  // previous tile consumed
@@ -193,7 +231,10 @@ CHPE_DEV bool attention_body(const AttnLaunch& P) {
       }
       *reinterpret_cast<uint4*>(&vs[r][c8]) = vr[u];
     }
-    if (tb + ATT_TT < t1) fetch(tb + ATT_TT);
+    if (tb + ATT_TT < t1) {
+      fetch(tb + ATT_TT);
+      own(tb + ATT_TT);
+    }
     __syncthreads();
     if (warp < G) {
       float sc = -INFINITY;  // lane = tile row
