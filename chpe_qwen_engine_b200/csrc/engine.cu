@@ -856,6 +856,12 @@ void Engine::add_linear_ops(std::vector<Op>& ops, const GemvSrc* src_in, float* 
     for (int i = 0; i < nseg; i++)
       if (src[i].has_aux) t.xn_out = d_xn_;
     if (tp_on) t.tp = *tp;
+    {
+      // CHPE_FLAT_PREFETCH=n: at most n pieces requested before the
+      // dependency wait (default: every free stage)
+      const char* e = getenv("CHPE_FLAT_PREFETCH");
+      t.npre = e ? (uint32_t)atoi(e) : 0u;
+    }
     // Row blocks on the tensor cores (gemv_rowblk.cuh): 4-bit group-scaled
     // flat cells whose rows do not start at cell boundaries (the down
     // projections), one segment, no fused norm, no down_aux fix-ups, rows in

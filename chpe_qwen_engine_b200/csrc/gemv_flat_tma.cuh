@@ -63,6 +63,7 @@ struct FlatTmaLaunch {
   int32_t max_gen;
   float* xn_out;           // normalised x for the down_aux fix-up op (or null)
   TpLink tp;               // tensor-parallel wait / exchange / signal (world 1: none)
+  uint32_t npre;           // pieces (rows) requested before the dependency wait at most (0: the free stages)
   float* part_buf;         // ROWBLK with column parts: [part][rows] row sums
   uint32_t* part_cnt;      // ROWBLK with column parts: arrival counters and abort flags per row range
 };
@@ -188,8 +189,13 @@ enum FlatMode : int { FLAT_STREAM = 0, FLAT_ALIGNED = 1, FLAT_COLOWN = 2, FLAT_M
 // A block is 16 consecutive rows (16 / rows-per-cell cells); warp w takes the
 // 128-column groups w, w + 16, ... (at most four: 8192 columns), their B
 // fragments in registers; lane (g, t) (g = lane / 4, t = lane % 4)
-// loads 16-byte chunk t of the group for rows g and g + 8, whose four words
-// are the A registers of the group's two k-steps.  The 16 warps' partial row
+// loads 16-byte chunk t of the group for MMA rows g and g + 8, whose four
+// words are the A registers of the group's two k-steps.  MMA row m is row
+// (m % 8) / 2 (+ 4 for m >= 8 with 8-row cells) of cell m % 2 (+ 2 for m >= 8
+// with 4-row cells) of the block: the rows of one quarter-warp (g = 2k, 2k+1)
+// then lie in consecutive ring stages, whose offsets differ by 64 modulo 128
+// bytes, so their 16-byte loads hit distinct banks (rows of one cell are a
+// multiple of 128 bytes apart).  The 16 warps' partial row
 // sums of a block meet in a shared slot; the warp that arrives last adds them
 // in warp order, so results do not depend on timing.
 
@@ -322,7 +328,8 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
     };
     if (L == 0) {
       // (MMA: the last stages hold the B fragments until the consumers' prologue ends)
-      const uint32_t nfree = MMA ? nst - flat_mma_b_stages(C) : nst;
+      uint32_t nfree = MMA ? nst - flat_mma_b_stages(C) : nst;
+      if (P.npre && P.npre < nfree) nfree = P.npre;
       const uint32_t npre = npieces < nfree ? npieces : nfree;
       for (; issued < npre; issued++) issue(issued);
     }
@@ -599,7 +606,9 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
     const uint32_t NG = C >> 7;                // 128-column groups
     const uint32_t g = L >> 2, t = L & 3u;
     const uint32_t rowB = C >> 1;              // code bytes per row
-    const uint32_t c1 = g / RC, r1 = g % RC, c2 = (g + 8u) / RC, r2 = (g + 8u) % RC;
+    // MMA rows g and g + 8 -> (cell of the block, row in the cell)
+    const uint32_t c1 = g & 1u, r1 = g >> 1;
+    const uint32_t c2 = CPB == 4u ? 2u + (g & 1u) : (g & 1u), r2 = CPB == 4u ? (g >> 1) : 4u + (g >> 1);
     const uint32_t off1 = r1 * rowB + t * 16u, off2 = r2 * rowB + t * 16u;
     const uint32_t soff1 = 16384u + 48u + 2u * r1 * NG, soff2 = 16384u + 48u + 2u * r2 * NG;
     // pieces 2t and 2t+1 sit in this lane's two D columns
@@ -679,7 +688,9 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
 #pragma unroll
           for (uint32_t w = 0; w < NW; w++) sum += bp[w * kMmaRows + L];
           const uint32_t k0 = r_k0 + (i0 - r_ps);  // first cell of the block
-          wacc[r_part * P.rpc + (uint32_t)((int32_t)(k0 * RC + L) + r_lrb)] = sum;
+          const uint32_t mc = L < 8u ? (L & 1u) : (CPB == 4u ? 2u + (L & 1u) : (L & 1u));
+          const uint32_t mr = L < 8u ? ((L & 7u) >> 1) : (CPB == 4u ? ((L & 7u) >> 1) : 4u + ((L & 7u) >> 1));
+          wacc[r_part * P.rpc + (uint32_t)((int32_t)((k0 + mc) * RC + mr) + r_lrb)] = sum;
         }
         if (L == 0) bcnt[slot] = 0u;
         __syncwarp();

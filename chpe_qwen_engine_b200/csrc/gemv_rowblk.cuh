@@ -50,7 +50,9 @@ constexpr uint32_t kRbMaxStages = 32;
 constexpr uint32_t kRbSlots = 4;                     // per-block partial slots
 
 struct RbLayout {
-  uint32_t stage, win;  // bytes per stage (== 16 mod 128: the 8 rows of a block sit in distinct banks), scale window
+  // bytes per stage (== 64 mod 128: rows g and g + 1 of a block, which one
+  // quarter-warp of 16-byte A loads reads, sit in distinct banks), scale window
+  uint32_t stage, win;
   uint32_t bst;         // B staging (over the last stages, until the consumers hold B in registers)
   uint32_t xs, bp, bc, wacc, bars, total;
   uint32_t nb;          // stages covered by the B staging
@@ -61,7 +63,7 @@ __host__ __device__ inline RbLayout rowblk_layout(uint32_t gp, uint32_t rpc, uin
   RbLayout l;
   l.win = (2u * gp + 30u + 15u) & ~15u;
   l.stage = gp * 64u + 2u * l.win;
-  l.stage += (16u - (l.stage & 127u) + 128u) & 127u;
+  l.stage += (64u - (l.stage & 127u) + 128u) & 127u;
   l.nb = (gp * 512u + l.stage - 1u) / l.stage;
   l.bst = (nst >= l.nb ? nst - l.nb : 0u) * l.stage;
   l.xs = nst * l.stage;                            // (1/S, x sum) per group of the part
@@ -141,7 +143,9 @@ __global__ void __launch_bounds__(kRbThreads, 1) gemv_rowblk_kernel(const __grid
     };
     {
       // the last nb stages hold the B staging until the consumers' prologue ends
-      const uint32_t nfree = nst - lay.nb, npre = nrows < nfree ? nrows : nfree;
+      uint32_t nfree = nst - lay.nb;
+      if (P.npre && P.npre < nfree) nfree = P.npre;
+      const uint32_t npre = nrows < nfree ? nrows : nfree;
       for (uint32_t i = L; i < npre; i += 32u) issue(i);
       issued = npre;
     }
