@@ -247,6 +247,29 @@ def run_reference(args, rank, world, dist):
     print(json.dumps(line), flush=True)
 
 
+class nvtx_range:
+    """An NVTX range around the timed steps (a profiler can restrict its
+    capture to it: ncu --nvtx --nvtx-include "chpe_timed/")."""
+
+    def __init__(self, name: str):
+        self.name = name
+
+    def __enter__(self):
+        try:
+            import torch
+            torch.cuda.nvtx.range_push(self.name)
+            self.pushed = True
+        except Exception:
+            self.pushed = False
+        return self
+
+    def __exit__(self, *exc):
+        if self.pushed:
+            import torch
+            torch.cuda.nvtx.range_pop()
+        return False
+
+
 def shared_archive_path(chpe, cfg: int, rank: int, dist) -> str:
     """Rank 0 writes the seeded archive once to a local file that every rank
     maps read-only (one copy in the page cache, not one per rank)."""
@@ -283,7 +306,7 @@ def run_ours(args, rank, world, local, dist):
     eng.forward_tokens(prompt)  # positions 0..prompt-1, untimed
     eng.bench_greedy(args.warmup)  # warm-up steps
     barrier(dist)
-    with ClockSampler(dev) as cs:
+    with ClockSampler(dev) as cs, nvtx_range("chpe_timed"):
         ms = eng.bench_greedy(args.steps)
     barrier(dist)
     ms_max = max_over_ranks(dist, ms)
