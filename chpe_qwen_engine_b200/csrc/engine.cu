@@ -792,6 +792,14 @@ void Engine::add_linear_ops(std::vector<Op>& ops, const GemvSrc* src_in, float* 
     t.row_start[nseg] = rows;
     if (epi == EPI_SWIGLU) t.row_start[1] = src[0].r_total;
     const uint32_t Rt = epi == EPI_SWIGLU ? src[0].r_total : rows;
+    // per segment, its leading rows with any weight in the tiles (the rest
+    // read as zero: the reference's flat loops stop at the available tiles)
+    for (int i = 0; i < nseg; i++) {
+      const uint64_t start = (uint64_t)src[i].row0 * ncols, lim = src[i].flat_limit;
+      const uint64_t c = lim <= start ? 0 : (lim - start + ncols - 1) / ncols;
+      t.cov[i] = (uint32_t)(c < src[i].r_total ? c : src[i].r_total);
+    }
+    if (epi == EPI_SWIGLU && t.cov[1] > t.cov[0]) t.cov[0] = t.cov[1];
     // Aligned cells (rows start at cell boundaries): 4/2-bit flat cells whose
     // width divides 32768 into 32..256 column chunks, every segment a whole
     // number of cells.

@@ -64,6 +64,8 @@ struct FlatTmaLaunch {
   float* xn_out;           // normalised x for the down_aux fix-up op (or null)
   TpLink tp;               // tensor-parallel wait / exchange / signal (world 1: none)
   uint32_t npre;           // pieces (rows) requested before the dependency wait at most (0: the free stages)
+  uint32_t cov[3];         // per segment (SwiGLU: cov[0] for the gate/up pair): its leading rows that
+                           // have weights in the tiles; the CTAs split these, the rest are zero sums
   float* part_buf;         // ROWBLK with column parts: [part][rows] row sums
   uint32_t* part_cnt;      // ROWBLK with column parts: arrival counters and abort flags per row range
 };
@@ -246,22 +248,29 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
   __shared__ volatile int s_bad;
 
   const uint32_t Rt = P.row_start[swig ? 1 : P.nseg];
-  // rows split evenly over the CTAs, in whole cells when aligned, whole
-  // 16-row blocks in the MMA mode
-  const uint32_t RU = MMA ? kMmaRows : ALIGNED ? P.rc : 1u, Ut = Rt / RU;
-  const uint32_t R0 = RU * (uint32_t)((uint64_t)Ut * blockIdx.x / gridDim.x);
+  // The CTAs split the rows that have weights in the tiles (each segment's
+  // covered leading rows, concatenated: "work rows" [cst(g), cst(g + 1)) are
+  // rows row_start[g] + ... of segment g), evenly, in whole cells when
+  // aligned, whole 16-row blocks in the MMA mode; rows past the tiles have
+  // zero sums and are written by the epilogue of every CTA in turn.
+  const uint32_t nsg = swig ? 1u : (uint32_t)P.nseg;
+  const uint32_t cs1 = P.cov[0], cs2 = cs1 + (nsg > 1u ? P.cov[1] : 0u), cs3 = cs2 + (nsg > 2u ? P.cov[2] : 0u);
+  auto cst = [&](uint32_t g) { return g == 0u ? 0u : g == 1u ? cs1 : g == 2u ? cs2 : cs3; };  // (registers)
+  const uint32_t Vt = cst(nsg);
+  const uint32_t RU = MMA ? kMmaRows : ALIGNED ? P.rc : 1u, Ut = Vt / RU;
+  const uint32_t R0 = RU * (uint32_t)((uint64_t)Ut * blockIdx.x / gridDim.x);  // work rows [R0, R1)
   const uint32_t R1 = RU * (uint32_t)((uint64_t)Ut * (blockIdx.x + 1) / gridDim.x);
 
   if (tid == 0) {
     // this CTA's flat ranges, gate pieces before up pieces for SwiGLU
     uint32_t n = 0, pieces = 0;
     for (uint32_t p = 0; p < nparts; p++) {
-      const uint32_t nsg = swig ? 1u : (uint32_t)P.nseg;
       for (uint32_t g = 0; g < nsg; g++) {
         const uint32_t si = swig ? p : g;
-        const uint32_t S0 = swig ? 0u : P.row_start[g], S1 = swig ? Rt : P.row_start[g + 1];
-        const uint32_t a = R0 > S0 ? R0 : S0, b = R1 < S1 ? R1 : S1;
-        if (a >= b) continue;
+        const uint32_t S0 = swig ? 0u : P.row_start[g];
+        const uint32_t va = R0 > cst(g) ? R0 : cst(g), vb = R1 < cst(g + 1) ? R1 : cst(g + 1);
+        if (va >= vb) continue;
+        const uint32_t a = S0 + (va - cst(g)), b = S0 + (vb - cst(g));  // rows of the call
         FlatRange r;
         r.src = si;
         r.part = p;
@@ -276,7 +285,7 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
         if (r.fb0 <= r.fa0) continue;
         r.k0 = r.fa0 / WPP;
         r.pstart = pieces;
-        r.lrbase = (int32_t)S0 - (int32_t)R0 - (int32_t)row0;
+        r.lrbase = (int32_t)cst(g) - (int32_t)R0 - (int32_t)row0;  // tensor row + lrbase = work row - R0
         r.pad = 0;
         rg[n++] = r;
         pieces += (r.fb0 - 1) / WPP - r.k0 + 1;
@@ -909,22 +918,16 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
   // ---- epilogue: rows of this CTA -----------------------------------------
   unsigned long long lbest = 0ull;
   uint32_t lfin = 1u;
-  const uint32_t nrows = R1 - R0;
-  for (uint32_t lr = tid; lr < nrows; lr += NCT) {
-    float d0 = 0.f, d1 = 0.f;
-#pragma unroll
-    for (uint32_t w = 0; w < NWR; w++) d0 += wacc[w * P.rpc + lr];
-    if constexpr (FMT == FMT_I8RAW) d0 *= 0.00373708f;  // raw int8 dot scale (chpe_engine.zig:1236)
-    if (swig) {
-#pragma unroll
-      for (uint32_t w = 0; w < NWR; w++) d1 += wacc[(NWR + w) * P.rpc + lr];
-      if constexpr (FMT == FMT_I8RAW) d1 *= 0.00373708f;
-      tp_put(P.tp, P.out[0], R0 + lr, silu_ref(d0) * d1);
-      continue;
+  // output row gr (of the call) of segment seg from its sums (SwiGLU: gate d0, up d1)
+  auto emit = [&](uint32_t seg, uint32_t gr, float d0, float d1) {
+    if constexpr (FMT == FMT_I8RAW) {  // raw int8 dot scale (chpe_engine.zig:1236)
+      d0 *= 0.00373708f;
+      d1 *= 0.00373708f;
     }
-    const uint32_t gr = R0 + lr;
-    uint32_t seg = 0;
-    while ((int)seg + 1 < P.nseg && gr >= P.row_start[seg + 1]) seg++;
+    if (swig) {
+      tp_put(P.tp, P.out[0], gr, silu_ref(d0) * d1);
+      return;
+    }
     const uint32_t r = gr - P.row_start[seg];
     const GemvSrc& s = P.src[seg];
     float* y = P.out[seg];
@@ -945,6 +948,35 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
       tp_put(P.tp, y, r, v);
     } else {
       tp_put(P.tp, y, r, s.bias ? d0 + s.bias[r] : d0);
+    }
+  };
+  const uint32_t nrows = R1 - R0;
+  for (uint32_t lr = tid; lr < nrows; lr += NCT) {
+    float d0 = 0.f, d1 = 0.f;
+#pragma unroll
+    for (uint32_t w = 0; w < NWR; w++) d0 += wacc[w * P.rpc + lr];
+    if (swig) {
+#pragma unroll
+      for (uint32_t w = 0; w < NWR; w++) d1 += wacc[(NWR + w) * P.rpc + lr];
+    }
+    const uint32_t v = R0 + lr;
+    uint32_t g = 0;
+    while (g + 1 < nsg && v >= cst(g + 1)) g++;
+    emit(swig ? 0u : g, (swig ? 0u : P.row_start[g]) + (v - cst(g)), d0, d1);
+  }
+  if (Vt < Rt) {
+    // rows past the tiles: zero sums, every CTA a share
+    for (uint32_t u = blockIdx.x * NCT + tid; u < Rt - Vt; u += gridDim.x * NCT) {
+      uint32_t g = 0, ub = 0;  // uncovered rows before segment g
+      for (;;) {
+        const uint32_t S0 = swig ? 0u : P.row_start[g], S1 = swig ? Rt : P.row_start[g + 1];
+        const uint32_t un = (S1 - S0) - (cst(g + 1) - cst(g));
+        if (u < ub + un || g + 1 >= nsg) break;
+        ub += un;
+        g++;
+      }
+      const uint32_t S0 = swig ? 0u : P.row_start[g];
+      emit(swig ? 0u : g, S0 + (cst(g + 1) - cst(g)) + (u - ub), 0.f, 0.f);
     }
   }
   if (P.epi == EPI_LOGITS) {
