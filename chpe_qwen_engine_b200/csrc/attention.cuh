@@ -13,6 +13,8 @@
 // that CTA) merges the splits: lanes over splits for the max and the sum,
 // lanes over head_dim for the weighted values.
 #pragma once
+#include <cstdlib>
+
 #include "device_common.cuh"
 
 namespace chpe {
@@ -59,6 +61,11 @@ constexpr int kAttnSplits = 16;
 constexpr int kAttnMaxSplits = 64;
 static_assert(kAttnMaxSplits <= 64, "attention merge holds at most 64 split weights");
 inline int attn_splits(int num_sms, int kv_heads, int max_seq) {
+  // CHPE_ATTN_SPLITS=n (1..64) fixes the count (measurements)
+  if (const char* e = getenv("CHPE_ATTN_SPLITS")) {
+    const int f = atoi(e);
+    if (f >= 1 && f <= kAttnMaxSplits) return f;
+  }
   int n = 2 * num_sms / (kv_heads > 0 ? kv_heads : 1);
   const int tiles = (max_seq + ATT_TT - 1) / ATT_TT;  // more splits than tiles only idle
   if (n > tiles) n = tiles;
