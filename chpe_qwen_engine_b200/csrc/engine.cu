@@ -945,21 +945,25 @@ void Engine::add_linear_ops(std::vector<Op>& ops, const GemvSrc* src_in, float* 
       }
     }
     t.nw = nw;
-    // Column owners: rows of 384..960 chunks (384..480 for 64-weight chunks,
-    // so that at least 4/5 of the first slots are busy) that do not start at
-    // cell boundaries, no fused norm (the down projections: 924 chunks on the
-    // 72B, 384 on the 9B; the 3B's 344 measured faster in the stream mode).
-    // x sits in registers, so the ring takes the shared memory x would have
-    // used.  CHPE_FLAT_COLOWN=0 keeps such calls on the stream mode.
+    // Column owners: rows that do not start at cell boundaries with 384..960
+    // 16-byte chunks (32 weights each; 384..480 for 64-weight chunks), so
+    // that at least 4/5 of the first slots are busy (the down projections:
+    // 924 chunks on the 72B, 384 on the 9B; the 3B's 344 measured faster in
+    // the stream mode), or FP16/BF16 rows of 384..1440 chunks of 8 weights
+    // with or without the fused norm (the 72B FP16 projections of 8192
+    // columns; the stream mode's per-piece reduction over 16 weights per
+    // lane held them near 2 TB/s).  x sits in registers, so the ring takes
+    // the shared memory x would have used.  CHPE_FLAT_COLOWN=0 keeps such
+    // calls on the stream mode.
     t.mode = rc ? FLAT_ALIGNED : FLAT_STREAM;
     {
-      const uint32_t ncc = ncols / cw, sl = cw <= 32 ? 2u : 1u, lanes = kFlatColownWarps * 32u;
+      const uint32_t ncc = ncols / cw, sl = cw <= 8 ? 3u : cw <= 32 ? 2u : 1u, lanes = kFlatColownWarps * 32u;
       const char* co = getenv("CHPE_FLAT_COLOWN");
       const bool on = !(co && co[0] == '0');
       const uint32_t fixed_co = flat_layout(ncols, cw, t.rpc, nparts, 0, kFlatColownWarps, false).total;
       uint32_t nst_co = kFlatSmemLimit > fixed_co ? (kFlatSmemLimit - fixed_co) / kFlatStageBytes : 0u;
       if (nst_co > kFlatStagesWanted) nst_co = kFlatStagesWanted;
-      if (on && !rc && !gamma && 5u * ncc >= 4u * lanes && ncc <= sl * lanes && nst_co >= 6) {
+      if (on && !rc && (!gamma || cw <= 8) && 5u * ncc >= 4u * lanes && ncc <= sl * lanes && nst_co >= 6) {
         t.mode = FLAT_COLOWN;
         t.nw = kFlatColownWarps;
         op.threads = (int)kFlatColownThreads;

@@ -391,7 +391,29 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
       for (uint32_t i = tid; i < kMmaSlots; i += NCT) reinterpret_cast<uint32_t*>(fsm + lay.bc)[i] = 0u;
     }
     if (MODE == FLAT_COLOWN) {
-      // column owners load their x chunks into registers in the main loop
+      // column owners load their x chunks into registers in the main loop;
+      // with the fused RMSNorm the sum of squares of x comes first (every
+      // chunk of the row is one lane's slot)
+      if (P.norm) {
+        float ss = 0.f;
+        for (uint32_t q = tid; q < nq; q += NCT) {
+          const float4 v = x4[q];
+          ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        }
+        ss = warp_sum(ss);
+        if (L == 0) sred[warp] = ss;
+        consumer_sync<NCT>();
+        for (uint32_t w = 0; w < NW; w++) tot += sred[w];
+        if (P.check_layer >= 0) {
+          // end-of-layer check of the reference's debug block (chpe_engine.zig:1753-1764)
+          const int l = P.check_layer;
+          const bool cond = l < 3 || (l >= 8 && l <= 16) || !isfinite(P.x[0]);
+          if (cond && !isfinite(tot)) {
+            if (blockIdx.x == 0 && tid == 0) P.st->stop = 1;
+            if (tid == 0) s_abort = 1;
+          }
+        }
+      }
     } else if (!P.norm) {
       // all loads of a batch in flight before any is stored
       for (uint32_t q0 = 0; q0 < nq; q0 += NCT * 8u) {
@@ -719,12 +741,13 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
     // in the row, and four consecutive rows per iteration share one 4-value
     // butterfly.
     const uint32_t NCC = C / CW;                         // chunks per row
-    constexpr uint32_t SL = CW <= 32 ? 2u : 1u;           // slots per lane
+    constexpr uint32_t SL = CW <= 8 ? 3u : CW <= 32 ? 2u : 1u;  // slots per lane
     constexpr uint32_t RI = 4;                            // rows per iteration
     f2x xr[SL][CW / 2];
     float xsj[SL];
     uint32_t scw[SL];                                     // first column of the slot
     bool act[SL];
+    const float inv = P.norm ? 1.0f / sqrtf(tot / (float)C + P.eps) : 1.0f;
 #pragma unroll
     for (uint32_t j = 0; j < SL; j++) {
       const uint32_t u = tid + NCT * j;
@@ -734,6 +757,18 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
       float4 t4[QPC];
 #pragma unroll
       for (uint32_t q = 0; q < QPC; q++) t4[q] = act[j] ? xp[q] : make_float4(0.f, 0.f, 0.f, 0.f);
+      if (P.norm) {  // x * inv * gamma, as the staged path normalises it
+        const float4* gp = reinterpret_cast<const float4*>(P.gamma + scw[j]);
+#pragma unroll
+        for (uint32_t q = 0; q < QPC; q++) {
+          const float4 gm = act[j] ? gp[q] : make_float4(0.f, 0.f, 0.f, 0.f);
+          t4[q].x = t4[q].x * inv * gm.x;
+          t4[q].y = t4[q].y * inv * gm.y;
+          t4[q].z = t4[q].z * inv * gm.z;
+          t4[q].w = t4[q].w * inv * gm.w;
+          if (P.xn_out && blockIdx.x == 0 && act[j]) reinterpret_cast<float4*>(P.xn_out + scw[j])[q] = t4[q];
+        }
+      }
       float sx = 0.f;
 #pragma unroll
       for (uint32_t q = 0; q < QPC; q++) {
