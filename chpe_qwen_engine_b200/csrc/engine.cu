@@ -963,8 +963,17 @@ void Engine::add_linear_ops(std::vector<Op>& ops, const GemvSrc* src_in, float* 
       const uint32_t fixed_co = flat_layout(ncols, cw, t.rpc, nparts, 0, kFlatColownWarps, false).total;
       uint32_t nst_co = kFlatSmemLimit > fixed_co ? (kFlatSmemLimit - fixed_co) / kFlatStageBytes : 0u;
       if (nst_co > kFlatStagesWanted) nst_co = kFlatStagesWanted;
-      if (on && !rc && (!gamma || cw <= 8) && 5u * ncc >= 4u * lanes && ncc <= sl * lanes && nst_co >= 6) {
-        t.mode = FLAT_COLOWN;
+      // wider FP16 / BF16 rows: eight slots per lane (x in as many registers
+      // as two slots of 32-weight chunks)
+      const bool wide = op.kind == SRC_RAW && (op.fmt == FMT_F16 || op.fmt == FMT_BF16) && ncc > sl * lanes &&
+                        ncc <= 8u * lanes;
+      // the ring holds every piece of the rows one iteration decodes (4, or 2
+      // in the eight-slot mode)
+      const uint64_t span = (uint64_t)(wide ? 2u : 4u) * ncols * (uint64_t)fmt_bits(op.fmt) / 8u;
+      const bool fits = (span + 16383u) / 16384u + 1u <= nst_co;
+      if (on && fits && !rc && (!gamma || cw <= 8) && 5u * ncc >= 4u * lanes && (ncc <= sl * lanes || wide) &&
+          nst_co >= 6) {
+        t.mode = wide ? FLAT_COLOWN8 : FLAT_COLOWN;
         t.nw = kFlatColownWarps;
         op.threads = (int)kFlatColownThreads;
         nst = nst_co;
@@ -982,7 +991,7 @@ void Engine::add_linear_ops(std::vector<Op>& ops, const GemvSrc* src_in, float* 
     }
     if (nst >= 2) {
       t.nst = nst;
-      op.smem = flat_layout(ncols, cw, t.rpc, nparts, nst, t.nw, t.mode != FLAT_COLOWN).total;
+      op.smem = flat_layout(ncols, cw, t.rpc, nparts, nst, t.nw, t.mode != FLAT_COLOWN && t.mode != FLAT_COLOWN8).total;
       op.grid = dim3(G);
       ops.push_back(op);
       for (int i = 0; i < nseg; i++) push_aux(src[i], epi == EPI_SWIGLU ? nullptr : out[i], gamma ? d_xn_ : x);
@@ -1528,7 +1537,7 @@ static void launch_flat_t(const Op& op, cudaStream_t s) {
       return;
     }
   }
-  constexpr int NWT = MODE == FLAT_COLOWN ? (int)kFlatColownWarps : 16;
+  constexpr int NWT = MODE == FLAT_COLOWN || MODE == FLAT_COLOWN8 ? (int)kFlatColownWarps : 16;
   auto k = gemv_flat_tma_kernel<FMT, KIND, MODE, NWT>;
   static bool configured = false;
   if (!configured) {
@@ -1578,6 +1587,11 @@ static void launch_flat(const Op& op, cudaStream_t s) {
       case FMT_F16: return launch_flat_t<FMT_F16, SRC_RAW, FLAT_COLOWN>(op, s);
       case FMT_BF16: return launch_flat_t<FMT_BF16, SRC_RAW, FLAT_COLOWN>(op, s);
       case FMT_I8RAW: return launch_flat_t<FMT_I8RAW, SRC_RAW, FLAT_COLOWN>(op, s);
+    }
+  } else if (op.kind == SRC_RAW && op.fl.mode == FLAT_COLOWN8) {
+    switch (op.fmt) {
+      case FMT_F16: return launch_flat_t<FMT_F16, SRC_RAW, FLAT_COLOWN8>(op, s);
+      case FMT_BF16: return launch_flat_t<FMT_BF16, SRC_RAW, FLAT_COLOWN8>(op, s);
     }
   } else if (op.kind == SRC_FLAT) {
     switch (op.fmt) {
@@ -1652,6 +1666,7 @@ std::string Engine::role_kernel_name(int role) const {
         return std::string(op.fl.mode == FLAT_ALIGNED
                                ? (op.fl.nw == 8 ? "gemv_flat_tma_kernel[aligned, 2 CTAs/SM]" : "gemv_flat_tma_kernel[aligned]")
                            : op.fl.mode == FLAT_COLOWN ? "gemv_flat_tma_kernel[column owners]"
+                           : op.fl.mode == FLAT_COLOWN8 ? "gemv_flat_tma_kernel[column owners, 8 slots]"
                                                        : "gemv_flat_tma_kernel") + fk;
       case OP_TMA: return "gemv_tma_kernel" + fk;
       case OP_GEMV: return "gemv_kernel" + fk;

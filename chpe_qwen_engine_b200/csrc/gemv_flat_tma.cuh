@@ -170,7 +170,9 @@ CHPE_DEV void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(NCT) : "mem
 // CW) of rows t / (cols / CW) + k * (256 / (cols / CW)): its x stays in
 // registers for the whole launch and shared memory carries only codes.
 // ROWBLK: the tensor-core kernel of gemv_rowblk.cuh (same launch record).
-enum FlatMode : int { FLAT_STREAM = 0, FLAT_ALIGNED = 1, FLAT_COLOWN = 2, FLAT_MMA = 3, FLAT_ROWBLK = 4 };
+// COLOWN8: column owners with eight slots per lane, for FP16 / BF16 rows of
+// 1441..3840 chunks (the 72B FP16 down projection, 3696).
+enum FlatMode : int { FLAT_STREAM = 0, FLAT_ALIGNED = 1, FLAT_COLOWN = 2, FLAT_MMA = 3, FLAT_ROWBLK = 4, FLAT_COLOWN8 = 5 };
 
 // MMA (aligned 4-bit group-scaled cells of 4096 or 8192 columns, every
 // segment a whole number of 16-row blocks): the products go through
@@ -216,13 +218,15 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
   constexpr uint32_t WPP = flat_wpp<FMT, KIND>();
   constexpr uint32_t NCH = WPP / CW;        // chunks in a full piece
   constexpr uint32_t NW = NWT, NCT = NWT * 32;
-  static_assert(MODE == FLAT_COLOWN ? NWT == (int)kFlatColownWarps : (NWT == 16 || (NWT == 8 && MODE == FLAT_ALIGNED)),
+  constexpr bool COLW = MODE == FLAT_COLOWN || MODE == FLAT_COLOWN8;  // column owners
+  static_assert(MODE != FLAT_COLOWN8 || FI::CW <= 8, "eight slots: chunks of 8 weights");
+  static_assert(COLW ? NWT == (int)kFlatColownWarps : (NWT == 16 || (NWT == 8 && MODE == FLAT_ALIGNED)),
                 "consumer warps: 16; 8 for aligned cells at two CTAs per SM; 15 for column owners");
   static_assert(MODE != FLAT_MMA || (FMT == FMT_W4G && KIND == SRC_FLAT && NWT == (int)kFlatConsumerWarps),
                 "MMA mode: 4-bit group-scaled flat cells, 16 consumer warps");
   constexpr uint32_t CPWARP = NCH / NW;     // chunks per consumer warp
   constexpr uint32_t CPL = CPWARP / 32;     // chunks per lane
-  static_assert(MODE == FLAT_COLOWN || (CPL >= 1 && CPWARP % 32 == 0), "piece geometry");
+  static_assert(COLW || (CPL >= 1 && CPWARP % 32 == 0), "piece geometry");
   constexpr bool MMA = MODE == FLAT_MMA;
   constexpr uint32_t NWR = MMA ? 1u : NW;   // per-row partial slots in wacc
   static_assert(NCH * 16 <= 16384, "a piece fits a stage");
@@ -232,7 +236,7 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
   const bool swig = P.epi == EPI_SWIGLU;
   const uint32_t nparts = swig ? 2u : 1u;
   const uint32_t C = P.ncols, nst = P.nst;
-  constexpr bool XSM = MODE != FLAT_COLOWN && !MMA;  // x staged in shared memory as f32
+  constexpr bool XSM = !COLW && !MMA;  // x staged in shared memory as f32
   const FlatLayout lay = MMA ? flat_layout_mma(C, P.rpc, nparts, nst) : flat_layout(C, CW, P.rpc, nparts, nst, NW, XSM);
   float* xsh = reinterpret_cast<float*>(fsm + lay.x);
   float* xsc = reinterpret_cast<float*>(fsm + lay.xs);
@@ -390,7 +394,7 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
     if constexpr (MMA) {
       for (uint32_t i = tid; i < kMmaSlots; i += NCT) reinterpret_cast<uint32_t*>(fsm + lay.bc)[i] = 0u;
     }
-    if (MODE == FLAT_COLOWN) {
+    if (COLW) {
       // column owners load their x chunks into registers in the main loop;
       // with the fused RMSNorm the sum of squares of x comes first (every
       // chunk of the row is one lane's slot)
@@ -734,15 +738,17 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
         phb ^= 1u;
       }
     }
-  } else if constexpr (MODE == FLAT_COLOWN) {
+  } else if constexpr (COLW) {
     // ---- main loop, column owners ------------------------------------------
     // One row per group (the host sends rows of 384..960 chunks for 16-byte
     // chunks of 32 weights, 384..480 for 64): every active slot of a lane lies
     // in the row, and four consecutive rows per iteration share one 4-value
     // butterfly.
     const uint32_t NCC = C / CW;                         // chunks per row
-    constexpr uint32_t SL = CW <= 8 ? 3u : CW <= 32 ? 2u : 1u;  // slots per lane
-    constexpr uint32_t RI = 4;                            // rows per iteration
+    constexpr uint32_t SL = MODE == FLAT_COLOWN8 ? 8u : CW <= 8 ? 3u : CW <= 32 ? 2u : 1u;  // slots per lane
+    // rows per iteration: the ring must hold every piece of them at once
+    // (two rows of up to 30720 FP16 weights: at most 9 pieces)
+    constexpr uint32_t RI = MODE == FLAT_COLOWN8 ? 2u : 4u;
     f2x xr[SL][CW / 2];
     float xsj[SL];
     uint32_t scw[SL];                                     // first column of the slot
@@ -843,15 +849,23 @@ __global__ void __launch_bounds__(NWT * 32 + 32, NWT == 8 ? 2 : 1)
           }
           (void)bi;
         }
+        // the RI row sums in one butterfly: lane (32 / RI) * rr holds row g0 + rr
         const bool h16 = (L & 16u) != 0, h8 = (L & 8u) != 0;
-        const float a0 = (h16 ? vrow[2] : vrow[0]) + __shfl_xor_sync(0xffffffffu, h16 ? vrow[0] : vrow[2], 16);
-        const float a1 = (h16 ? vrow[3] : vrow[1]) + __shfl_xor_sync(0xffffffffu, h16 ? vrow[1] : vrow[3], 16);
-        float bsum = (h8 ? a1 : a0) + __shfl_xor_sync(0xffffffffu, h8 ? a0 : a1, 8);
+        float bsum;
+        if constexpr (RI == 4) {
+          const float a0 = (h16 ? vrow[2] : vrow[0]) + __shfl_xor_sync(0xffffffffu, h16 ? vrow[0] : vrow[2], 16);
+          const float a1 = (h16 ? vrow[3] : vrow[1]) + __shfl_xor_sync(0xffffffffu, h16 ? vrow[1] : vrow[3], 16);
+          bsum = (h8 ? a1 : a0) + __shfl_xor_sync(0xffffffffu, h8 ? a0 : a1, 8);
+        } else {
+          (void)h8;
+          bsum = (h16 ? vrow[1] : vrow[0]) + __shfl_xor_sync(0xffffffffu, h16 ? vrow[0] : vrow[1], 16);
+          bsum += __shfl_xor_sync(0xffffffffu, bsum, 8);
+        }
         bsum += __shfl_xor_sync(0xffffffffu, bsum, 4);
         bsum += __shfl_xor_sync(0xffffffffu, bsum, 2);
         bsum += __shfl_xor_sync(0xffffffffu, bsum, 1);
-        if ((L & 7u) == 0u) {  // lane 8*rr holds row g0 + rr
-          const uint32_t row = g0 + (L >> 3);
+        if ((L & (32u / RI - 1u)) == 0u) {
+          const uint32_t row = g0 + L / (32u / RI);
           if (row < g1) wacc[(rgv.part * NW + warp) * P.rpc + (uint32_t)((int32_t)row + rgv.lrbase)] += bsum;
         }
         // pieces wholly before the next group's first weight are done
