@@ -804,11 +804,14 @@ void Engine::add_linear_ops(std::vector<Op>& ops, const GemvSrc* src_in, float* 
     // width divides 32768 into 32..256 column chunks, every segment a whole
     // number of cells.
     uint32_t rc = 0;
+    // Raw FP16 / BF16 / int8 streams the same, with their 16 KiB tiles as cells.
     {
       const uint32_t cw = (uint32_t)fmt_cw(op.fmt);
-      bool al = op.kind == SRC_FLAT && 32768u % ncols == 0 && (ncols / cw) % 32u == 0 &&
+      const bool raw_ok = op.kind == SRC_RAW && (op.fmt == FMT_F16 || op.fmt == FMT_BF16 || op.fmt == FMT_I8RAW);
+      const uint32_t wpp = op.kind == SRC_FLAT ? 32768u : 16384u * 8u / (uint32_t)fmt_bits(op.fmt);
+      bool al = (op.kind == SRC_FLAT || raw_ok) && wpp % ncols == 0 && (ncols / cw) % 32u == 0 &&
                 ncols / cw <= kFlatConsumers && kFlatConsumers % (ncols / cw) == 0 && !getenv("CHPE_NO_ALIGNED");
-      const uint32_t cell_rows = 32768u / ncols;
+      const uint32_t cell_rows = wpp / ncols;
       for (int i = 0; i < nseg && al; i++)
         al = src[i].r_total % cell_rows == 0 && src[i].row0 % cell_rows == 0;
       if (al) rc = cell_rows;
@@ -935,7 +938,9 @@ void Engine::add_linear_ops(std::vector<Op>& ops, const GemvSrc* src_in, float* 
     uint32_t nw = 16, G8 = 0, rpc8 = 0, nst8 = 0;
     {
       const char* one = getenv("CHPE_FLAT_ONE_CTA");
-      if (rc && !(one && one[0] == '1') && (!gamma || ncols <= 8192)) {
+      // (8 warps: a row's chunks must fit the 256 consumer lanes)
+      const uint32_t ncpr = ncols / (uint32_t)fmt_cw(op.fmt);
+      if (rc && !(one && one[0] == '1') && (!gamma || ncols <= 8192) && ncpr <= 256u && 256u % ncpr == 0) {
         G8 = Ut < 2u * (uint32_t)num_sms_ ? Ut : 2u * (uint32_t)num_sms_;
         rpc8 = RU * ((Ut + G8 - 1) / G8);
         const uint32_t f8 = flat_layout(ncols, cw, rpc8, nparts, 0, 8).total;
@@ -1574,6 +1579,12 @@ static void launch_flat(const Op& op, cudaStream_t s) {
       case FMT_W4SB: return launch_flat_t<FMT_W4SB, SRC_FLAT, FLAT_ALIGNED>(op, s);
       case FMT_W2G: return launch_flat_t<FMT_W2G, SRC_FLAT, FLAT_ALIGNED>(op, s);
       case FMT_W2SB: return launch_flat_t<FMT_W2SB, SRC_FLAT, FLAT_ALIGNED>(op, s);
+    }
+  } else if (op.kind == SRC_RAW && op.fl.mode == FLAT_ALIGNED) {
+    switch (op.fmt) {
+      case FMT_F16: return launch_flat_t<FMT_F16, SRC_RAW, FLAT_ALIGNED>(op, s);
+      case FMT_BF16: return launch_flat_t<FMT_BF16, SRC_RAW, FLAT_ALIGNED>(op, s);
+      case FMT_I8RAW: return launch_flat_t<FMT_I8RAW, SRC_RAW, FLAT_ALIGNED>(op, s);
     }
   } else if (op.kind == SRC_FLAT && op.fl.mode == FLAT_COLOWN) {
     switch (op.fmt) {
