@@ -61,6 +61,7 @@ SYMBOLS = [
     ("chpe_tp_export_handle", _I, [_P, C.c_char_p]),
     ("chpe_tp_connect", _I, [_P, C.c_char_p, _I]),
     ("chpe_tp_slice", _I, [_I, _I, _I, _U32P]),
+    ("chpe_tp_tile_runs", _I64, [_I, _I, _U64, _U64, _I, _I, C.POINTER(C.c_uint64), _S]),
     ("chpe_step_weight_bytes", C.c_double, [_P]),
     ("chpe_profile_step", _I, [_P, _FP, C.POINTER(C.c_int), _I]),
     ("chpe_verify", _I, [_P, _U32P, C.c_size_t, C.c_uint32, _FP, _U32P]),
@@ -180,6 +181,18 @@ def tp_slice(arch: int, rank: int, world: int) -> dict:
         raise ValueError(f"architecture {arch} does not split over {world} ranks")
     keys = ("hq", "h0", "kv0", "kvl", "dl", "d0", "fl", "f0", "vl", "v0")
     return {k: int(v) for k, v in zip(keys, out)}
+
+
+def tp_tile_runs(arch: int, is_raw: bool, wpt: int, record_count: int, rank: int,
+                 world: int) -> list[tuple[int, int]]:
+    """Archive tiles one tensor-parallel rank uploads (chpe_tp_tile_runs), as
+    disjoint ascending runs [lo, hi); no GPU needed."""
+    n = lib().chpe_tp_tile_runs(arch, int(is_raw), wpt, record_count, rank, world, None, 0)
+    if n < 0:
+        raise ValueError(f"architecture {arch} does not split over {world} ranks")
+    out = (C.c_uint64 * (2 * n))()
+    lib().chpe_tp_tile_runs(arch, int(is_raw), wpt, record_count, rank, world, out, n)
+    return [(int(out[2 * i]), int(out[2 * i + 1])) for i in range(n)]
 
 
 class Engine:

@@ -1,6 +1,8 @@
 /* chpe_maps.c -- see chpe_maps.h for the reference sources restated here. */
 #include "chpe_maps.h"
 
+#include <stdlib.h>
+
 static const ChpeArch PRESETS[3] = {
     /* chpe_engine.zig:110-145 */
     {"Qwen2.5-3B", 2048, 11008, 36, 16, 2, 128, 151936, 0, 1000000.0f, 1e-6f},
@@ -126,4 +128,97 @@ int chpe_tp_slice_of(int arch, int rank, int world, ChpeTpSlice *out) {
   s.v0 = R * s.vl;
   *out = s;
   return 0;
+}
+
+/* Tile runs of a tensor-parallel rank.  A flat GEMV over rows [r0, r0+n) of
+ * a tensor with C columns starting at tile `start` reads the weights
+ * [r0*C, (r0+n)*C) of its flat index, i.e. the tiles
+ * start + floor(r0*C/wpt) .. start + ceil((r0+n)*C/wpt) - 1, never past the
+ * tensor's own tile count (codes and their group scales live in the same
+ * record).  The embedding lookup reads record tok/rows_per_tile and up to two
+ * records past the table (the reference's over-reads), so the embedding
+ * records and two more are taken whole.  Norms and biases are read on the
+ * host and take no device tiles. */
+typedef struct {
+  uint64_t lo, hi;
+} TileSpan;
+
+static int span_cmp(const void *a, const void *b) {
+  const TileSpan *x = (const TileSpan *)a, *y = (const TileSpan *)b;
+  if (x->lo != y->lo) return x->lo < y->lo ? -1 : 1;
+  if (x->hi != y->hi) return x->hi < y->hi ? -1 : 1;
+  return 0;
+}
+
+typedef struct {
+  TileSpan *v;
+  size_t n;
+  uint64_t rc;
+} SpanList;
+
+static void span_add(SpanList *s, uint64_t lo, uint64_t hi) {
+  if (lo >= s->rc) return;
+  if (hi > s->rc) hi = s->rc;
+  if (hi > lo) {
+    s->v[s->n].lo = lo;
+    s->v[s->n].hi = hi;
+    s->n++;
+  }
+}
+
+static void span_rows(SpanList *s, int64_t start, int64_t tiles, uint64_t r0, uint64_t n,
+                      uint64_t C, uint64_t wpt) {
+  if (start < 0) return;
+  const uint64_t lo = (uint64_t)start + r0 * C / wpt;
+  const uint64_t hi = (uint64_t)start + ((r0 + n) * C + wpt - 1) / wpt;
+  const uint64_t end = (uint64_t)start + (uint64_t)tiles;
+  span_add(s, lo, hi < end ? hi : end);
+}
+
+int64_t chpe_tp_tile_runs(int arch, int is_raw, uint64_t wpt, uint64_t record_count, int rank,
+                          int world, uint64_t *runs, size_t cap) {
+  const ChpeArch *A = chpe_arch_preset(arch);
+  ChpeTpSlice sl;
+  if (!A || wpt == 0 || chpe_tp_slice_of(arch, rank, world, &sl) != 0) return -1;
+  SpanList s;
+  s.n = 0;
+  s.rc = record_count;
+  s.v = (TileSpan *)malloc(sizeof(TileSpan) * (2 + 7 * (size_t)A->L));
+  if (!s.v) return -1;
+  {
+    const uint64_t rows_per_tile = is_raw ? (wpt / A->D ? wpt / A->D : 1) : 16;
+    span_add(&s, 0, (A->V + rows_per_tile - 1) / rows_per_tile + 2);
+  }
+  for (uint32_t l = 0; l < A->L; l++) {
+    ChpeLayerInfo li;
+    chpe_layer_info(arch, is_raw, l, &li);
+    span_rows(&s, li.q_proj, li.q_tiles, (uint64_t)sl.h0 * A->HD, (uint64_t)sl.hq * A->HD, A->D, wpt);
+    span_rows(&s, li.k_proj, li.k_tiles, (uint64_t)sl.kv0 * A->HD, (uint64_t)sl.kvl * A->HD, A->D, wpt);
+    span_rows(&s, li.v_proj, li.v_tiles, (uint64_t)sl.kv0 * A->HD, (uint64_t)sl.kvl * A->HD, A->D, wpt);
+    span_rows(&s, li.o_proj, li.o_tiles, sl.d0, sl.dl, A->D, wpt);
+    span_rows(&s, li.gate_proj, li.gate_tiles, sl.f0, sl.fl, A->D, wpt);
+    span_rows(&s, li.up_proj, li.up_tiles, sl.f0, sl.fl, A->D, wpt);
+    span_rows(&s, li.down_proj, li.down_tiles, sl.d0, sl.dl, A->F, wpt);
+  }
+  {
+    int64_t lhs, lht;
+    chpe_lm_head_span(arch, &lhs, &lht);
+    span_rows(&s, lhs, lht, sl.v0, sl.vl, A->D, wpt);
+  }
+  qsort(s.v, s.n, sizeof(TileSpan), span_cmp);
+  /* merge overlapping and touching spans into runs */
+  size_t nr = 0;
+  for (size_t i = 0; i < s.n; i++) {
+    if (nr > 0 && s.v[i].lo <= s.v[nr - 1].hi) {
+      if (s.v[i].hi > s.v[nr - 1].hi) s.v[nr - 1].hi = s.v[i].hi;
+    } else {
+      s.v[nr++] = s.v[i];
+    }
+  }
+  for (size_t i = 0; i < nr && i < cap && runs; i++) {
+    runs[2 * i] = s.v[i].lo;
+    runs[2 * i + 1] = s.v[i].hi;
+  }
+  free(s.v);
+  return (int64_t)nr;
 }

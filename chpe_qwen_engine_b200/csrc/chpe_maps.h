@@ -70,6 +70,13 @@ typedef struct {
 const ChpeArch *chpe_arch_preset(int arch);
 /* 0, or -1 when the architecture does not split over `world` ranks. */
 int chpe_tp_slice_of(int arch, int rank, int world, ChpeTpSlice *out);
+/* The archive tiles a tensor-parallel rank's kernels read, merged into
+ * disjoint runs [lo, hi) in ascending order (runs[2i], runs[2i+1]; at most
+ * `cap` written).  wpt = weights per tile of the archive's projections,
+ * record_count bounds every run.  Returns the number of runs, or -1 when the
+ * architecture does not split over `world`. */
+int64_t chpe_tp_tile_runs(int arch, int is_raw, uint64_t wpt, uint64_t record_count, int rank,
+                          int world, uint64_t *runs, size_t cap);
 void chpe_layer_info(int arch, int is_raw, size_t l, ChpeLayerInfo *out);
 void chpe_9b_extra(size_t l, Chpe9bExtra *out);
 int64_t chpe_final_norm_index(int arch, int is_raw);

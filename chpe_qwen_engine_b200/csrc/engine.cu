@@ -195,61 +195,20 @@ void Engine::upload_archive(const uint8_t* bytes, uint64_t len) {
   dev_arc_bytes_ = len;
 }
 
-// Tensor parallelism: the tiles this rank's kernels read.  The embedding
-// lookups read the record tok/16 (or tok/rows-per-tile of a raw archive)
-// and a little past it (the reference's over-reads), so the embedding
-// records and two more are taken whole; each projection contributes the
-// tiles of its row slice.  Norms and biases are read on the host.
+// Tensor parallelism: the tiles this rank's kernels read (chpe_tp_tile_runs:
+// the embedding records and two more, and every projection's row slice),
+// one allocation per run.  Norms and biases are read on the host.
 void Engine::upload_shards(const uint8_t* bytes, uint64_t len) {
-  const ChpeArch& A = *arch_;
-  ChpeTpSlice sl;
-  if (chpe_tp_slice_of(arch_id_, tp_rank_, tp_world_, &sl) != 0) {
+  const uint64_t rc = f_.record_count, wpt = f_.is_raw ? f_.wpt : 32768ull;
+  const int64_t nr = chpe_tp_tile_runs(arch_id_, f_.is_raw, wpt, rc, tp_rank_, tp_world_, nullptr, 0);
+  if (nr < 0) {
     upload_archive(bytes, len);  // the step builder reports the unsplittable shape
     return;
   }
-  const uint64_t rc = f_.record_count, wpt = f_.is_raw ? f_.wpt : 32768ull;
-  std::vector<std::pair<uint64_t, uint64_t>> want;
-  auto add = [&](uint64_t lo, uint64_t hi) {
-    if (lo >= rc) return;
-    if (hi > rc) hi = rc;
-    if (hi > lo) want.push_back({lo, hi});
-  };
-  {
-    const uint64_t rows_per_tile = f_.is_raw ? (wpt / A.D ? wpt / A.D : 1) : 16;
-    add(0, (A.V + rows_per_tile - 1) / rows_per_tile + 2);
-  }
-  auto slice = [&](int64_t start, int64_t tiles, uint32_t r0, uint32_t n, uint32_t C) {
-    if (start < 0) return;
-    const uint64_t lo = (uint64_t)start + (uint64_t)r0 * C / wpt;
-    const uint64_t hi = (uint64_t)start + ((uint64_t)(r0 + n) * C + wpt - 1) / wpt;
-    const uint64_t end = (uint64_t)start + (uint64_t)tiles;
-    add(lo, hi < end ? hi : end);
-  };
-  for (uint32_t l = 0; l < A.L; l++) {
-    ChpeLayerInfo li;
-    chpe_layer_info(arch_id_, f_.is_raw, l, &li);
-    slice(li.q_proj, li.q_tiles, sl.h0 * A.HD, sl.hq * A.HD, A.D);
-    slice(li.k_proj, li.k_tiles, sl.kv0 * A.HD, sl.kvl * A.HD, A.D);
-    slice(li.v_proj, li.v_tiles, sl.kv0 * A.HD, sl.kvl * A.HD, A.D);
-    slice(li.o_proj, li.o_tiles, sl.d0, sl.dl, A.D);
-    slice(li.gate_proj, li.gate_tiles, sl.f0, sl.fl, A.D);
-    slice(li.up_proj, li.up_tiles, sl.f0, sl.fl, A.D);
-    slice(li.down_proj, li.down_tiles, sl.d0, sl.dl, A.F);
-  }
-  {
-    int64_t lhs, lht;
-    chpe_lm_head_span(arch_id_, &lhs, &lht);
-    slice(lhs, lht, sl.v0, sl.vl, A.D);
-  }
-  std::sort(want.begin(), want.end());
+  std::vector<uint64_t> rv(2 * (size_t)nr);
+  chpe_tp_tile_runs(arch_id_, f_.is_raw, wpt, rc, tp_rank_, tp_world_, rv.data(), (size_t)nr);
   std::vector<std::pair<uint64_t, uint64_t>> runs;
-  for (const auto& w : want) {
-    if (!runs.empty() && w.first <= runs.back().second) {
-      if (w.second > runs.back().second) runs.back().second = w.second;
-    } else {
-      runs.push_back(w);
-    }
-  }
+  for (int64_t i = 0; i < nr; i++) runs.push_back({rv[2 * i], rv[2 * i + 1]});
   const uint64_t pad = 1ull << 20;
   for (const auto& r : runs) {
     const uint64_t off = 4096 + r.first * f_.stride;

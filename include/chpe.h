@@ -101,6 +101,14 @@ int chpe_tp_connect(void *ctx, const uint8_t *handles, int world);
  * rows (count, first), vocabulary rows (count, first).  0, or -1 when the
  * architecture does not split evenly over `world`. */
 int chpe_tp_slice(int arch, int rank, int world, uint32_t out[10]);
+/* The archive tiles (records) one rank uploads and its kernels read, merged
+ * into disjoint ascending runs [lo, hi): runs[2i] = lo, runs[2i+1] = hi, at
+ * most `cap` runs written (no GPU needed).  wpt = weights per tile (32768 for
+ * cell archives, 16384 for int8 raw tiles, 8192 for FP16/BF16 raw tiles),
+ * record_count = the archive's record count.  Returns the number of runs, or -1 when the architecture does
+ * not split evenly over `world`. */
+int64_t chpe_tp_tile_runs(int arch, int is_raw, uint64_t wpt, uint64_t record_count, int rank,
+                          int world, uint64_t *runs, size_t cap);
 
 /* WeightArchive.validate (weight_archive.zig:152-172): 0 when valid, else the
  * error: 1 InvalidMagic, 2 UnsupportedVersion, 3 BadGeometry, 4 Truncated,

@@ -1,5 +1,5 @@
-"""Tensor-parallel host logic without a GPU, on gloo ranks (world size 2 and
-4, 127.0.0.1): every rank computes its slices with chpe_tp_slice (the
+"""Tensor-parallel host logic without a GPU, on gloo ranks (world size 2, 4
+and 8, 127.0.0.1): every rank computes its slices with chpe_tp_slice (the
 function the engine's tensor-parallel step uses), the ranks all-gather them,
 and together they must tile the query heads, the hidden, FFN and vocabulary
 rows exactly once, with every query head's kv head owned by its rank.  The
@@ -74,7 +74,7 @@ def _covers(parts, total):
     assert pos == total
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_tp_slices_tile_every_dimension(world):
     slices, handles = _run(world)
     assert handles == [bytes([r]) * 64 for r in range(world)]
@@ -101,3 +101,81 @@ def test_tp_slice_rejects_uneven_splits():
     assert (s["hq"], s["h0"], s["kv0"], s["kvl"]) == (8, 56, 7, 1)
     s = chpe.tp_slice(chpe.ARCH_9B, 5, 8)  # 2 query heads of kv group 2 (4 per group)
     assert (s["hq"], s["h0"], s["kv0"], s["kvl"]) == (2, 10, 2, 1)
+
+
+# Sharded loading: the tiles one rank uploads (chpe_tp_tile_runs, the function
+# the engine's loader calls) against what its kernels read, derived here from
+# the oracle's tensor maps (getLayerInfo, chpe_engine.zig:1035-1142) and the
+# untied LM head spans (qwen35_tensor_map.zig LM_HEAD_TILE, qwen72b_tensor_map.zig
+# LM_HEAD_RECORD_START).  A flat GEMV over rows [r0, r0+n) with C columns from
+# tile `start` reads tiles start + r0*C // 32768 .. ceil((r0+n)*C / 32768),
+# never past the tensor's own tiles.
+TOTAL = {chpe.ARCH_9B: 546681, chpe.ARCH_72B: 2219153}
+LM_HEAD = {chpe.ARCH_9B: (484601, 62080), chpe.ARCH_72B: (2181137, 38016)}
+HEAD_DIM = {chpe.ARCH_9B: 256, chpe.ARCH_72B: 128}
+LAYERS = {chpe.ARCH_9B: 32, chpe.ARCH_72B: 80}
+
+
+def _reads(start, tiles, r0, n, C, wpt=32768):
+    if start < 0:
+        return None
+    hi = min(start + -(-(r0 + n) * C // wpt), start + tiles)
+    return (start + r0 * C // wpt, hi)
+
+
+def _needed(arch, layers, s):
+    D, F, H, KV, V = ARCHS[arch]
+    HD = HEAD_DIM[arch]
+    out = [(0, -(-V // 16) + 2)]  # embedding records and two past them
+    for li in layers:
+        out += [_reads(li["q_proj"], li["q_tiles"], s["h0"] * HD, s["hq"] * HD, D),
+                _reads(li["k_proj"], li["k_tiles"], s["kv0"] * HD, s["kvl"] * HD, D),
+                _reads(li["v_proj"], li["v_tiles"], s["kv0"] * HD, s["kvl"] * HD, D),
+                _reads(li["o_proj"], li["o_tiles"], s["d0"], s["dl"], D),
+                _reads(li["gate_proj"], li["gate_tiles"], s["f0"], s["fl"], D),
+                _reads(li["up_proj"], li["up_tiles"], s["f0"], s["fl"], D),
+                _reads(li["down_proj"], li["down_tiles"], s["d0"], s["dl"], F)]
+    out.append(_reads(*LM_HEAD[arch], s["v0"], s["vl"], D))
+    return [r for r in out if r is not None and r[1] > r[0]]
+
+
+@pytest.mark.parametrize("arch", [chpe.ARCH_9B, chpe.ARCH_72B])
+def test_tp_tile_runs_hold_every_slice(arch):
+    import bisect
+
+    import numpy as np
+    import oracle_py as O
+    total = TOTAL[arch]
+    e = O.OracleEngine(np.zeros(8192, np.uint8), arch, 4)  # maps only; no archive bytes read
+    layers = [e.layer_info(l) for l in range(LAYERS[arch])]
+    D, F, H, KV, V = ARCHS[arch]
+    whole = {"hq": H, "h0": 0, "kv0": 0, "kvl": KV, "dl": D, "d0": 0, "fl": F, "f0": 0, "vl": V, "v0": 0}
+    for world in (2, 4, 8):
+        union = np.zeros(total, bool)
+        for rank in range(world):
+            runs = chpe.tp_tile_runs(arch, False, 32768, total, rank, world)
+            assert runs and all(0 <= lo < hi <= total for lo, hi in runs)
+            assert all(a[1] < b[0] for a, b in zip(runs, runs[1:])), "runs disjoint, ascending, merged"
+            los = [lo for lo, _ in runs]
+            for lo, hi in _needed(arch, layers, chpe.tp_slice(arch, rank, world)):
+                i = bisect.bisect_right(los, lo) - 1
+                assert i >= 0 and runs[i][0] <= lo and hi <= runs[i][1], (world, rank, lo, hi)
+            held = sum(hi - lo for lo, hi in runs)
+            embed = -(-V // 16) + 2
+            # a rank holds the embedding plus about 1/world of the rest
+            assert held <= embed + (total - embed) / world * 1.05 + 8 * len(layers), (world, rank, held)
+            for lo, hi in runs:
+                union[lo:hi] = True
+        # together the ranks hold everything one GPU's kernels read
+        for lo, hi in _needed(arch, layers, whole):
+            assert union[lo:hi].all(), (world, lo, hi)
+    # a rank of the 9B at 2 ranks uploads under 60 % of the archive (the
+    # tensor-parallel GPU test checks the same bound on the device)
+    if arch == chpe.ARCH_9B:
+        held = sum(hi - lo for lo, hi in chpe.tp_tile_runs(arch, False, 32768, total, 0, 2))
+        assert held < 0.6 * total
+
+
+def test_tp_tile_runs_rejects_uneven_splits():
+    with pytest.raises(ValueError):
+        chpe.tp_tile_runs(chpe.ARCH_72B, False, 32768, TOTAL[chpe.ARCH_72B], 0, 3)
