@@ -1,6 +1,7 @@
 """The C-ABI library loads and exports every symbol include/chpe.h declares;
 host-only semantics that need no GPU (NULL handling, validation, path and
-init failures).  No compute call is made here."""
+init failures, and the engine's refusal to start without a usable GPU).  No
+compute call is made here."""
 import ctypes as C
 import os
 import re
@@ -88,3 +89,24 @@ def test_init_rejects_invalid_file(tmp_path):
     p.write_bytes(bytes(8192))
     assert chpe.lib().chpe_init(str(p).encode()) is None
     assert b"validation" in chpe.lib().chpe_last_error(None)
+
+
+def _gpu_present() -> bool:
+    try:
+        import torch
+        return torch.cuda.is_available()
+    except Exception:
+        return False
+
+
+@pytest.mark.skipif(_gpu_present(), reason="checks the failure without a usable GPU")
+def test_engine_without_gpu_fails_loudly():
+    """No CPU fallback: without a usable GPU the engine (the mock archive the
+    reference's own test uses, chpe_engine.zig:1893-1933) refuses to start,
+    with the CUDA error in the message and through chpe_last_error."""
+    with pytest.raises(chpe.ChpeError, match="cuda|CUDA"):
+        chpe.Engine.from_bytes(np.zeros(8192, np.uint8), chpe.ARCH_3B, 16)
+    buf = np.zeros(8192, np.uint8)
+    ctx = chpe.lib().chpe_init_bytes(buf.ctypes.data, buf.size, chpe.ARCH_3B, 16, 0)
+    assert ctx is None
+    assert b"CUDA" in chpe.lib().chpe_last_error(None) or b"cuda" in chpe.lib().chpe_last_error(None)
