@@ -3,7 +3,8 @@ the oracle's restatement, byte for byte: standard records -> dense cells,
 -> raw tiles, -> raw FP16 tiles (BF16 rounded to FP16 on the GPU, 1-D cells
 copied verbatim).  The archives are small and hand-built: random bytes, so
 every BF16 class occurs (zeros, subnormals, values that overflow FP16, ties,
-infinities, NaNs), and some cells marked quant_bits 32 (1-D data)."""
+infinities, NaNs), and some cells marked quant_bits 32 (1-D data).  The
+dense and raw conversions need no GPU and also run in the CPU suite."""
 import struct
 
 import numpy as np
@@ -76,6 +77,22 @@ def test_convert_matches_oracle(tmp_path, mode):
         for i in range(0, N_REC, 97):
             assert np.array_equal(got[4096 + i * 16384:4096 + (i + 1) * 16384],
                                   O.convert_record(raw, chpe.CONVERT_RAW_FP16, i)), i
+
+
+@pytest.mark.parametrize("mode", [chpe.CONVERT_DENSE, chpe.CONVERT_RAW])
+def test_convert_host_modes(tmp_path, mode):
+    """The dense and raw conversions are byte copies on the host (no GPU
+    needed): byte for byte against the oracle, and a raw source refused for
+    the dense conversion (it holds no cells)."""
+    src = _standard_archive(np.random.default_rng(40 + mode))
+    sp = tmp_path / "src.chpe"
+    src.tofile(sp)
+    dp = tmp_path / "dst.chpe"
+    chpe.convert_archive(str(sp), str(dp), mode)
+    _check(dp, src, mode)
+    if mode == chpe.CONVERT_RAW:
+        with pytest.raises(chpe.ChpeError, match="raw archive"):
+            chpe.convert_archive(str(dp), str(tmp_path / "d.chpe"), chpe.CONVERT_DENSE)
 
 
 def test_convert_rejects_bad_input(tmp_path):
