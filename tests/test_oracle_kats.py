@@ -225,3 +225,40 @@ def test_deltanet_step_matches_transformers_golden():
         assert np.max(np.abs(out - ref)) <= 2e-5 * max(1.0, float(np.max(np.abs(ref)))), s
     assert np.array_equal(hist, g["hist_end"])
     assert np.max(np.abs(state - g["state_end"])) <= 1e-5 * max(1.0, float(np.max(np.abs(g["state_end"]))))
+
+
+def _defines(path: str) -> dict:
+    import re
+    out = {}
+    for m in re.finditer(r"^#define\s+(\w+)\s+(\d+)u?\b", open(path).read(), re.M):
+        out[m.group(1)] = int(m.group(2))
+    return out
+
+
+# geometry.zig:431-443 "cell is cache-line aligned and record is sector
+# aligned" / "the 4.25 ratio", :483-499 "cell struct matches 17,408 bytes" /
+# "record struct matches 20,480 bytes"; weight_archive.zig:897-910
+# "WeightArchiveHeader layout" / "TileMetadata layout fits in semantic payload"
+def test_archive_layout_constants_match_reference_tests():
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    prod = _defines(os.path.join(root, "chpe_qwen_engine_b200", "csrc", "chpe_maps.h"))
+    orac = _defines(os.path.join(root, "oracle", "chpe_oracle.c"))
+    cell, record, prefetch, header, tile = 17408, 20480, 3072, 4096, 16384
+    payload_off, payload_bytes, cell_header = 16448, 960, 64
+    assert cell % 64 == 0 and cell // 64 == 272 and record // 4096 == 5 and cell % 4096 != 0
+    assert cell + prefetch == record and cell_header + tile + payload_bytes == cell
+    assert cell_header + tile == payload_off
+    for d, names in ((prod, ("CHPE_CELL_BYTES", "CHPE_RECORD_BYTES", "CHPE_PREFETCH_BYTES",
+                             "CHPE_HEADER_BYTES", "CHPE_TILE_CODE_BYTES", "CHPE_PAYLOAD_OFF")),
+                     (orac, ("CELL_BYTES", "RECORD_BYTES", "PREFETCH_LABEL_BYTES", "HEADER_BYTES",
+                             "TILE_CODE_BYTES", "PAYLOAD_OFF"))):
+        assert [d[n] for n in names] == [cell, record, prefetch, header, tile, payload_off], names
+    assert prod["CHPE_CELL_HEADER_BYTES"] == cell_header
+    assert prod["CHPE_PAYLOAD_FROM_CODES"] == tile
+    # TileMetadata is 32 bytes at the payload start (quant_bits u8 @20,
+    # custom_flags u64 @24); TileDims follows at @32 and the group scales at @48
+    assert 32 <= payload_bytes and 48 + 2 * 256 <= payload_bytes
+    c = make_cell(4, flags=1, scale=0.5, bias=0.25, rows=16, cols=2048)
+    assert c[payload_off + 20] == 4
+    assert struct.unpack("<Q", c[payload_off + 24:payload_off + 32].tobytes())[0] == 1
+    assert struct.unpack("<ffII", c[payload_off + 32:payload_off + 48].tobytes()) == (0.5, 0.25, 16, 2048)
