@@ -262,3 +262,42 @@ def test_archive_layout_constants_match_reference_tests():
     assert c[payload_off + 20] == 4
     assert struct.unpack("<Q", c[payload_off + 24:payload_off + 32].tobytes())[0] == 1
     assert struct.unpack("<ffII", c[payload_off + 32:payload_off + 48].tobytes()) == (0.5, 0.25, 16, 2048)
+
+
+# weight_archive.zig:912-1007 "createArchive, mmap open, record slicing":
+# three standard records with known patterns, flags 0x1234; the file is
+# 4096 + 3 * 20480 = 65536 bytes, its header reads back, and each record's
+# cell, code tile and TileMetadata sit at the offsets the engine reads
+def test_created_archive_reads_back():
+    import chpe_qwen_engine_b200 as chpe
+    recs = np.zeros((3, 20480), np.uint8)
+    for i in range(3):
+        recs[i, :16] = 0xA0 + i                                          # prefetch seal
+        recs[i, 3072:3080] = np.frombuffer(struct.pack("<Q", 0x100 + i), np.uint8)  # bytecode opcode
+        for fp in range(32):                                             # fingerprint words
+            o = 3072 + 64 + fp * 512
+            recs[i, o:o + 4] = np.frombuffer(struct.pack("<I", 0xCAFE0000 + i), np.uint8)
+        pl = 3072 + 16448                                                # TileMetadata
+        recs[i, pl:pl + 32] = np.frombuffer(struct.pack("<IIQIB3xQ", i, 10 + i, 17408 * (i + 1), 4, 4, 0x55AA),
+                                            np.uint8)
+    hdr = np.zeros(4096, np.uint8)
+    hdr[:64] = np.frombuffer(struct.pack("<IIQQQQQQQ", 0x57415243, 1, 4096, 3, 3, 20480, 17408, 3072, 0x1234),
+                             np.uint8)
+    a = np.concatenate([hdr, recs.reshape(-1)])
+    assert a.size == 65536
+    rc, h = O.validate(a)
+    assert rc == 0 and chpe.validate_archive(a) == 0
+    assert (h.record_count, h.record_bytes, h.cell_bytes, h.prefetch_bytes, h.flags) == (3, 20480, 17408, 3072,
+                                                                                         0x1234)
+    f = O.OracleEngine(a, O.ARCH_3B, 4).facts()
+    assert (f["archive_valid"], f["record_count"], f["is_dense"], f["is_raw"], f["quant_bits"]) == (1, 3, 0, 0, 4)
+    for i in range(3):
+        rec = a[4096 + i * 20480:4096 + (i + 1) * 20480]
+        cell = rec[3072:]
+        assert rec[0] == 0xA0 + i
+        assert struct.unpack("<Q", cell[:8].tobytes())[0] == 0x100 + i
+        assert struct.unpack("<I", cell[64:68].tobytes())[0] == 0xCAFE0000 + i
+        meta = struct.unpack("<IIQIB3xQ", cell[16448:16480].tobytes())
+        assert meta == (i, 10 + i, 17408 * (i + 1), 4, 4, 0x55AA)
+    # a file that holds fewer records than its header promises is refused
+    assert O.validate(a[:65536 - 1])[0] == chpe.validate_archive(a[:65536 - 1]) != 0
