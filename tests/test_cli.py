@@ -1,9 +1,11 @@
 """The chpe_fwd command line (the reference's src/main.zig contract): flags,
 raw u32 tokens file, raw f32 logits of the last token, receipt lines.  The
-CPU tests run only what needs no GPU (help, argument errors); the GPU test
+CPU tests run only what needs no GPU (help, argument errors, the architecture
+rule, the prompt limit); the GPU test
 decodes a synthetic archive and checks the logits file against the oracle."""
 import os
 import re
+import struct
 import subprocess
 
 import numpy as np
@@ -34,6 +36,33 @@ def test_cli_help_and_missing_archive(tmp_path):
     arc.write_bytes(b"\0" * 64)
     r = subprocess.run([_cli(), str(arc), "--tokens-file", str(toks)], capture_output=True, text=True)
     assert r.returncode == 1 and "EmptyTokensFile" in r.stderr
+
+
+@pytest.mark.parametrize("name,override,want", [
+    ("Qwen2.5-3B.w2.chpe", None, "Qwen2.5-3B"),
+    ("Qwen3.5-9B.w4.chpe", None, "Qwen3.5-9B"),
+    ("qwen35.w4.chpe", None, "Qwen3.5-9B"),
+    ("qwen2.5-72b.w4.chpe", None, "Qwen2.5-72B"),
+    ("Qwen2.5-3B.w2.chpe", "qwen2_5_72b", "Qwen2.5-72B"),
+    ("Qwen2.5-72B.chpe", "qwen3_5_9b", "Qwen3.5-9B"),
+])
+def test_cli_arch_rule_and_prompt_limit(tmp_path, name, override, want):
+    """src/main.zig:86-106: --arch wins, else the archive path's substring
+    picks the model; a prompt longer than --max-seq-len is refused before any
+    GPU work; the receipt lines report the archive's record count."""
+    arc = tmp_path / name
+    hdr = struct.pack("<IIQQQQQQQ", 0x57415243, 1, 4096, 7, 7, 20480, 17408, 3072, 0)
+    arc.write_bytes(hdr + b"\0" * (4096 - len(hdr)))
+    toks = tmp_path / "p.bin"
+    np.arange(5, dtype="<u4").tofile(toks)
+    cmd = [_cli(), str(arc), "--tokens-file", str(toks), "--max-seq-len", "4"]
+    if override:
+        cmd += ["--arch", override]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    assert r.returncode == 1
+    assert f"Model Arch     : {want} " in r.stderr
+    assert "7 tiles" in r.stderr
+    assert "Loaded 5 tokens" in r.stderr and "5 tokens exceed --max-seq-len 4" in r.stderr
 
 
 @pytest.mark.gpu
