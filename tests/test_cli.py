@@ -1,8 +1,8 @@
 """The chpe_fwd command line (the reference's src/main.zig contract): flags,
 raw u32 tokens file, raw f32 logits of the last token, receipt lines.  The
 CPU tests run only what needs no GPU (help, argument errors, the architecture
-rule, the prompt limit); the GPU test
-decodes a synthetic archive and checks the logits file against the oracle."""
+rule, the prompt limit); the GPU test decodes a synthetic archive and checks
+the logits file against the oracle."""
 import os
 import re
 import struct
