@@ -12,8 +12,13 @@
  * restatement is pinned by the known-answer tests found in the reference's
  * own unit tests (RoPE, SiLU, SwiGLU, RMSNorm, attention pass-through, the
  * 2/4/8-bit cell GEMV tests, the zero-byte mock archive forward pass, the
- * tensor-map index tests and the archive corruption tests); see
- * tests/test_oracle_kats.py.
+ * tensor-map index tests, the archive layout, create/reopen and corruption
+ * tests); see tests/test_oracle_kats.py.  Beyond those constant cases, three
+ * independent float64 restatements check it on random hand-built archives:
+ * every tile format of gemvLinear (tests/test_oracle_formats_cpu.py), the
+ * embedding lookup, tied LM head and norm/bias unpacking
+ * (tests/test_oracle_embed_cpu.py), and the composition of forwardDecode
+ * around its weight readers (tests/test_oracle_forward_cpu.py).
  *
  * Numerics follow the reference: f32 everywhere, 8-lane accumulators where
  * the reference uses @Vector(8, f32), fmaf() where it uses @mulAdd, ordered
