@@ -15,7 +15,9 @@ scales, outliers and replacement lists:
   (count <= 64, offsets below the tile), cells of other widths read as
   zeros, rows wrapping across cells and stopping at r_total;
 * raw tiles through dotSegment (:1194-1286): FP16, BF16 and INT8 (global
-  scale 0.00373708).
+  scale 0.00373708);
+* the archive converters (weight_archive.zig:617-776) on the byte level,
+  from standard, dense and raw sources.
 
 The oracle accumulates in f32 in the reference's order; the restatement sums
 in float64, so the comparison allows 2e-5 of the largest output."""
@@ -292,3 +294,69 @@ def test_raw_tiles(kind, c_total):
     for r in (r_total, max(1, r_total // 3)):
         want = _segments(weights, x, r, c_total, np.zeros(r), scale)
         _close(e.gemv_linear(0, n_tiles, x, r, c_total), want, f"{kind} rows {r}")
+
+
+# weight_archive.zig:617-776: convertToDensePosix, convertToRawContiguousPosix,
+# convertToRawFp16ContiguousPosix, restated on the byte level
+def _convert_header(src: np.ndarray, mode: int) -> np.ndarray:
+    out = np.zeros(4096, np.uint8)
+    out[:64] = src[:64]
+    put = lambda off, v: out.__setitem__(slice(off, off + 8), np.frombuffer(struct.pack("<Q", v), np.uint8))
+    if mode == 0:        # dense: record_bytes = cell bytes, no prefetch area
+        put(32, 17408)
+        put(48, 0)
+    else:                # raw: 16 KiB tiles of codes only
+        put(32, 16384)
+        put(40, 16384)
+        put(48, 0)
+        if mode == 2:
+            put(56, struct.unpack("<Q", src[56:64].tobytes())[0] | 0x04)
+    return out
+
+
+def _convert_record(src: np.ndarray, mode: int, i: int) -> np.ndarray:
+    count, rb, pb = (struct.unpack("<Q", src[o:o + 8].tobytes())[0] for o in (16, 32, 48))
+    raw = rb == 16384 and pb == 0
+    cell = 4096 + i * rb + pb
+    if mode == 0:
+        return src[cell:cell + 17408].copy()
+    tile = src[4096 + i * 16384:4096 + (i + 1) * 16384] if raw else src[cell + 64:cell + 64 + 16384]
+    if mode == 1:
+        return tile.copy()
+    one_d = (count == 376853 and (i == 376852 or (i >= 37984 and (i - 37984) % 9413 in (0, 513, 578, 643, 1156))))
+    one_d = one_d or (not raw and src[cell + 16448 + 20] == 32)
+    if one_d:
+        return tile.copy()
+    f = (tile.copy().view(np.uint16).astype(np.uint32) << 16).view(np.float32)
+    with np.errstate(over="ignore", invalid="ignore"):
+        return f.astype(np.float16).view(np.uint8)
+
+
+def test_converters_match_restatement():
+    rng = np.random.default_rng(31)
+    n = 40
+    for rb, pb in ((20480, 3072), (17408, 0), (16384, 0)):
+        recs = [rng.integers(0, 256, rb, dtype=np.uint8) for _ in range(n)]
+        if rb != 16384:
+            for i, r in enumerate(recs):   # quant_bits 32 (1-D) for every 5th cell, else 16
+                r[pb + 16448 + 20] = 32 if i % 5 == 0 else 16
+        hdr = np.zeros(4096, np.uint8)
+        hdr[:64] = np.frombuffer(struct.pack("<IIQQQQQQQ", 0x57415243, 1, 4096, n, n, rb,
+                                             16384 if rb == 16384 else 17408, pb, 0x10), np.uint8)
+        src = np.concatenate([hdr] + recs)
+        for mode in (0, 1, 2):
+            if mode == 0 and rb == 16384:
+                continue   # a raw archive holds no cells to keep
+            assert np.array_equal(O.convert_header(src, mode), _convert_header(src, mode)), (rb, mode)
+            for i in range(n):
+                got, want = O.convert_record(src, mode, i), _convert_record(src, mode, i)
+                if mode == 2 and got.size == 16384 and not np.array_equal(got, want):
+                    # NaN payloads: both NaN with the same sign; every other value exact
+                    g, w = got.view(np.uint16), want.view(np.uint16)
+                    nan = (w & 0x7C00) == 0x7C00
+                    nan &= (w & 0x3FF) != 0
+                    assert np.array_equal(g[~nan], w[~nan]), (rb, i)
+                    assert np.all(((g[nan] & 0x7C00) == 0x7C00) & ((g[nan] & 0x3FF) != 0))
+                    assert np.array_equal(g[nan] >> 15, w[nan] >> 15)
+                else:
+                    assert np.array_equal(got, want), (rb, mode, i)
