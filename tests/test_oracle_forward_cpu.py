@@ -12,11 +12,13 @@ head.  A mistake in the order of operations, in which buffer feeds which
 projection, in the GQA head mapping or the RoPE pairing would show as a
 difference far above f32 rounding."""
 import numpy as np
+import pytest
 
 import chpe_qwen_engine_b200 as chpe
 import oracle_py as O
 
-D, F, L, H, KV, HD, V = 2048, 11008, 36, 16, 2, 128, 151936
+# chpe_engine.zig:110-145: hidden, FFN, layers, query heads, kv heads, head dim
+DIMS = {O.ARCH_3B: (2048, 11008, 36, 16, 2, 128), O.ARCH_9B: (4096, 12288, 32, 16, 4, 256)}
 THETA, EPS = 1e6, 1e-6
 
 
@@ -25,32 +27,34 @@ def rms(x, g):
     return x / np.sqrt(np.mean(x * x) + EPS) * g.astype(np.float64)
 
 
-def rope(v, pos, heads):
-    v = v.astype(np.float64).reshape(heads, HD).copy()
-    i = np.arange(HD // 2, dtype=np.float64)
-    ang = pos * (1.0 / THETA ** (2.0 * i / HD))
+def rope(v, pos, heads, hd):
+    v = v.astype(np.float64).reshape(heads, hd).copy()
+    i = np.arange(hd // 2, dtype=np.float64)
+    ang = pos * (1.0 / THETA ** (2.0 * i / hd))
     c, s = np.cos(ang), np.sin(ang)
-    x0, x1 = v[:, :HD // 2].copy(), v[:, HD // 2:].copy()
-    v[:, :HD // 2] = x0 * c - x1 * s
-    v[:, HD // 2:] = x0 * s + x1 * c
+    x0, x1 = v[:, :hd // 2].copy(), v[:, hd // 2:].copy()
+    v[:, :hd // 2] = x0 * c - x1 * s
+    v[:, hd // 2:] = x0 * s + x1 * c
     return v.reshape(-1)
 
 
 class Composition:
     """forwardDecode in float64 around the oracle's weight readers."""
 
-    def __init__(self, e: O.OracleEngine, k0=None, v0=None):
+    def __init__(self, e: O.OracleEngine, arch: int, k0=None, v0=None):
         self.e = e
+        self.D, self.F, L, self.H, self.KV, self.HD = DIMS[arch]
         self.layers = [e.layer_info(l) for l in range(L)]
         # cached K/V rows [layer][position][kv_heads * head_dim]
-        self.kc = np.zeros((L, 0, KV * HD)) if k0 is None else k0.astype(np.float64)
-        self.vc = np.zeros((L, 0, KV * HD)) if v0 is None else v0.astype(np.float64)
+        w = self.KV * self.HD
+        self.kc = np.zeros((L, 0, w)) if k0 is None else k0.astype(np.float64)
+        self.vc = np.zeros((L, 0, w)) if v0 is None else v0.astype(np.float64)
 
     def lin(self, start, tiles, x, rows, cols, bias=-1):
         return self.e.gemv_linear(start, tiles, x.astype(np.float32), rows, cols, bias_tile=bias).astype(np.float64)
 
     def step(self, tok, pos):
-        e = self.e
+        e, D, F, H, KV, HD = self.e, self.D, self.F, self.H, self.KV, self.HD
         h = e.embed(tok).astype(np.float64)
         ks, vs = [], []
         for l, li in enumerate(self.layers):
@@ -58,7 +62,7 @@ class Composition:
             q = self.lin(li["q_proj"], li["q_tiles"], xn, H * HD, D, li["q_bias"])
             k = self.lin(li["k_proj"], li["k_tiles"], xn, KV * HD, D, li["k_bias"])
             v = self.lin(li["v_proj"], li["v_tiles"], xn, KV * HD, D, li["v_bias"])
-            q, k = rope(q, pos, H), rope(k, pos, KV)
+            q, k = rope(q, pos, H, HD), rope(k, pos, KV, HD)
             K = np.concatenate([self.kc[l], k[None]])  # positions 0..pos
             Vc = np.concatenate([self.vc[l], v[None]])
             ks.append(k)
@@ -92,22 +96,26 @@ def _compare(comp, ref, toks, pos0):
         assert abs(hnorm - r.hidden_norm) <= 2e-5 * r.hidden_norm, (pos0 + i, hnorm, r.hidden_norm)
 
 
-def test_forward_composition():
-    """The 3B FP16 raw archive with q/k/v biases (it behaves like a random
-    transformer: the residual stays near unit scale, so attention moves the
-    logits).  Three tokens from position 0, then two more after 24 cached
-    positions of seeded K/V rows loaded into both, where the attention
-    output dominates the residual: swapping the rotate-half pairing for an
-    interleaved one, or the two kv heads, moves the logits by more than their
-    own scale, against ~1e-5 here."""
-    a = chpe.synth_archive(chpe.SYNTH_3B_FP16_RAW, chpe.SYNTH_BIAS, seed=3)
-    ref = O.OracleEngine(a, O.ARCH_3B, 40, threads=8)
-    _compare(Composition(O.OracleEngine(a, O.ARCH_3B, 40, threads=8)), ref, [151644, 872, 9707], 0)
+@pytest.mark.parametrize("cfg,arch,vscale", [(chpe.SYNTH_3B_FP16_RAW, O.ARCH_3B, 3.0),
+                                              (chpe.SYNTH_9B_I8_RAW, O.ARCH_9B, 30.0)])
+def test_forward_composition(cfg, arch, vscale):
+    """Archives that behave like a random transformer (the residual stays
+    near unit scale, so attention moves the logits): 3B FP16 with q/k/v
+    biases, and the 9B INT8 raw archive (linear layers as GQA with v from one
+    tile, Q8; BF16 norms).  Three tokens from position 0, then two more after
+    24 cached positions of seeded K/V rows loaded into both, where the
+    attention output dominates the residual: swapping the rotate-half
+    pairing for an interleaved one, or the kv heads, moves the logits by more
+    than their own scale, against ~1e-5 here."""
+    a = chpe.synth_archive(cfg, chpe.SYNTH_BIAS if arch == O.ARCH_3B else 0, seed=3)
+    L, KV, HD = DIMS[arch][2], DIMS[arch][4], DIMS[arch][5]
+    ref = O.OracleEngine(a, arch, 40, threads=8)
+    _compare(Composition(O.OracleEngine(a, arch, 40, threads=8), arch), ref, [151644, 872, 9707], 0)
     P = 24
     rng = np.random.default_rng(9)
     k0 = (rng.standard_normal((L, P, KV * HD)) * 3.0).astype(np.float32)
-    v0 = (rng.standard_normal((L, P, KV * HD)) * 3.0).astype(np.float32)
-    ref = O.OracleEngine(a, O.ARCH_3B, 40, threads=8)
+    v0 = (rng.standard_normal((L, P, KV * HD)) * vscale).astype(np.float32)
+    ref = O.OracleEngine(a, arch, 40, threads=8)
     for l in range(L):
         ref.kv_load(l, 0, k0[l], v0[l])
-    _compare(Composition(O.OracleEngine(a, O.ARCH_3B, 40, threads=8), k0, v0), ref, [5, 77], P)
+    _compare(Composition(O.OracleEngine(a, arch, 40, threads=8), arch, k0, v0), ref, [5, 77], P)
