@@ -4,9 +4,15 @@ function the engine's tensor-parallel step uses), the ranks all-gather them,
 and together they must tile the query heads, the hidden, FFN and vocabulary
 rows exactly once, with every query head's kv head owned by its rank.  The
 IPC-handle exchange of Engine.tensor_parallel (all_gather_object over the
-default group) is exercised with stand-in 64-byte handles."""
+default group) is exercised with stand-in 64-byte handles.  The sharded
+loader's tile runs are checked against the oracle's tensor maps, and the
+sharded math itself runs on CPU ranks: row slices computed from each rank's
+tiles, exchanged by an all-gather, equal the unsharded oracle bit for bit;
+a rank that leaves or never arrives ends the exchange with an error."""
+import bisect
 import os
 import socket
+import struct
 
 import pytest
 import torch.distributed as dist
@@ -179,3 +185,183 @@ def test_tp_tile_runs_hold_every_slice(arch):
 def test_tp_tile_runs_rejects_uneven_splits():
     with pytest.raises(ValueError):
         chpe.tp_tile_runs(chpe.ARCH_72B, False, 32768, TOTAL[chpe.ARCH_72B], 0, 3)
+
+
+# ---- sharded math on CPU ranks ------------------------------------------------
+# Each gloo rank computes its row slice of every projection of two 9B layers
+# (a Q8 linear layer and a full-attention layer) from the tiles its sharded
+# loader would upload (chpe_tp_tile_runs), tile by tile in the reference's
+# order through the oracle's gemvCellFlat; an all-gather stands in for the
+# peer-memory exchange, and the gathered outputs must equal the unsharded
+# oracle's gemvLinear bit for bit (each output element is computed whole on
+# one rank with the same f32 arithmetic).  A rank that never arrives makes
+# the others' exchange end with an error within the group's timeout.
+LAYERS_9B = (0, 3)
+CELL9 = 17408
+
+
+def _sparse_9b_archive(path: str) -> None:
+    """A dense 9B-sized archive file whose only written records are random
+    4-bit group-scaled cells (some with down_aux replacements) at the tiles
+    of LAYERS_9B's projections and record 0; the rest are holes."""
+    import numpy as np
+    import oracle_py as O
+    total = TOTAL[chpe.ARCH_9B]
+    hdr = np.zeros(4096, np.uint8)
+    hdr[:64] = np.frombuffer(struct.pack("<IIQQQQQQQ", 0x57415243, 1, 4096, total, total, CELL9, CELL9, 0, 0),
+                             np.uint8)
+    e = O.OracleEngine(np.zeros(8192, np.uint8), O.ARCH_9B, 4)  # maps only
+    rng = np.random.default_rng(17)
+    tiles = {0}
+    for l in LAYERS_9B:
+        li = e.layer_info(l)
+        for p in ("q", "k", "v", "o", "gate", "up", "down"):
+            tiles.update(range(li[f"{p}_proj"], li[f"{p}_proj"] + li[f"{p}_tiles"]))
+    with open(path, "wb") as f:
+        f.truncate(4096 + total * CELL9)
+        f.write(hdr.tobytes())
+        for t in sorted(tiles):
+            c = np.zeros(CELL9, np.uint8)
+            c[64:64 + 16384] = rng.integers(0, 256, 16384, dtype=np.uint8)
+            pl = 16448
+            c[pl + 20] = 4
+            c[pl + 24] = 1  # group-128 scales
+            c[pl + 48:pl + 560] = np.abs(rng.normal(0, 0.01, 256)).astype(np.float16).view(np.uint8)
+            n = int(rng.integers(0, 5)) if t % 7 == 0 else 0
+            c[pl + 560:pl + 562] = np.frombuffer(struct.pack("<H", n), np.uint8)
+            c[pl + 562:pl + 562 + 2 * n] = rng.normal(0, 0.5, n).astype(np.float16).view(np.uint8)
+            c[pl + 690:pl + 690 + 2 * n] = rng.integers(0, 32768, n).astype(np.uint16).view(np.uint8)
+            f.seek(4096 + t * CELL9)
+            f.write(c.tobytes())
+
+
+def _projections(li, s, D, F, HD):
+    """(name, first tile, tiles, rank's first row, rows, all rows, columns)."""
+    return [("q", li["q_proj"], li["q_tiles"], s["h0"] * HD, s["hq"] * HD, 16 * HD, D),
+            ("k", li["k_proj"], li["k_tiles"], s["kv0"] * HD, s["kvl"] * HD, 4 * HD, D),
+            ("v", li["v_proj"], li["v_tiles"], s["kv0"] * HD, s["kvl"] * HD, 4 * HD, D),
+            ("o", li["o_proj"], li["o_tiles"], s["d0"], s["dl"], D, D),
+            ("gate", li["gate_proj"], li["gate_tiles"], s["f0"], s["fl"], F, D),
+            ("up", li["up_proj"], li["up_tiles"], s["f0"], s["fl"], F, D),
+            ("down", li["down_proj"], li["down_tiles"], s["d0"], s["dl"], D, F)]
+
+
+def _inputs(D, F):
+    import numpy as np
+    rng = np.random.default_rng(23)
+    return rng.standard_normal(D).astype(np.float32), rng.standard_normal(F).astype(np.float32)
+
+
+def _shard_worker(rank, world, port, path, skip_rank, skip_mode, timeout_s, q):
+    import time
+
+    import numpy as np
+    import oracle_py as O
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=__import__("datetime").timedelta(seconds=timeout_s))
+    try:
+        if rank == skip_rank:
+            # this rank never arrives at the exchange: it leaves the group at
+            # once ("exit"), or stays alive past the group's timeout ("stall")
+            if skip_mode == "stall":
+                time.sleep(timeout_s + 6)
+            return
+        D, F, HD = 4096, 12288, 256
+        a = np.memmap(path, dtype=np.uint8, mode="r")
+        e = O.OracleEngine(np.zeros(8192, np.uint8), O.ARCH_9B, 4)
+        s = chpe.tp_slice(chpe.ARCH_9B, rank, world)
+        runs = chpe.tp_tile_runs(chpe.ARCH_9B, False, 32768, TOTAL[chpe.ARCH_9B], rank, world)
+        los = [lo for lo, _ in runs]
+        xd, xf = _inputs(D, F)
+        mine, used = {}, 0
+        for l in LAYERS_9B:
+            for name, start, tiles, r0, n, rows, cols in _projections(e.layer_info(l), s, D, F, HD):
+                x = xf if cols == F else xd
+                y = np.zeros(rows, np.float32)
+                t_hi = min(-(-(r0 + n) * cols // 32768), tiles)
+                for t in range(r0 * cols // 32768, t_hi):
+                    g = start + t
+                    i = bisect.bisect_right(los, g) - 1
+                    assert i >= 0 and g < runs[i][1], ("tile outside this rank's upload", g)
+                    cell = np.asarray(a[4096 + g * CELL9:4096 + (g + 1) * CELL9])
+                    O.gemv_cell_flat(cell, t, rows, cols, x, y)
+                    used += 1
+                mine[(l, name)] = y[r0:r0 + n].copy()
+        out = [None] * world
+        dist.all_gather_object(out, (rank, mine, used))
+        if rank == 0:
+            q.put(("ok", out))
+    except Exception as ex:  # the exchange with a missing rank ends here
+        q.put(("error", rank, type(ex).__name__, str(ex)[:200]))
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
+
+
+def _run_shards(world, path, skip_rank=-1, skip_mode="exit", timeout_s=60):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_shard_worker, args=(r, world, port, path, skip_rank, skip_mode, timeout_s, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = q.get(timeout=300)
+    for p in procs:
+        p.join(timeout=120)
+    return res, [p.exitcode for p in procs]
+
+
+@pytest.fixture(scope="module")
+def sparse_9b(tmp_path_factory):
+    path = str(tmp_path_factory.mktemp("tp") / "sparse_9b.chpe")
+    _sparse_9b_archive(path)
+    return path
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_sharded_projections_equal_unsharded_oracle(sparse_9b, world):
+    import numpy as np
+    import oracle_py as O
+    res, codes = _run_shards(world, sparse_9b)
+    assert res[0] == "ok", res
+    assert codes == [0] * world
+    parts = sorted(res[1], key=lambda t: t[0])
+    a = np.memmap(sparse_9b, dtype=np.uint8, mode="r")
+    e = O.OracleEngine(a, O.ARCH_9B, 4, threads=8)
+    D, F, HD = 4096, 12288, 256
+    xd, xf = _inputs(D, F)
+    whole = chpe.tp_slice(chpe.ARCH_9B, 0, 1)
+    for l in LAYERS_9B:
+        for name, start, tiles, _, _, rows, cols in _projections(e.layer_info(l), whole, D, F, HD):
+            want = e.gemv_linear(start, tiles, xf if cols == F else xd, rows, cols)
+            got = np.concatenate([p[1][(l, name)] for p in parts])  # rank order = row order
+            assert np.array_equal(got, want), (l, name, float(np.max(np.abs(got - want))))
+    assert all(p[2] > 0 for p in parts)
+    # the ranks together read each needed tile about once (row slices split tiles only at their edges)
+    assert sum(p[2] for p in parts) < 1.01 * _run_tiles_needed(e) + 2 * world * 7 * len(LAYERS_9B)
+
+
+def _run_tiles_needed(e) -> int:
+    n = 0
+    for l in LAYERS_9B:
+        for _, start, tiles, _, _, rows, cols in _projections(e.layer_info(l), chpe.tp_slice(chpe.ARCH_9B, 0, 1),
+                                                              4096, 12288, 256):
+            n += min(-(-rows * cols // 32768), tiles)
+    return n
+
+
+@pytest.mark.parametrize("mode", ["exit", "stall"])
+def test_missing_rank_ends_the_exchange_with_an_error(sparse_9b, mode):
+    """A rank that leaves, or one that never arrives, makes rank 0's
+    exchange raise (connection closed, or the group's 8 s timeout) instead
+    of waiting for good; every process then exits normally."""
+    import time
+    t0 = time.time()
+    res, codes = _run_shards(2, sparse_9b, skip_rank=1, skip_mode=mode, timeout_s=8)
+    assert res[0] == "error" and res[1] == 0, res
+    assert codes == [0, 0] and time.time() - t0 < 120
