@@ -306,13 +306,17 @@ def _run_shards(world, path, skip_rank=-1, skip_mode="exit", timeout_s=60):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_shard_worker, args=(r, world, port, path, skip_rank, skip_mode, timeout_s, q))
-             for r in range(world)]
+    procs = [ctx.Process(target=_shard_worker, args=(r, world, port, path, skip_rank, skip_mode, timeout_s, q),
+                         daemon=True) for r in range(world)]
     for p in procs:
         p.start()
-    res = q.get(timeout=300)
-    for p in procs:
-        p.join(timeout=120)
+    try:
+        res = q.get(timeout=300)
+    finally:
+        for p in procs:  # the processes this call started, by handle
+            p.join(timeout=120)
+            if p.is_alive():
+                p.terminate()
     return res, [p.exitcode for p in procs]
 
 
